@@ -1,0 +1,227 @@
+/*
+ * gcdr_cuda.h -- C ABI of the B200 (sm_100a) CUDA backend for GCDRNet
+ * document enhancement (u8 image -> GC-Net -> division correction ->
+ * DR-Net -> u8 image).
+ *
+ * The library is the drop-in for the `GcdrBackend.Cuda` arm of the
+ * reference's `GcdrEnhancer` (src/Sdcb.SimdGcdrNet/GcdrEnhancer.cs).  Two
+ * levels are exported, mirroring the reference's own two levels:
+ *
+ *   gcdr_enhancer_*  the public, thread-safe enhancer
+ *                    (GcdrEnhancer.FromBytes / Enhance / PoolStats / Dispose,
+ *                    GcdrEnhancer.cs:82-100, 181-271, 67-68, 325-331):
+ *                    argument validation, top/left pad to /32, a pool of
+ *                    workers rented per call, retry-once on device loss.
+ *   gcdr_cuda_*      one worker: a CUDA stream, a device arena and one
+ *                    CUDA graph per padded shape; NOT thread-safe
+ *                    (the VkGcdrPipeline contract,
+ *                    Backends/Vulkan/VkPipeline2.cs:21-379).
+ *
+ * Plain pointers and sizes only.  Source and destination images are HOST
+ * memory in the caller's layout (any row stride, dst may alias src when the
+ * strides are equal).  Pixel formats carry the values of GcdrPixelFormat
+ * (GcdrPixelFormat.cs:7-17).  Every entry point returns a GCDR_* status; on
+ * failure *_last_error() gives a message.
+ */
+#ifndef GCDR_CUDA_H
+#define GCDR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define GCDR_API __declspec(dllexport)
+#else
+#define GCDR_API __attribute__((visibility("default")))
+#endif
+
+/* Status codes.  The reference throws; the mapping is:
+ *   GCDR_ERR_RANGE       ArgumentOutOfRangeException (width/height < 1, stride
+ *                        < width*bpp, unknown pixel format; GcdrEnhancer.cs:184-188,
+ *                        GcdrPixelFormat.cs:21-26)
+ *   GCDR_ERR_ARG         ArgumentException (short buffers, GcdrEnhancer.cs:189-192),
+ *                        ArgumentNullException (null model streams, :97-98)
+ *   GCDR_ERR_UNSUPPORTED NotSupportedException (model graph not the GCDRNet
+ *                        topology, GC output shape mismatch, :249-250)
+ *   GCDR_ERR_DEVICE      VkDeviceLostException analogue: the CUDA context
+ *                        reported an error; the enhancer retries once on a
+ *                        fresh worker pool (GcdrEnhancer.cs:218-222)
+ *   GCDR_ERR_TIMEOUT     a device-side bounded wait expired (the kernel gave
+ *                        up and returned instead of hanging)
+ *   GCDR_ERR_OOM         device or pinned host allocation failed
+ *   GCDR_ERR_MODEL       the ONNX bytes could not be parsed
+ */
+#define GCDR_OK 0
+#define GCDR_ERR_ARG 1
+#define GCDR_ERR_RANGE 2
+#define GCDR_ERR_UNSUPPORTED 3
+#define GCDR_ERR_DEVICE 4
+#define GCDR_ERR_TIMEOUT 5
+#define GCDR_ERR_OOM 6
+#define GCDR_ERR_MODEL 7
+
+/* GcdrPixelFormat (GcdrPixelFormat.cs:7-17) */
+#define GCDR_BGR24 0
+#define GCDR_RGB24 1
+#define GCDR_BGRA32 2
+#define GCDR_RGBA32 3
+
+/* precision: the tensor-core layers' operand/storage type.  The stem conv,
+ * the head (UpHead) and the division glue always run in fp32. */
+#define GCDR_PRECISION_FP16 0
+
+typedef struct gcdr_model gcdr_model;       /* parsed GC-Net + DR-Net weights */
+typedef struct gcdr_cuda gcdr_cuda;         /* one worker (not thread-safe)   */
+typedef struct gcdr_enhancer gcdr_enhancer; /* thread-safe pooled enhancer    */
+
+/* ---------------------------------------------------------------- models */
+
+/* Parses both ONNX models and checks that each is the GCDRNet UNeXt
+ * topology.  Replaces OnnxModel.Load (GcdrEnhancer.cs:84,91,99) plus the part
+ * of GraphCompiler.Compile + the GCDR fusion passes that this backend needs
+ * (Extensions/GcdrExtensions.cs:12-15: FuseShiftPass, FuseUpHeadPass,
+ * UpHeadSkipRecomputePass).  The bytes are only read during the call.  No
+ * GPU is touched. */
+GCDR_API int gcdr_model_load(const void *gc_onnx, size_t gc_len,
+                             const void *dr_onnx, size_t dr_len,
+                             gcdr_model **out, char *err, size_t err_cap);
+GCDR_API void gcdr_model_free(gcdr_model *m);
+/* Writes a JSON description of the recognised topology (channels, shift
+ * groups and offsets) into buf; returns the length needed (excluding NUL). */
+GCDR_API size_t gcdr_model_describe(const gcdr_model *m, char *buf, size_t cap);
+
+/* ---------------------------------------------------------- one worker */
+
+/* Creates a worker on `device` (CUDA ordinal): uploads packed weights, owns
+ * one stream, a grow-only device arena and pinned staging.  Mirrors
+ * `new VkGcdrPipeline(backend, gc, dr)` (VkPipeline2.cs:42-64). */
+GCDR_API int gcdr_cuda_create(int device, const gcdr_model *m, int precision,
+                              gcdr_cuda **out);
+/* Legacy convenience matching the proposed shim: parse + create in one call. */
+GCDR_API int gcdr_cuda_create_from_onnx(int device, const void *gc_onnx, size_t gc_len,
+                                        const void *dr_onnx, size_t dr_len,
+                                        int precision, gcdr_cuda **out);
+/* Enhance one image (host buffers).  Binds the worker to the image's padded
+ * shape first (arena replan + CUDA-graph capture on a new shape), then
+ * copies the strided source to pinned staging, runs the graph, copies back
+ * with the destination stride.  VkGcdrPipeline.Enhance (VkPipeline2.cs:296-327). */
+GCDR_API int gcdr_cuda_enhance(gcdr_cuda *w, const uint8_t *src, int width, int height,
+                               int src_stride, uint8_t *dst, int dst_stride,
+                               int pixel_format);
+/* Same, device-resident: src/dst are DEVICE pointers of tight images
+ * (stride = width*bpp) and the call is asynchronous on the worker's stream
+ * (or `stream` when non-null).  Used for throughput runs with inputs
+ * already in HBM. */
+GCDR_API int gcdr_cuda_enhance_device(gcdr_cuda *w, const uint8_t *d_src, int width, int height,
+                                      uint8_t *d_dst, int pixel_format, void *stream);
+/* Device bytes held by the worker (arena + staging): VkPipeline2.cs:141. */
+GCDR_API int64_t gcdr_cuda_device_bytes(const gcdr_cuda *w);
+/* Debug: padded NHWC fp32 intermediates of the last enhance -- the GC
+ * input x [h][w][3], the shading map I_sm [h][w][3] and the DR input
+ * [h][w][6] -- as VkGcdrPipeline.DebugIntermediates (VkPipeline2.cs:356-364).
+ * Any pointer may be NULL.  Sizes use the padded h, w of the last call. */
+GCDR_API int gcdr_cuda_debug_intermediates(gcdr_cuda *w, float *gc_in, float *gc_out, float *dr_in);
+/* Debug: kernel launches per enhance in the captured graph, and the padded
+ * shape the worker is bound to. */
+GCDR_API int gcdr_cuda_launch_count(const gcdr_cuda *w);
+/* Debug mode: the heads also write the shading map I_sm and the DR output as
+ * fp32 planes, returned by gcdr_cuda_debug_intermediates (gc_out) and
+ * gcdr_cuda_debug_output.  Re-captures the graph on the next enhance. */
+GCDR_API int gcdr_cuda_set_debug(gcdr_cuda *w, int on);
+GCDR_API int gcdr_cuda_debug_output(gcdr_cuda *w, float *dr_out);
+/* Per-op profile of the bound shape (the analogue of the reference's
+ * GCDRNET_PROF per-op timers, bench/Sdcb.SimdGcdrNet.Benchmark/Program.cs:993-1010):
+ * runs the op sequence `reps` times eagerly with CUDA events around each op and
+ * fills up to `cap` entries with the mean duration and the op's algorithmic
+ * FLOPs and HBM bytes.  Returns the op count, or -GCDR_ERR_* on failure. */
+typedef struct {
+    char name[48];
+    double ms;
+    double flops;
+    double bytes;
+    int tensor_core;
+} gcdr_op_profile;
+GCDR_API int gcdr_cuda_profile(gcdr_cuda *w, int reps, gcdr_op_profile *out, int cap);
+GCDR_API const char *gcdr_cuda_last_error(const gcdr_cuda *w);
+GCDR_API void gcdr_cuda_destroy(gcdr_cuda *w);
+
+/* ----------------------------------------------------- pooled enhancer */
+
+/* GcdrEnhancer.FromBytes(gc, dr, GcdrBackend.Cuda) (GcdrEnhancer.cs:89-91). */
+GCDR_API int gcdr_enhancer_create(int device, const void *gc_onnx, size_t gc_len,
+                                  const void *dr_onnx, size_t dr_len, int precision,
+                                  gcdr_enhancer **out, char *err, size_t err_cap);
+/* GcdrEnhancer.Enhance(src, width, height, srcStride, dst, dstStride, format)
+ * (GcdrEnhancer.cs:181-271).  src_len/dst_len are the buffer lengths in bytes
+ * (the Span lengths).  Thread-safe; dst may alias src at equal strides. */
+GCDR_API int gcdr_enhancer_enhance(gcdr_enhancer *e, const uint8_t *src, size_t src_len,
+                                   int width, int height, int src_stride,
+                                   uint8_t *dst, size_t dst_len, int dst_stride,
+                                   int pixel_format, char *err, size_t err_cap);
+/* GcdrEnhancer.PoolStats (GcdrEnhancer.cs:67-68): pools created, workers
+ * created, pools evicted. */
+GCDR_API void gcdr_enhancer_pool_stats(const gcdr_enhancer *e, int64_t *pools,
+                                       int64_t *workers, int64_t *evicted);
+/* Test hook: the next `count` worker enhances report GCDR_ERR_DEVICE before
+ * touching the GPU (host-side fault injection, the analogue of setting
+ * Dev.Lost in VulkanDeviceLossTests.cs:14-33). */
+GCDR_API void gcdr_enhancer_inject_device_loss(gcdr_enhancer *e, int count);
+/* GcdrEnhancer.Dispose (GcdrEnhancer.cs:325-331). */
+GCDR_API void gcdr_enhancer_destroy(gcdr_enhancer *e);
+
+/* ------------------------------------------------- standalone kernels */
+
+/* The three glue stages as separate device kernels (the fused pipeline does
+ * them inside the stem and head kernels).  Pointers are DEVICE pointers,
+ * launches are asynchronous on `stream` (NULL = default stream).
+ *   bgr2nhwc  Shaders/bgr2nhwc.comp (u8 any format/stride -> padded NHWC fp32)
+ *   div6      Shaders/div6.comp / PixelOps.DivConcatNhwc
+ *   nhwc2bgr  Shaders/nhwc2bgr.comp (crop, round, R/B swap, alpha from src) */
+GCDR_API int gcdr_k_bgr2nhwc(const uint8_t *src, int w, int h, int stride, int fmt,
+                             float *x, int ph, int pw, void *stream);
+GCDR_API int gcdr_k_div6(const float *x, const float *shadow, size_t npx, float *out6, void *stream);
+GCDR_API int gcdr_k_nhwc2bgr(const float *y, int H, int W, int ph, int pw, uint8_t *dst,
+                             int w, int h, int dst_stride, int fmt, const uint8_t *alpha_src,
+                             int alpha_stride, void *stream);
+
+/* One tensor-core convolution layer, for layer-level parity tests and the
+ * conv microbenchmark.  All pointers are DEVICE pointers.
+ *   kind 0  3x3 stride 1, reflect pad 1   input [H+2][W+2][C] (gcdr_k_to_layout kind 1)
+ *   kind 1  3x3 stride 2, zero pad 1      input phase planes (gcdr_k_to_layout kind 2)
+ *   kind 2  1x1 (token Gemm)              input [H][W][C]
+ *   kind 3  3x3 stride 1, zero pad 1      input [H+2][W+2][C] with a zero border
+ *                                         (gcdr_k_to_layout kind 3)
+ * weight: fp16 [N][taps*C], k = (ky*3 + kx)*C + c (taps = 9, or 1 for kind 2).
+ * epilogue: 0 bias, 1 bias + maxpool 2x2 + relu, 2 bias + relu.
+ * out: fp16 [Ho][Wo][N].  reference != 0 runs the SIMT reference kernels
+ * instead of tcgen05 (scratch: ceil(Ho*pitch/128)*128*N floats of device memory). */
+typedef struct {
+    int kind;
+    int H, W, C, N;
+    const void *in;
+    const void *weight;
+    const float *bias;
+    int epilogue;
+    void *out;
+    float *scratch;
+} gcdr_conv_desc;
+GCDR_API int gcdr_k_conv(const gcdr_conv_desc *d, int reference, void *stream);
+/* Repacks fp16 NHWC [H][W][C] into a layer input layout:
+ *   kind 1  [H+2][W+2][C] with a reflect border
+ *   kind 2  four zero-bordered phase planes [(H+2)/2][(W+2)/2][C] (H, W even)
+ *   kind 3  [H+2][W+2][C] with a zero border
+ * Returns the element count of the layout when dst is NULL. */
+GCDR_API int64_t gcdr_k_to_layout(const void *src, int H, int W, int C, int kind, void *dst, void *stream);
+/* Scratch floats gcdr_k_conv needs with reference != 0. */
+GCDR_API int64_t gcdr_k_conv_scratch(const gcdr_conv_desc *d);
+/* Number of SMs the tcgen05 kernels use on the current device. */
+GCDR_API int gcdr_device_sms(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GCDR_CUDA_H */

@@ -1,0 +1,136 @@
+// common.cuh -- activation layouts and store helpers shared by every kernel.
+//
+// Activations are NHWC fp16 (the tensor-core operand type) in one of three
+// layouts, chosen by who reads them next:
+//
+//   LAY_PLAIN    [H][W][C]                       tokens, decoder conv outputs
+//   LAY_PADREFL  [H+2][W+2][C] with a 1-px reflect border (ONNX Pad
+//                mode=reflect, gc#22/26/30/234/...): the input of a stride-1
+//                3x3 conv.  Flattened to rows of C, every conv tap is then a
+//                constant row offset from the output position, so each tap's
+//                operand tile is one rectangular TMA box.
+//   LAY_PHASE    four planes P[dy][dx] of [(H+2)/2][(W+2)/2][C] holding the
+//                zero-padded input at (2Y+dy, 2X+dx): the input of a stride-2
+//                pad-1 3x3 conv (the patch embeds gc#34/134).  Tap (ky,kx)
+//                reads plane (ky&1,kx&1) at a constant row offset.  The zero
+//                border is written once when the arena is planned.
+//   LAY_PADZERO  as LAY_PADREFL with a zero border (a zero-padded stride-1
+//                conv; used by the conv microbenchmark).
+//
+// Producers write the interior and, for LAY_PADREFL, the mirrored border
+// copies (reflect of 1 px: padded row 0 = row 1, padded row H+1 = row H-2;
+// a dimension of size 1 mirrors onto itself).
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace gcdr {
+
+enum LayoutKind : int { LAY_PLAIN = 0, LAY_PADREFL = 1, LAY_PHASE = 2, LAY_PADZERO = 3 };
+
+struct Act {
+    __half *p = nullptr;
+    int H = 0, W = 0, C = 0;   // logical dims of the stored tensor
+    int kind = LAY_PLAIN;
+
+    __host__ __device__ int pitch() const {       // rows per padded image row
+        return (kind == LAY_PADREFL || kind == LAY_PADZERO) ? W + 2 : kind == LAY_PHASE ? (W + 2) / 2 : W;
+    }
+    __host__ __device__ long long plane_rows() const {
+        return (long long)((H + 2) / 2) * ((W + 2) / 2);
+    }
+    __host__ __device__ long long rows() const {  // rows of C elements allocated
+        return (kind == LAY_PADREFL || kind == LAY_PADZERO) ? (long long)(H + 2) * (W + 2)
+             : kind == LAY_PHASE ? 4 * plane_rows() : (long long)H * W;
+    }
+    __host__ __device__ size_t bytes() const { return (size_t)rows() * C * sizeof(__half); }
+    // Row index of logical pixel (y, x) (its interior copy).
+    __host__ __device__ long long row(int y, int x) const {
+        if (kind == LAY_PADREFL || kind == LAY_PADZERO) return (long long)(y + 1) * (W + 2) + (x + 1);
+        if (kind == LAY_PHASE) {
+            int py = y + 1, px = x + 1;
+            return ((py & 1) * 2 + (px & 1)) * plane_rows() + (long long)(py >> 1) * ((W + 2) / 2) + (px >> 1);
+        }
+        return (long long)y * W + x;
+    }
+};
+
+__host__ __device__ inline int refl_lo(int n) { return n > 1 ? 1 : 0; }      // source of padded index 0
+__host__ __device__ inline int refl_hi(int n) { return n > 1 ? n - 2 : 0; }  // source of padded index n+1
+
+// Stores `n` halves (n multiple of 2, 4-byte aligned) at channel c0 of pixel
+// (y, x), plus the reflect-border copies for LAY_PADREFL.
+__device__ inline void act_store(const Act &a, int y, int x, int c0, const __half *v, int n) {
+    auto put = [&](long long r) {
+        __half *d = a.p + r * a.C + c0;
+        if ((n & 7) == 0 && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
+            for (int k = 0; k < n; k += 8) *reinterpret_cast<uint4 *>(d + k) = *reinterpret_cast<const uint4 *>(v + k);
+        } else {
+            for (int k = 0; k < n; k += 2) *reinterpret_cast<__half2 *>(d + k) = *reinterpret_cast<const __half2 *>(v + k);
+        }
+    };
+    put(a.row(y, x));
+    if (a.kind == LAY_PADREFL) {
+        int ys[2], xs[2], ny = 0, nx = 0;
+        if (y == refl_lo(a.H)) ys[ny++] = 0;
+        if (y == refl_hi(a.H)) ys[ny++] = a.H + 1;
+        if (x == refl_lo(a.W)) xs[nx++] = 0;
+        if (x == refl_hi(a.W)) xs[nx++] = a.W + 1;
+        const int P = a.W + 2;
+        for (int i = 0; i < ny; i++) put((long long)ys[i] * P + (x + 1));
+        for (int j = 0; j < nx; j++) put((long long)(y + 1) * P + xs[j]);
+        for (int i = 0; i < ny; i++)
+            for (int j = 0; j < nx; j++) put((long long)ys[i] * P + xs[j]);
+    }
+}
+
+__device__ inline const __half *act_ptr(const Act &a, int y, int x) { return a.p + a.row(y, x) * a.C; }
+
+// Shift-MLP channel groups (Extensions/ChannelShiftOp.cs:8-13, GcdrKernels.cs:169-198):
+// out[y,x,c] = in[y+off_g, x, c] (axis 2) or in[y, x+off_g, c] (axis 3), zero fill.
+// Applied as a scatter by the producer: the value at source position s goes to
+// (s - off) mod L; the |off| sources that fall off the edge carry zeros into the
+// |off| vacated destinations, so every destination is written exactly once.
+struct ShiftSpec {
+    int ngroups = 0;
+    int ends[5] = {0, 0, 0, 0, 0};
+    int offs[5] = {0, 0, 0, 0, 0};
+};
+
+__device__ inline int shift_group(const ShiftSpec &s, int c) {
+    int g = 0;
+    while (g < s.ngroups - 1 && c >= s.ends[g]) g++;
+    return c < s.ends[s.ngroups - 1] ? g : -1;
+}
+
+// Destination of source coordinate `s` (along the shifted axis of length L)
+// for offset `off`; *zero tells whether the destination receives zeros.
+__device__ inline int shift_dest(int s, int off, int L, bool *zero) {
+    int d = s - off;
+    *zero = d < 0 || d >= L;
+    d %= L;
+    if (d < 0) d += L;
+    return d;
+}
+
+// Stores the channels [c0, c0+n) of token pixel (y, x) of a LAY_PLAIN [H][W][C]
+// tensor with the group shift along `axis` (2 = H, 3 = W) applied as a scatter.
+__device__ inline void shift_store(const Act &a, const ShiftSpec &s, int axis, int y, int x, int c0,
+                                   const float *v, int n) {
+    for (int k = 0; k < n; k++) {
+        int c = c0 + k;
+        int g = shift_group(s, c);
+        int dy = y, dx = x;
+        bool z = false;
+        if (g >= 0) {
+            if (axis == 2) dy = shift_dest(y, s.offs[g], a.H, &z);
+            else dx = shift_dest(x, s.offs[g], a.W, &z);
+        }
+        a.p[((long long)dy * a.W + dx) * a.C + c] = __float2half_rn(z ? 0.0f : v[k]);
+    }
+}
+
+#define GCDR_ERR_FLAG_TIMEOUT 1
+#define GCDR_ERR_FLAG_BOUNDS 2
+
+}  // namespace gcdr

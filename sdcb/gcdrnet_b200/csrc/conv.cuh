@@ -1,0 +1,39 @@
+// conv.cuh -- the implicit-GEMM convolution shared by every tensor-core layer.
+//
+//   out[q][n] = epilogue( sum_tap sum_c A[q + tap_off[tap]][c] * B[n][tap*C + c] )
+//
+// A is a flat fp16 matrix of `a_rows` rows of C channels (an activation in
+// LAY_PADREFL / LAY_PHASE / LAY_PLAIN), B the packed weights [N][taps*C]
+// (K-major, k = tap*C + c, tap = ky*3 + kx), q runs over the output grid.
+// A 3x3 stride-1 reflect conv is 9 taps over LAY_PADREFL with offsets
+// ky*(W+2)+kx; the stride-2 patch embeds are 9 taps over LAY_PHASE; the
+// shift-MLP Gemms (fc1/fc2) are 1 tap over tokens.  Rows past the end of A
+// read as zeros (TMA out-of-bounds fill), which only feeds discarded outputs.
+#pragma once
+#include "epilogue.cuh"
+
+namespace gcdr {
+
+struct ConvArgs {
+    int ntaps = 1;
+    int tap_off[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+    int C = 0;                 // channels per tap (K per tap)
+    int N = 0;                 // output channels (multiple of 16, <= 512)
+    long long a_rows = 0;
+    const __half *A = nullptr; // for the SIMT reference path and host checks
+    const __half *B = nullptr; // packed weights [N][ntaps*C]
+    TileGeom tg;
+    EpiParams ep;
+    int *err = nullptr;        // device error flag (GCDR_ERR_FLAG_*)
+};
+
+// First A row of sub-box `sub` (64 rows each) of `tile` for tap offset 0.
+__host__ __device__ inline long long tile_a_row(const TileGeom &tg, int tile, int sub) {
+    if (tg.pool) {
+        int y2 = tile / tg.tiles_x, xt = tile - y2 * tg.tiles_x;
+        return (long long)(2 * y2 + sub) * tg.pitch + xt * 64;
+    }
+    return (long long)tile * 128 + sub * 64;
+}
+
+}  // namespace gcdr

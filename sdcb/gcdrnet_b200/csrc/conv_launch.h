@@ -1,0 +1,31 @@
+// conv_launch.h -- host entry points of the implicit-GEMM convolution.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "conv.cuh"
+
+namespace gcdr {
+
+constexpr int kMaxStages = 8;
+
+struct TcConfig {
+    int bk = 64;           // channels per k-block (16/32/64 -> SWIZZLE_32B/64B/128B)
+    int stages = 2;        // shared-memory ring depth
+    int stage_bytes = 0;   // A tile + B tile, 1 KB aligned
+    int acc_cols = 32;     // TMEM columns per accumulator (power of two >= N)
+    int acc_bufs = 1;      // accumulator double buffering
+    int tmem_cols = 32;
+};
+
+int tc_pick_bk(int C);
+int tc_plan(const ConvArgs &a, TcConfig &cfg, std::string &err);
+// tcgen05 path (sm_100a).  mode = EpiMode.
+int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, std::string &err);
+// SIMT reference path: same math and epilogue, fp32 FMA, accumulators staged in
+// `scratch` (ntiles*128*N floats).  Used by the tests to check the tensor-core path.
+int ref_conv_launch(const ConvArgs &a, int mode, float *scratch, cudaStream_t st, std::string &err);
+size_t ref_conv_scratch_floats(const ConvArgs &a);
+
+}  // namespace gcdr

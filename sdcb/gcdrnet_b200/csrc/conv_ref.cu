@@ -1,0 +1,73 @@
+// conv_ref.cu -- SIMT reference of the implicit-GEMM convolution.
+//
+// Computes the same sum as conv_tc.cu with fp32 FMAs straight from global
+// memory, stages the accumulators in a scratch buffer laid out like the TMEM
+// tile (tile, row, column), then runs the identical epilogue.  It exists to
+// check the tensor-core kernel layer by layer on the GPU; the pipeline never
+// uses it.
+#include "conv_launch.h"
+
+namespace gcdr {
+namespace {
+
+__global__ void ref_gemm_kernel(const ConvArgs a, float *scratch) {
+    const int tile = blockIdx.x, row = threadIdx.x;
+    const int n0 = blockIdx.y * 16;
+    const int sub = row >> 6, r = row & 63;
+    const long long base = tile_a_row(a.tg, tile, sub) + r;
+    float acc[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) acc[k] = 0.f;
+    const int K = a.ntaps * a.C;
+    for (int tap = 0; tap < a.ntaps; tap++) {
+        const long long ar = base + a.tap_off[tap];
+        if (ar < 0 || ar >= a.a_rows) continue;   // TMA reads zeros out of bounds
+        const __half *ap = a.A + ar * a.C;
+        for (int c = 0; c < a.C; c++) {
+            const float x = __half2float(ap[c]);
+            const __half *bp = a.B + (long long)n0 * K + (long long)tap * a.C + c;
+#pragma unroll
+            for (int k = 0; k < 16; k++) acc[k] = fmaf(x, __half2float(bp[(long long)k * K]), acc[k]);
+        }
+    }
+    float *o = scratch + ((long long)tile * 128 + row) * a.N + n0;
+#pragma unroll
+    for (int k = 0; k < 16; k++) o[k] = acc[k];
+}
+
+struct ScratchLoader {
+    const float *p;
+    __device__ void load16(int c0, float *v) {
+#pragma unroll
+        for (int k = 0; k < 16; k++) v[k] = p[c0 + k];
+    }
+};
+
+template <int MODE>
+__global__ void ref_epilogue_kernel(const ConvArgs a, const float *scratch) {
+    __shared__ EpiSmem sm;
+    const int tile = blockIdx.x, row = threadIdx.x;
+    ScratchLoader ld{scratch + ((long long)tile * 128 + row) * a.N};
+    epilogue_tile<MODE>(a.ep, a.tg, tile, row, a.N, ld, &sm);
+}
+
+}  // namespace
+
+size_t ref_conv_scratch_floats(const ConvArgs &a) { return (size_t)a.tg.ntiles * 128 * a.N; }
+
+int ref_conv_launch(const ConvArgs &a, int mode, float *scratch, cudaStream_t st, std::string &err) {
+    if (a.N % 16 || a.tg.ntiles < 1) { err = "ref conv: bad shape"; return -1; }
+    ref_gemm_kernel<<<dim3(a.tg.ntiles, a.N / 16), 128, 0, st>>>(a, scratch);
+    switch (mode) {
+        case EPI_PLAIN: ref_epilogue_kernel<EPI_PLAIN><<<a.tg.ntiles, 128, 0, st>>>(a, scratch); break;
+        case EPI_POOL: ref_epilogue_kernel<EPI_POOL><<<a.tg.ntiles, 128, 0, st>>>(a, scratch); break;
+        case EPI_LN2: ref_epilogue_kernel<EPI_LN2><<<a.tg.ntiles, 128, 0, st>>>(a, scratch); break;
+        case EPI_RESLN: ref_epilogue_kernel<EPI_RESLN><<<a.tg.ntiles, 128, 0, st>>>(a, scratch); break;
+        default: err = "bad epilogue mode"; return -1;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { err = std::string("ref conv launch: ") + cudaGetErrorString(e); return -1; }
+    return 0;
+}
+
+}  // namespace gcdr

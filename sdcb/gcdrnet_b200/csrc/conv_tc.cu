@@ -1,0 +1,411 @@
+// conv_tc.cu -- tcgen05 (sm_100a) implicit-GEMM convolution.
+//
+// One persistent CTA per SM, 6 warps:
+//   warp 0      TMA producer: per (tap, k-block) one A tile (two 64-row boxes,
+//               SWIZZLE_{32,64,128}B K-major) and the B tile (weights) into a
+//               multi-stage shared-memory ring; also allocates TMEM.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma.kind::f16 (fp16 x
+//               fp16 -> fp32, M=128, N<=256 per instruction) into a TMEM
+//               accumulator, tcgen05.commit frees ring slots / publishes tiles.
+//   warps 2-5   epilogue: tcgen05.ld 32x32b rows out of TMEM (thread = output
+//               position), bias / pool / LayerNorm / residual / shift, stores.
+// Accumulators are double-buffered in TMEM when 2*N columns fit (N <= 256),
+// so the epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Every mbarrier wait is bounded (clock64 budget): on expiry the CTA raises the
+// abort flag, sets GCDR_ERR_FLAG_TIMEOUT in the global error word, drains its
+// own copies in flight (bounded), frees its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <string>
+
+#include "conv.cuh"
+#include "conv_launch.h"
+
+namespace gcdr {
+
+namespace {
+
+constexpr long long kWaitCycles = 4000000000LL;   // ~2 s at 1.9 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait; false when the budget ran out or another role aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err) {
+    if (mbar_try(b, parity)) return true;
+    long long t0 = clock64();
+    while (true) {
+        if (mbar_try(b, parity)) return true;
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitCycles) {
+            *abort_flag = 1;
+            atomicOr(err, GCDR_ERR_FLAG_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// UMMA shared-memory descriptor, K-major, swizzled (sm_100 format: start>>4 at
+// [0,14), LBO>>4 at [16,30) (unused for swizzled K-major: 1), SBO>>4 at
+// [32,46), version 1 at [46,48), layout at [61,64): 2 = 128B, 4 = 64B, 6 = 32B).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t sbo, uint32_t layout) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)layout << 61;
+    return d;
+}
+
+// Instruction descriptor kind::f16: D=f32 (bit 4), A=B=f16 (0), K-major both,
+// N>>3 at [17,23), M>>4 at [24,29).
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accum));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+struct TmemLoader {
+    uint32_t taddr;
+    __device__ __forceinline__ void load16(int c0, float *v) {
+        uint32_t r[16];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(taddr + (uint32_t)c0));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int k = 0; k < 16; k++) v[k] = __uint_as_float(r[k]);
+    }
+};
+
+struct TcShared {
+    uint64_t full[kMaxStages], empty[kMaxStages], tfull[2], tempty[2];
+    uint32_t tmem_base;
+    int abort_flag;
+    int issued, consumed;
+    EpiSmem epi;
+};
+
+template <int BK, int MODE>
+__global__ void __launch_bounds__(192, 1)
+    tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ ConvArgs args, const __grid_constant__ TcConfig cfg) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    TcShared *sh = reinterpret_cast<TcShared *>(ring + (size_t)cfg.stages * cfg.stage_bytes);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int N = args.N;
+    const int kb_per_tap = args.C / BK;
+    const int kblocks = args.ntaps * kb_per_tap;
+    const uint32_t a_bytes = 128u * BK * 2u;
+    const uint32_t b_bytes = (uint32_t)N * BK * 2u;
+    const int nsub = (N + 255) / 256;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < cfg.stages; s++) {
+            mbar_init(&sh->full[s], 1);
+            mbar_init(&sh->empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&sh->tfull[b], 1);
+            mbar_init(&sh->tempty[b], 4);
+        }
+        sh->abort_flag = 0;
+        sh->issued = 0;
+        sh->consumed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh->tmem_base)),
+                     "r"((uint32_t)cfg.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = sh->tmem_base;
+    volatile int *abort_flag = &sh->abort_flag;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            int issued = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < args.tg.ntiles && ok; tile += gridDim.x) {
+                const long long r0 = tile_a_row(args.tg, tile, 0), r1 = tile_a_row(args.tg, tile, 1);
+                for (int kb = 0; kb < kblocks && ok; kb++) {
+                    const int tap = kb / kb_per_tap, cb = kb - tap * kb_per_tap;
+                    if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err)) { ok = false; break; }
+                    uint8_t *sa = ring + (size_t)s * cfg.stage_bytes;
+                    uint8_t *sb = sa + a_bytes;
+                    mbar_expect_tx(&sh->full[s], a_bytes + b_bytes);
+                    const int off = args.tap_off[tap];
+                    tma_load_2d(sa, &tmA, cb * BK, (int)(r0 + off), &sh->full[s]);
+                    tma_load_2d(sa + a_bytes / 2, &tmA, cb * BK, (int)(r1 + off), &sh->full[s]);
+                    for (int h = 0; h < nsub; h++)
+                        tma_load_2d(sb + (size_t)h * 256 * BK * 2, &tmB, tap * args.C + cb * BK, h * 256, &sh->full[s]);
+                    issued++;
+                    if (++s == cfg.stages) { s = 0; ph ^= 1u; }
+                }
+            }
+            sh->issued = issued;
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t layout = BK == 64 ? 2u : BK == 32 ? 4u : 6u;
+            const uint32_t sbo = 8u * BK * 2u;
+            int s = 0;
+            uint32_t ph = 0;
+            int t = 0, consumed = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < args.tg.ntiles && ok; tile += gridDim.x, t++) {
+                const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
+                const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
+                if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err)) break;
+                tc_fence_after();
+                const uint32_t dcol = tmem_base + (uint32_t)(ab * cfg.acc_cols);
+                for (int kb = 0; kb < kblocks; kb++) {
+                    if (!mbar_wait(&sh->full[s], ph, abort_flag, args.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(ring + (size_t)s * cfg.stage_bytes);
+                    const uint32_t sb = sa + a_bytes;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; kk++) {
+                        const uint64_t ad = sdesc(sa + kk * 32, sbo, layout);
+                        for (int h = 0; h < nsub; h++) {
+                            const int nn = N - h * 256 < 256 ? N - h * 256 : 256;
+                            const uint64_t bd = sdesc(sb + (uint32_t)h * 256u * BK * 2u + kk * 32, sbo, layout);
+                            mma_f16(dcol + (uint32_t)(h * 256), ad, bd, idesc_f16(nn), (kb | kk) ? 1u : 0u);
+                        }
+                    }
+                    mma_commit(&sh->empty[s]);
+                    consumed++;
+                    if (++s == cfg.stages) { s = 0; ph ^= 1u; }
+                }
+                if (ok) mma_commit(&sh->tfull[ab]);
+            }
+            sh->consumed = consumed;
+        }
+    } else {
+        const int quad = warp & 3;          // TMEM lane quadrant this warp may read
+        const int row = quad * 32 + lane;   // tile row (output position) of this thread
+        int t = 0;
+        for (int tile = blockIdx.x; tile < args.tg.ntiles; tile += gridDim.x, t++) {
+            const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
+            const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
+            bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err);
+            // all four epilogue warps take the same branch (pool exchange uses named barriers)
+            uint32_t bad;
+            asm volatile(
+                "{\n\t.reg .pred p, q;\n\t"
+                "setp.eq.u32 p, %1, 0;\n\t"
+                "bar.red.or.pred q, 2, 128, p;\n\t"
+                "selp.u32 %0, 1, 0, q;\n\t}"
+                : "=r"(bad)
+                : "r"((uint32_t)ok));
+            if (bad) break;
+            tc_fence_after();
+            TmemLoader ld{tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(ab * cfg.acc_cols)};
+            epilogue_tile<MODE>(args.ep, args.tg, tile, row, N, ld, &sh->epi);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh->tempty[ab]);
+        }
+    }
+
+    __syncthreads();
+    if (sh->abort_flag && threadIdx.x == 0) {
+        // drain: TMA copies issued but never consumed, then the MMAs behind the last commit
+        int s = sh->consumed % cfg.stages;
+        uint32_t ph = (uint32_t)((sh->consumed / cfg.stages) & 1);
+        for (int i = sh->consumed; i < sh->issued; i++) {
+            long long t0 = clock64();
+            while (!mbar_try(&sh->full[s], ph) && clock64() - t0 < kWaitCycles) {}
+            if (++s == cfg.stages) { s = 0; ph ^= 1u; }
+        }
+        if (sh->consumed > 0) {
+            int ls = (sh->consumed - 1) % cfg.stages;
+            uint32_t lph = (uint32_t)(((sh->consumed - 1) / cfg.stages) & 1);
+            long long t0 = clock64();
+            while (!mbar_try(&sh->empty[ls], lph) && clock64() - t0 < kWaitCycles) {}
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)cfg.tmem_cols)
+                     : "memory");
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+bool get_encoder(std::string &err) {
+    if (g_encode) return true;
+    cudaDriverEntryPointQueryResult q;
+    void *fn = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+        err = "cuTensorMapEncodeTiled not available";
+        return false;
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return true;
+}
+
+bool encode_2d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+               uint32_t box_outer, int bk, std::string &err) {
+    if (!get_encoder(err)) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {inner * 2};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t es[2] = {1, 1};
+    CUtensorMapSwizzle sw = bk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : bk == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                                             : CU_TENSOR_MAP_SWIZZLE_32B;
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        err = "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
+        return false;
+    }
+    return true;
+}
+
+template <int BK, int MODE>
+int launch_bk_mode(const ConvArgs &a, const TcConfig &cfg, const CUtensorMap &ta, const CUtensorMap &tb, int grid,
+                   cudaStream_t st, std::string &err) {
+    auto k = tc_conv_kernel<BK, MODE>;
+    size_t smem = 1024 + (size_t)cfg.stages * cfg.stage_bytes + sizeof(TcShared);
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) { err = std::string("smem attribute: ") + cudaGetErrorString(e); return -1; }
+    k<<<grid, 192, smem, st>>>(ta, tb, a, cfg);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) { err = std::string("tc_conv launch: ") + cudaGetErrorString(e); return -1; }
+    return 0;
+}
+
+template <int BK>
+int launch_bk(const ConvArgs &a, int mode, const TcConfig &cfg, const CUtensorMap &ta, const CUtensorMap &tb,
+              int grid, cudaStream_t st, std::string &err) {
+    switch (mode) {
+        case EPI_PLAIN: return launch_bk_mode<BK, EPI_PLAIN>(a, cfg, ta, tb, grid, st, err);
+        case EPI_POOL: return launch_bk_mode<BK, EPI_POOL>(a, cfg, ta, tb, grid, st, err);
+        case EPI_LN2: return launch_bk_mode<BK, EPI_LN2>(a, cfg, ta, tb, grid, st, err);
+        case EPI_RESLN: return launch_bk_mode<BK, EPI_RESLN>(a, cfg, ta, tb, grid, st, err);
+    }
+    err = "bad epilogue mode";
+    return -1;
+}
+
+}  // namespace
+
+int tc_pick_bk(int C) { return C % 64 == 0 ? 64 : C % 32 == 0 ? 32 : C % 16 == 0 ? 16 : 0; }
+
+int tc_plan(const ConvArgs &a, TcConfig &cfg, std::string &err) {
+    const int bk = tc_pick_bk(a.C);
+    if (!bk) { err = "channels per tap must be a multiple of 16"; return -1; }
+    if (a.N < 16 || a.N > 512 || a.N % 16) { err = "N must be a multiple of 16 in [16, 512]"; return -1; }
+    if (a.N > 256 && a.N % 256) { err = "N above 256 must be a multiple of 256"; return -1; }
+    if (a.ntaps < 1 || a.ntaps > 9) { err = "1..9 taps"; return -1; }
+    for (int t = 0; t < a.ntaps; t++)
+        if (a.tap_off[t] < 0) { err = "negative tap offset"; return -1; }
+    if (a.tg.pool && a.tg.pitch < 64 && a.tg.tiles_x != 1) { err = "pool tiling"; return -1; }
+    cfg.bk = bk;
+    cfg.stage_bytes = 128 * bk * 2 + a.N * bk * 2;
+    cfg.stage_bytes = (cfg.stage_bytes + 1023) & ~1023;
+    const int budget = 220 * 1024 - (int)sizeof(TcShared) - 1024;
+    cfg.stages = budget / cfg.stage_bytes;
+    if (cfg.stages > kMaxStages) cfg.stages = kMaxStages;
+    if (cfg.stages < 2) { err = "shared-memory ring too small"; return -1; }
+    int cols = 32;
+    while (cols < a.N) cols <<= 1;
+    cfg.acc_cols = cols;
+    cfg.acc_bufs = 2 * cols <= 512 ? 2 : 1;
+    cfg.tmem_cols = cols * cfg.acc_bufs;
+    return 0;
+}
+
+int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, std::string &err) {
+    TcConfig cfg;
+    if (tc_plan(a, cfg, err)) return -1;
+    if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) {
+        err = "operands must be 16-byte aligned";
+        return -1;
+    }
+    CUtensorMap ta, tb;
+    if (!encode_2d(&ta, a.A, (uint64_t)a.C, (uint64_t)a.a_rows, (uint32_t)cfg.bk, 64, cfg.bk, err)) return -1;
+    if (!encode_2d(&tb, a.B, (uint64_t)a.C * a.ntaps, (uint64_t)a.N, (uint32_t)cfg.bk, (uint32_t)(a.N < 256 ? a.N : 256),
+                   cfg.bk, err))
+        return -1;
+    int grid = a.tg.ntiles < num_sms ? a.tg.ntiles : num_sms;
+    if (grid < 1) return 0;
+    switch (cfg.bk) {
+        case 64: return launch_bk<64>(a, mode, cfg, ta, tb, grid, st, err);
+        case 32: return launch_bk<32>(a, mode, cfg, ta, tb, grid, st, err);
+        case 16: return launch_bk<16>(a, mode, cfg, ta, tb, grid, st, err);
+    }
+    err = "bad k-block";
+    return -1;
+}
+
+}  // namespace gcdr

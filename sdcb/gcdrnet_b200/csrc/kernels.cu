@@ -1,0 +1,440 @@
+// kernels.cu -- the SIMT kernels of the pipeline: fp32 stem and head (with the
+// pixel glue fused in), the shift-MLP depthwise stage, the decoder joins and
+// the standalone glue kernels.
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+
+namespace gcdr {
+namespace {
+
+__device__ __forceinline__ int reflect1(int i, int n) {
+    // ONNX Pad mode=reflect by one pixel; a dimension of size 1 mirrors onto itself
+    if (n <= 1) return 0;
+    if (i < 0) return -i;
+    if (i >= n) return 2 * n - 2 - i;
+    return i;
+}
+
+// Net input x at padded coordinates (py, px): the source pixel with the
+// top/left edge replicated, channels in B,G,R order, scaled by 1/255
+// (bgr2nhwc.comp:28-34, GoldenDerive.cs:11-23).
+__device__ __forceinline__ float img_val(const ImgSpec &im, int py, int px, int c) {
+    int sy = py - im.ph, sx = px - im.pw;
+    sy = sy < 0 ? 0 : sy;
+    sx = sx < 0 ? 0 : sx;
+    const uint8_t *p = im.src + (size_t)sy * im.stride + (size_t)sx * im.bpp;
+    const int ob = im.swap ? 2 : 0;
+    const int off = c == 1 ? 1 : (c == 0 ? ob : 2 - ob);
+    return (float)p[off] / 255.0f;
+}
+
+template <int CIN>
+__device__ __forceinline__ void load_px(const ImgSpec &im, const float *r, int W, int py, int px, float *v) {
+#pragma unroll
+    for (int c = 0; c < 3; c++) v[c] = img_val(im, py, px, c);
+    if (CIN == 6) {
+        const float *rp = r + ((size_t)py * W + px) * 3;
+#pragma unroll
+        for (int c = 0; c < 3; c++) v[3 + c] = rp[c];
+    }
+}
+
+template <int CIN, int C1>
+__global__ void __launch_bounds__(128) stem_kernel(const StemArgs a) {
+    __shared__ float ws[9 * CIN * C1];
+    __shared__ float bs[C1];
+    for (int i = threadIdx.x; i < 9 * CIN * C1; i += blockDim.x) {
+        int co = i % C1, t = i / C1, ci = t % CIN, tap = t / CIN;
+        ws[i] = a.w[(co * CIN + ci) * 9 + tap];
+    }
+    for (int i = threadIdx.x; i < C1; i += blockDim.x) bs[i] = a.b[i];
+    __syncthreads();
+    const int Hh = a.H / 2, Wh = a.W / 2;
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= Hh * Wh) return;
+    const int y2 = idx / Wh, x2 = idx - y2 * Wh;
+    float patch[4][4][CIN];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int yy = reflect1(2 * y2 - 1 + i, a.H);
+#pragma unroll
+        for (int j = 0; j < 4; j++) load_px<CIN>(a.img, a.r, a.W, yy, reflect1(2 * x2 - 1 + j, a.W), patch[i][j]);
+    }
+    __align__(16) __half h[C1];
+#pragma unroll 1
+    for (int co = 0; co < C1; co++) {
+        float acc[4];
+#pragma unroll
+        for (int p = 0; p < 4; p++) acc[p] = bs[co];
+#pragma unroll
+        for (int ky = 0; ky < 3; ky++)
+#pragma unroll
+            for (int kx = 0; kx < 3; kx++)
+#pragma unroll
+                for (int ci = 0; ci < CIN; ci++) {
+                    const float w = ws[((ky * 3 + kx) * CIN + ci) * C1 + co];
+#pragma unroll
+                    for (int dy = 0; dy < 2; dy++)
+#pragma unroll
+                        for (int dx = 0; dx < 2; dx++)
+                            acc[dy * 2 + dx] = fmaf(patch[dy + ky][dx + kx][ci], w, acc[dy * 2 + dx]);
+                }
+        const float m = fmaxf(fmaxf(acc[0], acc[1]), fmaxf(acc[2], acc[3]));
+        h[co] = __float2half_rn(fmaxf(m, 0.0f));
+    }
+    act_store(a.out, y2, x2, 0, h, C1);
+}
+
+template <int CIN, int C1, bool DR>
+__global__ void __launch_bounds__(128) head_kernel(const HeadArgs a) {
+    __shared__ float ws[9 * CIN * C1];
+    __shared__ float bs[C1];
+    __shared__ float fw[3 * C1];
+    __shared__ float fb[3];
+    for (int i = threadIdx.x; i < 9 * CIN * C1; i += blockDim.x) {
+        int co = i % C1, t = i / C1, ci = t % CIN, tap = t / CIN;
+        ws[i] = a.w[(co * CIN + ci) * 9 + tap];
+    }
+    for (int i = threadIdx.x; i < C1; i += blockDim.x) bs[i] = a.b[i];
+    for (int i = threadIdx.x; i < 3 * C1; i += blockDim.x) fw[i] = a.fw[i];
+    if (threadIdx.x < 3) fb[threadIdx.x] = a.fb[threadIdx.x];
+    __syncthreads();
+    const int ow = DR ? a.img.w : a.W, oh = DR ? a.img.h : a.H;
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= ow * oh) return;
+    const int oy = idx / ow, ox = idx - oy * ow;
+    const int py = DR ? oy + a.img.ph : oy, px = DR ? ox + a.img.pw : ox;
+
+    // skip = relu(enc1 conv) recomputed at this pixel (uphead.glsl:200-229)
+    float patch[3][3][CIN];
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const int yy = reflect1(py - 1 + i, a.H);
+#pragma unroll
+        for (int j = 0; j < 3; j++) load_px<CIN>(a.img, a.r, a.W, yy, reflect1(px - 1 + j, a.W), patch[i][j]);
+    }
+    // bilinear x2, half_pixel, edge clamp (Resize gc#454)
+    const int Hh = a.H / 2, Wh = a.W / 2;
+    const float fy = ((float)py + 0.5f) / 2.0f - 0.5f, fx = ((float)px + 0.5f) / 2.0f - 0.5f;
+    const int y0 = (int)floorf(fy), x0 = (int)floorf(fx);
+    const float dy = fy - (float)y0, dx = fx - (float)x0;
+    const int ya = min(max(y0, 0), Hh - 1), yb = min(max(y0 + 1, 0), Hh - 1);
+    const int xa = min(max(x0, 0), Wh - 1), xb = min(max(x0 + 1, 0), Wh - 1);
+    const __half *p00 = a.dec5 + ((size_t)ya * Wh + xa) * C1, *p01 = a.dec5 + ((size_t)ya * Wh + xb) * C1;
+    const __half *p10 = a.dec5 + ((size_t)yb * Wh + xa) * C1, *p11 = a.dec5 + ((size_t)yb * Wh + xb) * C1;
+    float o0 = fb[0], o1 = fb[1], o2 = fb[2];
+#pragma unroll 1
+    for (int co = 0; co < C1; co++) {
+        float acc = bs[co];
+#pragma unroll
+        for (int ky = 0; ky < 3; ky++)
+#pragma unroll
+            for (int kx = 0; kx < 3; kx++)
+#pragma unroll
+                for (int ci = 0; ci < CIN; ci++) acc = fmaf(patch[ky][kx][ci], ws[((ky * 3 + kx) * CIN + ci) * C1 + co], acc);
+        const float v00 = __half2float(p00[co]), v01 = __half2float(p01[co]);
+        const float v10 = __half2float(p10[co]), v11 = __half2float(p11[co]);
+        const float top = v00 + (v01 - v00) * dx, bot = v10 + (v11 - v10) * dx;
+        const float up = top + (bot - top) * dy;
+        const float s = fmaxf(up, 0.0f) + fmaxf(acc, 0.0f);
+        o0 = fmaf(s, fw[co], o0);
+        o1 = fmaf(s, fw[C1 + co], o1);
+        o2 = fmaf(s, fw[2 * C1 + co], o2);
+    }
+    float o[3] = {1.0f / (1.0f + expf(-o0)), 1.0f / (1.0f + expf(-o1)), 1.0f / (1.0f + expf(-o2))};
+    if (!DR) {
+        const size_t base = ((size_t)py * a.W + px) * 3;
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+            const float d = o[c] > 1e-6f ? o[c] : 1e-6f;
+            float q = patch[1][1][c] / d;
+            q = q < 0.0f ? 0.0f : (q > 1.0f ? 1.0f : q);
+            a.r_out[base + c] = q;
+            if (a.ism_out) a.ism_out[base + c] = o[c];
+        }
+    } else {
+        if (a.y_out) {
+            const size_t base = ((size_t)py * a.W + px) * 3;
+            for (int c = 0; c < 3; c++) a.y_out[base + c] = o[c];
+        }
+        uint8_t q[3];
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+            float f = o[c] * 255.0f + 0.5f;
+            f = f < 0.0f ? 0.0f : (f > 255.0f ? 255.0f : f);
+            q[c] = (uint8_t)f;
+        }
+        const int bpp = a.img.bpp, ob = a.img.swap ? 2 : 0;
+        uint8_t *d = a.dst + ((size_t)oy * a.img.w + ox) * bpp;
+        if (bpp == 4) {
+            const uint8_t al = a.img.src[(size_t)oy * a.img.stride + (size_t)ox * 4 + 3];
+            uchar4 v;
+            v.x = ob ? q[2] : q[0];
+            v.y = q[1];
+            v.z = ob ? q[0] : q[2];
+            v.w = al;
+            *reinterpret_cast<uchar4 *>(d) = v;
+        } else {
+            d[ob] = q[0];
+            d[1] = q[1];
+            d[2 - ob] = q[2];
+        }
+    }
+}
+
+__device__ __forceinline__ float gelu_exact(float v) {
+    // gc#88-92: x * (0.5 * (erf(x / 1.4142135381698608) + 1))
+    return v * (0.5f * (erff(v / 1.4142135381698608f) + 1.0f));
+}
+
+__global__ void dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *w, const float *b,
+                                     const ShiftSpec s, __half *out) {
+    const int chunks = C / 8;
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)H * W * chunks) return;
+    const int ch = (int)(idx % chunks);
+    const long long p = idx / chunks;
+    const int y = (int)(p / W), x = (int)(p - (long long)y * W);
+    const int c0 = ch * 8;
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) acc[k] = b[c0 + k];
+#pragma unroll
+    for (int ky = 0; ky < 3; ky++) {
+        const int yy = y + ky - 1;
+        if (yy < 0 || yy >= H) continue;
+#pragma unroll
+        for (int kx = 0; kx < 3; kx++) {
+            const int xx = x + kx - 1;
+            if (xx < 0 || xx >= W) continue;
+            const uint4 raw = *reinterpret_cast<const uint4 *>(in + ((long long)yy * W + xx) * C + c0);
+            const __half *hv = reinterpret_cast<const __half *>(&raw);
+#pragma unroll
+            for (int k = 0; k < 8; k++) acc[k] = fmaf(w[(c0 + k) * 9 + ky * 3 + kx], __half2float(hv[k]), acc[k]);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) acc[k] = gelu_exact(acc[k]);
+    Act o;
+    o.p = out;
+    o.H = H;
+    o.W = W;
+    o.C = C;
+    o.kind = LAY_PLAIN;
+    shift_store(o, s, 3, y, x, c0, acc, 8);
+}
+
+__device__ __forceinline__ void bilin_coords(int Y, int n, int &a0, int &a1, float &f) {
+    const float fy = ((float)Y + 0.5f) / 2.0f - 0.5f;
+    const int y0 = (int)floorf(fy);
+    f = fy - (float)y0;
+    a0 = min(max(y0, 0), n - 1);
+    a1 = min(max(y0 + 1, 0), n - 1);
+}
+
+__global__ void up_add_pad_kernel(const UpAddArgs a) {
+    const int C = a.out.C, H = a.out.H, W = a.out.W, chunks = C / 8;
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)H * W * chunks) return;
+    const int ch = (int)(idx % chunks);
+    const long long p = idx / chunks;
+    const int Y = (int)(p / W), X = (int)(p - (long long)Y * W);
+    const int h = H / 2, w = W / 2, c0 = ch * 8;
+    int ya, yb, xa, xb;
+    float dy, dx;
+    bilin_coords(Y, h, ya, yb, dy);
+    bilin_coords(X, w, xa, xb, dx);
+    const uint4 r00 = *reinterpret_cast<const uint4 *>(a.d + ((long long)ya * w + xa) * C + c0);
+    const uint4 r01 = *reinterpret_cast<const uint4 *>(a.d + ((long long)ya * w + xb) * C + c0);
+    const uint4 r10 = *reinterpret_cast<const uint4 *>(a.d + ((long long)yb * w + xa) * C + c0);
+    const uint4 r11 = *reinterpret_cast<const uint4 *>(a.d + ((long long)yb * w + xb) * C + c0);
+    const uint4 rs = *reinterpret_cast<const uint4 *>(act_ptr(a.skip, Y, X) + c0);
+    const __half *h00 = reinterpret_cast<const __half *>(&r00), *h01 = reinterpret_cast<const __half *>(&r01);
+    const __half *h10 = reinterpret_cast<const __half *>(&r10), *h11 = reinterpret_cast<const __half *>(&r11);
+    const __half *hs = reinterpret_cast<const __half *>(&rs);
+    __align__(16) __half o[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const float v00 = __half2float(h00[k]), v01 = __half2float(h01[k]);
+        const float v10 = __half2float(h10[k]), v11 = __half2float(h11[k]);
+        const float top = v00 + (v01 - v00) * dx, bot = v10 + (v11 - v10) * dx;
+        const float up = top + (bot - top) * dy;
+        o[k] = __float2half_rn(fmaxf(up, 0.0f) + __half2float(hs[k]));
+    }
+    act_store(a.out, Y, X, c0, o, 8);
+}
+
+// One warp per output pixel: out = relu(up(d)) + skip as tokens, then
+// LN2(out) scattered with the H shift.
+__global__ void up_add_tok_kernel(const UpAddArgs a) {
+    const int C = a.out.C, H = a.out.H, W = a.out.W;
+    const long long p = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (p >= (long long)H * W) return;
+    const int Y = (int)(p / W), X = (int)(p - (long long)Y * W);
+    const int h = H / 2, w = W / 2;
+    int ya, yb, xa, xb;
+    float dy, dx;
+    bilin_coords(Y, h, ya, yb, dy);
+    bilin_coords(X, w, xa, xb, dx);
+    const __half *s = act_ptr(a.skip, Y, X);
+    __half *o = a.out.p + a.out.row(Y, X) * C;
+    float v[16];
+    const int per = C / 32;   // C is a multiple of 32 and at most 512
+    float sum = 0.f;
+    for (int j = 0; j < per; j++) {
+        const int c = lane + 32 * j;
+        const float v00 = __half2float(a.d[((long long)ya * w + xa) * C + c]);
+        const float v01 = __half2float(a.d[((long long)ya * w + xb) * C + c]);
+        const float v10 = __half2float(a.d[((long long)yb * w + xa) * C + c]);
+        const float v11 = __half2float(a.d[((long long)yb * w + xb) * C + c]);
+        const float top = v00 + (v01 - v00) * dx, bot = v10 + (v11 - v10) * dx;
+        const float up = top + (bot - top) * dy;
+        const float t = fmaxf(up, 0.0f) + __half2float(s[c]);
+        o[c] = __float2half_rn(t);
+        v[j] = t;
+        sum += t;
+    }
+    for (int m = 16; m; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+    const float mean = sum / C;
+    float q = 0.f;
+    for (int j = 0; j < per; j++) {
+        const float d = v[j] - mean;
+        q += d * d;
+    }
+    for (int m = 16; m; m >>= 1) q += __shfl_xor_sync(0xffffffffu, q, m);
+    const float rstd = rsqrtf(q / C + a.eps);
+    for (int j = 0; j < per; j++) {
+        const int c = lane + 32 * j;
+        const float t = (v[j] - mean) * rstd * a.g[c] + a.b[c];
+        shift_store(a.h, a.shift, 2, Y, X, c, &t, 1);
+    }
+}
+
+__global__ void bgr2nhwc_kernel(const ImgSpec im, float *x, int H, int W) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)H * W) return;
+    const int py = (int)(idx / W), px = (int)(idx - (long long)py * W);
+#pragma unroll
+    for (int c = 0; c < 3; c++) x[idx * 3 + c] = img_val(im, py, px, c);
+}
+
+__global__ void div6_kernel(const float *x, const float *s, size_t npx, float *out) {
+    const size_t p = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= npx) return;
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+        const float v = x[p * 3 + c];
+        const float d = s[p * 3 + c] > 1e-6f ? s[p * 3 + c] : 1e-6f;
+        float r = v / d;
+        r = r < 0.0f ? 0.0f : (r > 1.0f ? 1.0f : r);
+        out[p * 6 + c] = v;
+        out[p * 6 + 3 + c] = r;
+    }
+}
+
+__global__ void nhwc2bgr_kernel(const float *y, int W, int ph, int pw, uint8_t *dst, int w, int h, int dst_stride,
+                                int bpp, int swap, const uint8_t *alpha, int alpha_stride) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)w * h) return;
+    const int r = (int)(idx / w), c = (int)(idx - (long long)r * w);
+    const float *v = y + ((size_t)(r + ph) * W + (c + pw)) * 3;
+    uint8_t q[3];
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        float f = v[k] * 255.0f + 0.5f;
+        f = f < 0.0f ? 0.0f : (f > 255.0f ? 255.0f : f);
+        q[k] = (uint8_t)f;
+    }
+    const int ob = swap ? 2 : 0;
+    uint8_t *d = dst + (size_t)r * dst_stride + (size_t)c * bpp;
+    uint8_t al = bpp == 4 ? alpha[(size_t)r * alpha_stride + (size_t)c * 4 + 3] : 0;
+    d[ob] = q[0];
+    d[1] = q[1];
+    d[2 - ob] = q[2];
+    if (bpp == 4) d[3] = al;
+}
+
+inline int grid_for(long long n, int bs) { return (int)((n + bs - 1) / bs); }
+
+inline int launch_status() { return cudaGetLastError() == cudaSuccess ? 0 : -1; }
+
+}  // namespace
+
+int stem_launch(const StemArgs &a, cudaStream_t st) {
+    const long long n = (long long)(a.H / 2) * (a.W / 2);
+    if (a.cin == 3 && a.c1 == 16) stem_kernel<3, 16><<<grid_for(n, 128), 128, 0, st>>>(a);
+    else if (a.cin == 6 && a.c1 == 32) stem_kernel<6, 32><<<grid_for(n, 128), 128, 0, st>>>(a);
+    else if (a.cin == 3 && a.c1 == 32) stem_kernel<3, 32><<<grid_for(n, 128), 128, 0, st>>>(a);
+    else if (a.cin == 6 && a.c1 == 16) stem_kernel<6, 16><<<grid_for(n, 128), 128, 0, st>>>(a);
+    else return -2;
+    return launch_status();
+}
+
+int head_launch(const HeadArgs &a, cudaStream_t st) {
+    const long long n = a.is_dr ? (long long)a.img.w * a.img.h : (long long)a.H * a.W;
+    const int g = grid_for(n, 128);
+    if (!a.is_dr) {
+        if (a.cin == 3 && a.c1 == 16) head_kernel<3, 16, false><<<g, 128, 0, st>>>(a);
+        else if (a.cin == 3 && a.c1 == 32) head_kernel<3, 32, false><<<g, 128, 0, st>>>(a);
+        else return -2;
+    } else {
+        if (a.cin == 6 && a.c1 == 32) head_kernel<6, 32, true><<<g, 128, 0, st>>>(a);
+        else if (a.cin == 6 && a.c1 == 16) head_kernel<6, 16, true><<<g, 128, 0, st>>>(a);
+        else return -2;
+    }
+    return launch_status();
+}
+
+int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *w, const float *b, const ShiftSpec &s,
+                         __half *out, cudaStream_t st) {
+    if (C % 8) return -2;
+    const long long n = (long long)H * W * (C / 8);
+    dw_gelu_shift_kernel<<<grid_for(n, 256), 256, 0, st>>>(in, H, W, C, w, b, s, out);
+    return launch_status();
+}
+
+int up_add_launch(const UpAddArgs &a, cudaStream_t st) {
+    const int C = a.out.C;
+    if (!a.tokens) {
+        if (C % 8) return -2;
+        const long long n = (long long)a.out.H * a.out.W * (C / 8);
+        up_add_pad_kernel<<<grid_for(n, 256), 256, 0, st>>>(a);
+    } else {
+        if (C % 32 || C > 512) return -2;
+        const long long n = (long long)a.out.H * a.out.W * 32;
+        up_add_tok_kernel<<<grid_for(n, 256), 256, 0, st>>>(a);
+    }
+    return launch_status();
+}
+
+int k_bgr2nhwc(const uint8_t *src, int w, int h, int stride, int fmt, float *x, int ph, int pw, cudaStream_t st) {
+    ImgSpec im;
+    im.src = src;
+    im.w = w;
+    im.h = h;
+    im.stride = stride;
+    im.bpp = fmt >= 2 ? 4 : 3;
+    im.swap = (fmt == 1 || fmt == 3) ? 1 : 0;
+    im.ph = ph;
+    im.pw = pw;
+    const long long n = (long long)(h + ph) * (w + pw);
+    bgr2nhwc_kernel<<<grid_for(n, 256), 256, 0, st>>>(im, x, h + ph, w + pw);
+    return launch_status();
+}
+
+int k_div6(const float *x, const float *s, size_t npx, float *out6, cudaStream_t st) {
+    div6_kernel<<<grid_for((long long)npx, 256), 256, 0, st>>>(x, s, npx, out6);
+    return launch_status();
+}
+
+int k_nhwc2bgr(const float *y, int H, int W, int ph, int pw, uint8_t *dst, int w, int h, int dst_stride, int fmt,
+               const uint8_t *alpha, int alpha_stride, cudaStream_t st) {
+    (void)H;
+    nhwc2bgr_kernel<<<grid_for((long long)w * h, 256), 256, 0, st>>>(
+        y, W, ph, pw, dst, w, h, dst_stride, fmt >= 2 ? 4 : 3, (fmt == 1 || fmt == 3) ? 1 : 0, alpha, alpha_stride);
+    return launch_status();
+}
+
+}  // namespace gcdr

@@ -1,0 +1,79 @@
+// kernels.h -- launchers of the SIMT kernels around the tensor-core convs.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace gcdr {
+
+// Image source / destination as the caller laid it out (GcdrPixelFormat).
+struct ImgSpec {
+    const uint8_t *src = nullptr;   // device copy of the source image
+    int w = 0, h = 0, stride = 0;   // original dims, row stride in bytes
+    int bpp = 3, swap = 0;          // bytes per pixel, R/B swapped (Rgb24/Rgba32)
+    int ph = 0, pw = 0;             // top/left replicate pad to /32
+};
+
+// Stem: enc1 conv 3x3 reflect (Cin = 3 from the image, or 6 = image + the
+// division-corrected image `r`) + bias -> maxpool 2x2 -> relu, fp32 math,
+// fp16 LAY_PADREFL output (gc#22-25).  w is ONNX [C1][Cin][3][3].
+struct StemArgs {
+    ImgSpec img;
+    const float *r = nullptr;       // DR only: [H][W][3] fp32
+    int H = 0, W = 0;               // padded dims
+    int cin = 3, c1 = 16;
+    const float *w = nullptr, *b = nullptr;
+    Act out;
+};
+int stem_launch(const StemArgs &a, cudaStream_t st);
+
+// Head (UpHeadOp with the skip recomputed, Extensions/UpHeadOp.cs:8-28,249-279):
+//   s = relu(bilinear2x(dec5)) + relu(enc1conv(input)); o = sigmoid(fb + fw . s)
+// GC: writes r = clamp(x / max(o, 1e-6), 0, 1) (div6, PixelOps.cs:81-102) and
+//     optionally o itself (the shading map).
+// DR: writes the caller's u8 format, cropped, alpha from the source
+//     (nhwc2bgr.comp:23-55).
+struct HeadArgs {
+    ImgSpec img;
+    const float *r = nullptr;       // DR input half (DR only)
+    int H = 0, W = 0;
+    int cin = 3, c1 = 16;
+    const float *w = nullptr, *b = nullptr;     // enc1 conv (recomputed skip)
+    const float *fw = nullptr, *fb = nullptr;   // final 1x1 conv [3][c1], [3]
+    const __half *dec5 = nullptr;   // [H/2][W/2][c1] LAY_PLAIN
+    float *r_out = nullptr;         // GC: [H][W][3]
+    float *ism_out = nullptr;       // GC, optional: [H][W][3]
+    float *y_out = nullptr;         // DR, optional: [H][W][3] net output (debug)
+    uint8_t *dst = nullptr;         // DR: tight [h][w][bpp]
+    int is_dr = 0;
+};
+int head_launch(const HeadArgs &a, cudaStream_t st);
+
+// Depthwise 3x3 (zero pad 1) + bias -> exact GELU -> W-shift scatter
+// (gc#85-95 with ChannelShift along W).  w is [C][9] (ONNX [C][1][3][3]).
+int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *w, const float *b, const ShiftSpec &s,
+                         __half *out, cudaStream_t st);
+
+// Decoder join: out = relu(bilinear2x(d)) + skip  (gc#236-240, 444-446).
+//   tokens=false: out is an Act (LAY_PADREFL) for the next decoder conv.
+//   tokens=true : out is LAY_PLAIN tokens (the block residual) and h gets
+//                 LN2(out) with the H-shift scatter (the block's norm2 + shift).
+struct UpAddArgs {
+    const __half *d = nullptr;      // [h][w][C] LAY_PLAIN, h = H/2
+    Act skip;                       // [H][W][C]
+    Act out;                        // [H][W][C]
+    int tokens = 0;
+    const float *g = nullptr, *b = nullptr;
+    float eps = 1e-5f;
+    Act h;                          // tokens [H][W][C]
+    ShiftSpec shift;
+};
+int up_add_launch(const UpAddArgs &a, cudaStream_t st);
+
+// Standalone glue kernels (the C ABI's gcdr_k_*).
+int k_bgr2nhwc(const uint8_t *src, int w, int h, int stride, int fmt, float *x, int ph, int pw, cudaStream_t st);
+int k_div6(const float *x, const float *s, size_t npx, float *out6, cudaStream_t st);
+int k_nhwc2bgr(const float *y, int H, int W, int ph, int pw, uint8_t *dst, int w, int h, int dst_stride, int fmt,
+               const uint8_t *alpha, int alpha_stride, cudaStream_t st);
+
+}  // namespace gcdr

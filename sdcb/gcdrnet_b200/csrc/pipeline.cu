@@ -1,0 +1,640 @@
+// pipeline.cu -- weights upload, arena planning, the op sequence of GC-Net and
+// DR-Net, CUDA-graph capture and the worker's enhance entry points.
+#include "pipeline.h"
+
+#include <cstdlib>
+#include <cstring>
+
+#include "../../../include/gcdr_cuda.h"
+#include "conv_launch.h"
+#include "kernels.h"
+
+namespace gcdr {
+
+// ------------------------------------------------------------------ weights
+
+DevWeights::~DevWeights() {
+    if (mem) {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(device);
+        cudaFree(mem);
+        cudaSetDevice(prev);
+    }
+}
+
+namespace {
+
+struct Packer {
+    std::vector<uint8_t> host;
+    struct Fix { size_t off; const void **dst; };
+    std::vector<Fix> fixes;
+    size_t add(const void *p, size_t n, const void **dst) {
+        size_t off = (host.size() + 255) & ~size_t(255);
+        host.resize(off + n);
+        std::memcpy(host.data() + off, p, n);
+        fixes.push_back({off, dst});
+        return off;
+    }
+    void f32(const std::vector<float> &v, const float **dst) {
+        add(v.data(), v.size() * 4, reinterpret_cast<const void **>(dst));
+    }
+    void h16(const std::vector<__half> &v, const __half **dst) {
+        add(v.data(), v.size() * 2, reinterpret_cast<const void **>(dst));
+    }
+};
+
+// Conv weights ONNX [N][C][k][k] -> [N][k*k*C] fp16, k index = (ky*k + kx)*C + c.
+std::vector<__half> pack_conv(const ConvW &c) {
+    const int K = c.k * c.k * c.cin;
+    std::vector<__half> o((size_t)c.cout * K);
+    for (int n = 0; n < c.cout; n++)
+        for (int ci = 0; ci < c.cin; ci++)
+            for (int ky = 0; ky < c.k; ky++)
+                for (int kx = 0; kx < c.k; kx++)
+                    o[(size_t)n * K + (ky * c.k + kx) * c.cin + ci] =
+                        __float2half_rn(c.w[(((size_t)n * c.cin + ci) * c.k + ky) * c.k + kx]);
+    return o;
+}
+
+// Gemm B [K][N] -> [N][K] fp16.
+std::vector<__half> pack_fc(const std::vector<float> &b, int C) {
+    std::vector<__half> o((size_t)C * C);
+    for (int k = 0; k < C; k++)
+        for (int n = 0; n < C; n++) o[(size_t)n * C + k] = __float2half_rn(b[(size_t)k * C + n]);
+    return o;
+}
+
+ShiftSpec shift_spec(const ShiftW &s) {
+    ShiftSpec o;
+    o.ngroups = (int)s.ends.size();
+    for (int i = 0; i < o.ngroups && i < 5; i++) {
+        o.ends[i] = s.ends[i];
+        o.offs[i] = s.offs[i];
+    }
+    return o;
+}
+
+void pack_net(Packer &pk, const NetW &n, DevNet &d) {
+    d.cin = n.cin; d.c1 = n.c1; d.c2 = n.c2; d.c3 = n.c3; d.c4 = n.c4; d.c5 = n.c5;
+    pk.f32(n.enc[0].w, &d.enc1_w);
+    pk.f32(n.enc[0].b, &d.enc1_b);
+    pk.h16(pack_conv(n.enc[1]), &d.enc2); pk.f32(n.enc[1].b, &d.enc2_b);
+    pk.h16(pack_conv(n.enc[2]), &d.enc3); pk.f32(n.enc[2].b, &d.enc3_b);
+    pk.h16(pack_conv(n.pe3), &d.pe3); pk.f32(n.pe3.b, &d.pe3_b);
+    pk.h16(pack_conv(n.pe4), &d.pe4); pk.f32(n.pe4.b, &d.pe4_b);
+    for (int i = 0; i < 5; i++) { pk.h16(pack_conv(n.dec[i]), &d.dec[i]); pk.f32(n.dec[i].b, &d.dec_b[i]); }
+    pk.f32(n.pe3_norm.g, &d.pe3n_g); pk.f32(n.pe3_norm.b, &d.pe3n_b); d.pe3n_eps = n.pe3_norm.eps;
+    pk.f32(n.pe4_norm.g, &d.pe4n_g); pk.f32(n.pe4_norm.b, &d.pe4n_b); d.pe4n_eps = n.pe4_norm.eps;
+    for (int i = 0; i < 4; i++) {
+        const BlockW &b = n.blk[i];
+        DevBlock &o = d.blk[i];
+        o.C = b.norm2.c;
+        pk.h16(pack_fc(b.fc1_w, o.C), &o.fc1); pk.f32(b.fc1_b, &o.fc1_b);
+        pk.h16(pack_fc(b.fc2_w, o.C), &o.fc2); pk.f32(b.fc2_b, &o.fc2_b);
+        pk.f32(b.dw.w, &o.dw_w); pk.f32(b.dw.b, &o.dw_b);
+        pk.f32(b.norm2.g, &o.n2_g); pk.f32(b.norm2.b, &o.n2_b); o.n2_eps = b.norm2.eps;
+        pk.f32(b.norm_out.g, &o.no_g); pk.f32(b.norm_out.b, &o.no_b); o.no_eps = b.norm_out.eps;
+        o.sa = shift_spec(b.shift_a);
+        o.sb = shift_spec(b.shift_b);
+    }
+    pk.f32(n.fin.w, &d.fin_w);
+    pk.f32(n.fin.b, &d.fin_b);
+}
+
+}  // namespace
+
+int upload_weights(const Model &m, int device, std::shared_ptr<DevWeights> &out, std::string &err) {
+    auto dw = std::make_shared<DevWeights>();
+    dw->device = device;
+    Packer pk;
+    pack_net(pk, m.gc, dw->gc);
+    pack_net(pk, m.dr, dw->dr);
+    if (cudaSetDevice(device) != cudaSuccess) { err = "cudaSetDevice failed"; return GCDR_ERR_DEVICE; }
+    if (cudaMalloc(&dw->mem, pk.host.size()) != cudaSuccess) { err = "weights: cudaMalloc failed"; return GCDR_ERR_OOM; }
+    dw->bytes = pk.host.size();
+    if (cudaMemcpy(dw->mem, pk.host.data(), pk.host.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+        err = "weights upload failed";
+        return GCDR_ERR_DEVICE;
+    }
+    for (auto &f : pk.fixes) *f.dst = static_cast<uint8_t *>(dw->mem) + f.off;
+    out = dw;
+    return GCDR_OK;
+}
+
+// ------------------------------------------------------------------- worker
+
+Worker::Worker(int device, std::shared_ptr<DevWeights> w) : device_(device), weights_(std::move(w)) {}
+
+Worker::~Worker() {
+    cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    if (exec_) cudaGraphExecDestroy(exec_);
+    if (graph_) cudaGraphDestroy(graph_);
+    if (arena_) cudaFree(arena_);
+    if (h_src_) cudaFreeHost(h_src_);
+    if (h_dst_) cudaFreeHost(h_dst_);
+    if (h_err_) cudaFreeHost(h_err_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+int Worker::fail(int code, const std::string &m) {
+    err_ = m;
+    return code;
+}
+
+int Worker::init(std::string &err) {
+    if (cudaSetDevice(device_) != cudaSuccess) { err = "cudaSetDevice failed"; return GCDR_ERR_DEVICE; }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device_) != cudaSuccess) { err = "no CUDA device"; return GCDR_ERR_DEVICE; }
+    if (prop.major != 10) { err = "this backend is built for sm_100a (B200)"; return GCDR_ERR_UNSUPPORTED; }
+    num_sms_ = prop.multiProcessorCount;
+    if (cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking) != cudaSuccess) { err = "stream"; return GCDR_ERR_DEVICE; }
+    if (cudaMallocHost(&h_err_, sizeof(int)) != cudaSuccess) { err = "pinned alloc"; return GCDR_ERR_OOM; }
+    const char *g = std::getenv("GCDR_CUDA_GRAPH");
+    use_graph_ = !(g && g[0] == '0');
+    return GCDR_OK;
+}
+
+void Worker::set_debug(bool on) {
+    if (on != debug_) {
+        debug_ = on;
+        bound_ = false;   // re-plan: the head kernels write the debug planes
+    }
+}
+
+namespace {
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Alloc {
+    size_t off = 0;
+    std::vector<std::pair<void **, size_t>> items;   // (pointer slot, offset)
+    void take(void **slot, size_t bytes) {
+        items.push_back({slot, off});
+        off = align256(off + bytes);
+    }
+    void act(Act &a, int H, int W, int C, int kind) {
+        a.H = H; a.W = W; a.C = C; a.kind = kind;
+        take(reinterpret_cast<void **>(&a.p), a.bytes());
+    }
+};
+
+void plan_net(Alloc &al, NetBufs &b, const DevNet &n, int H, int W) {
+    const int H1 = H / 2, W1 = W / 2, H2 = H / 4, W2 = W / 4, H3 = H / 8, W3 = W / 8;
+    const int H4 = H / 16, W4 = W / 16, H5 = H / 32, W5 = W / 32;
+    al.act(b.t1, H1, W1, n.c1, LAY_PADREFL);
+    al.act(b.t2, H2, W2, n.c2, LAY_PADREFL);
+    al.act(b.t3, H3, W3, n.c3, LAY_PHASE);
+    al.act(b.t4, H4, W4, n.c4, LAY_PHASE);
+    al.act(b.b2o, H5, W5, n.c5, LAY_PADREFL);
+    al.act(b.db1o, H4, W4, n.c4, LAY_PADREFL);
+    al.act(b.db2o, H3, W3, n.c3, LAY_PADREFL);
+    al.act(b.d3, H2, W2, n.c2, LAY_PADREFL);
+    al.act(b.d4, H1, W1, n.c1, LAY_PADREFL);
+    size_t tok = std::max({(size_t)H4 * W4 * n.c4, (size_t)H5 * W5 * n.c5, (size_t)H3 * W3 * n.c3}) * 2;
+    al.take(reinterpret_cast<void **>(&b.y0), tok);
+    al.take(reinterpret_cast<void **>(&b.hs), tok);
+    al.take(reinterpret_cast<void **>(&b.f1), tok);
+    al.take(reinterpret_cast<void **>(&b.f2), tok);
+    size_t dc = std::max({(size_t)H5 * W5 * n.c4, (size_t)H4 * W4 * n.c3, (size_t)H3 * W3 * n.c2, (size_t)H2 * W2 * n.c1}) * 2;
+    al.take(reinterpret_cast<void **>(&b.dconv), dc);
+    al.take(reinterpret_cast<void **>(&b.dec5), (size_t)H1 * W1 * n.c1 * 2);
+}
+
+Act plain(__half *p, int H, int W, int C) {
+    Act a;
+    a.p = p; a.H = H; a.W = W; a.C = C; a.kind = LAY_PLAIN;
+    return a;
+}
+
+// 3x3 stride-1 conv over a LAY_PADREFL input.
+ConvArgs conv_s1(const Act &in, const __half *B, const float *bias, int N, bool pool) {
+    ConvArgs a;
+    a.ntaps = 9;
+    for (int ky = 0; ky < 3; ky++)
+        for (int kx = 0; kx < 3; kx++) a.tap_off[ky * 3 + kx] = ky * (in.W + 2) + kx;
+    a.C = in.C;
+    a.N = N;
+    a.A = in.p;
+    a.a_rows = in.rows();
+    a.B = B;
+    a.tg.pitch = in.W + 2;
+    a.tg.conv_h = in.H;
+    a.tg.conv_w = in.W;
+    if (pool) {
+        a.tg.pool = 1;
+        a.tg.tiles_x = (in.W + 63) / 64;
+        a.tg.ntiles = (in.H / 2) * a.tg.tiles_x;
+    } else {
+        a.tg.ntiles = (int)(((long long)in.H * (in.W + 2) + 127) / 128);
+    }
+    a.ep.bias = bias;
+    return a;
+}
+
+// 3x3 stride-2 zero-pad-1 conv over a LAY_PHASE input (logical H x W).
+ConvArgs conv_s2(const Act &in, const __half *B, const float *bias, int N) {
+    ConvArgs a;
+    const int Ho = in.H / 2, Wo = in.W / 2, P = (in.W + 2) / 2;
+    const long long Pp = in.plane_rows();
+    a.ntaps = 9;
+    for (int ky = 0; ky < 3; ky++)
+        for (int kx = 0; kx < 3; kx++)
+            a.tap_off[ky * 3 + kx] = (int)(((ky & 1) * 2 + (kx & 1)) * Pp + (ky >> 1) * P + (kx >> 1));
+    a.C = in.C;
+    a.N = N;
+    a.A = in.p;
+    a.a_rows = in.rows();
+    a.B = B;
+    a.tg.pitch = P;
+    a.tg.conv_h = Ho;
+    a.tg.conv_w = Wo;
+    a.tg.ntiles = (int)(((long long)Ho * P + 127) / 128);
+    a.ep.bias = bias;
+    return a;
+}
+
+// Token Gemm (1 tap) over [H][W][C] tokens.
+ConvArgs fc(const __half *in, int H, int W, int C, const __half *B, const float *bias) {
+    ConvArgs a;
+    a.ntaps = 1;
+    a.C = C;
+    a.N = C;
+    a.A = in;
+    a.a_rows = (long long)H * W;
+    a.B = B;
+    a.tg.pitch = W;
+    a.tg.conv_h = H;
+    a.tg.conv_w = W;
+    a.tg.ntiles = (int)(((long long)H * W + 127) / 128);
+    a.ep.bias = bias;
+    return a;
+}
+
+}  // namespace
+
+int Worker::plan_arena() {
+    const DevWeights &w = *weights_;
+    Alloc al;
+    plan_net(al, gcb_, w.gc, H_, W_);
+    plan_net(al, drb_, w.dr, H_, W_);
+    al.take(reinterpret_cast<void **>(&r_), (size_t)H_ * W_ * 3 * 4);
+    al.take(reinterpret_cast<void **>(&ism_), debug_ ? (size_t)H_ * W_ * 3 * 4 : 256);
+    al.take(reinterpret_cast<void **>(&ydbg_), debug_ ? (size_t)H_ * W_ * 3 * 4 : 256);
+    const size_t img = (size_t)h_ * w_ * bpp_;
+    al.take(reinterpret_cast<void **>(&d_src_), img + 16);
+    al.take(reinterpret_cast<void **>(&d_dst_), img + 16);
+    al.take(reinterpret_cast<void **>(&d_err_), 256);
+    const size_t need = al.off;
+    // grow-only within the budget (VkPipeline2.cs:104-117): 1/8 headroom first, 1/4 on regrowth
+    const size_t budget = size_t(3) << 30;
+    bool shrink = arena_ && arena_bytes_ > budget && need <= budget;
+    if (!arena_ || arena_bytes_ < need || shrink) {
+        if (arena_) { cudaFree(arena_); arena_ = nullptr; arena_bytes_ = 0; }
+        size_t div = arena_bytes_ ? 4 : 8;
+        size_t cap = need / div * (div + 1) <= budget ? need / div * (div + 1) : need;
+        if (cudaMalloc(&arena_, cap) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(GCDR_ERR_OOM, "arena: cudaMalloc failed");
+        }
+        arena_bytes_ = cap;
+    }
+    for (auto &it : al.items) *it.first = arena_ + it.second;
+    // zero borders of the stride-2 inputs (LAY_PHASE) and everything else once per plan
+    if (cudaMemsetAsync(arena_, 0, need, stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "arena memset failed");
+    // pinned staging (grow-only)
+    if (pin_bytes_ < img) {
+        if (h_src_) cudaFreeHost(h_src_);
+        if (h_dst_) cudaFreeHost(h_dst_);
+        h_src_ = h_dst_ = nullptr;
+        size_t cap = img + img / 4 + 64;
+        if (cudaMallocHost(&h_src_, cap) != cudaSuccess || cudaMallocHost(&h_dst_, cap) != cudaSuccess) {
+            pin_bytes_ = 0;
+            return fail(GCDR_ERR_OOM, "pinned staging alloc failed");
+        }
+        pin_bytes_ = cap;
+    }
+    return GCDR_OK;
+}
+
+int Worker::build_ops() {
+    ops_.clear();
+    launches_ = 0;
+    const DevWeights &wt = *weights_;
+    const int nsm = num_sms_;
+    int *errp = d_err_;
+    auto conv_op = [this, nsm, errp](ConvArgs a, int mode, const char *name) {
+        a.err = errp;
+        OpInfo oi;
+        oi.name = name;
+        oi.tensor = 1;
+        const double px = (double)a.tg.conv_h * a.tg.conv_w;
+        oi.flops = 2.0 * px * a.N * a.ntaps * a.C;
+        const double in_px = a.ntaps == 1 ? px : (a.tap_off[1] == 1 ? px : 4.0 * px);   // s2 reads 4x its outputs
+        double out_px = mode == EPI_POOL ? px / 4 : px;
+        oi.bytes = in_px * a.C * 2 + out_px * a.N * 2 * (mode == EPI_LN2 ? 2 : 1) + (double)a.N * a.ntaps * a.C * 2 +
+                   (mode == EPI_RESLN ? px * a.N * 2 : 0);
+        info_.push_back(oi);
+        ops_.push_back([a, mode, nsm, this](cudaStream_t st) {
+            std::string e;
+            if (tc_conv_launch(a, mode, nsm, st, e)) return fail(GCDR_ERR_DEVICE, e);
+            return 0;
+        });
+        launches_++;
+    };
+    ops_.push_back([errp](cudaStream_t st) { return cudaMemsetAsync(errp, 0, sizeof(int), st) == cudaSuccess ? 0 : GCDR_ERR_DEVICE; });
+    info_.clear();
+    info_.push_back(OpInfo{"reset_error_flag", 0, 4, 0});
+    auto simt = [this](const std::string &name, double flops, double bytes) { info_.push_back(OpInfo{name, flops, bytes, 0}); };
+
+    ImgSpec img;
+    img.src = d_src_;
+    img.w = w_;
+    img.h = h_;
+    img.stride = w_ * bpp_;
+    img.bpp = bpp_;
+    img.swap = (fmt_ == GCDR_RGB24 || fmt_ == GCDR_RGBA32) ? 1 : 0;
+    img.ph = ph_;
+    img.pw = pw_;
+
+    for (int which = 0; which < 2; which++) {
+        const DevNet &n = which ? wt.dr : wt.gc;
+        NetBufs &b = which ? drb_ : gcb_;
+        const int H1 = H_ / 2, W1 = W_ / 2, H2 = H_ / 4, W2 = W_ / 4, H3 = H_ / 8, W3 = W_ / 8;
+        const int H4 = H_ / 16, W4 = W_ / 16, H5 = H_ / 32, W5 = W_ / 32;
+        (void)H1; (void)W1; (void)H2; (void)W2;
+        // stem: enc1 conv + pool + relu (fp32)
+        StemArgs sa;
+        sa.img = img;
+        sa.r = which ? r_ : nullptr;
+        sa.H = H_; sa.W = W_; sa.cin = n.cin; sa.c1 = n.c1;
+        sa.w = n.enc1_w; sa.b = n.enc1_b; sa.out = b.t1;
+        ops_.push_back([sa, this](cudaStream_t st) { return stem_launch(sa, st) ? fail(GCDR_ERR_DEVICE, "stem launch") : 0; });
+        launches_++;
+        const std::string pre = which ? "dr." : "gc.";
+        simt(pre + "stem", 2.0 * H_ * W_ * n.c1 * 9 * n.cin,
+             (double)h_ * w_ * bpp_ + (which ? 12.0 * H_ * W_ : 0) + (double)H1 * W1 * n.c1 * 2);
+        // encoders 2, 3: conv + pool + relu
+        { ConvArgs a = conv_s1(b.t1, n.enc2, n.enc2_b, n.c2, true); a.ep.out = b.t2; conv_op(a, EPI_POOL, (pre + "enc2").c_str()); }
+        { ConvArgs a = conv_s1(b.t2, n.enc3, n.enc3_b, n.c3, true); a.ep.out = b.t3; conv_op(a, EPI_POOL, (pre + "enc3").c_str()); }
+
+        // shifted-MLP block body after its norm2+shift producer: fc1, dw+gelu+shift, fc2+res+norm
+        auto block = [&](const DevBlock &bk, int H, int W, const Act &out, const std::string &bn) {
+            { ConvArgs a = fc(b.hs, H, W, bk.C, bk.fc1, bk.fc1_b); a.ep.out = plain(b.f1, H, W, bk.C); conv_op(a, EPI_PLAIN, (bn + ".fc1").c_str()); }
+            const __half *f1 = b.f1; __half *f2 = b.f2;
+            const float *dw = bk.dw_w, *db = bk.dw_b;
+            ShiftSpec sb = bk.sb;
+            int C = bk.C;
+            ops_.push_back([=](cudaStream_t st) {
+                return dw_gelu_shift_launch(f1, H, W, C, dw, db, sb, f2, st) ? fail(GCDR_ERR_DEVICE, "dw launch") : 0;
+            });
+            launches_++;
+            simt(bn + ".dw_gelu_shift", 2.0 * 9 * H * W * C, 4.0 * H * W * C);
+            ConvArgs a = fc(b.f2, H, W, bk.C, bk.fc2, bk.fc2_b);
+            a.ep.res = b.y0;
+            a.ep.g1 = bk.no_g; a.ep.b1 = bk.no_b; a.ep.eps1 = bk.no_eps;
+            a.ep.out = out;
+            conv_op(a, EPI_RESLN, (bn + ".fc2_ln").c_str());
+        };
+        // patch embed 3 + norm + block1 norm2 + H shift
+        {
+            ConvArgs a = conv_s2(b.t3, n.pe3, n.pe3_b, n.c4);
+            a.ep.g1 = n.pe3n_g; a.ep.b1 = n.pe3n_b; a.ep.eps1 = n.pe3n_eps;
+            a.ep.g2 = n.blk[0].n2_g; a.ep.b2 = n.blk[0].n2_b; a.ep.eps2 = n.blk[0].n2_eps;
+            a.ep.out = plain(b.y0, H4, W4, n.c4);
+            a.ep.out2 = plain(b.hs, H4, W4, n.c4);
+            a.ep.shift = n.blk[0].sa;
+            conv_op(a, EPI_LN2, (pre + "pe3_ln").c_str());
+        }
+        block(n.blk[0], H4, W4, b.t4, pre + "block1");
+        {
+            ConvArgs a = conv_s2(b.t4, n.pe4, n.pe4_b, n.c5);
+            a.ep.g1 = n.pe4n_g; a.ep.b1 = n.pe4n_b; a.ep.eps1 = n.pe4n_eps;
+            a.ep.g2 = n.blk[1].n2_g; a.ep.b2 = n.blk[1].n2_b; a.ep.eps2 = n.blk[1].n2_eps;
+            a.ep.out = plain(b.y0, H5, W5, n.c5);
+            a.ep.out2 = plain(b.hs, H5, W5, n.c5);
+            a.ep.shift = n.blk[1].sa;
+            conv_op(a, EPI_LN2, (pre + "pe4_ln").c_str());
+        }
+        block(n.blk[1], H5, W5, b.b2o, pre + "block2");
+        // decoder 1 -> up + t4 -> dblock1
+        { ConvArgs a = conv_s1(b.b2o, n.dec[0], n.dec_b[0], n.c4, false); a.ep.out = plain(b.dconv, H5, W5, n.c4); conv_op(a, EPI_PLAIN, (pre + "dec1").c_str()); }
+        auto up_tok = [&](int H, int W, int C, const Act &skip, const DevBlock &bk) {
+            UpAddArgs u;
+            u.d = b.dconv;
+            u.skip = skip;
+            u.out = plain(b.y0, H, W, C);
+            u.tokens = 1;
+            u.g = bk.n2_g; u.b = bk.n2_b; u.eps = bk.n2_eps;
+            u.h = plain(b.hs, H, W, C);
+            u.shift = bk.sa;
+            ops_.push_back([u, this](cudaStream_t st) { return up_add_launch(u, st) ? fail(GCDR_ERR_DEVICE, "up_add launch") : 0; });
+            launches_++;
+            simt(pre + "join_ln" + std::to_string(H), 0, 2.0 * (H / 2) * (W / 2) * C + 6.0 * H * W * C);
+        };
+        auto up_pad = [&](const Act &skip, const Act &out) {
+            UpAddArgs u;
+            u.d = b.dconv;
+            u.skip = skip;
+            u.out = out;
+            ops_.push_back([u, this](cudaStream_t st) { return up_add_launch(u, st) ? fail(GCDR_ERR_DEVICE, "up_add launch") : 0; });
+            launches_++;
+            simt(pre + "join" + std::to_string(out.H), 0, 2.0 * (out.H / 2) * (out.W / 2) * out.C + 4.0 * out.H * out.W * out.C);
+        };
+        up_tok(H4, W4, n.c4, b.t4, n.blk[2]);
+        block(n.blk[2], H4, W4, b.db1o, pre + "dblock1");
+        { ConvArgs a = conv_s1(b.db1o, n.dec[1], n.dec_b[1], n.c3, false); a.ep.out = plain(b.dconv, H4, W4, n.c3); conv_op(a, EPI_PLAIN, (pre + "dec2").c_str()); }
+        up_tok(H3, W3, n.c3, b.t3, n.blk[3]);
+        block(n.blk[3], H3, W3, b.db2o, pre + "dblock2");
+        { ConvArgs a = conv_s1(b.db2o, n.dec[2], n.dec_b[2], n.c2, false); a.ep.out = plain(b.dconv, H3, W3, n.c2); conv_op(a, EPI_PLAIN, (pre + "dec3").c_str()); }
+        up_pad(b.t2, b.d3);
+        { ConvArgs a = conv_s1(b.d3, n.dec[3], n.dec_b[3], n.c1, false); a.ep.out = plain(b.dconv, H2, W2, n.c1); conv_op(a, EPI_PLAIN, (pre + "dec4").c_str()); }
+        up_pad(b.t1, b.d4);
+        { ConvArgs a = conv_s1(b.d4, n.dec[4], n.dec_b[4], n.c1, false); a.ep.out = plain(b.dec5, H1, W1, n.c1); conv_op(a, EPI_PLAIN, (pre + "dec5").c_str()); }
+        // head: recomputed stem skip + bilinear + 1x1 + sigmoid, then div6 (GC) or u8 out (DR)
+        HeadArgs ha;
+        ha.img = img;
+        ha.r = which ? r_ : nullptr;
+        ha.H = H_; ha.W = W_; ha.cin = n.cin; ha.c1 = n.c1;
+        ha.w = n.enc1_w; ha.b = n.enc1_b; ha.fw = n.fin_w; ha.fb = n.fin_b;
+        ha.dec5 = b.dec5;
+        ha.is_dr = which;
+        if (!which) {
+            ha.r_out = r_;
+            ha.ism_out = debug_ ? ism_ : nullptr;
+        } else {
+            ha.dst = d_dst_;
+            ha.y_out = debug_ ? ydbg_ : nullptr;
+        }
+        ops_.push_back([ha, this](cudaStream_t st) { return head_launch(ha, st) ? fail(GCDR_ERR_DEVICE, "head launch") : 0; });
+        launches_++;
+        {
+            const double px = which ? (double)h_ * w_ : (double)H_ * W_;
+            simt(pre + "head", px * 2.0 * (n.c1 * 9 * n.cin + 3 * n.c1),
+                 px * bpp_ + (which ? 12.0 * px + px * bpp_ : 12.0 * px) + (double)H1 * W1 * n.c1 * 2);
+        }
+    }
+    return info_.size() == ops_.size() ? GCDR_OK : fail(GCDR_ERR_DEVICE, "op metadata mismatch");
+}
+
+int Worker::profile(int reps, std::vector<double> &ms) {
+    if (!bound_) return fail(GCDR_ERR_ARG, "worker not bound to a size");
+    const size_t n = ops_.size();
+    std::vector<cudaEvent_t> ev(n + 1);
+    for (auto &e : ev) cudaEventCreate(&e);
+    ms.assign(n, 0.0);
+    int rc = GCDR_OK;
+    for (int r = 0; r < reps && !rc; r++) {
+        for (size_t i = 0; i < n && !rc; i++) {
+            cudaEventRecord(ev[i], stream_);
+            rc = ops_[i](stream_);
+        }
+        cudaEventRecord(ev[n], stream_);
+        if (cudaEventSynchronize(ev[n]) != cudaSuccess) rc = fail(GCDR_ERR_DEVICE, "profile sync");
+        for (size_t i = 0; i < n && !rc; i++) {
+            float t = 0;
+            cudaEventElapsedTime(&t, ev[i], ev[i + 1]);
+            ms[i] += t / reps;
+        }
+    }
+    for (auto &e : ev) cudaEventDestroy(e);
+    return rc;
+}
+
+int Worker::run_ops(cudaStream_t st) {
+    for (auto &op : ops_) {
+        int rc = op(st);
+        if (rc) return rc;
+    }
+    return GCDR_OK;
+}
+
+int Worker::capture() {
+    if (exec_) { cudaGraphExecDestroy(exec_); exec_ = nullptr; }
+    if (graph_) { cudaGraphDestroy(graph_); graph_ = nullptr; }
+    if (!use_graph_) return GCDR_OK;
+    if (cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        return fail(GCDR_ERR_DEVICE, "graph capture begin failed");
+    int rc = run_ops(stream_);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(stream_, &g);
+    if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+    if (e != cudaSuccess || !g) return fail(GCDR_ERR_DEVICE, std::string("graph capture failed: ") + cudaGetErrorString(e));
+    graph_ = g;
+    if (cudaGraphInstantiate(&exec_, graph_, 0) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "graph instantiate failed");
+    return GCDR_OK;
+}
+
+int Worker::bind(int w, int h, int fmt) {
+    if (bound_ && w == w_ && h == h_ && fmt == fmt_) return GCDR_OK;
+    bound_ = false;
+    w_ = w; h_ = h; fmt_ = fmt;
+    bpp_ = fmt >= 2 ? 4 : 3;
+    ph_ = (-h) & 31; pw_ = (-w) & 31;
+    H_ = h + ph_; W_ = w + pw_;
+    if (cudaSetDevice(device_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "cudaSetDevice");
+    if (cudaStreamSynchronize(stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "stream sync");
+    int rc = plan_arena();
+    if (rc) return rc;
+    rc = build_ops();
+    if (rc) return rc;
+    rc = capture();
+    if (rc) return rc;
+    bound_ = true;
+    return GCDR_OK;
+}
+
+int Worker::check_err_flag() {
+    if (*h_err_ & GCDR_ERR_FLAG_TIMEOUT) return fail(GCDR_ERR_TIMEOUT, "a device-side wait timed out");
+    if (*h_err_) return fail(GCDR_ERR_DEVICE, "device error flag set");
+    return GCDR_OK;
+}
+
+int Worker::enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8_t *dst, int dst_stride, int fmt) {
+    if (inject_device_loss > 0) {
+        inject_device_loss--;
+        return fail(GCDR_ERR_DEVICE, "injected device loss");
+    }
+    if (cudaSetDevice(device_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "cudaSetDevice");
+    int rc = bind(w, h, fmt);
+    if (rc) return rc;
+    const size_t row = (size_t)w * bpp_, img = row * h;
+    if ((size_t)src_stride == row) std::memcpy(h_src_, src, img);
+    else
+        for (int y = 0; y < h; y++) std::memcpy(h_src_ + y * row, src + (size_t)y * src_stride, row);
+    cudaError_t e = cudaMemcpyAsync(d_src_, h_src_, img, cudaMemcpyHostToDevice, stream_);
+    if (e == cudaSuccess) {
+        if (exec_) {
+            if (cudaGraphLaunch(exec_, stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "graph launch failed");
+        } else if ((rc = run_ops(stream_))) return rc;
+        e = cudaMemcpyAsync(h_dst_, d_dst_, img, cudaMemcpyDeviceToHost, stream_);
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h_err_, d_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess) return fail(GCDR_ERR_DEVICE, std::string("CUDA error: ") + cudaGetErrorString(e));
+    if ((rc = check_err_flag())) return rc;
+    if ((size_t)dst_stride == row) std::memcpy(dst, h_dst_, img);
+    else
+        for (int y = 0; y < h; y++) std::memcpy(dst + (size_t)y * dst_stride, h_dst_ + y * row, row);
+    return GCDR_OK;
+}
+
+int Worker::enhance_device(const uint8_t *d_src, int w, int h, uint8_t *d_dst, int fmt, cudaStream_t st) {
+    if (cudaSetDevice(device_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "cudaSetDevice");
+    int rc = bind(w, h, fmt);
+    if (rc) return rc;
+    cudaStream_t s = st ? st : stream_;
+    const size_t img = (size_t)w * h * bpp_;
+    if (s != stream_) {
+        // order the worker's own stream after the caller's
+        cudaEvent_t ev;
+        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        cudaEventRecord(ev, s);
+        cudaStreamWaitEvent(stream_, ev, 0);
+        cudaEventDestroy(ev);
+    }
+    cudaError_t e = cudaMemcpyAsync(d_src_, d_src, img, cudaMemcpyDeviceToDevice, stream_);
+    if (e != cudaSuccess) return fail(GCDR_ERR_DEVICE, "d2d copy");
+    if (exec_) {
+        if (cudaGraphLaunch(exec_, stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "graph launch failed");
+    } else if ((rc = run_ops(stream_))) return rc;
+    e = cudaMemcpyAsync(d_dst, d_dst_, img, cudaMemcpyDeviceToDevice, stream_);
+    if (e != cudaSuccess) return fail(GCDR_ERR_DEVICE, "d2d copy");
+    if (s != stream_) {
+        cudaEvent_t ev;
+        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        cudaEventRecord(ev, stream_);
+        cudaStreamWaitEvent(s, ev, 0);
+        cudaEventDestroy(ev);
+    }
+    return GCDR_OK;
+}
+
+int Worker::debug_intermediates(float *gc_in, float *gc_out, float *dr_in, float *dr_out) {
+    if (!bound_) return fail(GCDR_ERR_ARG, "worker not bound to a size");
+    if (cudaStreamSynchronize(stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "sync");
+    const size_t n3 = (size_t)H_ * W_ * 3;
+    std::vector<float> x(n3), r(n3);
+    float *dx = nullptr;
+    if (cudaMalloc(&dx, n3 * 4) != cudaSuccess) return fail(GCDR_ERR_OOM, "debug alloc");
+    int rc = k_bgr2nhwc(d_src_, w_, h_, w_ * bpp_, fmt_, dx, ph_, pw_, stream_);
+    cudaMemcpyAsync(x.data(), dx, n3 * 4, cudaMemcpyDeviceToHost, stream_);
+    cudaMemcpyAsync(r.data(), r_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
+    if (gc_out && debug_) cudaMemcpyAsync(gc_out, ism_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
+    if (dr_out && debug_) cudaMemcpyAsync(dr_out, ydbg_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
+    cudaError_t e = cudaStreamSynchronize(stream_);
+    cudaFree(dx);
+    if (rc || e != cudaSuccess) return fail(GCDR_ERR_DEVICE, "debug copy failed");
+    if ((gc_out || dr_out) && !debug_) return fail(GCDR_ERR_ARG, "shading map / output need debug mode (gcdr_cuda_set_debug)");
+    if (gc_in) std::memcpy(gc_in, x.data(), n3 * 4);
+    if (dr_in)
+        for (size_t p = 0; p < (size_t)H_ * W_; p++)
+            for (int c = 0; c < 3; c++) {
+                dr_in[p * 6 + c] = x[p * 3 + c];
+                dr_in[p * 6 + 3 + c] = r[p * 3 + c];
+            }
+    return GCDR_OK;
+}
+
+}  // namespace gcdr

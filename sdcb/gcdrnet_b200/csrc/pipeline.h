@@ -1,0 +1,123 @@
+// pipeline.h -- one CUDA worker: weights on the device, a per-shape arena
+// plan, the op sequence of both nets, and a CUDA graph per padded shape.
+//
+// The structure follows the reference's fused GPU worker
+// (Backends/Vulkan/VkPipeline2.cs:21-379): bind to a size (arena grow within a
+// budget, re-record on a size change), then per frame upload -> GC -> div6 ->
+// DR -> download as one submission.  Here the submission is one CUDA-graph
+// launch and the div6 / pixel glue live inside the stem and head kernels.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "model.h"
+
+namespace gcdr {
+
+// Device copy of one net's weights in the layouts the kernels read.
+struct DevBlock {
+    const __half *fc1 = nullptr, *fc2 = nullptr;   // [N][K] (Gemm B transposed)
+    const float *fc1_b = nullptr, *fc2_b = nullptr;
+    const float *dw_w = nullptr, *dw_b = nullptr;   // [C][9]
+    const float *n2_g = nullptr, *n2_b = nullptr, *no_g = nullptr, *no_b = nullptr;
+    float n2_eps = 1e-5f, no_eps = 1e-5f;
+    ShiftSpec sa, sb;
+    int C = 0;
+};
+
+struct DevNet {
+    int cin = 0, c1 = 0, c2 = 0, c3 = 0, c4 = 0, c5 = 0;
+    const float *enc1_w = nullptr, *enc1_b = nullptr;   // fp32 ONNX order (stem / head)
+    const __half *enc2 = nullptr, *enc3 = nullptr, *pe3 = nullptr, *pe4 = nullptr, *dec[5] = {};
+    const float *enc2_b = nullptr, *enc3_b = nullptr, *pe3_b = nullptr, *pe4_b = nullptr, *dec_b[5] = {};
+    const float *pe3n_g = nullptr, *pe3n_b = nullptr, *pe4n_g = nullptr, *pe4n_b = nullptr;
+    float pe3n_eps = 1e-5f, pe4n_eps = 1e-5f;
+    DevBlock blk[4];
+    const float *fin_w = nullptr, *fin_b = nullptr;
+};
+
+struct DevWeights {
+    int device = 0;
+    void *mem = nullptr;
+    size_t bytes = 0;
+    DevNet gc, dr;
+    ~DevWeights();
+};
+
+// Uploads both nets (packing conv weights to [N][9*C] fp16).  0 or GCDR_ERR_*.
+int upload_weights(const Model &m, int device, std::shared_ptr<DevWeights> &out, std::string &err);
+
+struct NetBufs {
+    Act t1, t2, t3, t4, b2o, db1o, db2o, d3, d4;
+    __half *y0 = nullptr, *hs = nullptr, *f1 = nullptr, *f2 = nullptr, *dconv = nullptr, *dec5 = nullptr;
+};
+
+struct OpInfo {
+    std::string name;
+    double flops = 0;    // algorithmic FLOPs of one launch
+    double bytes = 0;    // algorithmic HBM bytes of one launch (each tensor read/written once)
+    int tensor = 0;      // 1: tcgen05 kernel
+};
+
+class Worker {
+public:
+    Worker(int device, std::shared_ptr<DevWeights> w);
+    ~Worker();
+    int init(std::string &err);
+    int enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8_t *dst, int dst_stride, int fmt);
+    int enhance_device(const uint8_t *d_src, int w, int h, uint8_t *d_dst, int fmt, cudaStream_t st);
+    int debug_intermediates(float *gc_in, float *gc_out, float *dr_in, float *dr_out);
+    void set_debug(bool on);
+    int64_t device_bytes() const { return (int64_t)arena_bytes_; }
+    int launches() const { return launches_; }
+    const std::vector<OpInfo> &op_info() const { return info_; }
+    // Runs the bound op sequence `reps` times eagerly with CUDA events around each
+    // op; ms[i] = mean duration of op i.
+    int profile(int reps, std::vector<double> &ms);
+    const std::string &last_error() const { return err_; }
+    int device() const { return device_; }
+    int inject_device_loss = 0;   // test hook: the next N enhances fail with GCDR_ERR_DEVICE
+
+private:
+    int bind(int w, int h, int fmt);
+    int plan_arena();
+    int build_ops();
+    int run_ops(cudaStream_t st);
+    int capture();
+    int check_err_flag();
+    int fail(int code, const std::string &m);
+
+    int device_;
+    std::shared_ptr<DevWeights> weights_;
+    cudaStream_t stream_ = nullptr;
+    int num_sms_ = 148;
+    // bound shape
+    int w_ = 0, h_ = 0, fmt_ = -1, H_ = 0, W_ = 0, ph_ = 0, pw_ = 0, bpp_ = 3;
+    bool bound_ = false, debug_ = false, use_graph_ = true;
+    // arena
+    uint8_t *arena_ = nullptr;
+    size_t arena_bytes_ = 0;
+    NetBufs gcb_, drb_;
+    float *r_ = nullptr, *ism_ = nullptr, *ydbg_ = nullptr;
+    uint8_t *d_src_ = nullptr, *d_dst_ = nullptr;
+    int *d_err_ = nullptr;
+    // pinned staging
+    uint8_t *h_src_ = nullptr, *h_dst_ = nullptr;
+    int *h_err_ = nullptr;
+    size_t pin_bytes_ = 0;
+    // ops and graph
+    std::vector<std::function<int(cudaStream_t)>> ops_;
+    std::vector<OpInfo> info_;
+    cudaGraph_t graph_ = nullptr;
+    cudaGraphExec_t exec_ = nullptr;
+    int launches_ = 0;
+    std::string err_;
+};
+
+}  // namespace gcdr

@@ -1,0 +1,65 @@
+"""Layer-level GPU parity of the tcgen05 implicit-GEMM convolution.
+
+Each layer runs three ways on the same seeded inputs: the tcgen05 kernel,
+the SIMT reference kernel (same epilogue code, fp32 FMA) and torch fp32 on
+the CPU.  Mirrors the reference's GPU-kernel-vs-CPU-kernel tests
+(tests/Sdcb.SimdGcdrNet.Tests/VkKernelTests.cs:15-65) for the conv family;
+shapes are the GC/DR layer shapes at small spatial sizes.
+"""
+import numpy as np
+import pytest
+
+from gpu_util import run_conv, torch_conv
+
+pytestmark = pytest.mark.gpu
+
+# (kind, H, W, C, N, epilogue): kind 0 reflect s1, 1 stride-2 zero pad, 2 token Gemm, 3 zero-pad s1
+CASES = [
+    (0, 32, 48, 16, 32, 1),     # GC enc2 (+pool)
+    (0, 16, 24, 32, 128, 1),    # GC enc3 (+pool)
+    (0, 32, 40, 32, 64, 1),     # DR enc2 (+pool)
+    (0, 16, 20, 64, 128, 1),    # DR enc3 (+pool)
+    (0, 8, 10, 160, 128, 0),    # GC dec2
+    (0, 4, 6, 256, 160, 0),     # GC dec1
+    (0, 4, 5, 512, 256, 0),     # DR dec1 (N=256, C=512)
+    (0, 64, 80, 16, 16, 0),     # GC dec5 (N=16)
+    (0, 16, 20, 128, 32, 0),    # GC dec3
+    (0, 3, 7, 32, 32, 0),       # odd tiny
+    (1, 16, 20, 128, 160, 0),   # GC pe3 (stride 2)
+    (1, 8, 10, 160, 256, 0),    # GC pe4
+    (1, 8, 12, 256, 512, 0),    # DR pe4 (N=512)
+    (2, 9, 13, 160, 160, 0),    # GC fc
+    (2, 6, 7, 512, 512, 0),     # DR block2 fc (N=512)
+    (2, 18, 25, 128, 128, 0),   # dblock2 fc
+    (3, 24, 30, 32, 64, 2),     # zero-pad conv + relu (microbench form)
+    (0, 66, 130, 32, 64, 1),    # pool with two x tiles
+]
+
+
+def _inputs(kind, H, W, C, N, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((H, W, C)).astype(np.float32)
+    k = 1 if kind == 2 else 3
+    w = (rng.standard_normal((N, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32) * 0.1
+    return x, w, b
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "k%d_%dx%d_c%d_n%d_e%d" % c)
+def test_tc_conv_matches_reference_and_torch(case):
+    from sdcb.gcdrnet_b200 import lib
+    kind, H, W, C, N, ep = case
+    x, w, b = _inputs(kind, H, W, C, N, hash(case) & 0xFFFF)
+    L = lib()
+    tc = run_conv(L, kind, x, w, b, ep, reference=False)
+    ref = run_conv(L, kind, x, w, b, ep, reference=True)
+    want = torch_conv(kind, x, w, b, ep)
+    assert not np.isnan(tc).any(), "tcgen05 output left unwritten positions"
+    scale = np.abs(want).max() + 1e-6
+    # fp16 output rounding: 2^-11 relative, plus accumulation-order noise
+    d_ref = np.abs(tc - ref).max() / scale
+    d_torch = np.abs(tc - want).max() / scale
+    rel_l2 = np.linalg.norm(tc - want) / (np.linalg.norm(want) + 1e-12)
+    assert d_ref < 2e-3, f"tcgen05 vs SIMT reference max rel {d_ref}"
+    assert d_torch < 4e-3, f"tcgen05 vs torch fp32 max rel {d_torch}"
+    assert rel_l2 < 1e-3, f"rel L2 {rel_l2}"
