@@ -216,7 +216,8 @@ def main():
     d_src = [torch.from_numpy(im.reshape(-1)).to(dev) for im in imgs]
     d_dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    stream = torch.cuda.Stream(dev)   # a real stream handle (the legacy default stream is 0)
+    torch.cuda.set_stream(stream)
 
     worker = CudaWorker.from_files(GC, DR, device=local)
     for i in range(args.warmup):
@@ -257,6 +258,12 @@ def main():
 
     # live per-op profile -> dominant kernel roofline
     prof = worker.profile(reps=3)
+    if os.environ.get("GCDR_BENCH_PROFILE"):
+        for p in prof:
+            ai = p[2] / p[3] if p[3] else 0
+            print(f"{p[0]:24s} {p[1]*1000:9.1f} us  {p[2]/1e9:8.3f} GFLOP  {p[3]/1e6:8.2f} MB  AI {ai:7.1f}  "
+                  f"{p[2]/(p[1]*1e-3)/1e12 if p[1] else 0:7.2f} TFLOP/s  {p[3]/(p[1]*1e-3)/1e9 if p[1] else 0:8.1f} GB/s"
+                  f"{'  tc' if p[4] else ''}", file=sys.stderr)
     hbm, tflops, peak_src = peaks()
     kern = [p for p in prof if p[0] != "reset_error_flag"]
     top = max(kern, key=lambda p: p[1])

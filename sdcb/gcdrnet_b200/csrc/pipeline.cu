@@ -584,30 +584,16 @@ int Worker::enhance_device(const uint8_t *d_src, int w, int h, uint8_t *d_dst, i
     if (cudaSetDevice(device_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "cudaSetDevice");
     int rc = bind(w, h, fmt);
     if (rc) return rc;
+    // everything is enqueued on the caller's stream (or the worker's own)
     cudaStream_t s = st ? st : stream_;
     const size_t img = (size_t)w * h * bpp_;
-    if (s != stream_) {
-        // order the worker's own stream after the caller's
-        cudaEvent_t ev;
-        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-        cudaEventRecord(ev, s);
-        cudaStreamWaitEvent(stream_, ev, 0);
-        cudaEventDestroy(ev);
-    }
-    cudaError_t e = cudaMemcpyAsync(d_src_, d_src, img, cudaMemcpyDeviceToDevice, stream_);
+    cudaError_t e = cudaMemcpyAsync(d_src_, d_src, img, cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return fail(GCDR_ERR_DEVICE, "d2d copy");
     if (exec_) {
-        if (cudaGraphLaunch(exec_, stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "graph launch failed");
-    } else if ((rc = run_ops(stream_))) return rc;
-    e = cudaMemcpyAsync(d_dst, d_dst_, img, cudaMemcpyDeviceToDevice, stream_);
+        if (cudaGraphLaunch(exec_, s) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "graph launch failed");
+    } else if ((rc = run_ops(s))) return rc;
+    e = cudaMemcpyAsync(d_dst, d_dst_, img, cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return fail(GCDR_ERR_DEVICE, "d2d copy");
-    if (s != stream_) {
-        cudaEvent_t ev;
-        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-        cudaEventRecord(ev, stream_);
-        cudaStreamWaitEvent(s, ev, 0);
-        cudaEventDestroy(ev);
-    }
     return GCDR_OK;
 }
 

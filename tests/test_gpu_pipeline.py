@@ -50,7 +50,9 @@ def test_pipeline_matches_oracle_and_golden(worker, oracle, tag):
     assert rl2 <= 1e-2, f"I_sm rel L2 vs oracle {rl2}"
     gshadow = G.f32_nhwc(tag, "shadow")
     assert np.linalg.norm(ism - gshadow) / np.linalg.norm(gshadow) <= 1e-2
-    assert np.abs(y - oy).max() < 5e-2, f"DR output max abs {np.abs(y - oy).max()}"
+    # the DR head only evaluates the cropped (visible) pixels
+    dy = np.abs(y[ph:, pw:] - oy[ph:, pw:]).max()
+    assert dy < 5e-2, f"DR output max abs {dy}"
     want = np.zeros_like(src)
     O.post(oy, ow, oh, want, ow * 3, 0)
     u8_check(dst, want, f"u8[{tag}] vs oracle")
