@@ -113,20 +113,44 @@ __device__ inline int shift_dest(int s, int off, int L, bool *zero) {
     return d;
 }
 
-// Stores the channels [c0, c0+n) of token pixel (y, x) of a LAY_PLAIN [H][W][C]
-// tensor with the group shift along `axis` (2 = H, 3 = W) applied as a scatter.
+// Stores the channels [c0, c0+n) (n even, c0 even) of token pixel (y, x) of a
+// LAY_PLAIN [H][W][C] tensor with the group shift along `axis` (2 = H, 3 = W)
+// applied as a scatter; channel pairs in one group go out as one 4-byte store.
 __device__ inline void shift_store(const Act &a, const ShiftSpec &s, int axis, int y, int x, int c0,
                                    const float *v, int n) {
-    for (int k = 0; k < n; k++) {
-        int c = c0 + k;
-        int g = shift_group(s, c);
+    for (int k = 0; k < n; k += 2) {
+        const int c = c0 + k;
+        const int g0 = shift_group(s, c), g1 = shift_group(s, c + 1);
         int dy = y, dx = x;
         bool z = false;
-        if (g >= 0) {
-            if (axis == 2) dy = shift_dest(y, s.offs[g], a.H, &z);
-            else dx = shift_dest(x, s.offs[g], a.W, &z);
+        if (g0 >= 0) {
+            if (axis == 2) dy = shift_dest(y, s.offs[g0], a.H, &z);
+            else dx = shift_dest(x, s.offs[g0], a.W, &z);
         }
-        a.p[((long long)dy * a.W + dx) * a.C + c] = __float2half_rn(z ? 0.0f : v[k]);
+        __half *d = a.p + ((long long)dy * a.W + dx) * a.C + c;
+        if (g0 == g1) {
+            *reinterpret_cast<__half2 *>(d) = z ? __float2half2_rn(0.0f) : __floats2half2_rn(v[k], v[k + 1]);
+        } else {
+            d[0] = __float2half_rn(z ? 0.0f : v[k]);
+            int ey = y, ex = x;
+            bool z1 = false;
+            if (g1 >= 0) {
+                if (axis == 2) ey = shift_dest(y, s.offs[g1], a.H, &z1);
+                else ex = shift_dest(x, s.offs[g1], a.W, &z1);
+            }
+            a.p[((long long)ey * a.W + ex) * a.C + c + 1] = __float2half_rn(z1 ? 0.0f : v[k + 1]);
+        }
+    }
+}
+
+// Loads 16 consecutive halves (16-byte aligned) as floats.
+__device__ inline void load16h(const __half *p, float *v) {
+    const uint4 a = *reinterpret_cast<const uint4 *>(p), b = *reinterpret_cast<const uint4 *>(p + 8);
+    const __half2 *ha = reinterpret_cast<const __half2 *>(&a), *hb = reinterpret_cast<const __half2 *>(&b);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        float2 f = __half22float2(ha[k]), g = __half22float2(hb[k]);
+        v[2 * k] = f.x; v[2 * k + 1] = f.y; v[8 + 2 * k] = g.x; v[8 + 2 * k + 1] = g.y;
     }
 }
 

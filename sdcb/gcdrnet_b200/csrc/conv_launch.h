@@ -8,7 +8,7 @@
 
 namespace gcdr {
 
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 32;
 
 struct TcConfig {
     int bk = 64;           // channels per k-block (16/32/64 -> SWIZZLE_32B/64B/128B)

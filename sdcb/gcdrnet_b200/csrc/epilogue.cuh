@@ -54,25 +54,21 @@ template <class L>
 __device__ inline void ln_stats(L &ld, const EpiParams &ep, int N, long long tok, bool use_res, float &mean, float &rstd,
                                 float eps) {
     float s = 0.f;
-    float v[16];
+    float v[16], r[16];
     for (int c0 = 0; c0 < N; c0 += 16) {
         ld.load16(c0, v);
+        if (use_res) load16h(ep.res + tok * N + c0, r);
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-            float t = v[k] + ep.bias[c0 + k];
-            if (use_res) t += __half2float(ep.res[tok * N + c0 + k]);
-            s += t;
-        }
+        for (int k = 0; k < 16; k++) s += v[k] + ep.bias[c0 + k] + (use_res ? r[k] : 0.0f);
     }
     mean = s / N;
     float q = 0.f;
     for (int c0 = 0; c0 < N; c0 += 16) {
         ld.load16(c0, v);
+        if (use_res) load16h(ep.res + tok * N + c0, r);
 #pragma unroll
         for (int k = 0; k < 16; k++) {
-            float t = v[k] + ep.bias[c0 + k];
-            if (use_res) t += __half2float(ep.res[tok * N + c0 + k]);
-            float d = t - mean;
+            float d = v[k] + ep.bias[c0 + k] + (use_res ? r[k] : 0.0f) - mean;
             q += d * d;
         }
     }
@@ -135,14 +131,16 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     float mean, rstd;
     ln_stats(ld, ep, N, tok, use_res, mean, rstd, ep.eps1);
     if (MODE == EPI_RESLN) {
+        float r[16];
         for (int c0 = 0; c0 < N; c0 += 16) {
             ld.load16(c0, v);
             if (valid) {
+                load16h(ep.res + tok * N + c0, r);
                 __align__(16) __half h[16];
 #pragma unroll
                 for (int k = 0; k < 16; k++) {
                     int c = c0 + k;
-                    float t = v[k] + ep.bias[c] + __half2float(ep.res[tok * N + c]);
+                    float t = v[k] + ep.bias[c] + r[k];
                     h[k] = __float2half_rn((t - mean) * rstd * ep.g1[c] + ep.b1[c]);
                 }
                 act_store(ep.out, y, x, c0, h, 16);

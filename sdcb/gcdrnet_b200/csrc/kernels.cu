@@ -188,6 +188,25 @@ __device__ __forceinline__ float gelu_exact(float v) {
     return v * (0.5f * (erff(v / 1.4142135381698608f) + 1.0f));
 }
 
+// out[y][x][c] = gelu(dw(in))[y][x + off_g(c)][c] (zero outside): the W shift
+// that precedes fc2 (gc#95-126) is folded into the depthwise stage as a gather,
+// so every output chunk of 8 channels is one 16-byte store.
+__device__ __forceinline__ float dw_at(const __half *in, int H, int W, int C, const float *w, int y, int x, int c) {
+    float acc = 0.f;
+#pragma unroll
+    for (int ky = 0; ky < 3; ky++) {
+        const int yy = y + ky - 1;
+        if (yy < 0 || yy >= H) continue;
+#pragma unroll
+        for (int kx = 0; kx < 3; kx++) {
+            const int xx = x + kx - 1;
+            if (xx < 0 || xx >= W) continue;
+            acc = fmaf(w[c * 9 + ky * 3 + kx], __half2float(in[((long long)yy * W + xx) * C + c]), acc);
+        }
+    }
+    return acc;
+}
+
 __global__ void dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *w, const float *b,
                                      const ShiftSpec s, __half *out) {
     const int chunks = C / 8;
@@ -197,32 +216,50 @@ __global__ void dw_gelu_shift_kernel(const __half *in, int H, int W, int C, cons
     const long long p = idx / chunks;
     const int y = (int)(p / W), x = (int)(p - (long long)y * W);
     const int c0 = ch * 8;
+    int xs[8];
+    bool uniform = true;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int g = shift_group(s, c0 + k);
+        xs[k] = x + (g >= 0 ? s.offs[g] : 0);
+        uniform = uniform && xs[k] == xs[0];
+    }
     float acc[8];
+    if (uniform) {
+        const int sx = xs[0];
+        if (sx < 0 || sx >= W) {
+            *reinterpret_cast<uint4 *>(out + ((long long)y * W + x) * C + c0) = make_uint4(0, 0, 0, 0);
+            return;
+        }
 #pragma unroll
-    for (int k = 0; k < 8; k++) acc[k] = b[c0 + k];
+        for (int k = 0; k < 8; k++) acc[k] = b[c0 + k];
 #pragma unroll
-    for (int ky = 0; ky < 3; ky++) {
-        const int yy = y + ky - 1;
-        if (yy < 0 || yy >= H) continue;
+        for (int ky = 0; ky < 3; ky++) {
+            const int yy = y + ky - 1;
+            if (yy < 0 || yy >= H) continue;
 #pragma unroll
-        for (int kx = 0; kx < 3; kx++) {
-            const int xx = x + kx - 1;
-            if (xx < 0 || xx >= W) continue;
-            const uint4 raw = *reinterpret_cast<const uint4 *>(in + ((long long)yy * W + xx) * C + c0);
-            const __half *hv = reinterpret_cast<const __half *>(&raw);
+            for (int kx = 0; kx < 3; kx++) {
+                const int xx = sx + kx - 1;
+                if (xx < 0 || xx >= W) continue;
+                const uint4 raw = *reinterpret_cast<const uint4 *>(in + ((long long)yy * W + xx) * C + c0);
+                const __half *hv = reinterpret_cast<const __half *>(&raw);
 #pragma unroll
-            for (int k = 0; k < 8; k++) acc[k] = fmaf(w[(c0 + k) * 9 + ky * 3 + kx], __half2float(hv[k]), acc[k]);
+                for (int k = 0; k < 8; k++) acc[k] = fmaf(w[(c0 + k) * 9 + ky * 3 + kx], __half2float(hv[k]), acc[k]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) acc[k] = gelu_exact(acc[k]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int sx = xs[k];
+            acc[k] = (sx < 0 || sx >= W) ? 0.0f : gelu_exact(b[c0 + k] + dw_at(in, H, W, C, w, y, sx, c0 + k));
         }
     }
+    __align__(16) __half o[8];
 #pragma unroll
-    for (int k = 0; k < 8; k++) acc[k] = gelu_exact(acc[k]);
-    Act o;
-    o.p = out;
-    o.H = H;
-    o.W = W;
-    o.C = C;
-    o.kind = LAY_PLAIN;
-    shift_store(o, s, 3, y, x, c0, acc, 8);
+    for (int k = 0; k < 8; k++) o[k] = __float2half_rn(acc[k]);
+    *reinterpret_cast<uint4 *>(out + ((long long)y * W + x) * C + c0) = *reinterpret_cast<const uint4 *>(o);
 }
 
 __device__ __forceinline__ void bilin_coords(int Y, int n, int &a0, int &a1, float &f) {
@@ -266,7 +303,7 @@ __global__ void up_add_pad_kernel(const UpAddArgs a) {
 }
 
 // One warp per output pixel: out = relu(up(d)) + skip as tokens, then
-// LN2(out) scattered with the H shift.
+// LN2(out) scattered with the H shift.  Lanes own channel pairs.
 __global__ void up_add_tok_kernel(const UpAddArgs a) {
     const int C = a.out.C, H = a.out.H, W = a.out.W;
     const long long p = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -280,35 +317,52 @@ __global__ void up_add_tok_kernel(const UpAddArgs a) {
     bilin_coords(X, w, xa, xb, dx);
     const __half *s = act_ptr(a.skip, Y, X);
     __half *o = a.out.p + a.out.row(Y, X) * C;
+    const __half *d00 = a.d + ((long long)ya * w + xa) * C, *d01 = a.d + ((long long)ya * w + xb) * C;
+    const __half *d10 = a.d + ((long long)yb * w + xa) * C, *d11 = a.d + ((long long)yb * w + xb) * C;
+    const int pairs = C / 2;   // C even, at most 512
     float v[16];
-    const int per = C / 32;   // C is a multiple of 32 and at most 512
     float sum = 0.f;
-    for (int j = 0; j < per; j++) {
-        const int c = lane + 32 * j;
-        const float v00 = __half2float(a.d[((long long)ya * w + xa) * C + c]);
-        const float v01 = __half2float(a.d[((long long)ya * w + xb) * C + c]);
-        const float v10 = __half2float(a.d[((long long)yb * w + xa) * C + c]);
-        const float v11 = __half2float(a.d[((long long)yb * w + xb) * C + c]);
-        const float top = v00 + (v01 - v00) * dx, bot = v10 + (v11 - v10) * dx;
-        const float up = top + (bot - top) * dy;
-        const float t = fmaxf(up, 0.0f) + __half2float(s[c]);
-        o[c] = __float2half_rn(t);
-        v[j] = t;
-        sum += t;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int pi = lane + 32 * j;
+        if (pi >= pairs) break;
+        const int c = 2 * pi;
+        const float2 a00 = __half22float2(*reinterpret_cast<const __half2 *>(d00 + c));
+        const float2 a01 = __half22float2(*reinterpret_cast<const __half2 *>(d01 + c));
+        const float2 a10 = __half22float2(*reinterpret_cast<const __half2 *>(d10 + c));
+        const float2 a11 = __half22float2(*reinterpret_cast<const __half2 *>(d11 + c));
+        const float2 sk = __half22float2(*reinterpret_cast<const __half2 *>(s + c));
+        float t[2];
+        const float q00[2] = {a00.x, a00.y}, q01[2] = {a01.x, a01.y}, q10[2] = {a10.x, a10.y}, q11[2] = {a11.x, a11.y};
+        const float sq[2] = {sk.x, sk.y};
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const float top = q00[e] + (q01[e] - q00[e]) * dx, bot = q10[e] + (q11[e] - q10[e]) * dx;
+            t[e] = fmaxf(top + (bot - top) * dy, 0.0f) + sq[e];
+        }
+        *reinterpret_cast<__half2 *>(o + c) = __floats2half2_rn(t[0], t[1]);
+        v[2 * j] = t[0];
+        v[2 * j + 1] = t[1];
+        sum += t[0] + t[1];
     }
     for (int m = 16; m; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
     const float mean = sum / C;
     float q = 0.f;
-    for (int j = 0; j < per; j++) {
-        const float d = v[j] - mean;
-        q += d * d;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        if (lane + 32 * j >= pairs) break;
+        const float d0 = v[2 * j] - mean, d1 = v[2 * j + 1] - mean;
+        q += d0 * d0 + d1 * d1;
     }
     for (int m = 16; m; m >>= 1) q += __shfl_xor_sync(0xffffffffu, q, m);
     const float rstd = rsqrtf(q / C + a.eps);
-    for (int j = 0; j < per; j++) {
-        const int c = lane + 32 * j;
-        const float t = (v[j] - mean) * rstd * a.g[c] + a.b[c];
-        shift_store(a.h, a.shift, 2, Y, X, c, &t, 1);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int pi = lane + 32 * j;
+        if (pi >= pairs) break;
+        const int c = 2 * pi;
+        float t[2] = {(v[2 * j] - mean) * rstd * a.g[c] + a.b[c], (v[2 * j + 1] - mean) * rstd * a.g[c + 1] + a.b[c + 1]};
+        shift_store(a.h, a.shift, 2, Y, X, c, t, 2);
     }
 }
 
@@ -402,7 +456,7 @@ int up_add_launch(const UpAddArgs &a, cudaStream_t st) {
         const long long n = (long long)a.out.H * a.out.W * (C / 8);
         up_add_pad_kernel<<<grid_for(n, 256), 256, 0, st>>>(a);
     } else {
-        if (C % 32 || C > 512) return -2;
+        if (C % 2 || C > 512) return -2;
         const long long n = (long long)a.out.H * a.out.W * 32;
         up_add_tok_kernel<<<grid_for(n, 256), 256, 0, st>>>(a);
     }

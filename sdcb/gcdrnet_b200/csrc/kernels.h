@@ -49,6 +49,13 @@ struct HeadArgs {
 };
 int head_launch(const HeadArgs &a, cudaStream_t st);
 
+// Tensor-core versions of the stem and the head (stem_tc.cu): same results at
+// fp32-level accuracy (u8 operands exact, hi/lo fp16 weight and r splits).
+// bpack holds the weights packed by pack_stem_weights (4 x 32 x 128 fp16).
+int stem_tc_launch(const StemArgs &a, const __half *bpack, int num_sms, int *err, cudaStream_t st);
+int head_tc_launch(const HeadArgs &a, const __half *bpack, int num_sms, int *err, cudaStream_t st);
+void pack_stem_weights(const float *w, int c1, int cin, __half *out);
+
 // Depthwise 3x3 (zero pad 1) + bias -> exact GELU -> W-shift scatter
 // (gc#85-95 with ChannelShift along W).  w is [C][9] (ONNX [C][1][3][3]).
 int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *w, const float *b, const ShiftSpec &s,

@@ -79,6 +79,11 @@ void pack_net(Packer &pk, const NetW &n, DevNet &d) {
     d.cin = n.cin; d.c1 = n.c1; d.c2 = n.c2; d.c3 = n.c3; d.c4 = n.c4; d.c5 = n.c5;
     pk.f32(n.enc[0].w, &d.enc1_w);
     pk.f32(n.enc[0].b, &d.enc1_b);
+    {
+        std::vector<__half> sb(4 * 32 * 128);
+        pack_stem_weights(n.enc[0].w.data(), n.enc[0].cout, n.enc[0].cin, sb.data());
+        pk.h16(sb, &d.stem_b);
+    }
     pk.h16(pack_conv(n.enc[1]), &d.enc2); pk.f32(n.enc[1].b, &d.enc2_b);
     pk.h16(pack_conv(n.enc[2]), &d.enc3); pk.f32(n.enc[2].b, &d.enc3_b);
     pk.h16(pack_conv(n.pe3), &d.pe3); pk.f32(n.pe3.b, &d.pe3_b);
@@ -153,6 +158,8 @@ int Worker::init(std::string &err) {
     if (cudaMallocHost(&h_err_, sizeof(int)) != cudaSuccess) { err = "pinned alloc"; return GCDR_ERR_OOM; }
     const char *g = std::getenv("GCDR_CUDA_GRAPH");
     use_graph_ = !(g && g[0] == '0');
+    const char *sv = std::getenv("GCDR_CUDA_STEM");   // "simt": fp32 SIMT stem/head kernels
+    simt_stem_ = sv && std::string(sv) == "simt";
     return GCDR_OK;
 }
 
@@ -370,7 +377,14 @@ int Worker::build_ops() {
         sa.r = which ? r_ : nullptr;
         sa.H = H_; sa.W = W_; sa.cin = n.cin; sa.c1 = n.c1;
         sa.w = n.enc1_w; sa.b = n.enc1_b; sa.out = b.t1;
-        ops_.push_back([sa, this](cudaStream_t st) { return stem_launch(sa, st) ? fail(GCDR_ERR_DEVICE, "stem launch") : 0; });
+        if (simt_stem_) {
+            ops_.push_back([sa, this](cudaStream_t st) { return stem_launch(sa, st) ? fail(GCDR_ERR_DEVICE, "stem launch") : 0; });
+        } else {
+            const __half *bp = n.stem_b;
+            ops_.push_back([sa, bp, nsm, errp, this](cudaStream_t st) {
+                return stem_tc_launch(sa, bp, nsm, errp, st) ? fail(GCDR_ERR_DEVICE, "stem launch") : 0;
+            });
+        }
         launches_++;
         const std::string pre = which ? "dr." : "gc.";
         simt(pre + "stem", 2.0 * H_ * W_ * n.c1 * 9 * n.cin,
@@ -467,7 +481,14 @@ int Worker::build_ops() {
             ha.dst = d_dst_;
             ha.y_out = debug_ ? ydbg_ : nullptr;
         }
-        ops_.push_back([ha, this](cudaStream_t st) { return head_launch(ha, st) ? fail(GCDR_ERR_DEVICE, "head launch") : 0; });
+        if (simt_stem_) {
+            ops_.push_back([ha, this](cudaStream_t st) { return head_launch(ha, st) ? fail(GCDR_ERR_DEVICE, "head launch") : 0; });
+        } else {
+            const __half *bp = n.stem_b;
+            ops_.push_back([ha, bp, nsm, errp, this](cudaStream_t st) {
+                return head_tc_launch(ha, bp, nsm, errp, st) ? fail(GCDR_ERR_DEVICE, "head launch") : 0;
+            });
+        }
         launches_++;
         {
             const double px = which ? (double)h_ * w_ : (double)H_ * W_;

@@ -34,6 +34,7 @@ struct DevBlock {
 struct DevNet {
     int cin = 0, c1 = 0, c2 = 0, c3 = 0, c4 = 0, c5 = 0;
     const float *enc1_w = nullptr, *enc1_b = nullptr;   // fp32 ONNX order (stem / head)
+    const __half *stem_b = nullptr;                     // tensor-core stem weights (pack_stem_weights)
     const __half *enc2 = nullptr, *enc3 = nullptr, *pe3 = nullptr, *pe4 = nullptr, *dec[5] = {};
     const float *enc2_b = nullptr, *enc3_b = nullptr, *pe3_b = nullptr, *pe4_b = nullptr, *dec_b[5] = {};
     const float *pe3n_g = nullptr, *pe3n_b = nullptr, *pe4n_g = nullptr, *pe4n_b = nullptr;
@@ -99,7 +100,7 @@ private:
     int num_sms_ = 148;
     // bound shape
     int w_ = 0, h_ = 0, fmt_ = -1, H_ = 0, W_ = 0, ph_ = 0, pw_ = 0, bpp_ = 3;
-    bool bound_ = false, debug_ = false, use_graph_ = true;
+    bool bound_ = false, debug_ = false, use_graph_ = true, simt_stem_ = false;
     // arena
     uint8_t *arena_ = nullptr;
     size_t arena_bytes_ = 0;

@@ -97,3 +97,30 @@ def test_launch_count_and_native_graph(worker):
     # one graph per padded shape: stem + 9 tensor-core layers + dw + joins + head per net
     assert worker.launch_count >= 40
     assert worker.device_bytes > 0
+
+
+def test_tensor_core_stem_head_match_fp32_simt(monkeypatch):
+    """The tcgen05 stem/head (u8-exact operands, hi/lo fp16 splits) against the
+    fp32 SIMT stem/head on the same image.  Both pipelines store fp16
+    activations, so a last-bit difference in the stem can flip an fp16
+    rounding downstream: the shading maps agree to that level (2e-3 relative,
+    5x tighter than the 1e-2 parity bar) and the u8 outputs within 2 LSB."""
+    from sdcb.gcdrnet_b200 import CudaWorker
+    h, w, ph, pw, oh, ow = G.dims("pad")
+    src = G.bgr("pad")
+    outs = {}
+    for mode in ("simt", "tc"):
+        if mode == "simt":
+            monkeypatch.setenv("GCDR_CUDA_STEM", "simt")
+        else:
+            monkeypatch.delenv("GCDR_CUDA_STEM", raising=False)
+        with CudaWorker.from_files(G.GC_PATH, G.DR_PATH) as wk:
+            wk.set_debug(True)
+            dst = np.zeros_like(src)
+            wk.enhance(src, ow, oh, ow * 3, dst, ow * 3, 0)
+            _, ism, _ = wk.debug_intermediates(h, w)
+            outs[mode] = (dst, ism)
+    rel = np.abs(outs["tc"][1] - outs["simt"][1]).max() / np.abs(outs["simt"][1]).max()
+    assert rel < 2e-3, f"I_sm tensor-core vs fp32 SIMT: max rel {rel}"
+    d = np.abs(outs["tc"][0].astype(int) - outs["simt"][0].astype(int))
+    assert d.max() <= 2, f"u8 tensor-core vs fp32 SIMT: max {d.max()}"
