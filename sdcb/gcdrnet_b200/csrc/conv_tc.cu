@@ -170,8 +170,10 @@ __global__ void __launch_bounds__(192, 1)
     }
 
     __syncthreads();
-    if (sh->abort_flag && threadIdx.x == 0) {
-        // drain: TMA copies issued but never consumed, then the MMAs behind the last commit
+    if (threadIdx.x == 0) {
+        // drain before the CTA's shared memory and TMEM go away: TMA copies issued
+        // but never consumed (only after an abort), then the asynchronous mbarrier
+        // arrivals of the last tcgen05.commit (always)
         int s = sh->consumed % cfg.stages;
         uint32_t ph = (uint32_t)((sh->consumed / cfg.stages) & 1);
         for (int i = sh->consumed; i < sh->issued; i++) {
@@ -271,7 +273,9 @@ int tc_plan(const ConvArgs &a, TcConfig &cfg, std::string &err) {
     cfg.bk = bk;
     cfg.stage_bytes = 128 * bk * 2 + a.N * bk * 2;
     cfg.stage_bytes = (cfg.stage_bytes + 1023) & ~1023;
-    const int budget = 220 * 1024 - (int)sizeof(TcShared) - 1024;
+    // at most ~176 KB per CTA: deep enough for every layer here, with room to spare
+    // below the 227 KB limit (a profiler attached to the process may claim some)
+    const int budget = 176 * 1024 - (int)sizeof(TcShared) - 1024;
     cfg.stages = budget / cfg.stage_bytes;
     if (cfg.stages > kMaxStages) cfg.stages = kMaxStages;
     if (cfg.stages < 2) { err = "shared-memory ring too small"; return -1; }
