@@ -196,9 +196,13 @@ GCDR_API int gcdr_k_nhwc2bgr(const float *y, int H, int W, int ph, int pw, uint8
  *   kind 3  3x3 stride 1, zero pad 1      input [H+2][W+2][C] with a zero border
  *                                         (gcdr_k_to_layout kind 3)
  * weight: fp16 [N][taps*C], k = (ky*3 + kx)*C + c (taps = 9, or 1 for kind 2).
- * epilogue: 0 bias, 1 bias + maxpool 2x2 + relu, 2 bias + relu.
- * out: fp16 [Ho][Wo][N].  reference != 0 runs the SIMT reference kernels
- * instead of tcgen05 (scratch: ceil(Ho*pitch/128)*128*N floats of device memory). */
+ * epilogue: 0 bias, 1 bias + maxpool 2x2 + relu, 2 bias + relu,
+ *           3 raw fp32 split-K partial sums (no bias) into out as float
+ *             [ksplit][Ho*Wo][N] (the first stage of the LayerNorm layers).
+ * out: fp16 [Ho][Wo][N] (epilogue 0-2).  nsplit: N slices per 128-row tile
+ * (N/nsplit a multiple of 16); ksplit: k splits (epilogue 3 only; must divide
+ * 9*C/BK).  0 means 1.  reference != 0 runs the SIMT reference kernels instead
+ * of tcgen05 (nsplit = ksplit = 1; scratch: ceil(Ho*pitch/128)*128*N floats). */
 typedef struct {
     int kind;
     int H, W, C, N;
@@ -208,6 +212,8 @@ typedef struct {
     int epilogue;
     void *out;
     float *scratch;
+    int nsplit;
+    int ksplit;
 } gcdr_conv_desc;
 GCDR_API int gcdr_k_conv(const gcdr_conv_desc *d, int reference, void *stream);
 /* Repacks fp16 NHWC [H][W][C] into a layer input layout:

@@ -342,7 +342,8 @@ int conv_args_from_desc(const gcdr_conv_desc *d, ConvArgs &a, int &mode, std::st
     out.C = d->N;
     out.kind = LAY_PLAIN;
     const __half *B = static_cast<const __half *>(d->weight);
-    mode = d->epilogue == 1 ? EPI_POOL : EPI_PLAIN;
+    if (d->epilogue < 0 || d->epilogue > 3) { err = "bad epilogue"; return -1; }
+    mode = d->epilogue == 1 ? EPI_POOL : d->epilogue == 3 ? EPI_PARTIAL : EPI_PLAIN;
     if (d->kind == 0 || d->kind == 3) {
         in.kind = d->kind == 0 ? LAY_PADREFL : LAY_PADZERO;
         a.ntaps = 9;
@@ -400,6 +401,10 @@ int conv_args_from_desc(const gcdr_conv_desc *d, ConvArgs &a, int &mode, std::st
     a.ep.bias = d->bias;
     a.ep.relu = d->epilogue == 2;
     a.ep.out = out;
+    a.nsplit = d->nsplit > 0 ? d->nsplit : 1;
+    a.ksplit = d->ksplit > 0 ? d->ksplit : 1;
+    if (mode == EPI_PARTIAL) a.ep.partial = static_cast<float *>(d->out);
+    else if (a.ksplit != 1) { err = "k splits need the partial-sum epilogue"; return -1; }
     return 0;
 }
 

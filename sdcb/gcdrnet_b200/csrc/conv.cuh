@@ -19,6 +19,8 @@ struct ConvArgs {
     int tap_off[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
     int C = 0;                 // channels per tap (K per tap)
     int N = 0;                 // output channels (multiple of 16, <= 512)
+    int nsplit = 1;            // N slices per tile (each Nsub = N / nsplit channels)
+    int ksplit = 1;            // k-block splits (EPI_PARTIAL only)
     long long a_rows = 0;
     const __half *A = nullptr; // for the SIMT reference path and host checks
     const __half *B = nullptr; // packed weights [N][ntaps*C]
@@ -34,6 +36,15 @@ __host__ __device__ inline long long tile_a_row(const TileGeom &tg, int tile, in
         return (long long)(2 * y2 + sub) * tg.pitch + xt * 64;
     }
     return (long long)tile * 128 + sub * 64;
+}
+
+// Work unit u -> (tile, n slice, k split).
+__host__ __device__ inline void unit_coords(const ConvArgs &a, int u, int &tile, int &ni, int &ki) {
+    const int per = a.nsplit * a.ksplit;
+    tile = u / per;
+    const int r = u - tile * per;
+    ni = r / a.ksplit;
+    ki = r - ni * a.ksplit;
 }
 
 }  // namespace gcdr

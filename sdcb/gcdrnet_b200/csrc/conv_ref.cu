@@ -41,6 +41,10 @@ struct ScratchLoader {
 #pragma unroll
         for (int k = 0; k < 16; k++) v[k] = p[c0 + k];
     }
+    __device__ void load32(int c0, float *v) {
+#pragma unroll
+        for (int k = 0; k < 32; k++) v[k] = p[c0 + k];
+    }
 };
 
 template <int MODE>
@@ -48,7 +52,7 @@ __global__ void ref_epilogue_kernel(const ConvArgs a, const float *scratch) {
     __shared__ EpiSmem sm;
     const int tile = blockIdx.x, row = threadIdx.x;
     ScratchLoader ld{scratch + ((long long)tile * 128 + row) * a.N};
-    epilogue_tile<MODE>(a.ep, a.tg, tile, row, a.N, ld, &sm);
+    epilogue_tile<MODE>(a.ep, a.tg, tile, row, 0, a.N, a.N, 0, ld, &sm);
 }
 
 }  // namespace
@@ -56,7 +60,7 @@ __global__ void ref_epilogue_kernel(const ConvArgs a, const float *scratch) {
 size_t ref_conv_scratch_floats(const ConvArgs &a) { return (size_t)a.tg.ntiles * 128 * a.N; }
 
 int ref_conv_launch(const ConvArgs &a, int mode, float *scratch, cudaStream_t st, std::string &err) {
-    if (a.N % 16 || a.tg.ntiles < 1) { err = "ref conv: bad shape"; return -1; }
+    if (a.N % 16 || a.tg.ntiles < 1 || a.nsplit != 1 || a.ksplit != 1) { err = "ref conv: bad shape"; return -1; }
     ref_gemm_kernel<<<dim3(a.tg.ntiles, a.N / 16), 128, 0, st>>>(a, scratch);
     switch (mode) {
         case EPI_PLAIN: ref_epilogue_kernel<EPI_PLAIN><<<a.tg.ntiles, 128, 0, st>>>(a, scratch); break;

@@ -48,11 +48,13 @@ __global__ void __launch_bounds__(192, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int N = args.N;
+    const int Ns = N / args.nsplit;                       // channels of one unit
     const int kb_per_tap = args.C / BK;
-    const int kblocks = args.ntaps * kb_per_tap;
+    const int kblocks = args.ntaps * kb_per_tap / args.ksplit;   // k-blocks of one unit
+    const int nunits = args.tg.ntiles * args.nsplit * args.ksplit;
     const uint32_t a_bytes = 128u * BK * 2u;
-    const uint32_t b_bytes = (uint32_t)N * BK * 2u;
-    const int nsub = (N + 255) / 256;
+    const uint32_t b_bytes = (uint32_t)Ns * BK * 2u;
+    const int nsub = (Ns + 255) / 256;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < cfg.stages; s++) {
@@ -87,9 +89,12 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t ph = 0;
             int issued = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < args.tg.ntiles && ok; tile += gridDim.x) {
+            for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+                int tile, ni, ki;
+                unit_coords(args, u, tile, ni, ki);
                 const long long r0 = tile_a_row(args.tg, tile, 0), r1 = tile_a_row(args.tg, tile, 1);
-                for (int kb = 0; kb < kblocks && ok; kb++) {
+                for (int kk = 0; kk < kblocks && ok; kk++) {
+                    const int kb = ki * kblocks + kk;
                     const int tap = kb / kb_per_tap, cb = kb - tap * kb_per_tap;
                     if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err)) { ok = false; break; }
                     uint8_t *sa = ring + (size_t)s * cfg.stage_bytes;
@@ -99,7 +104,8 @@ __global__ void __launch_bounds__(192, 1)
                     tma_load_2d(sa, &tmA, cb * BK, (int)(r0 + off), &sh->full[s]);
                     tma_load_2d(sa + a_bytes / 2, &tmA, cb * BK, (int)(r1 + off), &sh->full[s]);
                     for (int h = 0; h < nsub; h++)
-                        tma_load_2d(sb + (size_t)h * 256 * BK * 2, &tmB, tap * args.C + cb * BK, h * 256, &sh->full[s]);
+                        tma_load_2d(sb + (size_t)h * 256 * BK * 2, &tmB, tap * args.C + cb * BK, ni * Ns + h * 256,
+                                    &sh->full[s]);
                     issued++;
                     if (++s == cfg.stages) { s = 0; ph ^= 1u; }
                 }
@@ -114,7 +120,7 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t ph = 0;
             int t = 0, consumed = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < args.tg.ntiles && ok; tile += gridDim.x, t++) {
+            for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, t++) {
                 const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
                 const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
                 if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err)) break;
@@ -129,7 +135,7 @@ __global__ void __launch_bounds__(192, 1)
                     for (int kk = 0; kk < BK / 16; kk++) {
                         const uint64_t ad = sdesc(sa + kk * 32, sbo, layout);
                         for (int h = 0; h < nsub; h++) {
-                            const int nn = N - h * 256 < 256 ? N - h * 256 : 256;
+                            const int nn = Ns - h * 256 < 256 ? Ns - h * 256 : 256;
                             const uint64_t bd = sdesc(sb + (uint32_t)h * 256u * BK * 2u + kk * 32, sbo, layout);
                             mma_f16(dcol + (uint32_t)(h * 256), ad, bd, idesc_f16(nn), (kb | kk) ? 1u : 0u);
                         }
@@ -146,7 +152,9 @@ __global__ void __launch_bounds__(192, 1)
         const int quad = warp & 3;          // TMEM lane quadrant this warp may read
         const int row = quad * 32 + lane;   // tile row (output position) of this thread
         int t = 0;
-        for (int tile = blockIdx.x; tile < args.tg.ntiles; tile += gridDim.x, t++) {
+        for (int u = blockIdx.x; u < nunits; u += gridDim.x, t++) {
+            int tile, ni, ki;
+            unit_coords(args, u, tile, ni, ki);
             const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
             const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
             bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err);
@@ -162,7 +170,7 @@ __global__ void __launch_bounds__(192, 1)
             if (bad) break;
             tc_fence_after();
             TmemLoader ld{tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(ab * cfg.acc_cols)};
-            epilogue_tile<MODE>(args.ep, args.tg, tile, row, N, ld, &sh->epi);
+            epilogue_tile<MODE>(args.ep, args.tg, tile, row, ni * Ns, Ns, N, ki, ld, &sh->epi);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh->tempty[ab]);
@@ -252,6 +260,7 @@ int launch_bk(const ConvArgs &a, int mode, const TcConfig &cfg, const CUtensorMa
         case EPI_POOL: return launch_bk_mode<BK, EPI_POOL>(a, cfg, ta, tb, grid, st, err);
         case EPI_LN2: return launch_bk_mode<BK, EPI_LN2>(a, cfg, ta, tb, grid, st, err);
         case EPI_RESLN: return launch_bk_mode<BK, EPI_RESLN>(a, cfg, ta, tb, grid, st, err);
+        case EPI_PARTIAL: return launch_bk_mode<BK, EPI_PARTIAL>(a, cfg, ta, tb, grid, st, err);
     }
     err = "bad epilogue mode";
     return -1;
@@ -264,14 +273,17 @@ int tc_pick_bk(int C) { return C % 64 == 0 ? 64 : C % 32 == 0 ? 32 : C % 16 == 0
 int tc_plan(const ConvArgs &a, TcConfig &cfg, std::string &err) {
     const int bk = tc_pick_bk(a.C);
     if (!bk) { err = "channels per tap must be a multiple of 16"; return -1; }
-    if (a.N < 16 || a.N > 512 || a.N % 16) { err = "N must be a multiple of 16 in [16, 512]"; return -1; }
-    if (a.N > 256 && a.N % 256) { err = "N above 256 must be a multiple of 256"; return -1; }
+    if (a.nsplit < 1 || a.ksplit < 1 || a.N % a.nsplit) { err = "bad N / k split"; return -1; }
+    const int Ns = a.N / a.nsplit;
+    if (Ns < 16 || Ns > 512 || Ns % 16) { err = "N slice must be a multiple of 16 in [16, 512]"; return -1; }
+    if (Ns > 256 && Ns % 256) { err = "N slices above 256 must be a multiple of 256"; return -1; }
+    if ((a.ntaps * (a.C / bk)) % a.ksplit) { err = "k split must divide the k-blocks"; return -1; }
     if (a.ntaps < 1 || a.ntaps > 9) { err = "1..9 taps"; return -1; }
     for (int t = 0; t < a.ntaps; t++)
         if (a.tap_off[t] < 0) { err = "negative tap offset"; return -1; }
     if (a.tg.pool && a.tg.pitch < 64 && a.tg.tiles_x != 1) { err = "pool tiling"; return -1; }
     cfg.bk = bk;
-    cfg.stage_bytes = 128 * bk * 2 + a.N * bk * 2;
+    cfg.stage_bytes = 128 * bk * 2 + Ns * bk * 2;
     cfg.stage_bytes = (cfg.stage_bytes + 1023) & ~1023;
     // at most ~176 KB per CTA: deep enough for every layer here, with room to spare
     // below the 227 KB limit (a profiler attached to the process may claim some)
@@ -280,7 +292,7 @@ int tc_plan(const ConvArgs &a, TcConfig &cfg, std::string &err) {
     if (cfg.stages > kMaxStages) cfg.stages = kMaxStages;
     if (cfg.stages < 2) { err = "shared-memory ring too small"; return -1; }
     int cols = 32;
-    while (cols < a.N) cols <<= 1;
+    while (cols < Ns) cols <<= 1;
     cfg.acc_cols = cols;
     cfg.acc_bufs = 2 * cols <= 512 ? 2 : 1;
     cfg.tmem_cols = cols * cfg.acc_bufs;
@@ -296,10 +308,12 @@ int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, st
     }
     CUtensorMap ta, tb;
     if (!encode_2d(&ta, a.A, (uint64_t)a.C, (uint64_t)a.a_rows, (uint32_t)cfg.bk, 64, cfg.bk, err)) return -1;
-    if (!encode_2d(&tb, a.B, (uint64_t)a.C * a.ntaps, (uint64_t)a.N, (uint32_t)cfg.bk, (uint32_t)(a.N < 256 ? a.N : 256),
+    const int Ns = a.N / a.nsplit;
+    if (!encode_2d(&tb, a.B, (uint64_t)a.C * a.ntaps, (uint64_t)a.N, (uint32_t)cfg.bk, (uint32_t)(Ns < 256 ? Ns : 256),
                    cfg.bk, err))
         return -1;
-    int grid = a.tg.ntiles < num_sms ? a.tg.ntiles : num_sms;
+    const int units = a.tg.ntiles * a.nsplit * a.ksplit;
+    int grid = units < num_sms ? units : num_sms;
     if (grid < 1) return 0;
     switch (cfg.bk) {
         case 64: return launch_bk<64>(a, mode, cfg, ta, tb, grid, st, err);

@@ -1,27 +1,31 @@
 // epilogue.cuh -- per-pixel epilogues of the implicit-GEMM convolutions.
 //
-// The GEMM tile is 128 output positions x N channels.  Thread `row` (0..127)
-// of the four epilogue warps owns one position; its N accumulators are read
-// in chunks of 16 columns through a Loader (TMEM for the tcgen05 kernel,
-// global scratch for the SIMT reference), so the same code finishes both.
-// Loader::load16 is warp-synchronous (tcgen05.ld is .sync.aligned): all
-// control flow around it is uniform; per-thread validity only masks stores.
+// The GEMM tile is 128 output positions x Nsub channels (a slice [n0, n0+Nsub)
+// of the layer's N).  Thread `row` (0..127) of the four epilogue warps owns
+// one position; its accumulators are read 32 (or 16) columns at a time through
+// a Loader (TMEM for the tcgen05 kernel, global scratch for the SIMT
+// reference), so the same code finishes both.  Loader loads are
+// warp-synchronous (tcgen05.ld is .sync.aligned): control flow around them is
+// uniform; per-thread validity only masks stores.
 //
 // Modes (the fusions the reference's CPU plan makes, EngineTests.cs:79-141):
-//   EPI_PLAIN  y = acc + bias                                 decoder convs, fc1
-//   EPI_POOL   y = relu(maxpool2x2(acc + bias))               encoder conv+pool+relu (gc#23-25)
-//   EPI_LN2    y0 = LN1(acc + bias) -> out (tokens);          patch embed + its norm (gc#34-37)
-//              h = LN2(y0) -> out2 with the H-shift scatter    and the block's norm2 + shift (gc#38-44)
-//   EPI_RESLN  y = LN(acc + bias + res) -> out                fc2 + residual + norm3 (gc#127-130)
+//   EPI_PLAIN    y = acc + bias [relu]                        decoder convs, fc1
+//   EPI_POOL     y = relu(maxpool2x2(acc + bias))             encoder conv+pool+relu (gc#23-25)
+//   EPI_LN2      y0 = LN1(acc + bias) -> out (tokens);        patch embed + its norm (gc#34-37)
+//                h = LN2(y0) -> out2 with the H-shift scatter  and the block's norm2 + shift (gc#38-44)
+//   EPI_RESLN    y = LN(acc + bias + res) -> out              fc2 + residual + norm3 (gc#127-130)
+//   EPI_PARTIAL  fp32 partial sums of one k-split -> partial[k][token][N] (no bias); a token
+//                kernel (ln_finalize) sums the splits in order and applies the LN modes above,
+//                for layers with too few tiles to fill the GPU.
 #pragma once
 #include "common.cuh"
 
 namespace gcdr {
 
-enum EpiMode : int { EPI_PLAIN = 0, EPI_POOL = 1, EPI_LN2 = 2, EPI_RESLN = 3 };
+enum EpiMode : int { EPI_PLAIN = 0, EPI_POOL = 1, EPI_LN2 = 2, EPI_RESLN = 3, EPI_PARTIAL = 4 };
 
 struct EpiParams {
-    const float *bias = nullptr;
+    const float *bias = nullptr;     // [N] (indexed with the slice offset)
     int relu = 0;                    // EPI_PLAIN: relu after the bias
     Act out;                         // primary output (logical dims = conv or pooled output)
     // LN modes
@@ -30,6 +34,7 @@ struct EpiParams {
     Act out2;                        // EPI_LN2: LN2 output, LAY_PLAIN tokens, H-shift scatter
     ShiftSpec shift;
     const __half *res = nullptr;     // EPI_RESLN residual tokens [T][N]
+    float *partial = nullptr;        // EPI_PARTIAL: [ksplit][T][N] fp32
 };
 
 // Geometry of the output grid: q = y * pitch + x over a flat row space; in pool
@@ -50,47 +55,44 @@ __device__ inline void named_bar_sync(int id, int n) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
+// Reads columns [c0, c0 + w) (w = 32 or 16) of this thread's accumulator row.
 template <class L>
-__device__ inline void ln_stats(L &ld, const EpiParams &ep, int N, long long tok, bool use_res, float &mean, float &rstd,
-                                float eps) {
-    float s = 0.f;
-    float v[16], r[16];
-    for (int c0 = 0; c0 < N; c0 += 16) {
-        ld.load16(c0, v);
-        if (use_res) load16h(ep.res + tok * N + c0, r);
-#pragma unroll
-        for (int k = 0; k < 16; k++) s += v[k] + ep.bias[c0 + k] + (use_res ? r[k] : 0.0f);
+__device__ __forceinline__ void load_cols(L &ld, int c0, int w, float *v) {
+    if (w == 32) ld.load32(c0, v);
+    else ld.load16(c0, v);
+}
+
+// t = acc + bias (+ residual) of columns [c0, c0+w) of the row.
+template <class L>
+__device__ __forceinline__ void row_vals(L &ld, const EpiParams &ep, int N, long long tok, bool use_res, int c0,
+                                         int w, float *v) {
+    load_cols(ld, c0, w, v);
+    float r[32];
+    if (use_res) {
+        load16h(ep.res + tok * N + c0, r);
+        if (w == 32) load16h(ep.res + tok * N + c0 + 16, r + 16);
     }
-    mean = s / N;
-    float q = 0.f;
-    for (int c0 = 0; c0 < N; c0 += 16) {
-        ld.load16(c0, v);
-        if (use_res) load16h(ep.res + tok * N + c0, r);
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-            float d = v[k] + ep.bias[c0 + k] + (use_res ? r[k] : 0.0f) - mean;
-            q += d * d;
-        }
-    }
-    rstd = rsqrtf(q / N + eps);
+    for (int k = 0; k < 32; k++)
+        if (k < w) v[k] += ep.bias[c0 + k] + (use_res ? r[k] : 0.0f);
 }
 
 template <int MODE, class L>
-__device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile, int row, int N, L &ld,
-                              EpiSmem *sm) {
-    float v[16];
+__device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile, int row, int n0, int Nsub, int N,
+                              int ksplit_idx, L &ld, EpiSmem *sm) {
+    float v[32];
+    const int cw = (Nsub % 32 == 0) ? 32 : 16;
     if (MODE == EPI_POOL) {
         const int y2 = tile / tg.tiles_x, xt = tile - y2 * tg.tiles_x;
         const int sub = row >> 6, xx = row & 63;
         const int cx = xt * 64 + xx;
         const bool writer = sub == 0 && (xx & 1) == 0 && cx < tg.conv_w;
-        for (int c0 = 0; c0 < N; c0 += 16) {
+        for (int c0 = 0; c0 < Nsub; c0 += 16) {
             ld.load16(c0, v);
 #pragma unroll
             for (int k = 0; k < 16; k++) {
-                float t = v[k] + ep.bias[c0 + k];
-                float o = __shfl_xor_sync(0xffffffffu, t, 1);
-                v[k] = fmaxf(t, o);
+                float t = v[k] + ep.bias[n0 + c0 + k];
+                v[k] = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, 1));
             }
             if (sub == 1) {
 #pragma unroll
@@ -101,7 +103,7 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
                 __align__(16) __half h[16];
 #pragma unroll
                 for (int k = 0; k < 16; k++) h[k] = __float2half_rn(fmaxf(fmaxf(v[k], sm->x[xx * 17 + k]), 0.0f));
-                act_store(ep.out, y2, cx >> 1, c0, h, 16);
+                act_store(ep.out, y2, cx >> 1, n0 + c0, h, 16);
             }
             named_bar_sync(1, 128);
         }
@@ -110,82 +112,99 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     const long long q = (long long)tile * 128 + row;
     const int y = (int)(q / tg.pitch), x = (int)(q - (long long)y * tg.pitch);
     const bool valid = y < tg.conv_h && x < tg.conv_w;
-    if (MODE == EPI_PLAIN) {
-        for (int c0 = 0; c0 < N; c0 += 16) {
-            ld.load16(c0, v);
-            if (valid) {
-                __align__(16) __half h[16];
-#pragma unroll
-                for (int k = 0; k < 16; k++) {
-                    float t = v[k] + ep.bias[c0 + k];
-                    h[k] = __float2half_rn(ep.relu ? fmaxf(t, 0.0f) : t);
-                }
-                act_store(ep.out, y, x, c0, h, 16);
-            }
-        }
-        return;
-    }
-    // LayerNorm modes: the whole row of N channels is in this thread's lane.
     const long long tok = valid ? (long long)y * tg.conv_w + x : 0;
-    const bool use_res = MODE == EPI_RESLN;
-    float mean, rstd;
-    ln_stats(ld, ep, N, tok, use_res, mean, rstd, ep.eps1);
-    if (MODE == EPI_RESLN) {
-        float r[16];
-        for (int c0 = 0; c0 < N; c0 += 16) {
-            ld.load16(c0, v);
+    if (MODE == EPI_PLAIN) {
+        for (int c0 = 0; c0 < Nsub; c0 += cw) {
+            load_cols(ld, c0, cw, v);
             if (valid) {
-                load16h(ep.res + tok * N + c0, r);
-                __align__(16) __half h[16];
+                __align__(16) __half h[32];
 #pragma unroll
-                for (int k = 0; k < 16; k++) {
-                    int c = c0 + k;
-                    float t = v[k] + ep.bias[c] + r[k];
-                    h[k] = __float2half_rn((t - mean) * rstd * ep.g1[c] + ep.b1[c]);
+                for (int k = 0; k < 32; k++) {
+                    if (k < cw) {
+                        float t = v[k] + ep.bias[n0 + c0 + k];
+                        h[k] = __float2half_rn(ep.relu ? fmaxf(t, 0.0f) : t);
+                    }
                 }
-                act_store(ep.out, y, x, c0, h, 16);
+                act_store(ep.out, y, x, n0 + c0, h, cw);
             }
         }
         return;
     }
-    // EPI_LN2: y0 = LN1(v) stored; LN2 statistics over the fp32 y0.
-    float s2 = 0.f;
-    for (int c0 = 0; c0 < N; c0 += 16) {
-        ld.load16(c0, v);
-        __align__(16) __half h[16];
+    if (MODE == EPI_PARTIAL) {
+        const long long T = (long long)tg.conv_h * tg.conv_w;
+        float *dst = ep.partial + ((long long)ksplit_idx * T + tok) * N + n0;
+        for (int c0 = 0; c0 < Nsub; c0 += cw) {
+            load_cols(ld, c0, cw, v);
+            if (valid) {
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-            int c = c0 + k;
-            float t = (v[k] + ep.bias[c] - mean) * rstd * ep.g1[c] + ep.b1[c];
-            s2 += t;
-            h[k] = __float2half_rn(t);
-        }
-        if (valid) act_store(ep.out, y, x, c0, h, 16);
-    }
-    const float mean2 = s2 / N;
-    float q2 = 0.f;
-    for (int c0 = 0; c0 < N; c0 += 16) {
-        ld.load16(c0, v);
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-            int c = c0 + k;
-            float t = (v[k] + ep.bias[c] - mean) * rstd * ep.g1[c] + ep.b1[c];
-            float d = t - mean2;
-            q2 += d * d;
-        }
-    }
-    const float rstd2 = rsqrtf(q2 / N + ep.eps2);
-    for (int c0 = 0; c0 < N; c0 += 16) {
-        ld.load16(c0, v);
-        if (valid) {
-            float o[16];
-#pragma unroll
-            for (int k = 0; k < 16; k++) {
-                int c = c0 + k;
-                float t = (v[k] + ep.bias[c] - mean) * rstd * ep.g1[c] + ep.b1[c];
-                o[k] = (t - mean2) * rstd2 * ep.g2[c] + ep.b2[c];
+                for (int k = 0; k < 32; k += 4)
+                    if (k < cw) *reinterpret_cast<float4 *>(dst + c0 + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
             }
-            shift_store(ep.out2, ep.shift, 2, y, x, c0, o, 16);
+        }
+        return;
+    }
+    // LayerNorm modes (the slice is the whole row: n0 = 0, Nsub = N): single-pass
+    // statistics shifted by the row's first value.
+    const bool use_res = MODE == EPI_RESLN;
+    float shift0 = 0.f, s1 = 0.f, s2 = 0.f;
+    for (int c0 = 0; c0 < N; c0 += cw) {
+        row_vals(ld, ep, N, tok, use_res, c0, cw, v);
+        if (c0 == 0) shift0 = v[0];
+#pragma unroll
+        for (int k = 0; k < 32; k++)
+            if (k < cw) {
+                const float d = v[k] - shift0;
+                s1 += d;
+                s2 += d * d;
+            }
+    }
+    const float m1 = s1 / N;
+    const float mean = shift0 + m1;
+    const float rstd = rsqrtf(fmaxf(s2 / N - m1 * m1, 0.0f) + ep.eps1);
+    if (MODE == EPI_RESLN) {
+        for (int c0 = 0; c0 < N; c0 += cw) {
+            row_vals(ld, ep, N, tok, true, c0, cw, v);
+            if (valid) {
+                __align__(16) __half h[32];
+#pragma unroll
+                for (int k = 0; k < 32; k++)
+                    if (k < cw) h[k] = __float2half_rn((v[k] - mean) * rstd * ep.g1[c0 + k] + ep.b1[c0 + k]);
+                act_store(ep.out, y, x, c0, h, cw);
+            }
+        }
+        return;
+    }
+    // EPI_LN2: y0 = LN1(v) stored; LN2 statistics over the fp32 y0 (shifted by its first value).
+    float t0 = 0.f, u1 = 0.f, u2 = 0.f;
+    for (int c0 = 0; c0 < N; c0 += cw) {
+        row_vals(ld, ep, N, tok, false, c0, cw, v);
+        __align__(16) __half h[32];
+#pragma unroll
+        for (int k = 0; k < 32; k++)
+            if (k < cw) {
+                const float t = (v[k] - mean) * rstd * ep.g1[c0 + k] + ep.b1[c0 + k];
+                if (c0 == 0 && k == 0) t0 = t;
+                const float d = t - t0;
+                u1 += d;
+                u2 += d * d;
+                h[k] = __float2half_rn(t);
+            }
+        if (valid) act_store(ep.out, y, x, c0, h, cw);
+    }
+    const float mu = u1 / N;
+    const float mean2 = t0 + mu;
+    const float rstd2 = rsqrtf(fmaxf(u2 / N - mu * mu, 0.0f) + ep.eps2);
+    for (int c0 = 0; c0 < N; c0 += cw) {
+        row_vals(ld, ep, N, tok, false, c0, cw, v);
+        if (valid) {
+            float o[32];
+#pragma unroll
+            for (int k = 0; k < 32; k++)
+                if (k < cw) {
+                    const float t = (v[k] - mean) * rstd * ep.g1[c0 + k] + ep.b1[c0 + k];
+                    o[k] = (t - mean2) * rstd2 * ep.g2[c0 + k] + ep.b2[c0 + k];
+                }
+            shift_store(ep.out2, ep.shift, 2, y, x, c0, o, cw);
         }
     }
 }

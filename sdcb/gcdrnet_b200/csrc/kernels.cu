@@ -366,6 +366,83 @@ __global__ void up_add_tok_kernel(const UpAddArgs a) {
     }
 }
 
+// One warp per token; lanes own channel pairs (N even, N <= 512).
+__global__ void ln_finalize_kernel(const LnFinalizeArgs a) {
+    const long long t = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const long long T = (long long)a.H * a.W;
+    if (t >= T) return;
+    const int y = (int)(t / a.W), x = (int)(t - (long long)y * a.W);
+    const int N = a.N, pairs = N / 2;
+    float v[16];
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int pi = lane + 32 * j;
+        if (pi >= pairs) break;
+        const int c = 2 * pi;
+        float2 acc = make_float2(a.bias[c], a.bias[c + 1]);
+        for (int k = 0; k < a.ksplit; k++) {
+            const float2 p = *reinterpret_cast<const float2 *>(a.partial + ((long long)k * T + t) * N + c);
+            acc.x += p.x;
+            acc.y += p.y;
+        }
+        if (a.res) {
+            const float2 r = __half22float2(*reinterpret_cast<const __half2 *>(a.res + t * N + c));
+            acc.x += r.x;
+            acc.y += r.y;
+        }
+        v[2 * j] = acc.x;
+        v[2 * j + 1] = acc.y;
+        sum += acc.x + acc.y;
+    }
+    for (int m = 16; m; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+    const float mean = sum / N;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        if (lane + 32 * j >= pairs) break;
+        const float d0 = v[2 * j] - mean, d1 = v[2 * j + 1] - mean;
+        q += d0 * d0 + d1 * d1;
+    }
+    for (int m = 16; m; m >>= 1) q += __shfl_xor_sync(0xffffffffu, q, m);
+    const float rstd = rsqrtf(q / N + a.eps1);
+    float s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int pi = lane + 32 * j;
+        if (pi >= pairs) break;
+        const int c = 2 * pi;
+        const float y0 = (v[2 * j] - mean) * rstd * a.g1[c] + a.b1[c];
+        const float y1 = (v[2 * j + 1] - mean) * rstd * a.g1[c + 1] + a.b1[c + 1];
+        __align__(4) __half h[2] = {__float2half_rn(y0), __float2half_rn(y1)};
+        act_store(a.out, y, x, c, h, 2);
+        v[2 * j] = y0;
+        v[2 * j + 1] = y1;
+        s2 += y0 + y1;
+    }
+    if (!a.ln2) return;
+    for (int m = 16; m; m >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, m);
+    const float mean2 = s2 / N;
+    float q2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        if (lane + 32 * j >= pairs) break;
+        const float d0 = v[2 * j] - mean2, d1 = v[2 * j + 1] - mean2;
+        q2 += d0 * d0 + d1 * d1;
+    }
+    for (int m = 16; m; m >>= 1) q2 += __shfl_xor_sync(0xffffffffu, q2, m);
+    const float rstd2 = rsqrtf(q2 / N + a.eps2);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int pi = lane + 32 * j;
+        if (pi >= pairs) break;
+        const int c = 2 * pi;
+        float o[2] = {(v[2 * j] - mean2) * rstd2 * a.g2[c] + a.b2[c], (v[2 * j + 1] - mean2) * rstd2 * a.g2[c + 1] + a.b2[c + 1]};
+        shift_store(a.out2, a.shift, 2, y, x, c, o, 2);
+    }
+}
+
 __global__ void bgr2nhwc_kernel(const ImgSpec im, float *x, int H, int W) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)H * W) return;
@@ -460,6 +537,13 @@ int up_add_launch(const UpAddArgs &a, cudaStream_t st) {
         const long long n = (long long)a.out.H * a.out.W * 32;
         up_add_tok_kernel<<<grid_for(n, 256), 256, 0, st>>>(a);
     }
+    return launch_status();
+}
+
+int ln_finalize_launch(const LnFinalizeArgs &a, cudaStream_t st) {
+    if (a.N % 2 || a.N > 512 || a.ksplit < 1) return -2;
+    const long long n = (long long)a.H * a.W * 32;
+    ln_finalize_kernel<<<grid_for(n, 256), 256, 0, st>>>(a);
     return launch_status();
 }
 

@@ -77,6 +77,27 @@ struct UpAddArgs {
 };
 int up_add_launch(const UpAddArgs &a, cudaStream_t st);
 
+// Finishes a split-K tensor-core layer (EPI_PARTIAL): per token, sums the
+// k-split partials in order, adds the bias (and the residual), then
+//   ln2 = 0: out = LN1(v)                               (fc2 + residual + norm)
+//   ln2 = 1: out = y0 = LN1(v) (tokens); out2 = LN2(y0) with the H shift
+//            (patch embed + its norm + the block's norm2 + shift)
+struct LnFinalizeArgs {
+    const float *partial = nullptr;   // [ksplit][T][N]
+    int ksplit = 1;
+    int H = 0, W = 0, N = 0;          // token grid (T = H*W) and channels
+    const float *bias = nullptr;
+    const __half *res = nullptr;      // optional residual tokens [T][N]
+    const float *g1 = nullptr, *b1 = nullptr;
+    float eps1 = 1e-5f;
+    int ln2 = 0;
+    const float *g2 = nullptr, *b2 = nullptr;
+    float eps2 = 1e-5f;
+    ShiftSpec shift;
+    Act out, out2;
+};
+int ln_finalize_launch(const LnFinalizeArgs &a, cudaStream_t st);
+
 // Standalone glue kernels (the C ABI's gcdr_k_*).
 int k_bgr2nhwc(const uint8_t *src, int w, int h, int stride, int fmt, float *x, int ph, int pw, cudaStream_t st);
 int k_div6(const float *x, const float *s, size_t npx, float *out6, cudaStream_t st);

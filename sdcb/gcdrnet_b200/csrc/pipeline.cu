@@ -279,6 +279,63 @@ ConvArgs fc(const __half *in, int H, int W, int C, const __half *B, const float 
     return a;
 }
 
+// How a tensor-core layer is spread over the GPU.  Layers with fewer 128-row
+// tiles than SMs get N slices (any mode) and, for the LayerNorm modes, k splits
+// whose fp32 partials a token kernel reduces in a fixed order (deterministic).
+struct Split {
+    int nsplit = 1, ksplit = 1;
+};
+
+Split split_policy(const ConvArgs &a, bool ln_mode, int nsm) {
+    Split s;
+    if (a.tg.ntiles >= nsm) return s;
+    auto units = [&] { return a.tg.ntiles * s.nsplit * s.ksplit; };
+    for (int ns = 1; ns <= a.N / 32; ns++) {
+        if (a.N % ns) continue;
+        const int Ns = a.N / ns;
+        if (Ns % 16 || (Ns > 256 && Ns % 256)) continue;
+        s.nsplit = ns;
+        if (units() >= nsm) break;
+    }
+    if (ln_mode) {
+        const int bk = tc_pick_bk(a.C);
+        const int kblocks = a.ntaps * (a.C / bk);
+        for (int ks = 1; ks <= 9; ks++) {
+            if (kblocks % ks) continue;
+            s.ksplit = ks;
+            if (units() >= 2 * nsm) break;
+        }
+    }
+    return s;
+}
+
+bool uses_partial(const ConvArgs &a, int mode, int nsm) {
+    if (mode != EPI_LN2 && mode != EPI_RESLN) return false;
+    Split s = split_policy(a, true, nsm);
+    return s.nsplit > 1 || s.ksplit > 1;
+}
+
+// fp32 floats of the split-K workspace the LayerNorm layers of one net need.
+size_t partial_floats(const DevNet &n, int H, int W, int nsm) {
+    const int H3 = H / 8, W3 = W / 8, H4 = H / 16, W4 = W / 16, H5 = H / 32, W5 = W / 32;
+    Act t3, t4;
+    t3.H = H3; t3.W = W3; t3.C = n.c3; t3.kind = LAY_PHASE;
+    t4.H = H4; t4.W = W4; t4.C = n.c4; t4.kind = LAY_PHASE;
+    std::vector<std::pair<ConvArgs, int>> layers;
+    layers.push_back({conv_s2(t3, nullptr, nullptr, n.c4), EPI_LN2});
+    layers.push_back({conv_s2(t4, nullptr, nullptr, n.c5), EPI_LN2});
+    layers.push_back({fc(nullptr, H4, W4, n.c4, nullptr, nullptr), EPI_RESLN});
+    layers.push_back({fc(nullptr, H5, W5, n.c5, nullptr, nullptr), EPI_RESLN});
+    layers.push_back({fc(nullptr, H3, W3, n.c3, nullptr, nullptr), EPI_RESLN});
+    size_t need = 0;
+    for (auto &l : layers) {
+        if (!uses_partial(l.first, l.second, nsm)) continue;
+        Split s = split_policy(l.first, true, nsm);
+        need = std::max(need, (size_t)s.ksplit * l.first.tg.conv_h * l.first.tg.conv_w * l.first.N);
+    }
+    return need;
+}
+
 }  // namespace
 
 int Worker::plan_arena() {
@@ -293,6 +350,8 @@ int Worker::plan_arena() {
     al.take(reinterpret_cast<void **>(&d_src_), img + 16);
     al.take(reinterpret_cast<void **>(&d_dst_), img + 16);
     al.take(reinterpret_cast<void **>(&d_err_), 256);
+    const size_t wsf = std::max(partial_floats(w.gc, H_, W_, num_sms_), partial_floats(w.dr, H_, W_, num_sms_));
+    al.take(reinterpret_cast<void **>(&ws_), std::max(wsf, (size_t)64) * 4);
     const size_t need = al.off;
     // grow-only within the budget (VkPipeline2.cs:104-117): 1/8 headroom first, 1/4 on regrowth
     const size_t budget = size_t(3) << 30;
@@ -331,24 +390,59 @@ int Worker::build_ops() {
     const DevWeights &wt = *weights_;
     const int nsm = num_sms_;
     int *errp = d_err_;
-    auto conv_op = [this, nsm, errp](ConvArgs a, int mode, const char *name) {
+    auto conv_op = [this, nsm, errp](ConvArgs a, int mode, const std::string &name) {
         a.err = errp;
+        const bool partial = uses_partial(a, mode, nsm);
+        int run_mode = mode;
+        if (mode == EPI_PLAIN || partial) {
+            Split sp = split_policy(a, mode != EPI_PLAIN, nsm);
+            a.nsplit = sp.nsplit;
+            if (partial) {
+                a.ksplit = sp.ksplit;
+                a.ep.partial = ws_;
+                run_mode = EPI_PARTIAL;
+            }
+        }
         OpInfo oi;
         oi.name = name;
         oi.tensor = 1;
         const double px = (double)a.tg.conv_h * a.tg.conv_w;
         oi.flops = 2.0 * px * a.N * a.ntaps * a.C;
         const double in_px = a.ntaps == 1 ? px : (a.tap_off[1] == 1 ? px : 4.0 * px);   // s2 reads 4x its outputs
-        double out_px = mode == EPI_POOL ? px / 4 : px;
-        oi.bytes = in_px * a.C * 2 + out_px * a.N * 2 * (mode == EPI_LN2 ? 2 : 1) + (double)a.N * a.ntaps * a.C * 2 +
-                   (mode == EPI_RESLN ? px * a.N * 2 : 0);
+        const double out_px = mode == EPI_POOL ? px / 4 : px;
+        oi.bytes = in_px * a.C * 2 + (double)a.N * a.ntaps * a.C * 2 +
+                   (partial ? 4.0 * px * a.N * a.ksplit
+                            : out_px * a.N * 2 * (mode == EPI_LN2 ? 2 : 1) + (mode == EPI_RESLN ? px * a.N * 2 : 0));
         info_.push_back(oi);
-        ops_.push_back([a, mode, nsm, this](cudaStream_t st) {
+        ops_.push_back([a, run_mode, nsm, this](cudaStream_t st) {
             std::string e;
-            if (tc_conv_launch(a, mode, nsm, st, e)) return fail(GCDR_ERR_DEVICE, e);
+            if (tc_conv_launch(a, run_mode, nsm, st, e)) return fail(GCDR_ERR_DEVICE, e);
             return 0;
         });
         launches_++;
+        if (partial) {
+            LnFinalizeArgs f;
+            f.partial = ws_;
+            f.ksplit = a.ksplit;
+            f.H = a.tg.conv_h;
+            f.W = a.tg.conv_w;
+            f.N = a.N;
+            f.bias = a.ep.bias;
+            f.res = mode == EPI_RESLN ? a.ep.res : nullptr;
+            f.g1 = a.ep.g1; f.b1 = a.ep.b1; f.eps1 = a.ep.eps1;
+            f.ln2 = mode == EPI_LN2;
+            f.g2 = a.ep.g2; f.b2 = a.ep.b2; f.eps2 = a.ep.eps2;
+            f.shift = a.ep.shift;
+            f.out = a.ep.out;
+            f.out2 = a.ep.out2;
+            ops_.push_back([f, this](cudaStream_t st) {
+                return ln_finalize_launch(f, st) ? fail(GCDR_ERR_DEVICE, "ln_finalize launch") : 0;
+            });
+            launches_++;
+            info_.push_back(OpInfo{name + ".ln", 0,
+                                   4.0 * px * a.N * a.ksplit + 2.0 * px * a.N * (f.ln2 ? 2 : 1) + (f.res ? 2.0 * px * a.N : 0),
+                                   0});
+        }
     };
     ops_.push_back([errp](cudaStream_t st) { return cudaMemsetAsync(errp, 0, sizeof(int), st) == cudaSuccess ? 0 : GCDR_ERR_DEVICE; });
     info_.clear();
@@ -390,12 +484,12 @@ int Worker::build_ops() {
         simt(pre + "stem", 2.0 * H_ * W_ * n.c1 * 9 * n.cin,
              (double)h_ * w_ * bpp_ + (which ? 12.0 * H_ * W_ : 0) + (double)H1 * W1 * n.c1 * 2);
         // encoders 2, 3: conv + pool + relu
-        { ConvArgs a = conv_s1(b.t1, n.enc2, n.enc2_b, n.c2, true); a.ep.out = b.t2; conv_op(a, EPI_POOL, (pre + "enc2").c_str()); }
-        { ConvArgs a = conv_s1(b.t2, n.enc3, n.enc3_b, n.c3, true); a.ep.out = b.t3; conv_op(a, EPI_POOL, (pre + "enc3").c_str()); }
+        { ConvArgs a = conv_s1(b.t1, n.enc2, n.enc2_b, n.c2, true); a.ep.out = b.t2; conv_op(a, EPI_POOL, pre + "enc2"); }
+        { ConvArgs a = conv_s1(b.t2, n.enc3, n.enc3_b, n.c3, true); a.ep.out = b.t3; conv_op(a, EPI_POOL, pre + "enc3"); }
 
         // shifted-MLP block body after its norm2+shift producer: fc1, dw+gelu+shift, fc2+res+norm
         auto block = [&](const DevBlock &bk, int H, int W, const Act &out, const std::string &bn) {
-            { ConvArgs a = fc(b.hs, H, W, bk.C, bk.fc1, bk.fc1_b); a.ep.out = plain(b.f1, H, W, bk.C); conv_op(a, EPI_PLAIN, (bn + ".fc1").c_str()); }
+            { ConvArgs a = fc(b.hs, H, W, bk.C, bk.fc1, bk.fc1_b); a.ep.out = plain(b.f1, H, W, bk.C); conv_op(a, EPI_PLAIN, bn + ".fc1"); }
             const __half *f1 = b.f1; __half *f2 = b.f2;
             const float *dw = bk.dw_w, *db = bk.dw_b;
             ShiftSpec sb = bk.sb;
@@ -409,7 +503,7 @@ int Worker::build_ops() {
             a.ep.res = b.y0;
             a.ep.g1 = bk.no_g; a.ep.b1 = bk.no_b; a.ep.eps1 = bk.no_eps;
             a.ep.out = out;
-            conv_op(a, EPI_RESLN, (bn + ".fc2_ln").c_str());
+            conv_op(a, EPI_RESLN, bn + ".fc2_ln");
         };
         // patch embed 3 + norm + block1 norm2 + H shift
         {
@@ -419,7 +513,7 @@ int Worker::build_ops() {
             a.ep.out = plain(b.y0, H4, W4, n.c4);
             a.ep.out2 = plain(b.hs, H4, W4, n.c4);
             a.ep.shift = n.blk[0].sa;
-            conv_op(a, EPI_LN2, (pre + "pe3_ln").c_str());
+            conv_op(a, EPI_LN2, pre + "pe3_ln");
         }
         block(n.blk[0], H4, W4, b.t4, pre + "block1");
         {
@@ -429,11 +523,11 @@ int Worker::build_ops() {
             a.ep.out = plain(b.y0, H5, W5, n.c5);
             a.ep.out2 = plain(b.hs, H5, W5, n.c5);
             a.ep.shift = n.blk[1].sa;
-            conv_op(a, EPI_LN2, (pre + "pe4_ln").c_str());
+            conv_op(a, EPI_LN2, pre + "pe4_ln");
         }
         block(n.blk[1], H5, W5, b.b2o, pre + "block2");
         // decoder 1 -> up + t4 -> dblock1
-        { ConvArgs a = conv_s1(b.b2o, n.dec[0], n.dec_b[0], n.c4, false); a.ep.out = plain(b.dconv, H5, W5, n.c4); conv_op(a, EPI_PLAIN, (pre + "dec1").c_str()); }
+        { ConvArgs a = conv_s1(b.b2o, n.dec[0], n.dec_b[0], n.c4, false); a.ep.out = plain(b.dconv, H5, W5, n.c4); conv_op(a, EPI_PLAIN, pre + "dec1"); }
         auto up_tok = [&](int H, int W, int C, const Act &skip, const DevBlock &bk) {
             UpAddArgs u;
             u.d = b.dconv;
@@ -458,14 +552,14 @@ int Worker::build_ops() {
         };
         up_tok(H4, W4, n.c4, b.t4, n.blk[2]);
         block(n.blk[2], H4, W4, b.db1o, pre + "dblock1");
-        { ConvArgs a = conv_s1(b.db1o, n.dec[1], n.dec_b[1], n.c3, false); a.ep.out = plain(b.dconv, H4, W4, n.c3); conv_op(a, EPI_PLAIN, (pre + "dec2").c_str()); }
+        { ConvArgs a = conv_s1(b.db1o, n.dec[1], n.dec_b[1], n.c3, false); a.ep.out = plain(b.dconv, H4, W4, n.c3); conv_op(a, EPI_PLAIN, pre + "dec2"); }
         up_tok(H3, W3, n.c3, b.t3, n.blk[3]);
         block(n.blk[3], H3, W3, b.db2o, pre + "dblock2");
-        { ConvArgs a = conv_s1(b.db2o, n.dec[2], n.dec_b[2], n.c2, false); a.ep.out = plain(b.dconv, H3, W3, n.c2); conv_op(a, EPI_PLAIN, (pre + "dec3").c_str()); }
+        { ConvArgs a = conv_s1(b.db2o, n.dec[2], n.dec_b[2], n.c2, false); a.ep.out = plain(b.dconv, H3, W3, n.c2); conv_op(a, EPI_PLAIN, pre + "dec3"); }
         up_pad(b.t2, b.d3);
-        { ConvArgs a = conv_s1(b.d3, n.dec[3], n.dec_b[3], n.c1, false); a.ep.out = plain(b.dconv, H2, W2, n.c1); conv_op(a, EPI_PLAIN, (pre + "dec4").c_str()); }
+        { ConvArgs a = conv_s1(b.d3, n.dec[3], n.dec_b[3], n.c1, false); a.ep.out = plain(b.dconv, H2, W2, n.c1); conv_op(a, EPI_PLAIN, pre + "dec4"); }
         up_pad(b.t1, b.d4);
-        { ConvArgs a = conv_s1(b.d4, n.dec[4], n.dec_b[4], n.c1, false); a.ep.out = plain(b.dec5, H1, W1, n.c1); conv_op(a, EPI_PLAIN, (pre + "dec5").c_str()); }
+        { ConvArgs a = conv_s1(b.d4, n.dec[4], n.dec_b[4], n.c1, false); a.ep.out = plain(b.dec5, H1, W1, n.c1); conv_op(a, EPI_PLAIN, pre + "dec5"); }
         // head: recomputed stem skip + bilinear + 1x1 + sigmoid, then div6 (GC) or u8 out (DR)
         HeadArgs ha;
         ha.img = img;

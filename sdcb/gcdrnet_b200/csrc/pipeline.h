@@ -106,6 +106,7 @@ private:
     size_t arena_bytes_ = 0;
     NetBufs gcb_, drb_;
     float *r_ = nullptr, *ism_ = nullptr, *ydbg_ = nullptr;
+    float *ws_ = nullptr;   // split-K partial sums (EPI_PARTIAL), shared by both nets
     uint8_t *d_src_ = nullptr, *d_dst_ = nullptr;
     int *d_err_ = nullptr;
     // pinned staging

@@ -11,7 +11,7 @@ class ConvDesc(ctypes.Structure):
     _fields_ = [("kind", ctypes.c_int), ("H", ctypes.c_int), ("W", ctypes.c_int), ("C", ctypes.c_int),
                 ("N", ctypes.c_int), ("inp", ctypes.c_void_p), ("weight", ctypes.c_void_p),
                 ("bias", ctypes.c_void_p), ("epilogue", ctypes.c_int), ("out", ctypes.c_void_p),
-                ("scratch", ctypes.c_void_p)]
+                ("scratch", ctypes.c_void_p), ("nsplit", ctypes.c_int), ("ksplit", ctypes.c_int)]
 
 
 def pack_weights(w_onnx: np.ndarray) -> np.ndarray:
@@ -20,8 +20,9 @@ def pack_weights(w_onnx: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(w_onnx.transpose(0, 2, 3, 1).reshape(N, k * k * C))
 
 
-def run_conv(lib, kind, x_hwc, w_onnx, bias, epilogue=0, reference=False):
-    """Runs one layer through gcdr_k_conv on cuda:0; returns fp32 numpy [Ho][Wo][N]."""
+def run_conv(lib, kind, x_hwc, w_onnx, bias, epilogue=0, reference=False, nsplit=1, ksplit=1):
+    """Runs one layer through gcdr_k_conv on cuda:0; returns fp32 numpy [Ho][Wo][N]
+    (epilogue 3: the split-K partials summed in order plus the bias)."""
     import torch
     H, W, C = x_hwc.shape
     N = w_onnx.shape[0]
@@ -43,8 +44,12 @@ def run_conv(lib, kind, x_hwc, w_onnx, bias, epilogue=0, reference=False):
         Ho, Wo = H // 2, W // 2
     else:
         Ho, Wo = H, W
-    out = torch.full((Ho, Wo, N), float("nan"), dtype=torch.float16, device=dev)
-    d = ConvDesc(kind, H, W, C, N, inp.data_ptr(), wt.data_ptr(), bt.data_ptr(), epilogue, out.data_ptr(), None)
+    if epilogue == 3:
+        out = torch.full((ksplit, Ho * Wo, N), float("nan"), dtype=torch.float32, device=dev)
+    else:
+        out = torch.full((Ho, Wo, N), float("nan"), dtype=torch.float16, device=dev)
+    d = ConvDesc(kind, H, W, C, N, inp.data_ptr(), wt.data_ptr(), bt.data_ptr(), epilogue, out.data_ptr(), None,
+                 nsplit, ksplit)
     scratch = None
     if reference:
         n = lib.gcdr_k_conv_scratch(ctypes.byref(d))
@@ -53,6 +58,11 @@ def run_conv(lib, kind, x_hwc, w_onnx, bias, epilogue=0, reference=False):
     rc = lib.gcdr_k_conv(ctypes.byref(d), 1 if reference else 0, None)
     assert rc == 0, rc
     torch.cuda.synchronize()
+    if epilogue == 3:
+        tot = out[0].clone()
+        for k in range(1, ksplit):
+            tot += out[k]
+        return (tot + bt[None, :]).reshape(Ho, Wo, N).cpu().numpy()
     return out.float().cpu().numpy()
 
 
@@ -75,4 +85,5 @@ def torch_conv(kind, x_hwc, w_onnx, bias, epilogue=0):
         y = F.relu(F.max_pool2d(y, 2))
     elif epilogue == 2:
         y = F.relu(y)
+    # epilogue 3 (partials + bias) is the plain conv
     return y[0].permute(1, 2, 0).numpy()

@@ -63,3 +63,31 @@ def test_tc_conv_matches_reference_and_torch(case):
     assert d_ref < 2e-3, f"tcgen05 vs SIMT reference max rel {d_ref}"
     assert d_torch < 4e-3, f"tcgen05 vs torch fp32 max rel {d_torch}"
     assert rel_l2 < 1e-3, f"rel L2 {rel_l2}"
+
+
+# N slices (any epilogue) and split-K fp32 partials (the first stage of the
+# LayerNorm layers with few tiles): (kind, H, W, C, N, epilogue, nsplit, ksplit)
+SPLIT_CASES = [
+    (2, 4, 5, 512, 512, 0, 4, 1),     # DR block2 fc1 at /32, 4 slices of 128
+    (0, 2, 3, 256, 160, 0, 5, 1),     # GC dec1 at /32, 5 slices of 32
+    (1, 4, 6, 256, 512, 3, 2, 9),     # DR pe4: 2 slices x 9 k splits (one tap each)
+    (1, 6, 8, 160, 256, 3, 1, 5),     # GC pe4: 5 k splits of 9 k-blocks
+    (2, 5, 7, 512, 512, 3, 2, 4),     # DR block2 fc2
+    (2, 9, 10, 256, 256, 3, 1, 2),    # block1 fc2 at /16
+    (0, 16, 20, 32, 64, 1, 2, 1),     # pool epilogue with 2 slices
+]
+
+
+@pytest.mark.parametrize("case", SPLIT_CASES, ids=lambda c: "k%d_%dx%d_c%d_n%d_e%d_ns%d_ks%d" % c)
+def test_tc_conv_splits(case):
+    from sdcb.gcdrnet_b200 import lib
+    kind, H, W, C, N, ep, ns, ks = case
+    x, w, b = _inputs(kind, H, W, C, N, hash(case) & 0xFFFF)
+    L = lib()
+    tc = run_conv(L, kind, x, w, b, ep, nsplit=ns, ksplit=ks)
+    want = torch_conv(kind, x, w, b, 1 if ep == 1 else 0)
+    assert not np.isnan(tc).any(), "unwritten outputs"
+    scale = np.abs(want).max() + 1e-6
+    d = np.abs(tc - want).max() / scale
+    tol = 2e-4 if ep == 3 else 4e-3   # partials are fp32 (no fp16 output rounding)
+    assert d < tol, f"split conv vs torch fp32: max rel {d}"
