@@ -13,7 +13,9 @@ constexpr int kMaxStages = 32;
 struct TcConfig {
     int bk = 64;           // channels per k-block (16/32/64 -> SWIZZLE_32B/64B/128B)
     int stages = 2;        // shared-memory ring depth
-    int stage_bytes = 0;   // A tile + B tile, 1 KB aligned
+    int kps = 1;           // k-blocks (A tile + B tile pairs) per ring stage
+    int sub_bytes = 0;     // one A tile + B tile, 1 KB aligned
+    int stage_bytes = 0;   // kps * sub_bytes
     int acc_cols = 32;     // TMEM columns per accumulator (power of two >= N)
     int acc_bufs = 1;      // accumulator double buffering
     int tmem_cols = 32;

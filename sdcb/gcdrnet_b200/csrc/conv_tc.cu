@@ -93,19 +93,22 @@ __global__ void __launch_bounds__(192, 1)
                 int tile, ni, ki;
                 unit_coords(args, u, tile, ni, ki);
                 const long long r0 = tile_a_row(args.tg, tile, 0), r1 = tile_a_row(args.tg, tile, 1);
-                for (int kk = 0; kk < kblocks && ok; kk++) {
-                    const int kb = ki * kblocks + kk;
-                    const int tap = kb / kb_per_tap, cb = kb - tap * kb_per_tap;
+                for (int st = 0; st < kblocks / cfg.kps && ok; st++) {
                     if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err)) { ok = false; break; }
-                    uint8_t *sa = ring + (size_t)s * cfg.stage_bytes;
-                    uint8_t *sb = sa + a_bytes;
-                    mbar_expect_tx(&sh->full[s], a_bytes + b_bytes);
-                    const int off = args.tap_off[tap];
-                    tma_load_2d(sa, &tmA, cb * BK, (int)(r0 + off), &sh->full[s]);
-                    tma_load_2d(sa + a_bytes / 2, &tmA, cb * BK, (int)(r1 + off), &sh->full[s]);
-                    for (int h = 0; h < nsub; h++)
-                        tma_load_2d(sb + (size_t)h * 256 * BK * 2, &tmB, tap * args.C + cb * BK, ni * Ns + h * 256,
-                                    &sh->full[s]);
+                    uint8_t *stage = ring + (size_t)s * cfg.stage_bytes;
+                    mbar_expect_tx(&sh->full[s], (uint32_t)cfg.kps * (a_bytes + b_bytes));
+                    for (int j = 0; j < cfg.kps; j++) {
+                        const int kb = ki * kblocks + st * cfg.kps + j;
+                        const int tap = kb / kb_per_tap, cb = kb - tap * kb_per_tap;
+                        uint8_t *sa = stage + (size_t)j * cfg.sub_bytes;
+                        uint8_t *sb = sa + a_bytes;
+                        const int off = args.tap_off[tap];
+                        tma_load_2d(sa, &tmA, cb * BK, (int)(r0 + off), &sh->full[s]);
+                        tma_load_2d(sa + a_bytes / 2, &tmA, cb * BK, (int)(r1 + off), &sh->full[s]);
+                        for (int h = 0; h < nsub; h++)
+                            tma_load_2d(sb + (size_t)h * 256 * BK * 2, &tmB, tap * args.C + cb * BK, ni * Ns + h * 256,
+                                        &sh->full[s]);
+                    }
                     issued++;
                     if (++s == cfg.stages) { s = 0; ph ^= 1u; }
                 }
@@ -126,18 +129,21 @@ __global__ void __launch_bounds__(192, 1)
                 if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err)) break;
                 tc_fence_after();
                 const uint32_t dcol = tmem_base + (uint32_t)(ab * cfg.acc_cols);
-                for (int kb = 0; kb < kblocks; kb++) {
+                for (int st = 0; st < kblocks / cfg.kps; st++) {
                     if (!mbar_wait(&sh->full[s], ph, abort_flag, args.err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(ring + (size_t)s * cfg.stage_bytes);
-                    const uint32_t sb = sa + a_bytes;
+                    const uint32_t stage = smem_u32(ring + (size_t)s * cfg.stage_bytes);
+                    for (int j = 0; j < cfg.kps; j++) {
+                        const uint32_t sa = stage + (uint32_t)(j * cfg.sub_bytes);
+                        const uint32_t sb = sa + a_bytes;
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; kk++) {
-                        const uint64_t ad = sdesc(sa + kk * 32, sbo, layout);
-                        for (int h = 0; h < nsub; h++) {
-                            const int nn = Ns - h * 256 < 256 ? Ns - h * 256 : 256;
-                            const uint64_t bd = sdesc(sb + (uint32_t)h * 256u * BK * 2u + kk * 32, sbo, layout);
-                            mma_f16(dcol + (uint32_t)(h * 256), ad, bd, idesc_f16(nn), (kb | kk) ? 1u : 0u);
+                        for (int kk = 0; kk < BK / 16; kk++) {
+                            const uint64_t ad = sdesc(sa + kk * 32, sbo, layout);
+                            for (int h = 0; h < nsub; h++) {
+                                const int nn = Ns - h * 256 < 256 ? Ns - h * 256 : 256;
+                                const uint64_t bd = sdesc(sb + (uint32_t)h * 256u * BK * 2u + kk * 32, sbo, layout);
+                                mma_f16(dcol + (uint32_t)(h * 256), ad, bd, idesc_f16(nn), (st | j | kk) ? 1u : 0u);
+                            }
                         }
                     }
                     mma_commit(&sh->empty[s]);
@@ -283,11 +289,17 @@ int tc_plan(const ConvArgs &a, TcConfig &cfg, std::string &err) {
         if (a.tap_off[t] < 0) { err = "negative tap offset"; return -1; }
     if (a.tg.pool && a.tg.pitch < 64 && a.tg.tiles_x != 1) { err = "pool tiling"; return -1; }
     cfg.bk = bk;
-    cfg.stage_bytes = 128 * bk * 2 + Ns * bk * 2;
-    cfg.stage_bytes = (cfg.stage_bytes + 1023) & ~1023;
+    cfg.sub_bytes = (128 * bk * 2 + Ns * bk * 2 + 1023) & ~1023;
     // at most ~176 KB per CTA: deep enough for every layer here, with room to spare
     // below the 227 KB limit (a profiler attached to the process may claim some)
     const int budget = 176 * 1024 - (int)sizeof(TcShared) - 1024;
+    // several k-blocks per stage when they are small (few channels per tap): one
+    // barrier round trip and one commit per stage instead of per k-block
+    const int kb_unit = a.ntaps * (a.C / bk) / a.ksplit;
+    cfg.kps = 1;
+    for (int k = 2; k <= 9; k++)
+        if (kb_unit % k == 0 && k * cfg.sub_bytes <= 48 * 1024 && budget / (k * cfg.sub_bytes) >= 3) cfg.kps = k;
+    cfg.stage_bytes = cfg.kps * cfg.sub_bytes;
     cfg.stages = budget / cfg.stage_bytes;
     if (cfg.stages > kMaxStages) cfg.stages = kMaxStages;
     if (cfg.stages < 2) { err = "shared-memory ring too small"; return -1; }

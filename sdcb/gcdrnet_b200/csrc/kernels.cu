@@ -190,25 +190,20 @@ __device__ __forceinline__ float gelu_exact(float v) {
 
 // out[y][x][c] = gelu(dw(in))[y][x + off_g(c)][c] (zero outside): the W shift
 // that precedes fc2 (gc#95-126) is folded into the depthwise stage as a gather,
-// so every output chunk of 8 channels is one 16-byte store.
-__device__ __forceinline__ float dw_at(const __half *in, int H, int W, int C, const float *w, int y, int x, int c) {
-    float acc = 0.f;
-#pragma unroll
-    for (int ky = 0; ky < 3; ky++) {
-        const int yy = y + ky - 1;
-        if (yy < 0 || yy >= H) continue;
-#pragma unroll
-        for (int kx = 0; kx < 3; kx++) {
-            const int xx = x + kx - 1;
-            if (xx < 0 || xx >= W) continue;
-            acc = fmaf(w[c * 9 + ky * 3 + kx], __half2float(in[((long long)yy * W + xx) * C + c]), acc);
-        }
-    }
-    return acc;
-}
+// so every output chunk of 8 channels is one 16-byte store.  The block stages
+// the weights tap-major ([9][C]) and the bias in shared memory.
+constexpr int kDwMaxC = 512;
 
-__global__ void dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *w, const float *b,
-                                     const ShiftSpec s, __half *out) {
+__global__ void __launch_bounds__(256) dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *w,
+                                                            const float *b, const ShiftSpec s, __half *out) {
+    __shared__ __align__(16) float ws[9 * kDwMaxC];
+    __shared__ __align__(16) float bs[kDwMaxC];
+    for (int i = threadIdx.x; i < 9 * C; i += blockDim.x) {
+        const int tap = i / C, c = i - tap * C;
+        ws[i] = w[c * 9 + tap];
+    }
+    for (int i = threadIdx.x; i < C; i += blockDim.x) bs[i] = b[i];
+    __syncthreads();
     const int chunks = C / 8;
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)H * W * chunks) return;
@@ -216,23 +211,18 @@ __global__ void dw_gelu_shift_kernel(const __half *in, int H, int W, int C, cons
     const long long p = idx / chunks;
     const int y = (int)(p / W), x = (int)(p - (long long)y * W);
     const int c0 = ch * 8;
-    int xs[8];
-    bool uniform = true;
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const int g = shift_group(s, c0 + k);
-        xs[k] = x + (g >= 0 ? s.offs[g] : 0);
-        uniform = uniform && xs[k] == xs[0];
-    }
+    // channel groups of this chunk: at most two (groups are wider than 8 channels)
+    const int ga = shift_group(s, c0), gb = shift_group(s, c0 + 7);
+    const int xa = x + (ga >= 0 ? s.offs[ga] : 0), xb = x + (gb >= 0 ? s.offs[gb] : 0);
+    const int split = ga == gb ? 8 : s.ends[ga] - c0;   // channels [0, split) read column xa, the rest xb
     float acc[8];
-    if (uniform) {
-        const int sx = xs[0];
-        if (sx < 0 || sx >= W) {
-            *reinterpret_cast<uint4 *>(out + ((long long)y * W + x) * C + c0) = make_uint4(0, 0, 0, 0);
-            return;
-        }
 #pragma unroll
-        for (int k = 0; k < 8; k++) acc[k] = b[c0 + k];
+    for (int k = 0; k < 8; k++) acc[k] = bs[c0 + k];
+#pragma unroll
+    for (int part = 0; part < 2; part++) {
+        const int sx = part ? xb : xa;
+        if (part && split == 8) break;
+        if (sx < 0 || sx >= W) continue;
 #pragma unroll
         for (int ky = 0; ky < 3; ky++) {
             const int yy = y + ky - 1;
@@ -243,22 +233,21 @@ __global__ void dw_gelu_shift_kernel(const __half *in, int H, int W, int C, cons
                 if (xx < 0 || xx >= W) continue;
                 const uint4 raw = *reinterpret_cast<const uint4 *>(in + ((long long)yy * W + xx) * C + c0);
                 const __half *hv = reinterpret_cast<const __half *>(&raw);
+                const float4 w0 = *reinterpret_cast<const float4 *>(ws + (ky * 3 + kx) * C + c0);
+                const float4 w1 = *reinterpret_cast<const float4 *>(ws + (ky * 3 + kx) * C + c0 + 4);
+                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-                for (int k = 0; k < 8; k++) acc[k] = fmaf(w[(c0 + k) * 9 + ky * 3 + kx], __half2float(hv[k]), acc[k]);
+                for (int k = 0; k < 8; k++)
+                    if ((k < split) == (part == 0)) acc[k] = fmaf(wv[k], __half2float(hv[k]), acc[k]);
             }
-        }
-#pragma unroll
-        for (int k = 0; k < 8; k++) acc[k] = gelu_exact(acc[k]);
-    } else {
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const int sx = xs[k];
-            acc[k] = (sx < 0 || sx >= W) ? 0.0f : gelu_exact(b[c0 + k] + dw_at(in, H, W, C, w, y, sx, c0 + k));
         }
     }
     __align__(16) __half o[8];
 #pragma unroll
-    for (int k = 0; k < 8; k++) o[k] = __float2half_rn(acc[k]);
+    for (int k = 0; k < 8; k++) {
+        const int sx = k < split ? xa : xb;
+        o[k] = __float2half_rn((sx < 0 || sx >= W) ? 0.0f : gelu_exact(acc[k]));
+    }
     *reinterpret_cast<uint4 *>(out + ((long long)y * W + x) * C + c0) = *reinterpret_cast<const uint4 *>(o);
 }
 
@@ -520,7 +509,7 @@ int head_launch(const HeadArgs &a, cudaStream_t st) {
 
 int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *w, const float *b, const ShiftSpec &s,
                          __half *out, cudaStream_t st) {
-    if (C % 8) return -2;
+    if (C % 8 || C > kDwMaxC) return -2;
     const long long n = (long long)H * W * (C / 8);
     dw_gelu_shift_kernel<<<grid_for(n, 256), 256, 0, st>>>(in, H, W, C, w, b, s, out);
     return launch_status();

@@ -24,9 +24,14 @@ namespace gcdr {
 namespace {
 
 constexpr int kABlock = 128 * 128;           // bytes of one 64-column SW128 block of the A tile
-constexpr int kBMat = 2 * 32 * 128;          // bytes of one B matrix (32 rows x 128 columns)
-constexpr int kBBytes = 4 * kBMat;           // x_hi, x_lo, r_hi, r_lo
-constexpr int kStemSmem = 1024 + 2 * kABlock + kBBytes + 1024 + 64 * 17 * 4;
+constexpr int kBBlock = 32 * 128;            // bytes of one 32-row x 64-column SW128 block of a B matrix
+// Staged B blocks: GC uses x_hi and x_lo over columns 0..63; DR adds r_hi over
+// columns 0..127 and r_lo over 0..63.  (matrix, 64-column block) -> slot:
+__host__ __device__ constexpr int bslot(int m, int blk) { return m == 0 ? 0 : m == 1 ? 1 : m == 2 ? 2 + blk : 4; }
+template <bool DR> constexpr int a_blocks() { return DR ? 2 : 1; }
+template <bool DR> constexpr int b_slots() { return DR ? 5 : 2; }
+template <bool DR> constexpr int tmem_cols() { return DR ? 64 : 32; }
+template <bool DR> constexpr int stem_smem() { return 1024 + a_blocks<DR>() * kABlock + b_slots<DR>() * kBBlock + 1024 + 64 * 17 * 4; }
 
 __device__ __forceinline__ int reflect1(int i, int n) {
     if (n <= 1) return 0;
@@ -106,7 +111,7 @@ template <bool DR>
 __device__ __forceinline__ void issue_mmas(uint32_t tmem, uint32_t a_s, uint32_t b_s, int c1) {
     const uint32_t idesc = (1u << 4) | ((uint32_t)(c1 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     auto ad = [&](int step) { return sdesc(a_s + (step >> 2) * kABlock + (step & 3) * 32, 1024, 2); };
-    auto bd = [&](int m, int step) { return sdesc(b_s + m * kBMat + (step >> 2) * 4096 + (step & 3) * 32, 1024, 2); };
+    auto bd = [&](int m, int step) { return sdesc(b_s + bslot(m, step >> 2) * kBBlock + (step & 3) * 32, 1024, 2); };
     // x part: u8 columns 0..31 with w_x_hi then w_x_lo
     mma_f16(tmem, ad(0), bd(0, 0), idesc, 0u);
     mma_f16(tmem, ad(1), bd(0, 1), idesc, 1u);
@@ -140,8 +145,8 @@ __global__ void __launch_bounds__(128) stem_tc_kernel(const StemArgs sa, const H
                                                       int ntiles, int tiles_x, int *err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *A = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *B = A + 2 * kABlock;
-    StemShared *sh = reinterpret_cast<StemShared *>(B + kBBytes);
+    uint8_t *B = A + a_blocks<DR>() * kABlock;
+    StemShared *sh = reinterpret_cast<StemShared *>(B + b_slots<DR>() * kBBlock);
     float *xchg = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(sh) + 1024);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const ImgSpec &im = HEAD ? ha.img : sa.img;
@@ -149,11 +154,14 @@ __global__ void __launch_bounds__(128) stem_tc_kernel(const StemArgs sa, const H
     const int H = HEAD ? ha.H : sa.H, W = HEAD ? ha.W : sa.W;
     const float *bias = HEAD ? ha.b : sa.b;
 
-    // zero the A tile (padding columns stay zero), stage the swizzled B matrices
-    for (int i = tid; i < 2 * kABlock / 16; i += 128) reinterpret_cast<uint4 *>(A)[i] = make_uint4(0, 0, 0, 0);
+    // zero the A tile (padding columns stay zero), stage the swizzled B blocks
+    for (int i = tid; i < a_blocks<DR>() * kABlock / 16; i += 128) reinterpret_cast<uint4 *>(A)[i] = make_uint4(0, 0, 0, 0);
     for (int i = tid; i < 4 * 32 * 16; i += 128) {
         const int m = i / (32 * 16), rem = i % (32 * 16), n = rem / 16, j = rem % 16;
-        *reinterpret_cast<uint4 *>(B + m * kBMat + sw_off(n, j, 32)) =
+        const int blk = j >> 3;
+        const bool staged = m < 2 ? blk == 0 : (DR && (m == 2 || blk == 0));
+        if (!staged) continue;
+        *reinterpret_cast<uint4 *>(B + bslot(m, blk) * kBBlock + sw_off(n, j & 7, 32)) =
             *reinterpret_cast<const uint4 *>(bpack + ((size_t)(m * 32 + n) * 128 + j * 8));
     }
     if (tid == 0) {
@@ -163,7 +171,7 @@ __global__ void __launch_bounds__(128) stem_tc_kernel(const StemArgs sa, const H
     }
     if (warp == 0) {
         __syncwarp();
-        tmem_alloc(&sh->tmem_base, 64);
+        tmem_alloc(&sh->tmem_base, tmem_cols<DR>());
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -199,6 +207,32 @@ __global__ void __launch_bounds__(128) stem_tc_kernel(const StemArgs sa, const H
             px = DR ? ox + im.pw : ox;
         }
         build_row<DR>(A, tid, im, rin, H, W, py, px);
+        // head: relu(bilinear x2 of dec5) at this pixel (half_pixel, edge clamp), loaded
+        // while the im2col loads are in flight, before waiting on the MMAs
+        float up[HEAD ? C1 : 1];
+        if (HEAD) {
+            const int Hh = H / 2, Wh = W / 2;
+            const float fy = ((float)py + 0.5f) / 2.0f - 0.5f, fx = ((float)px + 0.5f) / 2.0f - 0.5f;
+            const int y0 = (int)floorf(fy), x0 = (int)floorf(fx);
+            const float dy = fy - (float)y0, dx = fx - (float)x0;
+            const int ya = min(max(y0, 0), Hh - 1), yb = min(max(y0 + 1, 0), Hh - 1);
+            const int xa = min(max(x0, 0), Wh - 1), xb = min(max(x0 + 1, 0), Wh - 1);
+            const __half *p00 = ha.dec5 + ((size_t)ya * Wh + xa) * C1, *p01 = ha.dec5 + ((size_t)ya * Wh + xb) * C1;
+            const __half *p10 = ha.dec5 + ((size_t)yb * Wh + xa) * C1, *p11 = ha.dec5 + ((size_t)yb * Wh + xb) * C1;
+#pragma unroll
+            for (int c0 = 0; c0 < C1; c0 += 16) {
+                float q00[16], q01[16], q10[16], q11[16];
+                load16h(p00 + c0, q00);
+                load16h(p01 + c0, q01);
+                load16h(p10 + c0, q10);
+                load16h(p11 + c0, q11);
+#pragma unroll
+                for (int k = 0; k < 16; k++) {
+                    const float top = q00[k] + (q01[k] - q00[k]) * dx, bot = q10[k] + (q11[k] - q10[k]) * dx;
+                    up[c0 + k] = fmaxf(top + (bot - top) * dy, 0.0f);
+                }
+            }
+        }
         fence_proxy_async_smem();
         tc_fence_before();
         __syncthreads();
@@ -235,31 +269,17 @@ __global__ void __launch_bounds__(128) stem_tc_kernel(const StemArgs sa, const H
                 __syncthreads();
             }
         } else {
-            // bilinear x2 (half_pixel, edge clamp) of dec5 at this pixel
-            const int Hh = H / 2, Wh = W / 2;
-            const float fy = ((float)py + 0.5f) / 2.0f - 0.5f, fx = ((float)px + 0.5f) / 2.0f - 0.5f;
-            const int y0 = (int)floorf(fy), x0 = (int)floorf(fx);
-            const float dy = fy - (float)y0, dx = fx - (float)x0;
-            const int ya = min(max(y0, 0), Hh - 1), yb = min(max(y0 + 1, 0), Hh - 1);
-            const int xa = min(max(x0, 0), Wh - 1), xb = min(max(x0 + 1, 0), Wh - 1);
-            const __half *p00 = ha.dec5 + ((size_t)ya * Wh + xa) * C1, *p01 = ha.dec5 + ((size_t)ya * Wh + xb) * C1;
-            const __half *p10 = ha.dec5 + ((size_t)yb * Wh + xa) * C1, *p11 = ha.dec5 + ((size_t)yb * Wh + xb) * C1;
             float o0 = ha.fb[0], o1 = ha.fb[1], o2 = ha.fb[2];
 #pragma unroll
             for (int c0 = 0; c0 < C1; c0 += 16) {
-                float c1[16], q00[16], q01[16], q10[16], q11[16];
+                float c1[16];
                 load_c1<C1, DR>(taddr, c0, bias, c1);
-                load16h(p00 + c0, q00);
-                load16h(p01 + c0, q01);
-                load16h(p10 + c0, q10);
-                load16h(p11 + c0, q11);
 #pragma unroll
                 for (int k = 0; k < 16; k++) {
-                    const float top = q00[k] + (q01[k] - q00[k]) * dx, bot = q10[k] + (q11[k] - q10[k]) * dx;
-                    const float s = fmaxf(top + (bot - top) * dy, 0.0f) + fmaxf(c1[k], 0.0f);
-                    o0 = fmaf(s, ha.fw[c0 + k], o0);
-                    o1 = fmaf(s, ha.fw[C1 + c0 + k], o1);
-                    o2 = fmaf(s, ha.fw[2 * C1 + c0 + k], o2);
+                    const float sv = (HEAD ? up[c0 + k] : 0.0f) + fmaxf(c1[k], 0.0f);
+                    o0 = fmaf(sv, ha.fw[c0 + k], o0);
+                    o1 = fmaf(sv, ha.fw[C1 + c0 + k], o1);
+                    o2 = fmaf(sv, ha.fw[2 * C1 + c0 + k], o2);
                 }
             }
             if (valid) {
@@ -318,16 +338,29 @@ __global__ void __launch_bounds__(128) stem_tc_kernel(const StemArgs sa, const H
     if (warp == 0) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem, 64);
+        tmem_dealloc(tmem, tmem_cols<DR>());
     }
 }
 
 template <int C1, bool DR, bool HEAD>
 int launch_one(const StemArgs &sa, const HeadArgs &ha, const __half *bpack, int ntiles, int tiles_x, int *err,
-               int grid, cudaStream_t st) {
+               int num_sms, cudaStream_t st) {
     auto k = stem_tc_kernel<C1, DR, HEAD>;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kStemSmem) != cudaSuccess) return -1;
-    k<<<grid, 128, kStemSmem, st>>>(sa, ha, bpack, ntiles, tiles_x, err);
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, stem_smem<DR>()) != cudaSuccess) return -1;
+    // persistent grid: exactly the CTAs that can be resident at once, limited by
+    // shared memory, registers and TMEM (512 columns per SM); a second wave of a
+    // persistent kernel only adds start-up work and a tail
+    cudaFuncAttributes fa;
+    int dev = 0, smem_sm = 0, reserved = 0;
+    if (cudaFuncGetAttributes(&fa, k) != cudaSuccess || cudaGetDevice(&dev) != cudaSuccess) return -1;
+    cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    const int by_smem = smem_sm / (stem_smem<DR>() + (int)fa.sharedSizeBytes + reserved);
+    const int regs_per_warp = (fa.numRegs * 32 + 255) / 256 * 256;
+    const int by_regs = 65536 / (regs_per_warp * 4);
+    const int per_sm = max(1, min(min(by_smem, by_regs), min(512 / tmem_cols<DR>(), 16)));
+    const int grid = min(ntiles, num_sms * per_sm);
+    k<<<grid, 128, stem_smem<DR>(), st>>>(sa, ha, bpack, ntiles, tiles_x, err);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -335,24 +368,22 @@ int launch_one(const StemArgs &sa, const HeadArgs &ha, const __half *bpack, int 
 
 int stem_tc_launch(const StemArgs &a, const __half *bpack, int num_sms, int *err, cudaStream_t st) {
     const int tiles_x = (a.W + 63) / 64, ntiles = (a.H / 2) * tiles_x;
-    const int grid = min(ntiles, num_sms * 3);
     HeadArgs none;
-    if (a.cin == 3 && a.c1 == 16) return launch_one<16, false, false>(a, none, bpack, ntiles, tiles_x, err, grid, st);
-    if (a.cin == 6 && a.c1 == 32) return launch_one<32, true, false>(a, none, bpack, ntiles, tiles_x, err, grid, st);
-    if (a.cin == 3 && a.c1 == 32) return launch_one<32, false, false>(a, none, bpack, ntiles, tiles_x, err, grid, st);
-    if (a.cin == 6 && a.c1 == 16) return launch_one<16, true, false>(a, none, bpack, ntiles, tiles_x, err, grid, st);
+    if (a.cin == 3 && a.c1 == 16) return launch_one<16, false, false>(a, none, bpack, ntiles, tiles_x, err, num_sms, st);
+    if (a.cin == 6 && a.c1 == 32) return launch_one<32, true, false>(a, none, bpack, ntiles, tiles_x, err, num_sms, st);
+    if (a.cin == 3 && a.c1 == 32) return launch_one<32, false, false>(a, none, bpack, ntiles, tiles_x, err, num_sms, st);
+    if (a.cin == 6 && a.c1 == 16) return launch_one<16, true, false>(a, none, bpack, ntiles, tiles_x, err, num_sms, st);
     return -2;
 }
 
 int head_tc_launch(const HeadArgs &a, const __half *bpack, int num_sms, int *err, cudaStream_t st) {
     const long long n = a.is_dr ? (long long)a.img.w * a.img.h : (long long)a.H * a.W;
     const int ntiles = (int)((n + 127) / 128);
-    const int grid = min(ntiles, num_sms * 3);
     StemArgs none;
-    if (!a.is_dr && a.cin == 3 && a.c1 == 16) return launch_one<16, false, true>(none, a, bpack, ntiles, 0, err, grid, st);
-    if (!a.is_dr && a.cin == 3 && a.c1 == 32) return launch_one<32, false, true>(none, a, bpack, ntiles, 0, err, grid, st);
-    if (a.is_dr && a.cin == 6 && a.c1 == 32) return launch_one<32, true, true>(none, a, bpack, ntiles, 0, err, grid, st);
-    if (a.is_dr && a.cin == 6 && a.c1 == 16) return launch_one<16, true, true>(none, a, bpack, ntiles, 0, err, grid, st);
+    if (!a.is_dr && a.cin == 3 && a.c1 == 16) return launch_one<16, false, true>(none, a, bpack, ntiles, 0, err, num_sms, st);
+    if (!a.is_dr && a.cin == 3 && a.c1 == 32) return launch_one<32, false, true>(none, a, bpack, ntiles, 0, err, num_sms, st);
+    if (a.is_dr && a.cin == 6 && a.c1 == 32) return launch_one<32, true, true>(none, a, bpack, ntiles, 0, err, num_sms, st);
+    if (a.is_dr && a.cin == 6 && a.c1 == 16) return launch_one<16, true, true>(none, a, bpack, ntiles, 0, err, num_sms, st);
     return -2;
 }
 
