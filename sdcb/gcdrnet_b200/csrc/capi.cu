@@ -355,8 +355,7 @@ int conv_args_from_desc(const gcdr_conv_desc *d, ConvArgs &a, int &mode, std::st
         if (mode == EPI_POOL) {
             if (in.H % 2 || in.W % 2) { err = "pool needs even dims"; return -1; }
             a.tg.pool = 1;
-            a.tg.tiles_x = (in.W + 63) / 64;
-            a.tg.ntiles = (in.H / 2) * a.tg.tiles_x;
+            a.tg.ntiles = m_units(a.tg, 1);   // pooled rows x 128-pixel segments
             out.H = in.H / 2;
             out.W = in.W / 2;
         } else {

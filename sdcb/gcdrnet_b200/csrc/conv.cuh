@@ -29,16 +29,7 @@ struct ConvArgs {
     int *err = nullptr;        // device error flag (GCDR_ERR_FLAG_*)
 };
 
-// First A row of sub-box `sub` (64 rows each) of `tile` for tap offset 0.
-__host__ __device__ inline long long tile_a_row(const TileGeom &tg, int tile, int sub) {
-    if (tg.pool) {
-        int y2 = tile / tg.tiles_x, xt = tile - y2 * tg.tiles_x;
-        return (long long)(2 * y2 + sub) * tg.pitch + xt * 64;
-    }
-    return (long long)tile * 128 + sub * 64;
-}
-
-// Work unit u -> (tile, n slice, k split).
+// Work unit u -> (m unit, n slice, k split).
 __host__ __device__ inline void unit_coords(const ConvArgs &a, int u, int &tile, int &ni, int &ki) {
     const int per = a.nsplit * a.ksplit;
     tile = u / per;

@@ -14,6 +14,7 @@ struct TcConfig {
     int bk = 64;           // channels per k-block (16/32/64 -> SWIZZLE_32B/64B/128B)
     int stages = 2;        // shared-memory ring depth
     int kps = 1;           // k-blocks (A tile + B tile pairs) per ring stage
+    int rt = 1;            // consecutive 128-row tiles per work unit (one B tile feeds rt MMAs)
     int sub_bytes = 0;     // one A tile + B tile, 1 KB aligned
     int stage_bytes = 0;   // kps * sub_bytes
     int acc_cols = 32;     // TMEM columns per accumulator (power of two >= N)
@@ -22,7 +23,7 @@ struct TcConfig {
 };
 
 int tc_pick_bk(int C);
-int tc_plan(const ConvArgs &a, TcConfig &cfg, std::string &err);
+int tc_plan(const ConvArgs &a, int num_sms, TcConfig &cfg, std::string &err);
 // tcgen05 path (sm_100a).  mode = EpiMode.
 int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, std::string &err);
 // SIMT reference path: same math and epilogue, fp32 FMA, accumulators staged in

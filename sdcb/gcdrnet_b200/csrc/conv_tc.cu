@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <string>
 
 #include "conv.cuh"
@@ -35,9 +36,11 @@ struct TcShared {
     uint32_t tmem_base;
     int abort_flag;
     int issued, consumed;
-    EpiSmem epi;
 };
 
+// A work unit covers `nst` 128-row MMA sub-tiles: rt consecutive tiles (plain),
+// or the two conv rows of a pooled row x 128*rt pixels (pool: nst = 2*rt, the
+// top row's sub-tiles first).  Its A rows arrive as two TMA boxes of nst*64 rows.
 template <int BK, int MODE>
 __global__ void __launch_bounds__(192, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -47,12 +50,16 @@ __global__ void __launch_bounds__(192, 1)
     TcShared *sh = reinterpret_cast<TcShared *>(ring + (size_t)cfg.stages * cfg.stage_bytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const TileGeom &tg = args.tg;
     const int N = args.N;
-    const int Ns = N / args.nsplit;                       // channels of one unit
+    const int Ns = N / args.nsplit;                               // channels of one unit
     const int kb_per_tap = args.C / BK;
-    const int kblocks = args.ntaps * kb_per_tap / args.ksplit;   // k-blocks of one unit
-    const int nunits = args.tg.ntiles * args.nsplit * args.ksplit;
-    const uint32_t a_bytes = 128u * BK * 2u;
+    const int kblocks = args.ntaps * kb_per_tap / args.ksplit;    // k-blocks of one unit
+    const int nst = MODE == EPI_POOL ? 2 * cfg.rt : cfg.rt;      // 128-row sub-tiles per unit
+    const int munits = m_units(tg, cfg.rt);
+    const int segs = MODE == EPI_POOL ? (tg.conv_w + 128 * cfg.rt - 1) / (128 * cfg.rt) : 1;
+    const int nunits = munits * args.nsplit * args.ksplit;
+    const uint32_t a_bytes = 128u * nst * BK * 2u;
     const uint32_t b_bytes = (uint32_t)Ns * BK * 2u;
     const int nsub = (Ns + 255) / 256;
 
@@ -90,9 +97,17 @@ __global__ void __launch_bounds__(192, 1)
             int issued = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
-                int tile, ni, ki;
-                unit_coords(args, u, tile, ni, ki);
-                const long long r0 = tile_a_row(args.tg, tile, 0), r1 = tile_a_row(args.tg, tile, 1);
+                int mu, ni, ki;
+                unit_coords(args, u, mu, ni, ki);
+                long long r0, r1;
+                if (MODE == EPI_POOL) {
+                    const int y2 = mu / segs, x0 = (mu - y2 * segs) * 128 * cfg.rt;
+                    r0 = (long long)(2 * y2) * tg.pitch + x0;
+                    r1 = r0 + tg.pitch;
+                } else {
+                    r0 = (long long)mu * cfg.rt * 128;
+                    r1 = r0 + 64 * nst;
+                }
                 for (int st = 0; st < kblocks / cfg.kps && ok; st++) {
                     if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err)) { ok = false; break; }
                     uint8_t *stage = ring + (size_t)s * cfg.stage_bytes;
@@ -117,8 +132,12 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t layout = BK == 64 ? 2u : BK == 32 ? 4u : 6u;
-            const uint32_t sbo = 8u * BK * 2u;
+            constexpr uint32_t layout = BK == 64 ? 2u : BK == 32 ? 4u : 6u;
+            constexpr uint32_t sbo = 8u * BK * 2u;
+            // descriptors are built once; per MMA only the start-address field moves
+            const uint64_t desc0 = sdesc(0, sbo, layout);
+            const uint32_t idesc_lo = idesc_f16(Ns < 256 ? Ns : 256);
+            const uint32_t idesc_hi = idesc_f16(Ns - 256 > 0 ? Ns - 256 : 16);
             int s = 0;
             uint32_t ph = 0;
             int t = 0, consumed = 0;
@@ -128,21 +147,24 @@ __global__ void __launch_bounds__(192, 1)
                 const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
                 if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err)) break;
                 tc_fence_after();
-                const uint32_t dcol = tmem_base + (uint32_t)(ab * cfg.acc_cols);
+                const uint32_t dcol = tmem_base + (uint32_t)(ab * nst * cfg.acc_cols);
                 for (int st = 0; st < kblocks / cfg.kps; st++) {
                     if (!mbar_wait(&sh->full[s], ph, abort_flag, args.err)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t stage = smem_u32(ring + (size_t)s * cfg.stage_bytes);
                     for (int j = 0; j < cfg.kps; j++) {
                         const uint32_t sa = stage + (uint32_t)(j * cfg.sub_bytes);
-                        const uint32_t sb = sa + a_bytes;
+                        const uint64_t ad0 = desc0 | (uint64_t)((sa & 0x3FFFFu) >> 4);
+                        const uint64_t bd0 = desc0 | (uint64_t)(((sa + a_bytes) & 0x3FFFFu) >> 4);
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; kk++) {
-                            const uint64_t ad = sdesc(sa + kk * 32, sbo, layout);
-                            for (int h = 0; h < nsub; h++) {
-                                const int nn = Ns - h * 256 < 256 ? Ns - h * 256 : 256;
-                                const uint64_t bd = sdesc(sb + (uint32_t)h * 256u * BK * 2u + kk * 32, sbo, layout);
-                                mma_f16(dcol + (uint32_t)(h * 256), ad, bd, idesc_f16(nn), (st | j | kk) ? 1u : 0u);
+                            const uint32_t acc = (st | j | kk) ? 1u : 0u;
+                            for (int i = 0; i < nst; i++) {
+                                const uint64_t ad = ad0 + (uint64_t)((i * 128 * BK * 2 + kk * 32) >> 4);
+                                mma_f16(dcol + (uint32_t)(i * cfg.acc_cols), ad, bd0 + (uint64_t)((kk * 32) >> 4), idesc_lo, acc);
+                                if (nsub > 1)
+                                    mma_f16(dcol + (uint32_t)(i * cfg.acc_cols + 256), ad,
+                                            bd0 + (uint64_t)((256 * BK * 2 + kk * 32) >> 4), idesc_hi, acc);
                             }
                         }
                     }
@@ -156,15 +178,16 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else {
         const int quad = warp & 3;          // TMEM lane quadrant this warp may read
-        const int row = quad * 32 + lane;   // tile row (output position) of this thread
+        const int row = quad * 32 + lane;   // sub-tile row (output position) of this thread
+        const uint32_t lane_base = tmem_base + ((uint32_t)(quad * 32) << 16);
         int t = 0;
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, t++) {
-            int tile, ni, ki;
-            unit_coords(args, u, tile, ni, ki);
+            int mu, ni, ki;
+            unit_coords(args, u, mu, ni, ki);
             const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
             const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
             bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err);
-            // all four epilogue warps take the same branch (pool exchange uses named barriers)
+            // all four epilogue warps leave together (bar.red.or over the 128 threads)
             uint32_t bad;
             asm volatile(
                 "{\n\t.reg .pred p, q;\n\t"
@@ -175,8 +198,22 @@ __global__ void __launch_bounds__(192, 1)
                 : "r"((uint32_t)ok));
             if (bad) break;
             tc_fence_after();
-            TmemLoader ld{tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(ab * cfg.acc_cols)};
-            epilogue_tile<MODE>(args.ep, args.tg, tile, row, ni * Ns, Ns, N, ki, ld, &sh->epi);
+            const uint32_t acc0 = lane_base + (uint32_t)(ab * nst * cfg.acc_cols);
+            if (MODE == EPI_POOL) {
+                const int y2 = mu / segs, x0 = (mu - y2 * segs) * 128 * cfg.rt;
+                for (int i = 0; i < cfg.rt; i++) {
+                    TmemLoader top{acc0 + (uint32_t)(i * cfg.acc_cols)};
+                    TmemLoader bot{acc0 + (uint32_t)((cfg.rt + i) * cfg.acc_cols)};
+                    epilogue_pool(args.ep, tg, y2, x0 + 128 * i + row, ni * Ns, Ns, top, bot);
+                }
+            } else {
+                for (int i = 0; i < cfg.rt; i++) {
+                    const int tile = mu * cfg.rt + i;
+                    if (tile >= tg.ntiles) break;
+                    TmemLoader ld{acc0 + (uint32_t)(i * cfg.acc_cols)};
+                    epilogue_tile<MODE>(args.ep, tg, tile, row, ni * Ns, Ns, N, ki, ld);
+                }
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh->tempty[ab]);
@@ -276,7 +313,7 @@ int launch_bk(const ConvArgs &a, int mode, const TcConfig &cfg, const CUtensorMa
 
 int tc_pick_bk(int C) { return C % 64 == 0 ? 64 : C % 32 == 0 ? 32 : C % 16 == 0 ? 16 : 0; }
 
-int tc_plan(const ConvArgs &a, TcConfig &cfg, std::string &err) {
+int tc_plan(const ConvArgs &a, int num_sms, TcConfig &cfg, std::string &err) {
     const int bk = tc_pick_bk(a.C);
     if (!bk) { err = "channels per tap must be a multiple of 16"; return -1; }
     if (a.nsplit < 1 || a.ksplit < 1 || a.N % a.nsplit) { err = "bad N / k split"; return -1; }
@@ -287,9 +324,22 @@ int tc_plan(const ConvArgs &a, TcConfig &cfg, std::string &err) {
     if (a.ntaps < 1 || a.ntaps > 9) { err = "1..9 taps"; return -1; }
     for (int t = 0; t < a.ntaps; t++)
         if (a.tap_off[t] < 0) { err = "negative tap offset"; return -1; }
-    if (a.tg.pool && a.tg.pitch < 64 && a.tg.tiles_x != 1) { err = "pool tiling"; return -1; }
+    if (a.tg.pool && (a.tg.conv_h % 2 || a.tg.conv_w % 2)) { err = "pool needs even conv dims"; return -1; }
     cfg.bk = bk;
-    cfg.sub_bytes = (128 * bk * 2 + Ns * bk * 2 + 1023) & ~1023;
+    int cols = 32;
+    while (cols < Ns) cols <<= 1;
+    // Units of several 128-row sub-tiles: one B tile and two TMA boxes feed them all.
+    //   plain, thin layers (Ns <= 64): up to 4 consecutive tiles;
+    //   pool: the two conv rows of a pooled row x 128*rt pixels (2*rt sub-tiles).
+    // Both TMEM accumulator buffers must fit in 512 columns, with one wave of units.
+    cfg.rt = 1;
+    for (int r = 4; r > 1; r >>= 1) {
+        const int nst = a.tg.pool ? 2 * r : r;
+        if (a.ksplit != 1 || nst > 4 || (!a.tg.pool && Ns > 64)) continue;
+        if (2 * nst * cols <= 512 && m_units(a.tg, r) * a.nsplit >= num_sms) { cfg.rt = r; break; }
+    }
+    const int nst = a.tg.pool ? 2 * cfg.rt : cfg.rt;
+    cfg.sub_bytes = (128 * nst * bk * 2 + Ns * bk * 2 + 1023) & ~1023;
     // at most ~176 KB per CTA: deep enough for every layer here, with room to spare
     // below the 227 KB limit (a profiler attached to the process may claim some)
     const int budget = 176 * 1024 - (int)sizeof(TcShared) - 1024;
@@ -303,29 +353,36 @@ int tc_plan(const ConvArgs &a, TcConfig &cfg, std::string &err) {
     cfg.stages = budget / cfg.stage_bytes;
     if (cfg.stages > kMaxStages) cfg.stages = kMaxStages;
     if (cfg.stages < 2) { err = "shared-memory ring too small"; return -1; }
-    int cols = 32;
-    while (cols < Ns) cols <<= 1;
     cfg.acc_cols = cols;
-    cfg.acc_bufs = 2 * cols <= 512 ? 2 : 1;
-    cfg.tmem_cols = cols * cfg.acc_bufs;
+    cfg.acc_bufs = 2 * nst * cols <= 512 ? 2 : 1;
+    cfg.tmem_cols = cols * nst * cfg.acc_bufs;
+    if (cfg.tmem_cols > 512) { err = "accumulators exceed TMEM"; return -1; }
     return 0;
 }
 
 int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, std::string &err) {
     TcConfig cfg;
-    if (tc_plan(a, cfg, err)) return -1;
+    if (tc_plan(a, num_sms, cfg, err)) return -1;
     if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) {
         err = "operands must be 16-byte aligned";
         return -1;
     }
     CUtensorMap ta, tb;
-    if (!encode_2d(&ta, a.A, (uint64_t)a.C, (uint64_t)a.a_rows, (uint32_t)cfg.bk, 64, cfg.bk, err)) return -1;
+    const int box_rows = 64 * (a.tg.pool ? 2 * cfg.rt : cfg.rt);
+    if (!encode_2d(&ta, a.A, (uint64_t)a.C, (uint64_t)a.a_rows, (uint32_t)cfg.bk, (uint32_t)box_rows, cfg.bk, err))
+        return -1;
     const int Ns = a.N / a.nsplit;
     if (!encode_2d(&tb, a.B, (uint64_t)a.C * a.ntaps, (uint64_t)a.N, (uint32_t)cfg.bk, (uint32_t)(Ns < 256 ? Ns : 256),
                    cfg.bk, err))
         return -1;
-    const int units = a.tg.ntiles * a.nsplit * a.ksplit;
+    const int units = m_units(a.tg, cfg.rt) * a.nsplit * a.ksplit;
     int grid = units < num_sms ? units : num_sms;
+    static const bool verbose = [] { const char *v = std::getenv("GCDR_CUDA_VERBOSE"); return v && v[0] == '1'; }();
+    if (verbose)
+        std::fprintf(stderr, "tc_conv mode %d C %d N %d taps %d tiles %d rt %d nsplit %d ksplit %d units %d grid %d | bk %d "
+                             "kps %d stages %d stage_bytes %d tmem %d\n",
+                     mode, a.C, a.N, a.ntaps, a.tg.ntiles, cfg.rt, a.nsplit, a.ksplit, units, grid, cfg.bk, cfg.kps,
+                     cfg.stages, cfg.stage_bytes, cfg.tmem_cols);
     if (grid < 1) return 0;
     switch (cfg.bk) {
         case 64: return launch_bk<64>(a, mode, cfg, ta, tb, grid, st, err);

@@ -10,7 +10,9 @@
 //
 // Modes (the fusions the reference's CPU plan makes, EngineTests.cs:79-141):
 //   EPI_PLAIN    y = acc + bias [relu]                        decoder convs, fc1
-//   EPI_POOL     y = relu(maxpool2x2(acc + bias))             encoder conv+pool+relu (gc#23-25)
+//   EPI_POOL     y = relu(maxpool2x2(acc + bias))             encoder conv+pool+relu (gc#23-25):
+//                a unit holds the two conv rows of a pooled row in two accumulators, so a
+//                thread maxes its own pair of rows and one shuffle finishes the 2x2 window
 //   EPI_LN2      y0 = LN1(acc + bias) -> out (tokens);        patch embed + its norm (gc#34-37)
 //                h = LN2(y0) -> out2 with the H-shift scatter  and the block's norm2 + shift (gc#38-44)
 //   EPI_RESLN    y = LN(acc + bias + res) -> out              fc2 + residual + norm3 (gc#127-130)
@@ -37,22 +39,20 @@ struct EpiParams {
     float *partial = nullptr;        // EPI_PARTIAL: [ksplit][T][N] fp32
 };
 
-// Geometry of the output grid: q = y * pitch + x over a flat row space; in pool
-// mode a tile is a pair of conv rows x 64 columns.
+// Geometry of the output grid: q = y * pitch + x over a flat row space.
+//   plain: work units of rt consecutive 128-row tiles (ntiles tiles in all);
+//   pool:  work units of two conv rows (2*y2, 2*y2+1) x 128*rt pixels.
 struct TileGeom {
     int pool = 0;
     int pitch = 0;        // grid rows per image row (>= out_w; extra columns are discarded)
     int conv_h = 0, conv_w = 0;   // conv output dims (valid region of the grid)
-    int tiles_x = 0;      // pool mode: tiles per row pair
-    int ntiles = 0;
+    int ntiles = 0;       // plain: 128-row tiles
 };
 
-struct EpiSmem {
-    float x[128 * 17];    // pool exchange
-};
-
-__device__ inline void named_bar_sync(int id, int n) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+// Work units along M for `rt` (tiles per unit, or 128-pixel segments per pooled row).
+__host__ __device__ inline int m_units(const TileGeom &tg, int rt) {
+    if (tg.pool) return (tg.conv_h / 2) * ((tg.conv_w + 128 * rt - 1) / (128 * rt));
+    return (tg.ntiles + rt - 1) / rt;
 }
 
 // Reads columns [c0, c0 + w) (w = 32 or 16) of this thread's accumulator row.
@@ -79,36 +79,9 @@ __device__ __forceinline__ void row_vals(L &ld, const EpiParams &ep, int N, long
 
 template <int MODE, class L>
 __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile, int row, int n0, int Nsub, int N,
-                              int ksplit_idx, L &ld, EpiSmem *sm) {
+                              int ksplit_idx, L &ld) {
     float v[32];
     const int cw = (Nsub % 32 == 0) ? 32 : 16;
-    if (MODE == EPI_POOL) {
-        const int y2 = tile / tg.tiles_x, xt = tile - y2 * tg.tiles_x;
-        const int sub = row >> 6, xx = row & 63;
-        const int cx = xt * 64 + xx;
-        const bool writer = sub == 0 && (xx & 1) == 0 && cx < tg.conv_w;
-        for (int c0 = 0; c0 < Nsub; c0 += 16) {
-            ld.load16(c0, v);
-#pragma unroll
-            for (int k = 0; k < 16; k++) {
-                float t = v[k] + ep.bias[n0 + c0 + k];
-                v[k] = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, 1));
-            }
-            if (sub == 1) {
-#pragma unroll
-                for (int k = 0; k < 16; k++) sm->x[xx * 17 + k] = v[k];
-            }
-            named_bar_sync(1, 128);
-            if (writer) {
-                __align__(16) __half h[16];
-#pragma unroll
-                for (int k = 0; k < 16; k++) h[k] = __float2half_rn(fmaxf(fmaxf(v[k], sm->x[xx * 17 + k]), 0.0f));
-                act_store(ep.out, y2, cx >> 1, n0 + c0, h, 16);
-            }
-            named_bar_sync(1, 128);
-        }
-        return;
-    }
     const long long q = (long long)tile * 128 + row;
     const int y = (int)(q / tg.pitch), x = (int)(q - (long long)y * tg.pitch);
     const bool valid = y < tg.conv_h && x < tg.conv_w;
@@ -206,6 +179,30 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
                 }
             shift_store(ep.out2, ep.shift, 2, y, x, c0, o, cw);
         }
+    }
+}
+
+// Pool epilogue: this thread's conv pixel (2*y2, x) is in `top`, (2*y2+1, x) in
+// `bot` (same TMEM lane, two accumulators); lanes L and L^1 hold x and x^1.
+template <class L>
+__device__ void epilogue_pool(const EpiParams &ep, const TileGeom &tg, int y2, int x, int n0, int Nsub, L &top,
+                              L &bot) {
+    float a[32], b[32];
+    const int cw = (Nsub % 32 == 0) ? 32 : 16;
+    const bool writer = (x & 1) == 0 && x < tg.conv_w;
+    for (int c0 = 0; c0 < Nsub; c0 += cw) {
+        load_cols(top, c0, cw, a);
+        load_cols(bot, c0, cw, b);
+        __align__(16) __half h[32];
+#pragma unroll
+        for (int k = 0; k < 32; k++) {
+            if (k < cw) {
+                float v = fmaxf(a[k], b[k]);
+                v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1)) + ep.bias[n0 + c0 + k];
+                h[k] = __float2half_rn(fmaxf(v, 0.0f));
+            }
+        }
+        if (writer) act_store(ep.out, y2, x >> 1, n0 + c0, h, cw);
     }
 }
 

@@ -231,8 +231,7 @@ ConvArgs conv_s1(const Act &in, const __half *B, const float *bias, int N, bool 
     a.tg.conv_w = in.W;
     if (pool) {
         a.tg.pool = 1;
-        a.tg.tiles_x = (in.W + 63) / 64;
-        a.tg.ntiles = (in.H / 2) * a.tg.tiles_x;
+        a.tg.ntiles = m_units(a.tg, 1);   // pooled rows x 128-pixel segments
     } else {
         a.tg.ntiles = (int)(((long long)in.H * (in.W + 2) + 127) / 128);
     }

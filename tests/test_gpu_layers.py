@@ -33,6 +33,9 @@ CASES = [
     (2, 18, 25, 128, 128, 0),   # dblock2 fc
     (3, 24, 30, 32, 64, 2),     # zero-pad conv + relu (microbench form)
     (0, 66, 130, 32, 64, 1),    # pool with two x tiles
+    (0, 256, 320, 16, 16, 0),   # dec5-like, 4 tiles per work unit
+    (0, 128, 200, 32, 32, 0),   # 2 tiles per work unit
+    (0, 96, 150, 64, 64, 2),    # thin layer + relu
 ]
 
 
