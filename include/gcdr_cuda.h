@@ -227,6 +227,26 @@ GCDR_API int64_t gcdr_k_conv_scratch(const gcdr_conv_desc *d);
 /* Number of SMs the tcgen05 kernels use on the current device. */
 GCDR_API int gcdr_device_sms(void);
 
+/* gcdr_k_conv_static -- no counterpart in the reference (its CPU and Vulkan
+ * engines have no layer-level entry of this kind).  Runs the layer described
+ * by `d` as a k-split tensor-core convolution without allocating any device
+ * memory, for callers that must not allocate: the d->ksplit fp32 partial sums
+ * (and the kernels' error word) live in a static workspace compiled into the
+ * library, GCDR_STATIC_WS_BYTES per device, and are summed in order with the
+ * bias (epilogue 2: then relu) into d->out, fp16 [Ho][Wo][N].
+ *   - epilogue must be 0 or 2 (no pool); d->scratch is ignored; nsplit as in
+ *     gcdr_k_conv; ksplit (0 = 1) must divide the layer's k-blocks.
+ *   - ksplit * Ho * Wo * N must not exceed GCDR_STATIC_WS_BYTES / 4 floats,
+ *     else GCDR_ERR_RANGE (nothing is launched, a message goes to stderr).
+ *   - The first call on a device loads the workspace's address with
+ *     cudaGetSymbolAddress (the driver reserves the workspace then): make it
+ *     before any stream capture.
+ *   - Returns after the layer has finished on `stream` (GCDR_ERR_TIMEOUT if a
+ *     device-side wait expired).
+ *   - One workspace per device: calls that overlap in time race on it. */
+#define GCDR_STATIC_WS_BYTES (16 * 1024 * 1024)
+GCDR_API int gcdr_k_conv_static(const gcdr_conv_desc *d, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -143,6 +143,7 @@ def lib():
         L.gcdr_k_to_layout.argtypes = [vp, i, i, i, i, vp, vp]
         L.gcdr_k_to_layout.restype = i64
         L.gcdr_device_sms.restype = i
+        L.gcdr_k_conv_static.argtypes = [vp, vp]
         _lib = L
         return L
 

@@ -328,8 +328,9 @@ extern "C" int gcdr_k_nhwc2bgr(const float *y, int H, int W, int ph, int pw, uin
 }
 
 // Layer-level entry (tests, microbenchmark).
-namespace {
+namespace gcdr {
 
+// Layer descriptor -> ConvArgs (also used by the static-workspace entry, noalloc.cu).
 int conv_args_from_desc(const gcdr_conv_desc *d, ConvArgs &a, int &mode, std::string &err) {
     if (!d || !d->in || !d->weight || !d->bias || !d->out || d->H < 1 || d->W < 1) { err = "bad descriptor"; return -1; }
     Act in;
@@ -406,6 +407,10 @@ int conv_args_from_desc(const gcdr_conv_desc *d, ConvArgs &a, int &mode, std::st
     else if (a.ksplit != 1) { err = "k splits need the partial-sum epilogue"; return -1; }
     return 0;
 }
+
+}  // namespace gcdr
+
+namespace {
 
 __global__ void to_layout_kernel(const __half *src, int H, int W, int C, Act dst) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;

@@ -14,7 +14,8 @@ struct TcConfig {
     int bk = 64;           // channels per k-block (16/32/64 -> SWIZZLE_32B/64B/128B)
     int stages = 2;        // shared-memory ring depth
     int kps = 1;           // k-blocks (A tile + B tile pairs) per ring stage
-    int rt = 1;            // consecutive 128-row tiles per work unit (one B tile feeds rt MMAs)
+    int rt = 1;            // plain: consecutive 128-row tiles per work unit; pool: 128-pixel
+                           // segments per pooled row (2*rt sub-tiles); one B tile feeds them all
     int sub_bytes = 0;     // one A tile + B tile, 1 KB aligned
     int stage_bytes = 0;   // kps * sub_bytes
     int acc_cols = 32;     // TMEM columns per accumulator (power of two >= N)
@@ -27,7 +28,8 @@ int tc_plan(const ConvArgs &a, int num_sms, TcConfig &cfg, std::string &err);
 // tcgen05 path (sm_100a).  mode = EpiMode.
 int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, std::string &err);
 // SIMT reference path: same math and epilogue, fp32 FMA, accumulators staged in
-// `scratch` (ntiles*128*N floats).  Used by the tests to check the tensor-core path.
+// `scratch` (ref_conv_scratch_floats: one row of N per output-grid position).
+// Used by the tests to check the tensor-core path.
 int ref_conv_launch(const ConvArgs &a, int mode, float *scratch, cudaStream_t st, std::string &err);
 size_t ref_conv_scratch_floats(const ConvArgs &a);
 
