@@ -1,16 +1,20 @@
 // conv_tc.cu -- tcgen05 (sm_100a) implicit-GEMM convolution.
 //
-// One persistent CTA per SM, 6 warps:
-//   warp 0      TMA producer: per (tap, k-block) one A tile (two 64-row boxes,
+// One persistent CTA per SM, 13 warps:
+//   warp 0      TMA producer: per (tap, k-block) the unit's A rows (two boxes,
 //               SWIZZLE_{32,64,128}B K-major) and the B tile (weights) into a
 //               multi-stage shared-memory ring; also allocates TMEM.
-//   warp 1      MMA issuer: one thread issues tcgen05.mma.kind::f16 (fp16 x
-//               fp16 -> fp32, M=128, N<=256 per instruction) into a TMEM
-//               accumulator, tcgen05.commit frees ring slots / publishes tiles.
-//   warps 2-5   epilogue: tcgen05.ld 32x32b rows out of TMEM (thread = output
-//               position), bias / pool / LayerNorm / residual / shift, stores.
-// Accumulators are double-buffered in TMEM when 2*N columns fit (N <= 256),
-// so the epilogue of tile i overlaps the MMAs of tile i+1.
+//   warps 1-4   MMA issuers, one per accumulator of the unit (a 128-row
+//               sub-tile, or one 256-column half of N): each issues its own
+//               tcgen05.mma.kind::f16 chain (fp16 x fp16 -> fp32, M=128,
+//               N<=256) and commits.  A single issuing thread spends ~100-200
+//               cycles per MMA whatever N is, so thin layers (N <= 64) are
+//               issue-bound with one issuer; four issuers overlap their chains.
+//   warps 5-12  epilogue: tcgen05.ld 32x32b rows out of TMEM (thread = output
+//               position; two warps per TMEM lane quadrant share the column
+//               chunks), bias / pool / LayerNorm / residual / shift, stores.
+// Accumulators are double-buffered in TMEM when both buffers fit in 512
+// columns, so the epilogue of unit i overlaps the MMAs of unit i+1.
 //
 // Every mbarrier wait is bounded (clock64 budget): on expiry the CTA raises the
 // abort flag, sets GCDR_ERR_FLAG_TIMEOUT in the global error word, drains its
@@ -31,6 +35,10 @@ namespace gcdr {
 
 namespace {
 
+constexpr int kMmaWarps = 4;
+constexpr int kEpiWarps = 8;
+constexpr int kConvThreads = (1 + kMmaWarps + kEpiWarps) * 32;
+
 struct TcShared {
     uint64_t full[kMaxStages], empty[kMaxStages], tfull[2], tempty[2];
     uint32_t tmem_base;
@@ -42,7 +50,7 @@ struct TcShared {
 // or the two conv rows of a pooled row x 128*rt pixels (pool: nst = 2*rt, the
 // top row's sub-tiles first).  Its A rows arrive as two TMA boxes of nst*64 rows.
 template <int BK, int MODE>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kConvThreads, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ ConvArgs args, const __grid_constant__ TcConfig cfg) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -62,15 +70,16 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t a_bytes = 128u * nst * BK * 2u;
     const uint32_t b_bytes = (uint32_t)Ns * BK * 2u;
     const int nsub = (Ns + 255) / 256;
+    const int nacc = nst * nsub;                                  // accumulators = active MMA warps (<= 4)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < cfg.stages; s++) {
             mbar_init(&sh->full[s], 1);
-            mbar_init(&sh->empty[s], 1);
+            mbar_init(&sh->empty[s], (uint32_t)nacc);
         }
         for (int b = 0; b < 2; b++) {
-            mbar_init(&sh->tfull[b], 1);
-            mbar_init(&sh->tempty[b], 4);
+            mbar_init(&sh->tfull[b], (uint32_t)nacc);
+            mbar_init(&sh->tempty[b], kEpiWarps);
         }
         sh->abort_flag = 0;
         sh->issued = 0;
@@ -130,14 +139,17 @@ __global__ void __launch_bounds__(192, 1)
             }
             sh->issued = issued;
         }
-    } else if (warp == 1) {
-        if (lane == 0) {
+    } else if (warp <= kMmaWarps) {
+        const int m = warp - 1;                    // accumulator m: sub-tile m / nsub, N half m % nsub
+        if (lane == 0 && m < nacc) {
+            const int i = m / nsub, h = m - i * nsub;
             constexpr uint32_t layout = BK == 64 ? 2u : BK == 32 ? 4u : 6u;
             constexpr uint32_t sbo = 8u * BK * 2u;
             // descriptors are built once; per MMA only the start-address field moves
             const uint64_t desc0 = sdesc(0, sbo, layout);
-            const uint32_t idesc_lo = idesc_f16(Ns < 256 ? Ns : 256);
-            const uint32_t idesc_hi = idesc_f16(Ns - 256 > 0 ? Ns - 256 : 16);
+            const int nh = h == 0 ? (Ns < 256 ? Ns : 256) : Ns - 256;
+            const uint32_t idesc = idesc_f16(nh);
+            const uint32_t a_off = (uint32_t)(i * 128 * BK * 2), b_off = a_bytes + (uint32_t)(h * 256 * BK * 2);
             int s = 0;
             uint32_t ph = 0;
             int t = 0, consumed = 0;
@@ -147,26 +159,19 @@ __global__ void __launch_bounds__(192, 1)
                 const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
                 if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err)) break;
                 tc_fence_after();
-                const uint32_t dcol = tmem_base + (uint32_t)(ab * nst * cfg.acc_cols);
+                const uint32_t dcol = tmem_base + (uint32_t)((ab * nst + i) * cfg.acc_cols + h * 256);
                 for (int st = 0; st < kblocks / cfg.kps; st++) {
                     if (!mbar_wait(&sh->full[s], ph, abort_flag, args.err)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t stage = smem_u32(ring + (size_t)s * cfg.stage_bytes);
                     for (int j = 0; j < cfg.kps; j++) {
                         const uint32_t sa = stage + (uint32_t)(j * cfg.sub_bytes);
-                        const uint64_t ad0 = desc0 | (uint64_t)((sa & 0x3FFFFu) >> 4);
-                        const uint64_t bd0 = desc0 | (uint64_t)(((sa + a_bytes) & 0x3FFFFu) >> 4);
+                        const uint64_t ad0 = desc0 | (uint64_t)(((sa + a_off) & 0x3FFFFu) >> 4);
+                        const uint64_t bd0 = desc0 | (uint64_t)(((sa + b_off) & 0x3FFFFu) >> 4);
 #pragma unroll
-                        for (int kk = 0; kk < BK / 16; kk++) {
-                            const uint32_t acc = (st | j | kk) ? 1u : 0u;
-                            for (int i = 0; i < nst; i++) {
-                                const uint64_t ad = ad0 + (uint64_t)((i * 128 * BK * 2 + kk * 32) >> 4);
-                                mma_f16(dcol + (uint32_t)(i * cfg.acc_cols), ad, bd0 + (uint64_t)((kk * 32) >> 4), idesc_lo, acc);
-                                if (nsub > 1)
-                                    mma_f16(dcol + (uint32_t)(i * cfg.acc_cols + 256), ad,
-                                            bd0 + (uint64_t)((256 * BK * 2 + kk * 32) >> 4), idesc_hi, acc);
-                            }
-                        }
+                        for (int kk = 0; kk < BK / 16; kk++)
+                            mma_f16(dcol, ad0 + (uint64_t)(kk * 2), bd0 + (uint64_t)(kk * 2), idesc,
+                                    (st | j | kk) ? 1u : 0u);
                     }
                     mma_commit(&sh->empty[s]);
                     consumed++;
@@ -174,11 +179,13 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 if (ok) mma_commit(&sh->tfull[ab]);
             }
-            sh->consumed = consumed;
+            if (m == 0) sh->consumed = consumed;
         }
     } else {
-        const int quad = warp & 3;          // TMEM lane quadrant this warp may read
-        const int row = quad * 32 + lane;   // sub-tile row (output position) of this thread
+        const int e = warp - 1 - kMmaWarps;         // epilogue warp 0..7
+        const int quad = warp & 3;                  // TMEM lane quadrant this warp may read
+        const int part = e >> 2;                    // which half of the column chunks
+        const int row = quad * 32 + lane;           // sub-tile row (output position) of this thread
         const uint32_t lane_base = tmem_base + ((uint32_t)(quad * 32) << 16);
         int t = 0;
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, t++) {
@@ -187,15 +194,15 @@ __global__ void __launch_bounds__(192, 1)
             const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
             const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
             bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err);
-            // all four epilogue warps leave together (bar.red.or over the 128 threads)
+            // all epilogue warps leave together (bar.red.or over their threads)
             uint32_t bad;
             asm volatile(
                 "{\n\t.reg .pred p, q;\n\t"
                 "setp.eq.u32 p, %1, 0;\n\t"
-                "bar.red.or.pred q, 2, 128, p;\n\t"
+                "bar.red.or.pred q, 2, %2, p;\n\t"
                 "selp.u32 %0, 1, 0, q;\n\t}"
                 : "=r"(bad)
-                : "r"((uint32_t)ok));
+                : "r"((uint32_t)ok), "n"(kEpiWarps * 32));
             if (bad) break;
             tc_fence_after();
             const uint32_t acc0 = lane_base + (uint32_t)(ab * nst * cfg.acc_cols);
@@ -204,14 +211,16 @@ __global__ void __launch_bounds__(192, 1)
                 for (int i = 0; i < cfg.rt; i++) {
                     TmemLoader top{acc0 + (uint32_t)(i * cfg.acc_cols)};
                     TmemLoader bot{acc0 + (uint32_t)((cfg.rt + i) * cfg.acc_cols)};
-                    epilogue_pool(args.ep, tg, y2, x0 + 128 * i + row, ni * Ns, Ns, top, bot);
+                    epilogue_pool(args.ep, tg, y2, x0 + 128 * i + row, ni * Ns, Ns, top, bot, part, 2);
                 }
-            } else {
+            } else if (MODE == EPI_PLAIN || MODE == EPI_PARTIAL || part == 0) {
+                // LayerNorm modes need whole rows: the first four warps finish them
+                const int nparts = (MODE == EPI_PLAIN || MODE == EPI_PARTIAL) ? 2 : 1;
                 for (int i = 0; i < cfg.rt; i++) {
                     const int tile = mu * cfg.rt + i;
                     if (tile >= tg.ntiles) break;
                     TmemLoader ld{acc0 + (uint32_t)(i * cfg.acc_cols)};
-                    epilogue_tile<MODE>(args.ep, tg, tile, row, ni * Ns, Ns, N, ki, ld);
+                    epilogue_tile<MODE>(args.ep, tg, tile, row, ni * Ns, Ns, N, ki, ld, part, nparts);
                 }
             }
             tc_fence_before();
@@ -289,7 +298,7 @@ int launch_bk_mode(const ConvArgs &a, const TcConfig &cfg, const CUtensorMap &ta
     size_t smem = 1024 + (size_t)cfg.stages * cfg.stage_bytes + sizeof(TcShared);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) { err = std::string("smem attribute: ") + cudaGetErrorString(e); return -1; }
-    k<<<grid, 192, smem, st>>>(ta, tb, a, cfg);
+    k<<<grid, kConvThreads, smem, st>>>(ta, tb, a, cfg);
     e = cudaGetLastError();
     if (e != cudaSuccess) { err = std::string("tc_conv launch: ") + cudaGetErrorString(e); return -1; }
     return 0;
@@ -329,13 +338,14 @@ int tc_plan(const ConvArgs &a, int num_sms, TcConfig &cfg, std::string &err) {
     int cols = 32;
     while (cols < Ns) cols <<= 1;
     // Units of several 128-row sub-tiles: one B tile and two TMA boxes feed them all.
-    //   plain, thin layers (Ns <= 64): up to 4 consecutive tiles;
+    //   plain: up to 4 consecutive tiles;
     //   pool: the two conv rows of a pooled row x 128*rt pixels (2*rt sub-tiles).
-    // Both TMEM accumulator buffers must fit in 512 columns, with one wave of units.
+    // Each sub-tile is its own accumulator with its own issuing warp (at most 4);
+    // both TMEM accumulator buffers must fit in 512 columns, with one wave of units.
     cfg.rt = 1;
     for (int r = 4; r > 1; r >>= 1) {
         const int nst = a.tg.pool ? 2 * r : r;
-        if (a.ksplit != 1 || nst > 4 || (!a.tg.pool && Ns > 64)) continue;
+        if (a.ksplit != 1 || nst > 4 || Ns > 256) continue;
         if (2 * nst * cols <= 512 && m_units(a.tg, r) * a.nsplit >= num_sms) { cfg.rt = r; break; }
     }
     const int nst = a.tg.pool ? 2 * cfg.rt : cfg.rt;

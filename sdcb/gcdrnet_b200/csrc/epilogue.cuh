@@ -77,9 +77,11 @@ __device__ __forceinline__ void row_vals(L &ld, const EpiParams &ep, int N, long
         if (k < w) v[k] += ep.bias[c0 + k] + (use_res ? r[k] : 0.0f);
 }
 
+// PLAIN and PARTIAL finish the column chunks c0 = part*cw, (part + nparts)*cw, ...
+// (several warps may share a row); the LayerNorm modes need the whole row (nparts = 1).
 template <int MODE, class L>
 __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile, int row, int n0, int Nsub, int N,
-                              int ksplit_idx, L &ld) {
+                              int ksplit_idx, L &ld, int part = 0, int nparts = 1) {
     float v[32];
     const int cw = (Nsub % 32 == 0) ? 32 : 16;
     const long long q = (long long)tile * 128 + row;
@@ -87,7 +89,7 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     const bool valid = y < tg.conv_h && x < tg.conv_w;
     const long long tok = valid ? (long long)y * tg.conv_w + x : 0;
     if (MODE == EPI_PLAIN) {
-        for (int c0 = 0; c0 < Nsub; c0 += cw) {
+        for (int c0 = part * cw; c0 < Nsub; c0 += nparts * cw) {
             load_cols(ld, c0, cw, v);
             if (valid) {
                 __align__(16) __half h[32];
@@ -106,7 +108,7 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     if (MODE == EPI_PARTIAL) {
         const long long T = (long long)tg.conv_h * tg.conv_w;
         float *dst = ep.partial + ((long long)ksplit_idx * T + tok) * N + n0;
-        for (int c0 = 0; c0 < Nsub; c0 += cw) {
+        for (int c0 = part * cw; c0 < Nsub; c0 += nparts * cw) {
             load_cols(ld, c0, cw, v);
             if (valid) {
 #pragma unroll
@@ -186,11 +188,11 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
 // `bot` (same TMEM lane, two accumulators); lanes L and L^1 hold x and x^1.
 template <class L>
 __device__ void epilogue_pool(const EpiParams &ep, const TileGeom &tg, int y2, int x, int n0, int Nsub, L &top,
-                              L &bot) {
+                              L &bot, int part = 0, int nparts = 1) {
     float a[32], b[32];
     const int cw = (Nsub % 32 == 0) ? 32 : 16;
     const bool writer = (x & 1) == 0 && x < tg.conv_w;
-    for (int c0 = 0; c0 < Nsub; c0 += cw) {
+    for (int c0 = part * cw; c0 < Nsub; c0 += nparts * cw) {
         load_cols(top, c0, cw, a);
         load_cols(bot, c0, cw, b);
         __align__(16) __half h[32];
