@@ -37,13 +37,14 @@ namespace {
 
 constexpr int kMmaWarps = 4;
 constexpr int kEpiWarps = 8;
-constexpr int kConvThreads = (1 + kMmaWarps + kEpiWarps) * 32;
+constexpr int kConvThreads = (2 + kMmaWarps + kEpiWarps) * 32;
+constexpr int kProducer2Warp = 1 + kMmaWarps + kEpiWarps;     // the second TMA producer
 
 struct TcShared {
     uint64_t full[kMaxStages], empty[kMaxStages], tfull[2], tempty[2];
     uint32_t tmem_base;
     int abort_flag;
-    int issued, consumed;
+    int issued[2], consumed;
 };
 
 // A work unit covers `nst` 128-row MMA sub-tiles: rt consecutive tiles (plain),
@@ -82,7 +83,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             mbar_init(&sh->tempty[b], kEpiWarps);
         }
         sh->abort_flag = 0;
-        sh->issued = 0;
+        sh->issued[0] = sh->issued[1] = 0;
         sh->consumed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -99,11 +100,14 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     const uint32_t tmem_base = sh->tmem_base;
     volatile int *abort_flag = &sh->abort_flag;
 
-    if (warp == 0) {
+    if (warp == 0 || warp == kProducer2Warp) {
+        // two producers take the ring stages alternately: the per-stage cost of one
+        // thread (barrier round trip + a few TMA issues) is what bounds thin layers
+        const int p = warp == 0 ? 0 : 1;
         if (lane == 0) {
             int s = 0;
             uint32_t ph = 0;
-            int issued = 0;
+            int g = 0, issued = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
                 int mu, ni, ki;
@@ -117,27 +121,29 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                     r0 = (long long)mu * cfg.rt * 128;
                     r1 = r0 + 64 * nst;
                 }
-                for (int st = 0; st < kblocks / cfg.kps && ok; st++) {
-                    if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err)) { ok = false; break; }
-                    uint8_t *stage = ring + (size_t)s * cfg.stage_bytes;
-                    mbar_expect_tx(&sh->full[s], (uint32_t)cfg.kps * (a_bytes + b_bytes));
-                    for (int j = 0; j < cfg.kps; j++) {
-                        const int kb = ki * kblocks + st * cfg.kps + j;
-                        const int tap = kb / kb_per_tap, cb = kb - tap * kb_per_tap;
-                        uint8_t *sa = stage + (size_t)j * cfg.sub_bytes;
-                        uint8_t *sb = sa + a_bytes;
-                        const int off = args.tap_off[tap];
-                        tma_load_2d(sa, &tmA, cb * BK, (int)(r0 + off), &sh->full[s]);
-                        tma_load_2d(sa + a_bytes / 2, &tmA, cb * BK, (int)(r1 + off), &sh->full[s]);
-                        for (int h = 0; h < nsub; h++)
-                            tma_load_2d(sb + (size_t)h * 256 * BK * 2, &tmB, tap * args.C + cb * BK, ni * Ns + h * 256,
-                                        &sh->full[s]);
+                for (int st = 0; st < kblocks / cfg.kps; st++, g++) {
+                    if ((g & 1) == p) {
+                        if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err)) { ok = false; break; }
+                        uint8_t *stage = ring + (size_t)s * cfg.stage_bytes;
+                        mbar_expect_tx(&sh->full[s], (uint32_t)cfg.kps * (a_bytes + b_bytes));
+                        for (int j = 0; j < cfg.kps; j++) {
+                            const int kb = ki * kblocks + st * cfg.kps + j;
+                            const int tap = kb / kb_per_tap, cb = kb - tap * kb_per_tap;
+                            uint8_t *sa = stage + (size_t)j * cfg.sub_bytes;
+                            uint8_t *sb = sa + a_bytes;
+                            const int off = args.tap_off[tap];
+                            tma_load_2d(sa, &tmA, cb * BK, (int)(r0 + off), &sh->full[s]);
+                            tma_load_2d(sa + a_bytes / 2, &tmA, cb * BK, (int)(r1 + off), &sh->full[s]);
+                            for (int h = 0; h < nsub; h++)
+                                tma_load_2d(sb + (size_t)h * 256 * BK * 2, &tmB, tap * args.C + cb * BK,
+                                            ni * Ns + h * 256, &sh->full[s]);
+                        }
+                        issued++;
                     }
-                    issued++;
                     if (++s == cfg.stages) { s = 0; ph ^= 1u; }
                 }
             }
-            sh->issued = issued;
+            sh->issued[p] = issued;
         }
     } else if (warp <= kMmaWarps) {
         const int m = warp - 1;                    // accumulator m: sub-tile m / nsub, N half m % nsub
@@ -232,14 +238,15 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     __syncthreads();
     if (threadIdx.x == 0) {
         // drain before the CTA's shared memory and TMEM go away: TMA copies issued
-        // but never consumed (only after an abort), then the asynchronous mbarrier
-        // arrivals of the last tcgen05.commit (always)
-        int s = sh->consumed % cfg.stages;
-        uint32_t ph = (uint32_t)((sh->consumed / cfg.stages) & 1);
-        for (int i = sh->consumed; i < sh->issued; i++) {
+        // but never consumed (only after an abort; producer p issued stages p, p+2, ...),
+        // then the asynchronous mbarrier arrivals of the last tcgen05.commit (always)
+        const int issued_end = max(2 * sh->issued[0], 2 * sh->issued[1] + 1);
+        for (int g = sh->consumed; g < issued_end; g++) {
+            if (g / 2 >= sh->issued[g & 1]) continue;
+            const int s = g % cfg.stages;
+            const uint32_t ph = (uint32_t)((g / cfg.stages) & 1);
             long long t0 = clock64();
             while (!mbar_try(&sh->full[s], ph) && clock64() - t0 < kWaitCycles) {}
-            if (++s == cfg.stages) { s = 0; ph ^= 1u; }
         }
         if (sh->consumed > 0) {
             int ls = (sh->consumed - 1) % cfg.stages;
@@ -358,7 +365,7 @@ int tc_plan(const ConvArgs &a, int num_sms, TcConfig &cfg, std::string &err) {
     const int kb_unit = a.ntaps * (a.C / bk) / a.ksplit;
     cfg.kps = 1;
     for (int k = 2; k <= 9; k++)
-        if (kb_unit % k == 0 && k * cfg.sub_bytes <= 48 * 1024 && budget / (k * cfg.sub_bytes) >= 3) cfg.kps = k;
+        if (kb_unit % k == 0 && k * cfg.sub_bytes <= 64 * 1024 && budget / (k * cfg.sub_bytes) >= 3) cfg.kps = k;
     cfg.stage_bytes = cfg.kps * cfg.sub_bytes;
     cfg.stages = budget / cfg.stage_bytes;
     if (cfg.stages > kMaxStages) cfg.stages = kMaxStages;
