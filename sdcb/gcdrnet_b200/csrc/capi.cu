@@ -353,6 +353,7 @@ int conv_args_from_desc(const gcdr_conv_desc *d, ConvArgs &a, int &mode, std::st
         a.tg.pitch = in.W + 2;
         a.tg.conv_h = in.H;
         a.tg.conv_w = in.W;
+        a.rw = 1;
         if (mode == EPI_POOL) {
             if (in.H % 2 || in.W % 2) { err = "pool needs even dims"; return -1; }
             a.tg.pool = 1;

@@ -21,6 +21,8 @@ struct ConvArgs {
     int N = 0;                 // output channels (multiple of 16, <= 512)
     int nsplit = 1;            // N slices per tile (each Nsub = N / nsplit channels)
     int ksplit = 1;            // k-block splits (EPI_PARTIAL only)
+    int rw = 0;                // 3x3 stride-1 over a [H+2][W+2][C] layout (taps ky*pitch + kx):
+                               // eligible for the row-window kernel (conv_rw.cu)
     long long a_rows = 0;
     const __half *A = nullptr; // for the SIMT reference path and host checks
     const __half *B = nullptr; // packed weights [N][ntaps*C]

@@ -1,5 +1,6 @@
 // conv_launch.h -- host entry points of the implicit-GEMM convolution.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <string>
@@ -23,7 +24,28 @@ struct TcConfig {
     int tmem_cols = 32;
 };
 
+// Row-window plan (conv_rw.cu): a unit is R output rows x 128 pixels; each ring
+// stage holds the unit's R+2 input row segments (136 pixels) of one k-block, and
+// all nine taps read them through shifted descriptors; weights stay resident.
+struct RwConfig {
+    int bk = 64;
+    int R = 2;             // output rows per unit (sub-tiles, one MMA warp each)
+    int segs_x = 1;        // 128-pixel segments per row
+    int units = 0;
+    int seg_bytes = 0;     // one input row segment (136 rows of bk channels), 1 KB aligned
+    int stage_bytes = 0;   // (R + 2) * seg_bytes
+    int stages = 2;
+    int b_block = 0;       // one (k-block, tap) weight block: N rows x bk, 1 KB aligned
+    int b_bytes = 0;       // all weights: 9 * C/bk blocks
+    int acc_cols = 32, acc_bufs = 1, tmem_cols = 32;
+};
+
 int tc_pick_bk(int C);
+bool tma_encode_2d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                   uint32_t box_outer, int bk, std::string &err);
+// 0 and a plan when the layer suits the row-window kernel, -1 otherwise.
+int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg);
+int rw_conv_launch(const ConvArgs &a, int mode, const RwConfig &cfg, int num_sms, cudaStream_t st, std::string &err);
 int tc_plan(const ConvArgs &a, int num_sms, TcConfig &cfg, std::string &err);
 // tcgen05 path (sm_100a).  mode = EpiMode.
 int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, std::string &err);

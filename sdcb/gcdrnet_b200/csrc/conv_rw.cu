@@ -1,0 +1,354 @@
+// conv_rw.cu -- row-window tcgen05 convolution for 3x3 stride-1 layers.
+//
+// The flat implicit GEMM (conv_tc.cu) re-reads the input once per tap: nine
+// ring stages per work unit, each a barrier round trip plus TMA issues by one
+// thread, which is what bounds the thin layers.  Here a work unit is R output
+// rows x 128 pixels of one image window:
+//   * each ring stage holds the unit's R + 2 input row segments (136 pixels:
+//     the 128 outputs plus the 3x3 halo) for one k-block of channels, loaded
+//     once as R + 2 TMA boxes in the layer's swizzled K-major layout;
+//   * the nine taps read those segments in place: tap (ky, kx) of output row j
+//     starts at segment j + ky, row kx.  tcgen05 applies the shared-memory
+//     swizzle on absolute addresses, so a descriptor may start on any row of a
+//     swizzled tile (base offset 0);
+//   * the weights (9 taps x C/bk k-blocks of N x bk) stay resident in shared
+//     memory for the whole persistent CTA.
+// Roles: warp 0 (and warp 13) TMA producers taking alternate stages, warps 1..R
+// MMA issuers (one accumulator = one output row each), warps 5-12 epilogue
+// (bias [+ relu], or the 2x2 max-pool + relu of two accumulators).
+// Every mbarrier wait is bounded; on expiry the CTA raises the abort flag and the
+// global error word, drains its copies in flight and its last commit, and frees TMEM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <string>
+
+#include "conv.cuh"
+#include "conv_launch.h"
+#include "tc_util.cuh"
+
+namespace gcdr {
+
+namespace {
+
+constexpr int kRwMmaWarps = 4;
+constexpr int kRwEpiWarps = 8;
+constexpr int kRwThreads = (2 + kRwMmaWarps + kRwEpiWarps) * 32;
+constexpr int kRwProducer2 = 1 + kRwMmaWarps + kRwEpiWarps;
+constexpr int kSegRows = 136;          // 128 outputs + 2 halo, rounded up to 8 rows
+constexpr int kRwSmemCap = 210 * 1024;
+
+struct RwShared {
+    uint64_t full[kMaxStages], empty[kMaxStages], tfull[2], tempty[2], bfull;
+    uint32_t tmem_base;
+    int abort_flag;
+    int issued[2], consumed;
+    int b_issued;
+};
+
+__host__ __device__ inline int round1k(int b) { return (b + 1023) & ~1023; }
+
+template <int BK, int MODE>
+__global__ void __launch_bounds__(kRwThreads, 1)
+    rw_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ ConvArgs args, const __grid_constant__ RwConfig cfg) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *bres = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *ring = bres + cfg.b_bytes;
+    RwShared *sh = reinterpret_cast<RwShared *>(ring + (size_t)cfg.stages * cfg.stage_bytes);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const TileGeom &tg = args.tg;
+    const int N = args.N, C = args.C, R = cfg.R;
+    const int kbs = C / BK;                     // k-blocks (ring stages) per unit
+    const int pitch = tg.pitch;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < cfg.stages; s++) {
+            mbar_init(&sh->full[s], 1);
+            mbar_init(&sh->empty[s], (uint32_t)R);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&sh->tfull[b], (uint32_t)R);
+            mbar_init(&sh->tempty[b], kRwEpiWarps);
+        }
+        mbar_init(&sh->bfull, 1);
+        sh->abort_flag = 0;
+        sh->issued[0] = sh->issued[1] = 0;
+        sh->consumed = 0;
+        sh->b_issued = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh->tmem_base)),
+                     "r"((uint32_t)cfg.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = sh->tmem_base;
+    volatile int *abort_flag = &sh->abort_flag;
+
+    // unit -> (first output row, first pixel); pool units cover R conv rows = R/2 pooled rows
+    auto unit_origin = [&](int u, int &y0, int &x0) {
+        const int yb = u / cfg.segs_x;
+        y0 = yb * R;
+        x0 = (u - yb * cfg.segs_x) * 128;
+    };
+
+    if (warp == 0 || warp == kRwProducer2) {
+        const int p = warp == 0 ? 0 : 1;
+        if (lane == 0) {
+            if (p == 0) {
+                // resident weights: block (kb, tap) = rows [0, N) x columns tap*C + kb*BK
+                mbar_expect_tx(&sh->bfull, (uint32_t)(9 * kbs * N * BK * 2));
+                for (int kb = 0; kb < kbs; kb++)
+                    for (int tap = 0; tap < 9; tap++)
+                        tma_load_2d(bres + (size_t)(kb * 9 + tap) * cfg.b_block, &tmB, tap * C + kb * BK, 0, &sh->bfull);
+                sh->b_issued = 1;
+            }
+            int s = 0;
+            uint32_t ph = 0;
+            int g = 0, issued = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < cfg.units && ok; u += gridDim.x) {
+                int y0, x0;
+                unit_origin(u, y0, x0);
+                for (int kb = 0; kb < kbs; kb++, g++) {
+                    if ((g & 1) == p) {
+                        if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err)) { ok = false; break; }
+                        uint8_t *stage = ring + (size_t)s * cfg.stage_bytes;
+                        mbar_expect_tx(&sh->full[s], (uint32_t)((R + 2) * kSegRows * BK * 2));
+                        for (int r = 0; r < R + 2; r++)
+                            tma_load_2d(stage + (size_t)r * cfg.seg_bytes, &tmA, kb * BK, (y0 + r) * pitch + x0, &sh->full[s]);
+                        issued++;
+                    }
+                    if (++s == cfg.stages) { s = 0; ph ^= 1u; }
+                }
+            }
+            sh->issued[p] = issued;
+        }
+    } else if (warp <= kRwMmaWarps) {
+        const int j = warp - 1;                    // output row of the unit = accumulator
+        if (lane == 0 && j < R) {
+            constexpr uint32_t layout = BK == 64 ? 2u : BK == 32 ? 4u : 6u;
+            constexpr uint32_t sbo = 8u * BK * 2u;
+            const uint64_t desc0 = sdesc(0, sbo, layout);
+            const uint32_t idesc = idesc_f16(N);
+            const uint32_t b_s = smem_u32(bres);
+            int s = 0;
+            uint32_t ph = 0;
+            int t = 0, consumed = 0;
+            bool ok = mbar_wait(&sh->bfull, 0, abort_flag, args.err);
+            for (int u = blockIdx.x; u < cfg.units && ok; u += gridDim.x, t++) {
+                const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
+                const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
+                if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err)) break;
+                tc_fence_after();
+                const uint32_t dcol = tmem_base + (uint32_t)((ab * R + j) * cfg.acc_cols);
+                for (int kb = 0; kb < kbs; kb++) {
+                    if (!mbar_wait(&sh->full[s], ph, abort_flag, args.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t stage = smem_u32(ring + (size_t)s * cfg.stage_bytes);
+#pragma unroll
+                    for (int ky = 0; ky < 3; ky++) {
+                        const uint32_t seg = stage + (uint32_t)((j + ky) * cfg.seg_bytes);
+#pragma unroll
+                        for (int kx = 0; kx < 3; kx++) {
+                            const uint64_t ad = desc0 | (uint64_t)(((seg + (uint32_t)(kx * BK * 2)) & 0x3FFFFu) >> 4);
+                            const uint64_t bd = desc0 | (uint64_t)(((b_s + (uint32_t)((kb * 9 + ky * 3 + kx) * cfg.b_block)) & 0x3FFFFu) >> 4);
+#pragma unroll
+                            for (int kk = 0; kk < BK / 16; kk++)
+                                mma_f16(dcol, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                                        (kb | ky | kx | kk) ? 1u : 0u);
+                        }
+                    }
+                    mma_commit(&sh->empty[s]);
+                    consumed++;
+                    if (++s == cfg.stages) { s = 0; ph ^= 1u; }
+                }
+                if (ok) mma_commit(&sh->tfull[ab]);
+            }
+            if (j == 0) sh->consumed = consumed;
+        }
+    } else {
+        const int e = warp - 1 - kRwMmaWarps;       // epilogue warp 0..7
+        const int quad = warp & 3;
+        const int part = e >> 2;
+        const int row = quad * 32 + lane;           // pixel within the unit's 128
+        const uint32_t lane_base = tmem_base + ((uint32_t)(quad * 32) << 16);
+        int t = 0;
+        for (int u = blockIdx.x; u < cfg.units; u += gridDim.x, t++) {
+            int y0, x0;
+            unit_origin(u, y0, x0);
+            const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
+            const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
+            bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err);
+            uint32_t bad;
+            asm volatile(
+                "{\n\t.reg .pred p, q;\n\t"
+                "setp.eq.u32 p, %1, 0;\n\t"
+                "bar.red.or.pred q, 2, %2, p;\n\t"
+                "selp.u32 %0, 1, 0, q;\n\t}"
+                : "=r"(bad)
+                : "r"((uint32_t)ok), "n"(kRwEpiWarps * 32));
+            if (bad) break;
+            tc_fence_after();
+            const uint32_t acc0 = lane_base + (uint32_t)(ab * R * cfg.acc_cols);
+            const int x = x0 + row;
+            if (MODE == EPI_POOL) {
+                for (int q = 0; q < R / 2; q++) {
+                    const int y2 = y0 / 2 + q;
+                    if (y2 >= tg.conv_h / 2) break;   // uniform over the CTA
+                    TmemLoader top{acc0 + (uint32_t)(2 * q * cfg.acc_cols)};
+                    TmemLoader bot{acc0 + (uint32_t)((2 * q + 1) * cfg.acc_cols)};
+                    epilogue_pool(args.ep, tg, y2, x, 0, N, top, bot, part, 2);
+                }
+            } else {
+                for (int jj = 0; jj < R; jj++) {
+                    TmemLoader ld{acc0 + (uint32_t)(jj * cfg.acc_cols)};
+                    epilogue_plain_yx(args.ep, tg, y0 + jj, x, 0, N, ld, part, 2);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh->tempty[ab]);
+        }
+    }
+
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // drain: unconsumed TMA stages (after an abort only), the weights, the last commit
+        const int issued_end = max(2 * sh->issued[0], 2 * sh->issued[1] + 1);
+        for (int g = sh->consumed; g < issued_end; g++) {
+            if (g / 2 >= sh->issued[g & 1]) continue;
+            const int s = g % cfg.stages;
+            const uint32_t ph = (uint32_t)((g / cfg.stages) & 1);
+            long long t0 = clock64();
+            while (!mbar_try(&sh->full[s], ph) && clock64() - t0 < kWaitCycles) {}
+        }
+        if (sh->b_issued) {
+            long long t0 = clock64();
+            while (!mbar_try(&sh->bfull, 0) && clock64() - t0 < kWaitCycles) {}
+        }
+        if (sh->consumed > 0) {
+            const int ls = (sh->consumed - 1) % cfg.stages;
+            const uint32_t lph = (uint32_t)(((sh->consumed - 1) / cfg.stages) & 1);
+            long long t0 = clock64();
+            while (!mbar_try(&sh->empty[ls], lph) && clock64() - t0 < kWaitCycles) {}
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)cfg.tmem_cols)
+                     : "memory");
+    }
+}
+
+size_t rw_smem(const RwConfig &cfg) {
+    return 1024 + (size_t)cfg.b_bytes + (size_t)cfg.stages * cfg.stage_bytes + sizeof(RwShared);
+}
+
+template <int BK, int MODE>
+int rw_launch_bk_mode(const ConvArgs &a, const RwConfig &cfg, const CUtensorMap &ta, const CUtensorMap &tb, int grid,
+                      cudaStream_t st, std::string &err) {
+    auto k = rw_conv_kernel<BK, MODE>;
+    const size_t smem = rw_smem(cfg);
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) { err = std::string("rw smem attribute: ") + cudaGetErrorString(e); return -1; }
+    k<<<grid, kRwThreads, smem, st>>>(ta, tb, a, cfg);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) { err = std::string("rw_conv launch: ") + cudaGetErrorString(e); return -1; }
+    return 0;
+}
+
+}  // namespace
+
+int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
+    if (!a.rw || (mode != EPI_PLAIN && mode != EPI_POOL) || a.nsplit != 1 || a.ksplit != 1) return -1;
+    if (a.ntaps != 9 || a.N < 16 || a.N > 256 || a.N % 16) return -1;
+    const TileGeom &tg = a.tg;
+    if (tg.pool && (tg.conv_h % 2 || tg.conv_w % 2)) return -1;
+    int cols = 32;
+    while (cols < a.N) cols <<= 1;
+    const int segs_x = (tg.conv_w + 127) / 128;
+    const int r_min = tg.pool ? 2 : 1;
+    // (k-block, rows per unit): the most rows that fit TMEM (two buffers), keep >= 3
+    // ring stages and still fill the GPU in one wave; narrower k-blocks when the
+    // widest leave too few stages.  Weights must stay resident.
+    bool found = false;
+    // pass 0: R = 4 or 2 with a full wave of units (pool: R = 2 always qualifies);
+    // pass 1 (small layers): the fewest rows per unit that fit, for the most units
+    for (int pass = 0; pass < 2 && !found; pass++) {
+        for (int bk = tc_pick_bk(a.C); bk >= 16 && !found; bk >>= 1) {
+            if (a.C % bk) continue;
+            const int b_block = round1k(a.N * bk * 2);
+            const int b_bytes = 9 * (a.C / bk) * b_block;
+            if (b_bytes > 96 * 1024) continue;
+            const int seg_bytes = round1k(kSegRows * bk * 2);
+            const int avail = kRwSmemCap - 1024 - b_bytes - (int)sizeof(RwShared);
+            for (int i = 0; i < 3 && !found; i++) {
+                const int R = pass == 0 ? (i == 0 ? 4 : i == 1 ? 2 : 0) : (r_min << i);
+                if (R < r_min || R > 4) continue;
+                const int units = ((tg.conv_h + R - 1) / R) * segs_x;
+                const int stages = avail / ((R + 2) * seg_bytes);
+                if (2 * R * cols > 512 || stages < 3) continue;
+                if (pass == 0 && units < num_sms && !(tg.pool && R == 2)) continue;
+                cfg.bk = bk;
+                cfg.R = R;
+                cfg.b_block = b_block;
+                cfg.b_bytes = b_bytes;
+                cfg.seg_bytes = seg_bytes;
+                cfg.segs_x = segs_x;
+                cfg.units = units;
+                cfg.stage_bytes = (R + 2) * seg_bytes;
+                cfg.stages = stages > kMaxStages ? kMaxStages : stages;
+                found = true;
+            }
+        }
+    }
+    if (!found) return -1;
+    cfg.acc_cols = cols;
+    cfg.acc_bufs = 2;
+    cfg.tmem_cols = cols * cfg.R * 2;
+    return 0;
+}
+
+int rw_conv_launch(const ConvArgs &a, int mode, const RwConfig &cfg, int num_sms, cudaStream_t st, std::string &err) {
+    if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) {
+        err = "operands must be 16-byte aligned";
+        return -1;
+    }
+    CUtensorMap ta, tb;
+    if (!tma_encode_2d(&ta, a.A, (uint64_t)a.C, (uint64_t)a.a_rows, (uint32_t)cfg.bk, (uint32_t)kSegRows, cfg.bk, err))
+        return -1;
+    if (!tma_encode_2d(&tb, a.B, (uint64_t)a.C * 9, (uint64_t)a.N, (uint32_t)cfg.bk, (uint32_t)a.N, cfg.bk, err))
+        return -1;
+    const int grid = cfg.units < num_sms ? cfg.units : num_sms;
+    static const bool verbose = [] { const char *v = std::getenv("GCDR_CUDA_VERBOSE"); return v && v[0] == '1'; }();
+    if (verbose)
+        std::fprintf(stderr, "rw_conv mode %d C %d N %d H %d W %d | bk %d R %d units %d grid %d stages %d stage_bytes %d "
+                             "b_bytes %d tmem %d smem %zu\n",
+                     mode, a.C, a.N, a.tg.conv_h, a.tg.conv_w, cfg.bk, cfg.R, cfg.units, grid, cfg.stages,
+                     cfg.stage_bytes, cfg.b_bytes, cfg.tmem_cols, rw_smem(cfg));
+    if (grid < 1) return 0;
+    switch (cfg.bk * 8 + mode) {
+        case 64 * 8 + EPI_PLAIN: return rw_launch_bk_mode<64, EPI_PLAIN>(a, cfg, ta, tb, grid, st, err);
+        case 64 * 8 + EPI_POOL: return rw_launch_bk_mode<64, EPI_POOL>(a, cfg, ta, tb, grid, st, err);
+        case 32 * 8 + EPI_PLAIN: return rw_launch_bk_mode<32, EPI_PLAIN>(a, cfg, ta, tb, grid, st, err);
+        case 32 * 8 + EPI_POOL: return rw_launch_bk_mode<32, EPI_POOL>(a, cfg, ta, tb, grid, st, err);
+        case 16 * 8 + EPI_PLAIN: return rw_launch_bk_mode<16, EPI_PLAIN>(a, cfg, ta, tb, grid, st, err);
+        case 16 * 8 + EPI_POOL: return rw_launch_bk_mode<16, EPI_POOL>(a, cfg, ta, tb, grid, st, err);
+    }
+    err = "rw_conv: bad k-block / mode";
+    return -1;
+}
+
+}  // namespace gcdr

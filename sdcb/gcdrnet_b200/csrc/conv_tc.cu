@@ -329,6 +329,11 @@ int launch_bk(const ConvArgs &a, int mode, const TcConfig &cfg, const CUtensorMa
 
 int tc_pick_bk(int C) { return C % 64 == 0 ? 64 : C % 32 == 0 ? 32 : C % 16 == 0 ? 16 : 0; }
 
+bool tma_encode_2d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                   uint32_t box_outer, int bk, std::string &err) {
+    return encode_2d(m, base, inner, outer, box_inner, box_outer, bk, err);
+}
+
 int tc_plan(const ConvArgs &a, int num_sms, TcConfig &cfg, std::string &err) {
     const int bk = tc_pick_bk(a.C);
     if (!bk) { err = "channels per tap must be a multiple of 16"; return -1; }
@@ -378,6 +383,11 @@ int tc_plan(const ConvArgs &a, int num_sms, TcConfig &cfg, std::string &err) {
 }
 
 int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, std::string &err) {
+    static const bool flat_only = [] { const char *v = std::getenv("GCDR_CUDA_CONV"); return v && std::string(v) == "flat"; }();
+    if (!flat_only) {
+        RwConfig rc;
+        if (rw_plan(a, mode, num_sms, rc) == 0) return rw_conv_launch(a, mode, rc, num_sms, st, err);
+    }
     TcConfig cfg;
     if (tc_plan(a, num_sms, cfg, err)) return -1;
     if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) {

@@ -77,6 +77,30 @@ __device__ __forceinline__ void row_vals(L &ld, const EpiParams &ep, int N, long
         if (k < w) v[k] += ep.bias[c0 + k] + (use_res ? r[k] : 0.0f);
 }
 
+// PLAIN epilogue of output pixel (y, x): bias [+ relu] -> fp16 store of the
+// column chunks c0 = part*cw, (part + nparts)*cw, ... (several warps may share a row).
+template <class L>
+__device__ __forceinline__ void epilogue_plain_yx(const EpiParams &ep, const TileGeom &tg, int y, int x, int n0,
+                                                  int Nsub, L &ld, int part, int nparts) {
+    float v[32];
+    const int cw = (Nsub % 32 == 0) ? 32 : 16;
+    const bool valid = y < tg.conv_h && x < tg.conv_w;
+    for (int c0 = part * cw; c0 < Nsub; c0 += nparts * cw) {
+        load_cols(ld, c0, cw, v);
+        if (valid) {
+            __align__(16) __half h[32];
+#pragma unroll
+            for (int k = 0; k < 32; k++) {
+                if (k < cw) {
+                    float t = v[k] + ep.bias[n0 + c0 + k];
+                    h[k] = __float2half_rn(ep.relu ? fmaxf(t, 0.0f) : t);
+                }
+            }
+            act_store(ep.out, y, x, n0 + c0, h, cw);
+        }
+    }
+}
+
 // PLAIN and PARTIAL finish the column chunks c0 = part*cw, (part + nparts)*cw, ...
 // (several warps may share a row); the LayerNorm modes need the whole row (nparts = 1).
 template <int MODE, class L>
@@ -89,20 +113,7 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     const bool valid = y < tg.conv_h && x < tg.conv_w;
     const long long tok = valid ? (long long)y * tg.conv_w + x : 0;
     if (MODE == EPI_PLAIN) {
-        for (int c0 = part * cw; c0 < Nsub; c0 += nparts * cw) {
-            load_cols(ld, c0, cw, v);
-            if (valid) {
-                __align__(16) __half h[32];
-#pragma unroll
-                for (int k = 0; k < 32; k++) {
-                    if (k < cw) {
-                        float t = v[k] + ep.bias[n0 + c0 + k];
-                        h[k] = __float2half_rn(ep.relu ? fmaxf(t, 0.0f) : t);
-                    }
-                }
-                act_store(ep.out, y, x, n0 + c0, h, cw);
-            }
-        }
+        epilogue_plain_yx(ep, tg, y, x, n0, Nsub, ld, part, nparts);
         return;
     }
     if (MODE == EPI_PARTIAL) {

@@ -229,6 +229,7 @@ ConvArgs conv_s1(const Act &in, const __half *B, const float *bias, int N, bool 
     a.tg.pitch = in.W + 2;
     a.tg.conv_h = in.H;
     a.tg.conv_w = in.W;
+    a.rw = 1;
     if (pool) {
         a.tg.pool = 1;
         a.tg.ntiles = m_units(a.tg, 1);   // pooled rows x 128-pixel segments

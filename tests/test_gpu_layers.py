@@ -36,6 +36,11 @@ CASES = [
     (0, 256, 320, 16, 16, 0),   # dec5-like, 4 tiles per work unit
     (0, 128, 200, 32, 32, 0),   # 2 tiles per work unit
     (0, 96, 150, 64, 64, 2),    # thin layer + relu
+    # row-window kernel edges: 4 rows per unit with a ragged last unit (rows past the
+    # image), odd pooled-row count, segments past the right edge, zero padding
+    (0, 150, 1100, 16, 32, 1),
+    (0, 150, 1100, 32, 32, 0),
+    (3, 150, 600, 16, 16, 2),
 ]
 
 
@@ -94,3 +99,37 @@ def test_tc_conv_splits(case):
     d = np.abs(tc - want).max() / scale
     tol = 2e-4 if ep == 3 else 4e-3   # partials are fp32 (no fp16 output rounding)
     assert d < tol, f"split conv vs torch fp32: max rel {d}"
+
+
+_FLAT_SCRIPT = r"""
+import sys, json
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + '/tests')
+import numpy as np
+from gpu_util import run_conv, torch_conv
+from sdcb.gcdrnet_b200 import lib
+from test_gpu_layers import CASES, _inputs
+L = lib()
+out = []
+for case in CASES[:8] + CASES[-3:]:
+    kind, H, W, C, N, ep = case
+    x, w, b = _inputs(kind, H, W, C, N, 7)
+    tc = run_conv(L, kind, x, w, b, ep)
+    want = torch_conv(kind, x, w, b, ep)
+    out.append(float(np.abs(tc - want).max() / (np.abs(want).max() + 1e-6)))
+print(json.dumps(out))
+"""
+
+
+def test_flat_kernel_still_matches_torch():
+    """The flat implicit-GEMM kernel (the row-window kernel's fallback) on the
+    layers the row-window kernel would otherwise take (GCDR_CUDA_CONV=flat)."""
+    import json
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, GCDR_CUDA_CONV="flat")
+    r = subprocess.run([sys.executable, "-c", _FLAT_SCRIPT, root], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    errs = json.loads(r.stdout.strip().splitlines()[-1])
+    assert max(errs) < 4e-3, errs
