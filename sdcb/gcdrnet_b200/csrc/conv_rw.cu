@@ -201,18 +201,22 @@ __global__ void __launch_bounds__(kRwThreads, 1)
             tc_fence_after();
             const uint32_t acc0 = lane_base + (uint32_t)(ab * R * cfg.acc_cols);
             const int x = x0 + row;
+            // work items (output row or pooled row, 32/16-column chunk), alternating
+            // between the two warps of each TMEM lane quadrant
+            const int cw = (N % 32 == 0) ? 32 : 16, nch = N / cw;
             if (MODE == EPI_POOL) {
-                for (int q = 0; q < R / 2; q++) {
-                    const int y2 = y0 / 2 + q;
-                    if (y2 >= tg.conv_h / 2) break;   // uniform over the CTA
+                const int rows2 = min(R / 2, tg.conv_h / 2 - y0 / 2);   // uniform over the CTA
+                for (int it = part; it < rows2 * nch; it += 2) {
+                    const int q = it / nch, ch = it - q * nch;
                     TmemLoader top{acc0 + (uint32_t)(2 * q * cfg.acc_cols)};
                     TmemLoader bot{acc0 + (uint32_t)((2 * q + 1) * cfg.acc_cols)};
-                    epilogue_pool(args.ep, tg, y2, x, 0, N, top, bot, part, 2);
+                    epilogue_pool(args.ep, tg, y0 / 2 + q, x, 0, N, top, bot, ch, nch);
                 }
             } else {
-                for (int jj = 0; jj < R; jj++) {
+                for (int it = part; it < R * nch; it += 2) {
+                    const int jj = it / nch, ch = it - jj * nch;
                     TmemLoader ld{acc0 + (uint32_t)(jj * cfg.acc_cols)};
-                    epilogue_plain_yx(args.ep, tg, y0 + jj, x, 0, N, ld, part, 2);
+                    epilogue_plain_yx(args.ep, tg, y0 + jj, x, 0, N, ld, ch, nch, args.ep.bias);
                 }
             }
             tc_fence_before();

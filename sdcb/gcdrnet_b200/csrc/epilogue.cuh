@@ -81,7 +81,7 @@ __device__ __forceinline__ void row_vals(L &ld, const EpiParams &ep, int N, long
 // column chunks c0 = part*cw, (part + nparts)*cw, ... (several warps may share a row).
 template <class L>
 __device__ __forceinline__ void epilogue_plain_yx(const EpiParams &ep, const TileGeom &tg, int y, int x, int n0,
-                                                  int Nsub, L &ld, int part, int nparts) {
+                                                  int Nsub, L &ld, int part, int nparts, const float *bias) {
     float v[32];
     const int cw = (Nsub % 32 == 0) ? 32 : 16;
     const bool valid = y < tg.conv_h && x < tg.conv_w;
@@ -92,7 +92,7 @@ __device__ __forceinline__ void epilogue_plain_yx(const EpiParams &ep, const Til
 #pragma unroll
             for (int k = 0; k < 32; k++) {
                 if (k < cw) {
-                    float t = v[k] + ep.bias[n0 + c0 + k];
+                    float t = v[k] + bias[n0 + c0 + k];
                     h[k] = __float2half_rn(ep.relu ? fmaxf(t, 0.0f) : t);
                 }
             }
@@ -113,7 +113,7 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     const bool valid = y < tg.conv_h && x < tg.conv_w;
     const long long tok = valid ? (long long)y * tg.conv_w + x : 0;
     if (MODE == EPI_PLAIN) {
-        epilogue_plain_yx(ep, tg, y, x, n0, Nsub, ld, part, nparts);
+        epilogue_plain_yx(ep, tg, y, x, n0, Nsub, ld, part, nparts, ep.bias);
         return;
     }
     if (MODE == EPI_PARTIAL) {
