@@ -23,7 +23,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-I", SRC, "-I", INCLUDE]
 
-SOURCES = ["model.cpp", "conv_tc.cu", "conv_rw.cu", "conv_ref.cu", "kernels.cu", "stem_tc.cu", "pipeline.cu", "capi.cu", "noalloc.cu"]
+SOURCES = ["model.cpp", "conv_tc.cu", "conv_rw.cu", "conv_ref.cu", "kernels.cu", "pipeline.cu", "capi.cu", "noalloc.cu"]
 
 
 def _headers():

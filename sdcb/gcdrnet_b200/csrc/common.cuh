@@ -28,6 +28,14 @@ namespace gcdr {
 
 enum LayoutKind : int { LAY_PLAIN = 0, LAY_PADREFL = 1, LAY_PHASE = 2, LAY_PADZERO = 3 };
 
+// Image source / destination as the caller laid it out (GcdrPixelFormat).
+struct ImgSpec {
+    const uint8_t *src = nullptr;   // device copy of the source image
+    int w = 0, h = 0, stride = 0;   // original dims, row stride in bytes
+    int bpp = 3, swap = 0;          // bytes per pixel, R/B swapped (Rgb24/Rgba32)
+    int ph = 0, pw = 0;             // top/left replicate pad to /32
+};
+
 struct Act {
     __half *p = nullptr;
     int H = 0, W = 0, C = 0;   // logical dims of the stored tensor

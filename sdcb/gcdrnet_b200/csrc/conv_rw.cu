@@ -212,6 +212,12 @@ __global__ void __launch_bounds__(kRwThreads, 1)
                     TmemLoader bot{acc0 + (uint32_t)((2 * q + 1) * cfg.acc_cols)};
                     epilogue_pool(args.ep, tg, y0 / 2 + q, x, 0, N, top, bot, ch, nch);
                 }
+            } else if (MODE == EPI_HEAD) {
+                // a whole channel row per pixel (the 1x1 over C1): rows alternate between the warps
+                for (int jj = part; jj < R; jj += 2) {
+                    TmemLoader ld{acc0 + (uint32_t)(jj * cfg.acc_cols)};
+                    epilogue_head(args.ep, tg, y0 + jj, x, N, ld);
+                }
             } else {
                 for (int it = part; it < R * nch; it += 2) {
                     const int jj = it / nch, ch = it - jj * nch;
@@ -265,7 +271,10 @@ int rw_launch_bk_mode(const ConvArgs &a, const RwConfig &cfg, const CUtensorMap 
                       cudaStream_t st, std::string &err) {
     auto k = rw_conv_kernel<BK, MODE>;
     const size_t smem = rw_smem(cfg);
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // the attribute is per kernel, shared by every layer (and every thread) launching it:
+    // always the same cap, never a layer's own size, so concurrent workers cannot lower it
+    // under one another's launches
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kRwSmemCap);
     if (e != cudaSuccess) { err = std::string("rw smem attribute: ") + cudaGetErrorString(e); return -1; }
     k<<<grid, kRwThreads, smem, st>>>(ta, tb, a, cfg);
     e = cudaGetLastError();
@@ -276,7 +285,9 @@ int rw_launch_bk_mode(const ConvArgs &a, const RwConfig &cfg, const CUtensorMap 
 }  // namespace
 
 int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
-    if (!a.rw || (mode != EPI_PLAIN && mode != EPI_POOL) || a.nsplit != 1 || a.ksplit != 1) return -1;
+    if (!a.rw || (mode != EPI_PLAIN && mode != EPI_POOL && mode != EPI_HEAD) || a.nsplit != 1 || a.ksplit != 1)
+        return -1;
+    if (mode == EPI_HEAD && (a.C != kStemInC || (a.N != 16 && a.N != 32))) return -1;
     if (a.ntaps != 9 || a.N < 16 || a.N > 256 || a.N % 16) return -1;
     const TileGeom &tg = a.tg;
     if (tg.pool && (tg.conv_h % 2 || tg.conv_w % 2)) return -1;
@@ -343,6 +354,7 @@ int rw_conv_launch(const ConvArgs &a, int mode, const RwConfig &cfg, int num_sms
                      mode, a.C, a.N, a.tg.conv_h, a.tg.conv_w, cfg.bk, cfg.R, cfg.units, grid, cfg.stages,
                      cfg.stage_bytes, cfg.b_bytes, cfg.tmem_cols, rw_smem(cfg));
     if (grid < 1) return 0;
+    if (rw_smem(cfg) > (size_t)kRwSmemCap) { err = "rw_conv: shared memory plan over the cap"; return -1; }
     switch (cfg.bk * 8 + mode) {
         case 64 * 8 + EPI_PLAIN: return rw_launch_bk_mode<64, EPI_PLAIN>(a, cfg, ta, tb, grid, st, err);
         case 64 * 8 + EPI_POOL: return rw_launch_bk_mode<64, EPI_POOL>(a, cfg, ta, tb, grid, st, err);
@@ -350,6 +362,7 @@ int rw_conv_launch(const ConvArgs &a, int mode, const RwConfig &cfg, int num_sms
         case 32 * 8 + EPI_POOL: return rw_launch_bk_mode<32, EPI_POOL>(a, cfg, ta, tb, grid, st, err);
         case 16 * 8 + EPI_PLAIN: return rw_launch_bk_mode<16, EPI_PLAIN>(a, cfg, ta, tb, grid, st, err);
         case 16 * 8 + EPI_POOL: return rw_launch_bk_mode<16, EPI_POOL>(a, cfg, ta, tb, grid, st, err);
+        case 16 * 8 + EPI_HEAD: return rw_launch_bk_mode<16, EPI_HEAD>(a, cfg, ta, tb, grid, st, err);
     }
     err = "rw_conv: bad k-block / mode";
     return -1;

@@ -37,6 +37,7 @@ namespace {
 
 constexpr int kMmaWarps = 4;
 constexpr int kEpiWarps = 8;
+constexpr int kTcSmemCap = 176 * 1024;   // the ring budget below plus the barriers and alignment
 constexpr int kConvThreads = (2 + kMmaWarps + kEpiWarps) * 32;
 constexpr int kProducer2Warp = 1 + kMmaWarps + kEpiWarps;     // the second TMA producer
 
@@ -303,7 +304,9 @@ int launch_bk_mode(const ConvArgs &a, const TcConfig &cfg, const CUtensorMap &ta
                    cudaStream_t st, std::string &err) {
     auto k = tc_conv_kernel<BK, MODE>;
     size_t smem = 1024 + (size_t)cfg.stages * cfg.stage_bytes + sizeof(TcShared);
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem > (size_t)kTcSmemCap) { err = "tc_conv: shared memory plan over the cap"; return -1; }
+    // one cap for every layer and thread (the attribute is per kernel): see conv_rw.cu
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemCap);
     if (e != cudaSuccess) { err = std::string("smem attribute: ") + cudaGetErrorString(e); return -1; }
     k<<<grid, kConvThreads, smem, st>>>(ta, tb, a, cfg);
     e = cudaGetLastError();
@@ -384,7 +387,7 @@ int tc_plan(const ConvArgs &a, int num_sms, TcConfig &cfg, std::string &err) {
 
 int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, std::string &err) {
     static const bool flat_only = [] { const char *v = std::getenv("GCDR_CUDA_CONV"); return v && std::string(v) == "flat"; }();
-    if (!flat_only) {
+    if (!flat_only || mode == EPI_HEAD) {   // the head epilogue exists only in the row-window kernel
         RwConfig rc;
         if (rw_plan(a, mode, num_sms, rc) == 0) return rw_conv_launch(a, mode, rc, num_sms, st, err);
     }

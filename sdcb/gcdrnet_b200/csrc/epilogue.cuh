@@ -24,7 +24,33 @@
 
 namespace gcdr {
 
-enum EpiMode : int { EPI_PLAIN = 0, EPI_POOL = 1, EPI_LN2 = 2, EPI_RESLN = 3, EPI_PARTIAL = 4 };
+enum EpiMode : int { EPI_PLAIN = 0, EPI_POOL = 1, EPI_LN2 = 2, EPI_RESLN = 3, EPI_PARTIAL = 4, EPI_HEAD = 5 };
+
+// Stem input layout: LAY_PADREFL [H+2][W+2][16] fp16 per padded image pixel,
+//   GC: [xb, xg, xr, xb, xg, xr, 0 x 10]
+//   DR: [xb, xg, xr, xb, xg, xr, rh x3, rl x3, rh x3, 0]
+// with x the u8 pixel (exact in fp16) and r = rh + rl the division-corrected
+// image.  The stem weights pair with it as [w'_hi, w'_lo, wr_hi, wr_hi, wr_lo]
+// (w' = w_x / 255), so one fp16 GEMM with fp32 accumulation yields
+// sum x*w_x/255 + r*w_r to fp32-level accuracy (the r_lo*wr_lo term, ~2^-22
+// relative, is dropped).
+constexpr int kStemInC = 16;
+
+// UpHead epilogue (EPI_HEAD): s = relu(bilinear x2 of dec5) + relu(conv + bias),
+// o = sigmoid(fb + fw . s), then GC: I_sm -> r = clamp(x / max(I_sm, 1e-6), 0, 1)
+// written as the DR stem input (the div6 stage); DR: crop, round, R/B swap and
+// alpha from the source into the caller's u8 image.
+struct HeadParams {
+    const __half *dec5 = nullptr;   // [H/2][W/2][C1] fp16 tokens
+    const float *fw = nullptr;      // 1x1 [3][C1]
+    const float *fb = nullptr;      // [3]
+    Act si_in;                      // this net's stem input (GC reads x from it)
+    Act si_out;                     // GC: the DR stem input
+    float *r_out = nullptr, *ism_out = nullptr, *y_out = nullptr;   // debug [H][W][3] fp32
+    ImgSpec img;                    // DR: destination format and the alpha source
+    uint8_t *dst = nullptr;
+    int is_dr = 0;
+};
 
 struct EpiParams {
     const float *bias = nullptr;     // [N] (indexed with the slice offset)
@@ -37,6 +63,7 @@ struct EpiParams {
     ShiftSpec shift;
     const __half *res = nullptr;     // EPI_RESLN residual tokens [T][N]
     float *partial = nullptr;        // EPI_PARTIAL: [ksplit][T][N] fp32
+    HeadParams head;                 // EPI_HEAD
 };
 
 // Geometry of the output grid: q = y * pitch + x over a flat row space.
@@ -216,6 +243,95 @@ __device__ void epilogue_pool(const EpiParams &ep, const TileGeom &tg, int y2, i
             }
         }
         if (writer) act_store(ep.out, y2, x >> 1, n0 + c0, h, cw);
+    }
+}
+
+// EPI_HEAD for padded-image pixel (y, x): the accumulator row holds the stem conv
+// (C1 = 16 or 32 columns).  Warp-collective (the TMEM load); stores are masked.
+template <class L>
+__device__ void epilogue_head(const EpiParams &ep, const TileGeom &tg, int y, int x, int C1, L &ld) {
+    const HeadParams &hp = ep.head;
+    float c1[32];
+    load_cols(ld, 0, C1, c1);
+    if (y >= tg.conv_h || x >= tg.conv_w) return;
+    const int H = tg.conv_h, W = tg.conv_w, Hh = H / 2, Wh = W / 2;
+    // bilinear x2 of dec5, half_pixel, edge clamp (ONNX Resize linear)
+    const float fy = ((float)y + 0.5f) * 0.5f - 0.5f, fx = ((float)x + 0.5f) * 0.5f - 0.5f;
+    const int y0 = (int)floorf(fy), x0 = (int)floorf(fx);
+    const float dy = fy - (float)y0, dx = fx - (float)x0;
+    const int ya = min(max(y0, 0), Hh - 1), yb = min(max(y0 + 1, 0), Hh - 1);
+    const int xa = min(max(x0, 0), Wh - 1), xb = min(max(x0 + 1, 0), Wh - 1);
+    const __half *p00 = hp.dec5 + ((size_t)ya * Wh + xa) * C1, *p01 = hp.dec5 + ((size_t)ya * Wh + xb) * C1;
+    const __half *p10 = hp.dec5 + ((size_t)yb * Wh + xa) * C1, *p11 = hp.dec5 + ((size_t)yb * Wh + xb) * C1;
+    float o0 = hp.fb[0], o1 = hp.fb[1], o2 = hp.fb[2];
+    for (int c0 = 0; c0 < C1; c0 += 16) {
+        float q00[16], q01[16], q10[16], q11[16];
+        load16h(p00 + c0, q00);
+        load16h(p01 + c0, q01);
+        load16h(p10 + c0, q10);
+        load16h(p11 + c0, q11);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            const float top = q00[k] + (q01[k] - q00[k]) * dx, bot = q10[k] + (q11[k] - q10[k]) * dx;
+            const float up = fmaxf(top + (bot - top) * dy, 0.0f);
+            const float sv = up + fmaxf(c1[c0 + k] + ep.bias[c0 + k], 0.0f);
+            o0 = fmaf(sv, hp.fw[c0 + k], o0);
+            o1 = fmaf(sv, hp.fw[C1 + c0 + k], o1);
+            o2 = fmaf(sv, hp.fw[2 * C1 + c0 + k], o2);
+        }
+    }
+    const float o[3] = {1.0f / (1.0f + expf(-o0)), 1.0f / (1.0f + expf(-o1)), 1.0f / (1.0f + expf(-o2))};
+    const size_t pix = (size_t)y * W + x;
+    if (!hp.is_dr) {
+        // div6: r = clamp(x / max(I_sm, 1e-6), 0, 1) with x = u8 / 255, written as the DR stem input
+        const __half *xin = hp.si_in.p + hp.si_in.row(y, x) * kStemInC;
+        __align__(16) __half v[kStemInC];
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+            const __half u = xin[c];
+            const float xv = __half2float(u) / 255.0f;
+            const float d = o[c] > 1e-6f ? o[c] : 1e-6f;
+            float r = xv / d;
+            r = r < 0.0f ? 0.0f : (r > 1.0f ? 1.0f : r);
+            const __half rh = __float2half_rn(r);
+            const __half rl = __float2half_rn(r - __half2float(rh));
+            v[c] = u;
+            v[3 + c] = u;
+            v[6 + c] = rh;
+            v[9 + c] = rl;
+            v[12 + c] = rh;
+            if (hp.r_out) hp.r_out[pix * 3 + c] = r;
+            if (hp.ism_out) hp.ism_out[pix * 3 + c] = o[c];
+        }
+        v[15] = __float2half_rn(0.0f);
+        act_store(hp.si_out, y, x, 0, v, kStemInC);
+    } else {
+        if (hp.y_out)
+            for (int c = 0; c < 3; c++) hp.y_out[pix * 3 + c] = o[c];
+        const ImgSpec &im = hp.img;
+        const int oy = y - im.ph, ox = x - im.pw;
+        if (oy < 0 || ox < 0) return;
+        uint8_t q[3];
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+            float f = o[c] * 255.0f + 0.5f;
+            f = f < 0.0f ? 0.0f : (f > 255.0f ? 255.0f : f);
+            q[c] = (uint8_t)f;
+        }
+        const int ob = im.swap ? 2 : 0;
+        uint8_t *d = hp.dst + ((size_t)oy * im.w + ox) * im.bpp;
+        if (im.bpp == 4) {
+            uchar4 v;
+            v.x = ob ? q[2] : q[0];
+            v.y = q[1];
+            v.z = ob ? q[0] : q[2];
+            v.w = im.src[(size_t)oy * im.stride + (size_t)ox * 4 + 3];
+            *reinterpret_cast<uchar4 *>(d) = v;
+        } else {
+            d[ob] = q[0];
+            d[1] = q[1];
+            d[2 - ob] = q[2];
+        }
     }
 }
 

@@ -476,11 +476,59 @@ __global__ void nhwc2bgr_kernel(const float *y, int W, int ph, int pw, uint8_t *
     if (bpp == 4) d[3] = al;
 }
 
+__global__ void stem_in_kernel(const ImgSpec im, Act si) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)si.H * si.W) return;
+    const int y = (int)(idx / si.W), x = (int)(idx - (long long)y * si.W);
+    const int sy = max(y - im.ph, 0), sx = max(x - im.pw, 0);
+    const uint8_t *p = im.src + (size_t)sy * im.stride + (size_t)sx * im.bpp;
+    const int ob = im.swap ? 2 : 0;
+    const __half b = __ushort2half_rn(p[ob]), g = __ushort2half_rn(p[1]), r = __ushort2half_rn(p[2 - ob]);
+    const __half z = __ushort2half_rn(0);
+    __align__(16) __half v[16] = {b, g, r, b, g, r, z, z, z, z, z, z, z, z, z, z};
+    act_store(si, y, x, 0, v, 16);
+}
+
 inline int grid_for(long long n, int bs) { return (int)((n + bs - 1) / bs); }
 
-inline int launch_status() { return cudaGetLastError() == cudaSuccess ? 0 : -1; }
+thread_local cudaError_t t_last_launch = cudaSuccess;
+
+inline int launch_status() {
+    t_last_launch = cudaGetLastError();
+    return t_last_launch == cudaSuccess ? 0 : -1;
+}
 
 }  // namespace
+
+const char *last_launch_error() { return cudaGetErrorString(t_last_launch); }
+
+int stem_in_launch(const ImgSpec &im, const Act &si, cudaStream_t st) {
+    if (si.C != 16 || si.kind != LAY_PADREFL) return -2;
+    stem_in_kernel<<<grid_for((long long)si.H * si.W, 256), 256, 0, st>>>(im, si);
+    return launch_status();
+}
+
+void pack_stem_conv(const float *w, int c1, int cin, __half *out) {
+    for (int i = 0; i < c1 * 9 * 16; i++) out[i] = __float2half_rn(0.0f);
+    for (int n = 0; n < c1; n++)
+        for (int tap = 0; tap < 9; tap++)
+            for (int ci = 0; ci < cin; ci++) {
+                const float v = w[((size_t)n * cin + ci) * 9 + tap];
+                __half *o = out + ((size_t)n * 9 + tap) * 16;
+                if (ci < 3) {
+                    const float s = v / 255.0f;
+                    const __half hi = __float2half_rn(s);
+                    o[ci] = hi;
+                    o[3 + ci] = __float2half_rn(s - __half2float(hi));
+                } else {
+                    const int c = ci - 3;
+                    const __half hi = __float2half_rn(v);
+                    o[6 + c] = hi;
+                    o[9 + c] = hi;
+                    o[12 + c] = __float2half_rn(v - __half2float(hi));
+                }
+            }
+}
 
 int stem_launch(const StemArgs &a, cudaStream_t st) {
     const long long n = (long long)(a.H / 2) * (a.W / 2);

@@ -6,14 +6,6 @@
 
 namespace gcdr {
 
-// Image source / destination as the caller laid it out (GcdrPixelFormat).
-struct ImgSpec {
-    const uint8_t *src = nullptr;   // device copy of the source image
-    int w = 0, h = 0, stride = 0;   // original dims, row stride in bytes
-    int bpp = 3, swap = 0;          // bytes per pixel, R/B swapped (Rgb24/Rgba32)
-    int ph = 0, pw = 0;             // top/left replicate pad to /32
-};
-
 // Stem: enc1 conv 3x3 reflect (Cin = 3 from the image, or 6 = image + the
 // division-corrected image `r`) + bias -> maxpool 2x2 -> relu, fp32 math,
 // fp16 LAY_PADREFL output (gc#22-25).  w is ONNX [C1][Cin][3][3].
@@ -49,12 +41,21 @@ struct HeadArgs {
 };
 int head_launch(const HeadArgs &a, cudaStream_t st);
 
-// Tensor-core versions of the stem and the head (stem_tc.cu): same results at
-// fp32-level accuracy (u8 operands exact, hi/lo fp16 weight and r splits).
-// bpack holds the weights packed by pack_stem_weights (4 x 32 x 128 fp16).
-int stem_tc_launch(const StemArgs &a, const __half *bpack, int num_sms, int *err, cudaStream_t st);
-int head_tc_launch(const HeadArgs &a, const __half *bpack, int num_sms, int *err, cudaStream_t st);
-void pack_stem_weights(const float *w, int c1, int cin, __half *out);
+
+// The stem and the head on the tensor cores are row-window convs (conv_rw.cu)
+// over a 16-channel stem input; these kernels (SIMT, fp32) are the reference
+// path selected by GCDR_CUDA_STEM=simt.
+//
+// The GC stem input (the stem-input layout of epilogue.cuh, LAY_PADREFL
+// [H+2][W+2][16] fp16): [x, x, 0] with x the u8 pixel of the top/left
+// replicate-padded source in B,G,R order (GcdrEnhancer.cs:242-243 pads and reads it).
+int stem_in_launch(const ImgSpec &im, const Act &si, cudaStream_t st);
+// CUDA error string of this thread's last failed launch of the kernels above.
+const char *last_launch_error();
+// Stem conv weights for that layout: ONNX [C1][Cin][3][3] -> [C1][9 taps][16]
+// with w' = w_x / 255 split hi+lo for the image channels and w_r split hi+lo
+// for the r channels (DR).
+void pack_stem_conv(const float *w, int c1, int cin, __half *out);
 
 // Depthwise 3x3 (zero pad 1) + bias -> exact GELU -> W-shift scatter
 // (gc#85-95 with ChannelShift along W).  w is [C][9] (ONNX [C][1][3][3]).

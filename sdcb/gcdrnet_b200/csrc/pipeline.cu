@@ -80,9 +80,9 @@ void pack_net(Packer &pk, const NetW &n, DevNet &d) {
     pk.f32(n.enc[0].w, &d.enc1_w);
     pk.f32(n.enc[0].b, &d.enc1_b);
     {
-        std::vector<__half> sb(4 * 32 * 128);
-        pack_stem_weights(n.enc[0].w.data(), n.enc[0].cout, n.enc[0].cin, sb.data());
-        pk.h16(sb, &d.stem_b);
+        std::vector<__half> sw((size_t)n.enc[0].cout * 9 * 16);
+        pack_stem_conv(n.enc[0].w.data(), n.enc[0].cout, n.enc[0].cin, sw.data());
+        pk.h16(sw, &d.stem_w16);
     }
     pk.h16(pack_conv(n.enc[1]), &d.enc2); pk.f32(n.enc[1].b, &d.enc2_b);
     pk.h16(pack_conv(n.enc[2]), &d.enc3); pk.f32(n.enc[2].b, &d.enc3_b);
@@ -343,7 +343,9 @@ int Worker::plan_arena() {
     Alloc al;
     plan_net(al, gcb_, w.gc, H_, W_);
     plan_net(al, drb_, w.dr, H_, W_);
-    al.take(reinterpret_cast<void **>(&r_), (size_t)H_ * W_ * 3 * 4);
+    al.take(reinterpret_cast<void **>(&r_), simt_stem_ || debug_ ? (size_t)H_ * W_ * 3 * 4 : 256);
+    al.act(si_gc_, H_, W_, kStemInC, LAY_PADREFL);
+    al.act(si_dr_, H_, W_, kStemInC, LAY_PADREFL);
     al.take(reinterpret_cast<void **>(&ism_), debug_ ? (size_t)H_ * W_ * 3 * 4 : 256);
     al.take(reinterpret_cast<void **>(&ydbg_), debug_ ? (size_t)H_ * W_ * 3 * 4 : 256);
     const size_t img = (size_t)h_ * w_ * bpp_;
@@ -390,7 +392,8 @@ int Worker::build_ops() {
     const DevWeights &wt = *weights_;
     const int nsm = num_sms_;
     int *errp = d_err_;
-    auto conv_op = [this, nsm, errp](ConvArgs a, int mode, const std::string &name) {
+    auto conv_op = [this, nsm, errp](ConvArgs a, int mode, const std::string &name, double flops_override = -1,
+                                      double bytes_override = -1) {
         a.err = errp;
         const bool partial = uses_partial(a, mode, nsm);
         int run_mode = mode;
@@ -413,6 +416,8 @@ int Worker::build_ops() {
         oi.bytes = in_px * a.C * 2 + (double)a.N * a.ntaps * a.C * 2 +
                    (partial ? 4.0 * px * a.N * a.ksplit
                             : out_px * a.N * 2 * (mode == EPI_LN2 ? 2 : 1) + (mode == EPI_RESLN ? px * a.N * 2 : 0));
+        if (flops_override >= 0) oi.flops = flops_override;
+        if (bytes_override >= 0) oi.bytes = bytes_override;
         info_.push_back(oi);
         ops_.push_back([a, run_mode, nsm, this](cudaStream_t st) {
             std::string e;
@@ -436,7 +441,7 @@ int Worker::build_ops() {
             f.out = a.ep.out;
             f.out2 = a.ep.out2;
             ops_.push_back([f, this](cudaStream_t st) {
-                return ln_finalize_launch(f, st) ? fail(GCDR_ERR_DEVICE, "ln_finalize launch") : 0;
+                return ln_finalize_launch(f, st) ? fail(GCDR_ERR_DEVICE, std::string("ln_finalize launch: ") + last_launch_error()) : 0;
             });
             launches_++;
             info_.push_back(OpInfo{name + ".ln", 0,
@@ -465,24 +470,34 @@ int Worker::build_ops() {
         const int H1 = H_ / 2, W1 = W_ / 2, H2 = H_ / 4, W2 = W_ / 4, H3 = H_ / 8, W3 = W_ / 8;
         const int H4 = H_ / 16, W4 = W_ / 16, H5 = H_ / 32, W5 = W_ / 32;
         (void)H1; (void)W1; (void)H2; (void)W2;
-        // stem: enc1 conv + pool + relu (fp32)
-        StemArgs sa;
-        sa.img = img;
-        sa.r = which ? r_ : nullptr;
-        sa.H = H_; sa.W = W_; sa.cin = n.cin; sa.c1 = n.c1;
-        sa.w = n.enc1_w; sa.b = n.enc1_b; sa.out = b.t1;
-        if (simt_stem_) {
-            ops_.push_back([sa, this](cudaStream_t st) { return stem_launch(sa, st) ? fail(GCDR_ERR_DEVICE, "stem launch") : 0; });
-        } else {
-            const __half *bp = n.stem_b;
-            ops_.push_back([sa, bp, nsm, errp, this](cudaStream_t st) {
-                return stem_tc_launch(sa, bp, nsm, errp, st) ? fail(GCDR_ERR_DEVICE, "stem launch") : 0;
-            });
-        }
-        launches_++;
+        // stem: enc1 conv + pool + relu
         const std::string pre = which ? "dr." : "gc.";
-        simt(pre + "stem", 2.0 * H_ * W_ * n.c1 * 9 * n.cin,
-             (double)h_ * w_ * bpp_ + (which ? 12.0 * H_ * W_ : 0) + (double)H1 * W1 * n.c1 * 2);
+        const double stem_flops = 2.0 * H_ * W_ * n.c1 * 9 * n.cin;
+        const double stem_bytes = (double)h_ * w_ * bpp_ + (which ? 12.0 * H_ * W_ : 0) + (double)H1 * W1 * n.c1 * 2;
+        if (simt_stem_) {
+            StemArgs sa;
+            sa.img = img;
+            sa.r = which ? r_ : nullptr;
+            sa.H = H_; sa.W = W_; sa.cin = n.cin; sa.c1 = n.c1;
+            sa.w = n.enc1_w; sa.b = n.enc1_b; sa.out = b.t1;
+            ops_.push_back([sa, this](cudaStream_t st) { return stem_launch(sa, st) ? fail(GCDR_ERR_DEVICE, std::string("stem launch: ") + last_launch_error()) : 0; });
+            launches_++;
+            simt(pre + "stem", stem_flops, stem_bytes);
+        } else {
+            // the stem as a tensor-core conv over the stem input (GC: built from the image here;
+            // DR: written by the GC head)
+            if (!which) {
+                const Act si = si_gc_;
+                ops_.push_back([img, si, this](cudaStream_t st) {
+                    return stem_in_launch(img, si, st) ? fail(GCDR_ERR_DEVICE, std::string("stem input launch: ") + last_launch_error()) : 0;
+                });
+                launches_++;
+                simt(pre + "stem_in", 0, (double)h_ * w_ * bpp_ + (double)(H_ + 2) * (W_ + 2) * kStemInC * 2);
+            }
+            ConvArgs a = conv_s1(which ? si_dr_ : si_gc_, n.stem_w16, n.enc1_b, n.c1, true);
+            a.ep.out = b.t1;
+            conv_op(a, EPI_POOL, pre + "stem", stem_flops, stem_bytes);
+        }
         // encoders 2, 3: conv + pool + relu
         { ConvArgs a = conv_s1(b.t1, n.enc2, n.enc2_b, n.c2, true); a.ep.out = b.t2; conv_op(a, EPI_POOL, pre + "enc2"); }
         { ConvArgs a = conv_s1(b.t2, n.enc3, n.enc3_b, n.c3, true); a.ep.out = b.t3; conv_op(a, EPI_POOL, pre + "enc3"); }
@@ -495,7 +510,7 @@ int Worker::build_ops() {
             ShiftSpec sb = bk.sb;
             int C = bk.C;
             ops_.push_back([=](cudaStream_t st) {
-                return dw_gelu_shift_launch(f1, H, W, C, dw, db, sb, f2, st) ? fail(GCDR_ERR_DEVICE, "dw launch") : 0;
+                return dw_gelu_shift_launch(f1, H, W, C, dw, db, sb, f2, st) ? fail(GCDR_ERR_DEVICE, std::string("dw launch: ") + last_launch_error()) : 0;
             });
             launches_++;
             simt(bn + ".dw_gelu_shift", 2.0 * 9 * H * W * C, 4.0 * H * W * C);
@@ -537,7 +552,7 @@ int Worker::build_ops() {
             u.g = bk.n2_g; u.b = bk.n2_b; u.eps = bk.n2_eps;
             u.h = plain(b.hs, H, W, C);
             u.shift = bk.sa;
-            ops_.push_back([u, this](cudaStream_t st) { return up_add_launch(u, st) ? fail(GCDR_ERR_DEVICE, "up_add launch") : 0; });
+            ops_.push_back([u, this](cudaStream_t st) { return up_add_launch(u, st) ? fail(GCDR_ERR_DEVICE, std::string("up_add launch: ") + last_launch_error()) : 0; });
             launches_++;
             simt(pre + "join_ln" + std::to_string(H), 0, 2.0 * (H / 2) * (W / 2) * C + 6.0 * H * W * C);
         };
@@ -546,7 +561,7 @@ int Worker::build_ops() {
             u.d = b.dconv;
             u.skip = skip;
             u.out = out;
-            ops_.push_back([u, this](cudaStream_t st) { return up_add_launch(u, st) ? fail(GCDR_ERR_DEVICE, "up_add launch") : 0; });
+            ops_.push_back([u, this](cudaStream_t st) { return up_add_launch(u, st) ? fail(GCDR_ERR_DEVICE, std::string("up_add launch: ") + last_launch_error()) : 0; });
             launches_++;
             simt(pre + "join" + std::to_string(out.H), 0, 2.0 * (out.H / 2) * (out.W / 2) * out.C + 4.0 * out.H * out.W * out.C);
         };
@@ -561,33 +576,45 @@ int Worker::build_ops() {
         up_pad(b.t1, b.d4);
         { ConvArgs a = conv_s1(b.d4, n.dec[4], n.dec_b[4], n.c1, false); a.ep.out = plain(b.dec5, H1, W1, n.c1); conv_op(a, EPI_PLAIN, pre + "dec5"); }
         // head: recomputed stem skip + bilinear + 1x1 + sigmoid, then div6 (GC) or u8 out (DR)
-        HeadArgs ha;
-        ha.img = img;
-        ha.r = which ? r_ : nullptr;
-        ha.H = H_; ha.W = W_; ha.cin = n.cin; ha.c1 = n.c1;
-        ha.w = n.enc1_w; ha.b = n.enc1_b; ha.fw = n.fin_w; ha.fb = n.fin_b;
-        ha.dec5 = b.dec5;
-        ha.is_dr = which;
-        if (!which) {
-            ha.r_out = r_;
-            ha.ism_out = debug_ ? ism_ : nullptr;
-        } else {
-            ha.dst = d_dst_;
-            ha.y_out = debug_ ? ydbg_ : nullptr;
-        }
+        const double hpx = which ? (double)h_ * w_ : (double)H_ * W_;
+        const double head_flops = hpx * 2.0 * (n.c1 * 9 * n.cin + 3 * n.c1);
+        const double head_bytes = hpx * bpp_ + (which ? 12.0 * hpx + hpx * bpp_ : 12.0 * hpx) + (double)H1 * W1 * n.c1 * 2;
         if (simt_stem_) {
-            ops_.push_back([ha, this](cudaStream_t st) { return head_launch(ha, st) ? fail(GCDR_ERR_DEVICE, "head launch") : 0; });
+            HeadArgs ha;
+            ha.img = img;
+            ha.r = which ? r_ : nullptr;
+            ha.H = H_; ha.W = W_; ha.cin = n.cin; ha.c1 = n.c1;
+            ha.w = n.enc1_w; ha.b = n.enc1_b; ha.fw = n.fin_w; ha.fb = n.fin_b;
+            ha.dec5 = b.dec5;
+            ha.is_dr = which;
+            if (!which) {
+                ha.r_out = r_;
+                ha.ism_out = debug_ ? ism_ : nullptr;
+            } else {
+                ha.dst = d_dst_;
+                ha.y_out = debug_ ? ydbg_ : nullptr;
+            }
+            ops_.push_back([ha, this](cudaStream_t st) { return head_launch(ha, st) ? fail(GCDR_ERR_DEVICE, std::string("head launch: ") + last_launch_error()) : 0; });
+            launches_++;
+            simt(pre + "head", head_flops, head_bytes);
         } else {
-            const __half *bp = n.stem_b;
-            ops_.push_back([ha, bp, nsm, errp, this](cudaStream_t st) {
-                return head_tc_launch(ha, bp, nsm, errp, st) ? fail(GCDR_ERR_DEVICE, "head launch") : 0;
-            });
-        }
-        launches_++;
-        {
-            const double px = which ? (double)h_ * w_ : (double)H_ * W_;
-            simt(pre + "head", px * 2.0 * (n.c1 * 9 * n.cin + 3 * n.c1),
-                 px * bpp_ + (which ? 12.0 * px + px * bpp_ : 12.0 * px) + (double)H1 * W1 * n.c1 * 2);
+            ConvArgs a = conv_s1(which ? si_dr_ : si_gc_, n.stem_w16, n.enc1_b, n.c1, false);
+            HeadParams &hp = a.ep.head;
+            hp.dec5 = b.dec5;
+            hp.fw = n.fin_w;
+            hp.fb = n.fin_b;
+            hp.si_in = which ? si_dr_ : si_gc_;
+            hp.is_dr = which;
+            if (!which) {
+                hp.si_out = si_dr_;
+                hp.r_out = debug_ ? r_ : nullptr;
+                hp.ism_out = debug_ ? ism_ : nullptr;
+            } else {
+                hp.img = img;
+                hp.dst = d_dst_;
+                hp.y_out = debug_ ? ydbg_ : nullptr;
+            }
+            conv_op(a, EPI_HEAD, pre + "head", head_flops, head_bytes);
         }
     }
     return info_.size() == ops_.size() ? GCDR_OK : fail(GCDR_ERR_DEVICE, "op metadata mismatch");
@@ -721,13 +748,27 @@ int Worker::debug_intermediates(float *gc_in, float *gc_out, float *dr_in, float
     if (cudaMalloc(&dx, n3 * 4) != cudaSuccess) return fail(GCDR_ERR_OOM, "debug alloc");
     int rc = k_bgr2nhwc(d_src_, w_, h_, w_ * bpp_, fmt_, dx, ph_, pw_, stream_);
     cudaMemcpyAsync(x.data(), dx, n3 * 4, cudaMemcpyDeviceToHost, stream_);
-    cudaMemcpyAsync(r.data(), r_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
+    std::vector<__half> si;
+    if (simt_stem_ || debug_) {
+        cudaMemcpyAsync(r.data(), r_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
+    } else {
+        // r = r_hi + r_lo from the DR stem input (interior rows of [H+2][W+2][16])
+        si.resize((size_t)si_dr_.rows() * kStemInC);
+        cudaMemcpyAsync(si.data(), si_dr_.p, si.size() * 2, cudaMemcpyDeviceToHost, stream_);
+    }
     if (gc_out && debug_) cudaMemcpyAsync(gc_out, ism_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
     if (dr_out && debug_) cudaMemcpyAsync(dr_out, ydbg_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
     cudaError_t e = cudaStreamSynchronize(stream_);
     cudaFree(dx);
     if (rc || e != cudaSuccess) return fail(GCDR_ERR_DEVICE, "debug copy failed");
     if ((gc_out || dr_out) && !debug_) return fail(GCDR_ERR_ARG, "shading map / output need debug mode (gcdr_cuda_set_debug)");
+    if (!si.empty())
+        for (int yy = 0; yy < H_; yy++)
+            for (int xx = 0; xx < W_; xx++) {
+                const __half *v = si.data() + si_dr_.row(yy, xx) * kStemInC;
+                for (int c = 0; c < 3; c++)
+                    r[((size_t)yy * W_ + xx) * 3 + c] = __half2float(v[6 + c]) + __half2float(v[9 + c]);
+            }
     if (gc_in) std::memcpy(gc_in, x.data(), n3 * 4);
     if (dr_in)
         for (size_t p = 0; p < (size_t)H_ * W_; p++)

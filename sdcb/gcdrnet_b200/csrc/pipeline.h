@@ -34,7 +34,7 @@ struct DevBlock {
 struct DevNet {
     int cin = 0, c1 = 0, c2 = 0, c3 = 0, c4 = 0, c5 = 0;
     const float *enc1_w = nullptr, *enc1_b = nullptr;   // fp32 ONNX order (stem / head)
-    const __half *stem_b = nullptr;                     // tensor-core stem weights (pack_stem_weights)
+    const __half *stem_w16 = nullptr;                   // stem conv over the stem-input layout (pack_stem_conv)
     const __half *enc2 = nullptr, *enc3 = nullptr, *pe3 = nullptr, *pe4 = nullptr, *dec[5] = {};
     const float *enc2_b = nullptr, *enc3_b = nullptr, *pe3_b = nullptr, *pe4_b = nullptr, *dec_b[5] = {};
     const float *pe3n_g = nullptr, *pe3n_b = nullptr, *pe4n_g = nullptr, *pe4n_b = nullptr;
@@ -106,6 +106,7 @@ private:
     size_t arena_bytes_ = 0;
     NetBufs gcb_, drb_;
     float *r_ = nullptr, *ism_ = nullptr, *ydbg_ = nullptr;
+    Act si_gc_, si_dr_;     // stem inputs [H+2][W+2][16] fp16 (GC: from the image; DR: from the GC head)
     float *ws_ = nullptr;   // split-K partial sums (EPI_PARTIAL), shared by both nets
     uint8_t *d_src_ = nullptr, *d_dst_ = nullptr;
     int *d_err_ = nullptr;
