@@ -216,7 +216,8 @@ __global__ void __launch_bounds__(kRwThreads, 1)
                 // a whole channel row per pixel (the 1x1 over C1): rows alternate between the warps
                 for (int jj = part; jj < R; jj += 2) {
                     TmemLoader ld{acc0 + (uint32_t)(jj * cfg.acc_cols)};
-                    epilogue_head(args.ep, tg, y0 + jj, x, N, ld);
+                    if (N == 32) epilogue_head<32>(args.ep, tg, y0 + jj, x, ld);
+                    else epilogue_head<16>(args.ep, tg, y0 + jj, x, ld);
                 }
             } else {
                 for (int it = part; it < R * nch; it += 2) {

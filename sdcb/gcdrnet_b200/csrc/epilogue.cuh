@@ -42,8 +42,11 @@ constexpr int kStemInC = 16;
 // alpha from the source into the caller's u8 image.
 struct HeadParams {
     const __half *dec5 = nullptr;   // [H/2][W/2][C1] fp16 tokens
-    const float *fw = nullptr;      // 1x1 [3][C1]
-    const float *fb = nullptr;      // [3]
+    // the 1x1 head and the stem bias by value: kernel-parameter (constant bank)
+    // operands of the per-pixel FMAs instead of per-pixel loads
+    float fw[3 * 32];               // 1x1 [3][C1]
+    float fb[3];
+    float b1[32];                   // stem conv bias [C1]
     Act si_in;                      // this net's stem input (GC reads x from it)
     Act si_out;                     // GC: the DR stem input
     float *r_out = nullptr, *ism_out = nullptr, *y_out = nullptr;   // debug [H][W][3] fp32
@@ -248,11 +251,12 @@ __device__ void epilogue_pool(const EpiParams &ep, const TileGeom &tg, int y2, i
 
 // EPI_HEAD for padded-image pixel (y, x): the accumulator row holds the stem conv
 // (C1 = 16 or 32 columns).  Warp-collective (the TMEM load); stores are masked.
-template <class L>
-__device__ void epilogue_head(const EpiParams &ep, const TileGeom &tg, int y, int x, int C1, L &ld) {
+template <int C1, class L>
+__device__ void epilogue_head(const EpiParams &ep, const TileGeom &tg, int y, int x, L &ld) {
     const HeadParams &hp = ep.head;
-    float c1[32];
-    load_cols(ld, 0, C1, c1);
+    float c1[C1];
+    if (C1 == 32) ld.load32(0, c1);
+    else ld.load16(0, c1);
     if (y >= tg.conv_h || x >= tg.conv_w) return;
     const int H = tg.conv_h, W = tg.conv_w, Hh = H / 2, Wh = W / 2;
     // bilinear x2 of dec5, half_pixel, edge clamp (ONNX Resize linear)
@@ -264,6 +268,7 @@ __device__ void epilogue_head(const EpiParams &ep, const TileGeom &tg, int y, in
     const __half *p00 = hp.dec5 + ((size_t)ya * Wh + xa) * C1, *p01 = hp.dec5 + ((size_t)ya * Wh + xb) * C1;
     const __half *p10 = hp.dec5 + ((size_t)yb * Wh + xa) * C1, *p11 = hp.dec5 + ((size_t)yb * Wh + xb) * C1;
     float o0 = hp.fb[0], o1 = hp.fb[1], o2 = hp.fb[2];
+#pragma unroll
     for (int c0 = 0; c0 < C1; c0 += 16) {
         float q00[16], q01[16], q10[16], q11[16];
         load16h(p00 + c0, q00);
@@ -274,7 +279,7 @@ __device__ void epilogue_head(const EpiParams &ep, const TileGeom &tg, int y, in
         for (int k = 0; k < 16; k++) {
             const float top = q00[k] + (q01[k] - q00[k]) * dx, bot = q10[k] + (q11[k] - q10[k]) * dx;
             const float up = fmaxf(top + (bot - top) * dy, 0.0f);
-            const float sv = up + fmaxf(c1[c0 + k] + ep.bias[c0 + k], 0.0f);
+            const float sv = up + fmaxf(c1[c0 + k] + hp.b1[c0 + k], 0.0f);
             o0 = fmaf(sv, hp.fw[c0 + k], o0);
             o1 = fmaf(sv, hp.fw[C1 + c0 + k], o1);
             o2 = fmaf(sv, hp.fw[2 * C1 + c0 + k], o2);
@@ -284,11 +289,12 @@ __device__ void epilogue_head(const EpiParams &ep, const TileGeom &tg, int y, in
     const size_t pix = (size_t)y * W + x;
     if (!hp.is_dr) {
         // div6: r = clamp(x / max(I_sm, 1e-6), 0, 1) with x = u8 / 255, written as the DR stem input
-        const __half *xin = hp.si_in.p + hp.si_in.row(y, x) * kStemInC;
+        const uint4 xin = *reinterpret_cast<const uint4 *>(hp.si_in.p + hp.si_in.row(y, x) * kStemInC);
+        const __half *xu = reinterpret_cast<const __half *>(&xin);
         __align__(16) __half v[kStemInC];
 #pragma unroll
         for (int c = 0; c < 3; c++) {
-            const __half u = xin[c];
+            const __half u = xu[c];
             const float xv = __half2float(u) / 255.0f;
             const float d = o[c] > 1e-6f ? o[c] : 1e-6f;
             float r = xv / d;

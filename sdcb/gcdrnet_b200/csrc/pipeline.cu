@@ -105,6 +105,9 @@ void pack_net(Packer &pk, const NetW &n, DevNet &d) {
     }
     pk.f32(n.fin.w, &d.fin_w);
     pk.f32(n.fin.b, &d.fin_b);
+    for (size_t i = 0; i < n.fin.w.size() && i < 3 * 32; i++) d.head_fw[i] = n.fin.w[i];
+    for (size_t i = 0; i < n.fin.b.size() && i < 3; i++) d.head_fb[i] = n.fin.b[i];
+    for (size_t i = 0; i < n.enc[0].b.size() && i < 32; i++) d.head_b1[i] = n.enc[0].b[i];
 }
 
 }  // namespace
@@ -601,8 +604,9 @@ int Worker::build_ops() {
             ConvArgs a = conv_s1(which ? si_dr_ : si_gc_, n.stem_w16, n.enc1_b, n.c1, false);
             HeadParams &hp = a.ep.head;
             hp.dec5 = b.dec5;
-            hp.fw = n.fin_w;
-            hp.fb = n.fin_b;
+            for (int i = 0; i < 3 * n.c1; i++) hp.fw[i] = n.head_fw[i];
+            for (int i = 0; i < 3; i++) hp.fb[i] = n.head_fb[i];
+            for (int i = 0; i < n.c1; i++) hp.b1[i] = n.head_b1[i];
             hp.si_in = which ? si_dr_ : si_gc_;
             hp.is_dr = which;
             if (!which) {

@@ -41,6 +41,8 @@ struct DevNet {
     float pe3n_eps = 1e-5f, pe4n_eps = 1e-5f;
     DevBlock blk[4];
     const float *fin_w = nullptr, *fin_b = nullptr;
+    // host copies of the head's constants (passed by value to the head kernel)
+    float head_fw[3 * 32] = {}, head_fb[3] = {}, head_b1[32] = {};
 };
 
 struct DevWeights {
