@@ -22,11 +22,39 @@
 // a dimension of size 1 mirrors onto itself).
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <utility>
 
 namespace gcdr {
 
 enum LayoutKind : int { LAY_PLAIN = 0, LAY_PADREFL = 1, LAY_PHASE = 2, LAY_PADZERO = 3 };
+
+// Programmatic dependent launch: every pipeline kernel is launched with
+// launch_pdl, waits for its predecessor grid before its first access to
+// activations (read or write), and lets its successor launch early: persistent
+// kernels right after their setup, the others when each block is done.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();   // GCDR_CUDA_PDL=0 turns it off (kernels.cu)
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Image source / destination as the caller laid it out (GcdrPixelFormat).
 struct ImgSpec {
@@ -116,8 +144,10 @@ __device__ inline int shift_group(const ShiftSpec &s, int c) {
 __device__ inline int shift_dest(int s, int off, int L, bool *zero) {
     int d = s - off;
     *zero = d < 0 || d >= L;
-    d %= L;
-    if (d < 0) d += L;
+    if (*zero) {                        // rare: the wrapped column gets the zero (L may be 1 or 2)
+        d %= L;
+        if (d < 0) d += L;
+    }
     return d;
 }
 
@@ -135,7 +165,7 @@ __device__ inline void shift_store(const Act &a, const ShiftSpec &s, int axis, i
             if (axis == 2) dy = shift_dest(y, s.offs[g0], a.H, &z);
             else dx = shift_dest(x, s.offs[g0], a.W, &z);
         }
-        __half *d = a.p + ((long long)dy * a.W + dx) * a.C + c;
+        __half *d = a.p + ((size_t)dy * a.W + dx) * a.C + c;
         if (g0 == g1) {
             *reinterpret_cast<__half2 *>(d) = z ? __float2half2_rn(0.0f) : __floats2half2_rn(v[k], v[k + 1]);
         } else {
@@ -146,7 +176,7 @@ __device__ inline void shift_store(const Act &a, const ShiftSpec &s, int axis, i
                 if (axis == 2) ey = shift_dest(y, s.offs[g1], a.H, &z1);
                 else ex = shift_dest(x, s.offs[g1], a.W, &z1);
             }
-            a.p[((long long)ey * a.W + ex) * a.C + c + 1] = __float2half_rn(z1 ? 0.0f : v[k + 1]);
+            a.p[((size_t)ey * a.W + ex) * a.C + c + 1] = __float2half_rn(z1 ? 0.0f : v[k + 1]);
         }
     }
 }

@@ -93,6 +93,9 @@ __global__ void __launch_bounds__(kRwThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = sh->tmem_base;
     volatile int *abort_flag = &sh->abort_flag;
+    pdl_trigger();                          // all CTAs are resident: the next kernel may start launching
+    const bool b_loader = (warp == 0 && lane == 0);
+    if (!b_loader) pdl_wait();              // activations of the previous kernels
 
     // unit -> (first output row, first pixel); pool units cover R conv rows = R/2 pooled rows
     auto unit_origin = [&](int u, int &y0, int &x0) {
@@ -111,6 +114,7 @@ __global__ void __launch_bounds__(kRwThreads, 1)
                     for (int tap = 0; tap < 9; tap++)
                         tma_load_2d(bres + (size_t)(kb * 9 + tap) * cfg.b_block, &tmB, tap * C + kb * BK, 0, &sh->bfull);
                 sh->b_issued = 1;
+                pdl_wait();                 // the weights are constant; the activations are not
             }
             int s = 0;
             uint32_t ph = 0;
@@ -277,8 +281,8 @@ int rw_launch_bk_mode(const ConvArgs &a, const RwConfig &cfg, const CUtensorMap 
     // under one another's launches
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kRwSmemCap);
     if (e != cudaSuccess) { err = std::string("rw smem attribute: ") + cudaGetErrorString(e); return -1; }
-    k<<<grid, kRwThreads, smem, st>>>(ta, tb, a, cfg);
-    e = cudaGetLastError();
+    e = launch_pdl(k, dim3(grid), dim3(kRwThreads), smem, st, ta, tb, a, cfg);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { err = std::string("rw_conv launch: ") + cudaGetErrorString(e); return -1; }
     return 0;
 }

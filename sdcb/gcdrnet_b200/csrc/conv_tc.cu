@@ -100,6 +100,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = sh->tmem_base;
     volatile int *abort_flag = &sh->abort_flag;
+    pdl_trigger();                          // all CTAs are resident: the next kernel may start launching
+    pdl_wait();                             // activations of the previous kernels
 
     if (warp == 0 || warp == kProducer2Warp) {
         // two producers take the ring stages alternately: the per-stage cost of one
@@ -308,8 +310,8 @@ int launch_bk_mode(const ConvArgs &a, const TcConfig &cfg, const CUtensorMap &ta
     // one cap for every layer and thread (the attribute is per kernel): see conv_rw.cu
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemCap);
     if (e != cudaSuccess) { err = std::string("smem attribute: ") + cudaGetErrorString(e); return -1; }
-    k<<<grid, kConvThreads, smem, st>>>(ta, tb, a, cfg);
-    e = cudaGetLastError();
+    e = launch_pdl(k, dim3(grid), dim3(kConvThreads), smem, st, ta, tb, a, cfg);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { err = std::string("tc_conv launch: ") + cudaGetErrorString(e); return -1; }
     return 0;
 }

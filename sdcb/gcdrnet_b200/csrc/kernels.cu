@@ -42,6 +42,7 @@ __device__ __forceinline__ void load_px(const ImgSpec &im, const float *r, int W
 
 template <int CIN, int C1>
 __global__ void __launch_bounds__(128) stem_kernel(const StemArgs a) {
+    pdl_wait();
     __shared__ float ws[9 * CIN * C1];
     __shared__ float bs[C1];
     for (int i = threadIdx.x; i < 9 * CIN * C1; i += blockDim.x) {
@@ -84,10 +85,12 @@ __global__ void __launch_bounds__(128) stem_kernel(const StemArgs a) {
         h[co] = __float2half_rn(fmaxf(m, 0.0f));
     }
     act_store(a.out, y2, x2, 0, h, C1);
+    pdl_trigger();
 }
 
 template <int CIN, int C1, bool DR>
 __global__ void __launch_bounds__(128) head_kernel(const HeadArgs a) {
+    pdl_wait();
     __shared__ float ws[9 * CIN * C1];
     __shared__ float bs[C1];
     __shared__ float fw[3 * C1];
@@ -181,74 +184,103 @@ __global__ void __launch_bounds__(128) head_kernel(const HeadArgs a) {
             d[2 - ob] = q[2];
         }
     }
+    pdl_trigger();
 }
 
 __device__ __forceinline__ float gelu_exact(float v) {
-    // gc#88-92: x * (0.5 * (erf(x / 1.4142135381698608) + 1))
-    return v * (0.5f * (erff(v / 1.4142135381698608f) + 1.0f));
+    // gc#88-92: x * (0.5 * (erf(x / 1.4142135381698608) + 1)); the division by
+    // sqrt(2) as a product with its reciprocal (within 1 ulp of the quotient)
+    return v * (0.5f * (erff(v * 0.70710678118654752f) + 1.0f));
 }
 
-// out[y][x][c] = gelu(dw(in))[y][x + off_g(c)][c] (zero outside): the W shift
-// that precedes fc2 (gc#95-126) is folded into the depthwise stage as a gather,
-// so every output chunk of 8 channels is one 16-byte store.  The block stages
-// the weights tap-major ([9][C]) and the bias in shared memory.
+// out = shiftW(gelu(dw(in))): depthwise 3x3 (zero pad 1) + bias + exact GELU,
+// then the W shift that precedes fc2 (gc#95-126) as a scatter: channel group g
+// of pixel x goes to column x - off_g, and a source whose destination falls
+// outside the row writes the zero that its wrapped column must receive (each
+// output element is written exactly once).  A thread computes one 8-channel
+// chunk of two neighbouring pixels (x, x+1) from a shared 3 x 4 input window;
+// only the stores of chunks that straddle a group boundary split.  Grid (row
+// segments, y); the tap-major weights ([9][C] fp32) are staged in shared memory.
 constexpr int kDwMaxC = 512;
 
-__global__ void __launch_bounds__(256) dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *w,
+__device__ __forceinline__ void dw_acc8(float *acc, const uint4 raw, const float *wp) {
+    const float4 w0 = *reinterpret_cast<const float4 *>(wp), w1 = *reinterpret_cast<const float4 *>(wp + 4);
+    const __half2 *hv = reinterpret_cast<const __half2 *>(&raw);
+    const float2 f0 = __half22float2(hv[0]), f1 = __half22float2(hv[1]), f2 = __half22float2(hv[2]),
+                 f3 = __half22float2(hv[3]);
+    acc[0] = fmaf(w0.x, f0.x, acc[0]);
+    acc[1] = fmaf(w0.y, f0.y, acc[1]);
+    acc[2] = fmaf(w0.z, f1.x, acc[2]);
+    acc[3] = fmaf(w0.w, f1.y, acc[3]);
+    acc[4] = fmaf(w1.x, f2.x, acc[4]);
+    acc[5] = fmaf(w1.y, f2.y, acc[5]);
+    acc[6] = fmaf(w1.z, f3.x, acc[6]);
+    acc[7] = fmaf(w1.w, f3.y, acc[7]);
+}
+
+__global__ void __launch_bounds__(256) dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *wt,
                                                             const float *b, const ShiftSpec s, __half *out) {
+    pdl_wait();
     __shared__ __align__(16) float ws[9 * kDwMaxC];
-    __shared__ __align__(16) float bs[kDwMaxC];
-    for (int i = threadIdx.x; i < 9 * C; i += blockDim.x) {
-        const int tap = i / C, c = i - tap * C;
-        ws[i] = w[c * 9 + tap];
-    }
-    for (int i = threadIdx.x; i < C; i += blockDim.x) bs[i] = b[i];
+    for (int i = threadIdx.x * 4; i < 9 * C; i += blockDim.x * 4)
+        *reinterpret_cast<float4 *>(ws + i) = __ldg(reinterpret_cast<const float4 *>(wt + i));
     __syncthreads();
-    const int chunks = C / 8;
-    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (long long)H * W * chunks) return;
-    const int ch = (int)(idx % chunks);
-    const long long p = idx / chunks;
-    const int y = (int)(p / W), x = (int)(p - (long long)y * W);
-    const int c0 = ch * 8;
-    // channel groups of this chunk: at most two (groups are wider than 8 channels)
-    const int ga = shift_group(s, c0), gb = shift_group(s, c0 + 7);
-    const int xa = x + (ga >= 0 ? s.offs[ga] : 0), xb = x + (gb >= 0 ? s.offs[gb] : 0);
-    const int split = ga == gb ? 8 : s.ends[ga] - c0;   // channels [0, split) read column xa, the rest xb
-    float acc[8];
+    const int chunks = C >> 3;
+    const int Wp = (W + 1) >> 1;                       // pixel pairs per row
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const int y = blockIdx.y;
+    if (t < Wp * chunks) {
+        const int xp = t / chunks, ch = t - xp * chunks;
+        const int x = 2 * xp, c0 = ch * 8;
+        float acc[2][8];
+        {
+            const float4 b0 = __ldg(reinterpret_cast<const float4 *>(b + c0));
+            const float4 b1 = __ldg(reinterpret_cast<const float4 *>(b + c0 + 4));
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-    for (int k = 0; k < 8; k++) acc[k] = bs[c0 + k];
-#pragma unroll
-    for (int part = 0; part < 2; part++) {
-        const int sx = part ? xb : xa;
-        if (part && split == 8) break;
-        if (sx < 0 || sx >= W) continue;
+            for (int k = 0; k < 8; k++) acc[0][k] = acc[1][k] = bv[k];
+        }
+        const __half *col = in + c0;
 #pragma unroll
         for (int ky = 0; ky < 3; ky++) {
             const int yy = y + ky - 1;
             if (yy < 0 || yy >= H) continue;
+            const __half *rowp = col + (size_t)yy * W * C;
 #pragma unroll
-            for (int kx = 0; kx < 3; kx++) {
-                const int xx = sx + kx - 1;
+            for (int j = 0; j < 4; j++) {
+                const int xx = x - 1 + j;             // pixel x uses columns x-1..x+1, pixel x+1 x..x+2
                 if (xx < 0 || xx >= W) continue;
-                const uint4 raw = *reinterpret_cast<const uint4 *>(in + ((long long)yy * W + xx) * C + c0);
-                const __half *hv = reinterpret_cast<const __half *>(&raw);
-                const float4 w0 = *reinterpret_cast<const float4 *>(ws + (ky * 3 + kx) * C + c0);
-                const float4 w1 = *reinterpret_cast<const float4 *>(ws + (ky * 3 + kx) * C + c0 + 4);
-                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                const uint4 raw = *reinterpret_cast<const uint4 *>(rowp + (size_t)xx * C);
+                if (j < 3) dw_acc8(acc[0], raw, ws + (ky * 3 + j) * C + c0);
+                if (j > 0) dw_acc8(acc[1], raw, ws + (ky * 3 + j - 1) * C + c0);
+            }
+        }
+        const int ga = shift_group(s, c0), gb = shift_group(s, c0 + 7);
+        const int offa = ga >= 0 ? s.offs[ga] : 0, offb = gb >= 0 ? s.offs[gb] : 0;
+        const int split = ga == gb ? 8 : s.ends[ga] - c0;   // channels [0, split) shift by offa, the rest offb
 #pragma unroll
-                for (int k = 0; k < 8; k++)
-                    if ((k < split) == (part == 0)) acc[k] = fmaf(wv[k], __half2float(hv[k]), acc[k]);
+        for (int px = 0; px < 2; px++) {
+            if (x + px >= W) break;
+            __align__(16) __half o[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) o[k] = __float2half_rn(gelu_exact(acc[px][k]));
+            bool za, zb;
+            const int da = shift_dest(x + px, offa, W, &za);
+            __half *rowo = out + (size_t)y * W * C + c0;
+            if (split == 8) {
+                if (za) *reinterpret_cast<uint4 *>(rowo + (size_t)da * C) = make_uint4(0, 0, 0, 0);
+                else *reinterpret_cast<uint4 *>(rowo + (size_t)da * C) = *reinterpret_cast<const uint4 *>(o);
+            } else {
+                const int db = shift_dest(x + px, offb, W, &zb);
+                const __half zero = __float2half_rn(0.0f);
+                for (int k = 0; k < 8; k++) {
+                    if (k < split) rowo[(size_t)da * C + k] = za ? zero : o[k];
+                    else rowo[(size_t)db * C + k] = zb ? zero : o[k];
+                }
             }
         }
     }
-    __align__(16) __half o[8];
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const int sx = k < split ? xa : xb;
-        o[k] = __float2half_rn((sx < 0 || sx >= W) ? 0.0f : gelu_exact(acc[k]));
-    }
-    *reinterpret_cast<uint4 *>(out + ((long long)y * W + x) * C + c0) = *reinterpret_cast<const uint4 *>(o);
+    pdl_trigger();
 }
 
 __device__ __forceinline__ void bilin_coords(int Y, int n, int &a0, int &a1, float &f) {
@@ -260,45 +292,48 @@ __device__ __forceinline__ void bilin_coords(int Y, int n, int &a0, int &a1, flo
 }
 
 __global__ void up_add_pad_kernel(const UpAddArgs a) {
+    pdl_wait();
     const int C = a.out.C, H = a.out.H, W = a.out.W, chunks = C / 8;
-    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (long long)H * W * chunks) return;
-    const int ch = (int)(idx % chunks);
-    const long long p = idx / chunks;
-    const int Y = (int)(p / W), X = (int)(p - (long long)Y * W);
-    const int h = H / 2, w = W / 2, c0 = ch * 8;
-    int ya, yb, xa, xb;
-    float dy, dx;
-    bilin_coords(Y, h, ya, yb, dy);
-    bilin_coords(X, w, xa, xb, dx);
-    const uint4 r00 = *reinterpret_cast<const uint4 *>(a.d + ((long long)ya * w + xa) * C + c0);
-    const uint4 r01 = *reinterpret_cast<const uint4 *>(a.d + ((long long)ya * w + xb) * C + c0);
-    const uint4 r10 = *reinterpret_cast<const uint4 *>(a.d + ((long long)yb * w + xa) * C + c0);
-    const uint4 r11 = *reinterpret_cast<const uint4 *>(a.d + ((long long)yb * w + xb) * C + c0);
-    const uint4 rs = *reinterpret_cast<const uint4 *>(act_ptr(a.skip, Y, X) + c0);
-    const __half *h00 = reinterpret_cast<const __half *>(&r00), *h01 = reinterpret_cast<const __half *>(&r01);
-    const __half *h10 = reinterpret_cast<const __half *>(&r10), *h11 = reinterpret_cast<const __half *>(&r11);
-    const __half *hs = reinterpret_cast<const __half *>(&rs);
-    __align__(16) __half o[8];
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const int Y = blockIdx.y;
+    if (t < W * chunks) {
+        const int X = t / chunks, ch = t - X * chunks;
+        const int h = H / 2, w = W / 2, c0 = ch * 8;
+        int ya, yb, xa, xb;
+        float dy, dx;
+        bilin_coords(Y, h, ya, yb, dy);
+        bilin_coords(X, w, xa, xb, dx);
+        const uint4 r00 = *reinterpret_cast<const uint4 *>(a.d + ((size_t)ya * w + xa) * C + c0);
+        const uint4 r01 = *reinterpret_cast<const uint4 *>(a.d + ((size_t)ya * w + xb) * C + c0);
+        const uint4 r10 = *reinterpret_cast<const uint4 *>(a.d + ((size_t)yb * w + xa) * C + c0);
+        const uint4 r11 = *reinterpret_cast<const uint4 *>(a.d + ((size_t)yb * w + xb) * C + c0);
+        const uint4 rs = *reinterpret_cast<const uint4 *>(act_ptr(a.skip, Y, X) + c0);
+        const __half2 *h00 = reinterpret_cast<const __half2 *>(&r00), *h01 = reinterpret_cast<const __half2 *>(&r01);
+        const __half2 *h10 = reinterpret_cast<const __half2 *>(&r10), *h11 = reinterpret_cast<const __half2 *>(&r11);
+        const __half2 *hs = reinterpret_cast<const __half2 *>(&rs);
+        __align__(16) __half2 o[4];
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const float v00 = __half2float(h00[k]), v01 = __half2float(h01[k]);
-        const float v10 = __half2float(h10[k]), v11 = __half2float(h11[k]);
-        const float top = v00 + (v01 - v00) * dx, bot = v10 + (v11 - v10) * dx;
-        const float up = top + (bot - top) * dy;
-        o[k] = __float2half_rn(fmaxf(up, 0.0f) + __half2float(hs[k]));
+        for (int k = 0; k < 4; k++) {
+            const float2 v00 = __half22float2(h00[k]), v01 = __half22float2(h01[k]);
+            const float2 v10 = __half22float2(h10[k]), v11 = __half22float2(h11[k]), sk = __half22float2(hs[k]);
+            const float t0 = v00.x + (v01.x - v00.x) * dx, b0 = v10.x + (v11.x - v10.x) * dx;
+            const float t1 = v00.y + (v01.y - v00.y) * dx, b1 = v10.y + (v11.y - v10.y) * dx;
+            o[k] = __floats2half2_rn(fmaxf(t0 + (b0 - t0) * dy, 0.0f) + sk.x, fmaxf(t1 + (b1 - t1) * dy, 0.0f) + sk.y);
+        }
+        act_store(a.out, Y, X, c0, reinterpret_cast<const __half *>(o), 8);
     }
-    act_store(a.out, Y, X, c0, o, 8);
+    pdl_trigger();
 }
 
 // One warp per output pixel: out = relu(up(d)) + skip as tokens, then
 // LN2(out) scattered with the H shift.  Lanes own channel pairs.
 __global__ void up_add_tok_kernel(const UpAddArgs a) {
+    pdl_wait();
     const int C = a.out.C, H = a.out.H, W = a.out.W;
-    const long long p = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    if (p >= (long long)H * W) return;
-    const int Y = (int)(p / W), X = (int)(p - (long long)Y * W);
+    if (p >= H * W) return;
+    const int Y = p / W, X = p - Y * W;
     const int h = H / 2, w = W / 2;
     int ya, yb, xa, xb;
     float dy, dx;
@@ -306,8 +341,8 @@ __global__ void up_add_tok_kernel(const UpAddArgs a) {
     bilin_coords(X, w, xa, xb, dx);
     const __half *s = act_ptr(a.skip, Y, X);
     __half *o = a.out.p + a.out.row(Y, X) * C;
-    const __half *d00 = a.d + ((long long)ya * w + xa) * C, *d01 = a.d + ((long long)ya * w + xb) * C;
-    const __half *d10 = a.d + ((long long)yb * w + xa) * C, *d11 = a.d + ((long long)yb * w + xb) * C;
+    const __half *d00 = a.d + ((size_t)ya * w + xa) * C, *d01 = a.d + ((size_t)ya * w + xb) * C;
+    const __half *d10 = a.d + ((size_t)yb * w + xa) * C, *d11 = a.d + ((size_t)yb * w + xb) * C;
     const int pairs = C / 2;   // C even, at most 512
     float v[16];
     float sum = 0.f;
@@ -353,37 +388,57 @@ __global__ void up_add_tok_kernel(const UpAddArgs a) {
         float t[2] = {(v[2 * j] - mean) * rstd * a.g[c] + a.b[c], (v[2 * j + 1] - mean) * rstd * a.g[c + 1] + a.b[c + 1]};
         shift_store(a.h, a.shift, 2, Y, X, c, t, 2);
     }
+    pdl_trigger();
 }
 
-// One warp per token; lanes own channel pairs (N even, N <= 512).
+// One warp per token; lanes own channel pairs (N even, N <= 512).  The k-split
+// partials are summed in order (k ascending); all pairs of one k are loaded together.
 __global__ void ln_finalize_kernel(const LnFinalizeArgs a) {
-    const long long t = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    pdl_wait();
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    const long long T = (long long)a.H * a.W;
+    const int T = a.H * a.W;
     if (t >= T) return;
-    const int y = (int)(t / a.W), x = (int)(t - (long long)y * a.W);
+    const int y = t / a.W, x = t - y * a.W;
     const int N = a.N, pairs = N / 2;
     float v[16];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int c = 2 * (lane + 32 * j);
+        if (c < N) {
+            const float2 bb = *reinterpret_cast<const float2 *>(a.bias + c);
+            v[2 * j] = bb.x;
+            v[2 * j + 1] = bb.y;
+        }
+    }
+    for (int k = 0; k < a.ksplit; k++) {
+        const float *pk = a.partial + ((size_t)k * T + t) * N;
+        float2 pv[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int c = 2 * (lane + 32 * j);
+            if (c < N) pv[j] = *reinterpret_cast<const float2 *>(pk + c);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (2 * (lane + 32 * j) < N) {
+                v[2 * j] += pv[j].x;
+                v[2 * j + 1] += pv[j].y;
+            }
+        }
+    }
     float sum = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
         const int pi = lane + 32 * j;
         if (pi >= pairs) break;
         const int c = 2 * pi;
-        float2 acc = make_float2(a.bias[c], a.bias[c + 1]);
-        for (int k = 0; k < a.ksplit; k++) {
-            const float2 p = *reinterpret_cast<const float2 *>(a.partial + ((long long)k * T + t) * N + c);
-            acc.x += p.x;
-            acc.y += p.y;
-        }
         if (a.res) {
-            const float2 r = __half22float2(*reinterpret_cast<const __half2 *>(a.res + t * N + c));
-            acc.x += r.x;
-            acc.y += r.y;
+            const float2 r = __half22float2(*reinterpret_cast<const __half2 *>(a.res + (size_t)t * N + c));
+            v[2 * j] += r.x;
+            v[2 * j + 1] += r.y;
         }
-        v[2 * j] = acc.x;
-        v[2 * j + 1] = acc.y;
-        sum += acc.x + acc.y;
+        sum += v[2 * j] + v[2 * j + 1];
     }
     for (int m = 16; m; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
     const float mean = sum / N;
@@ -430,6 +485,7 @@ __global__ void ln_finalize_kernel(const LnFinalizeArgs a) {
         float o[2] = {(v[2 * j] - mean2) * rstd2 * a.g2[c] + a.b2[c], (v[2 * j + 1] - mean2) * rstd2 * a.g2[c + 1] + a.b2[c + 1]};
         shift_store(a.out2, a.shift, 2, y, x, c, o, 2);
     }
+    pdl_trigger();
 }
 
 __global__ void bgr2nhwc_kernel(const ImgSpec im, float *x, int H, int W) {
@@ -477,6 +533,7 @@ __global__ void nhwc2bgr_kernel(const float *y, int W, int ph, int pw, uint8_t *
 }
 
 __global__ void stem_in_kernel(const ImgSpec im, Act si) {
+    pdl_wait();
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)si.H * si.W) return;
     const int y = (int)(idx / si.W), x = (int)(idx - (long long)y * si.W);
@@ -487,6 +544,7 @@ __global__ void stem_in_kernel(const ImgSpec im, Act si) {
     const __half z = __ushort2half_rn(0);
     __align__(16) __half v[16] = {b, g, r, b, g, r, z, z, z, z, z, z, z, z, z, z};
     act_store(si, y, x, 0, v, 16);
+    pdl_trigger();
 }
 
 inline int grid_for(long long n, int bs) { return (int)((n + bs - 1) / bs); }
@@ -502,9 +560,18 @@ inline int launch_status() {
 
 const char *last_launch_error() { return cudaGetErrorString(t_last_launch); }
 
+}  // namespace gcdr
+#include <cstdlib>
+namespace gcdr {
+bool pdl_enabled() {
+    static const bool on = [] { const char *v = std::getenv("GCDR_CUDA_PDL"); return !(v && v[0] == '0'); }();
+    return on;
+}
+
 int stem_in_launch(const ImgSpec &im, const Act &si, cudaStream_t st) {
     if (si.C != 16 || si.kind != LAY_PADREFL) return -2;
-    stem_in_kernel<<<grid_for((long long)si.H * si.W, 256), 256, 0, st>>>(im, si);
+    if (launch_pdl(stem_in_kernel, dim3(grid_for((long long)si.H * si.W, 256)), dim3(256), 0, st, im, si) != cudaSuccess)
+        return launch_status();
     return launch_status();
 }
 
@@ -532,10 +599,10 @@ void pack_stem_conv(const float *w, int c1, int cin, __half *out) {
 
 int stem_launch(const StemArgs &a, cudaStream_t st) {
     const long long n = (long long)(a.H / 2) * (a.W / 2);
-    if (a.cin == 3 && a.c1 == 16) stem_kernel<3, 16><<<grid_for(n, 128), 128, 0, st>>>(a);
-    else if (a.cin == 6 && a.c1 == 32) stem_kernel<6, 32><<<grid_for(n, 128), 128, 0, st>>>(a);
-    else if (a.cin == 3 && a.c1 == 32) stem_kernel<3, 32><<<grid_for(n, 128), 128, 0, st>>>(a);
-    else if (a.cin == 6 && a.c1 == 16) stem_kernel<6, 16><<<grid_for(n, 128), 128, 0, st>>>(a);
+    if (a.cin == 3 && a.c1 == 16) launch_pdl(stem_kernel<3, 16>, dim3(grid_for(n, 128)), dim3(128), 0, st, a);
+    else if (a.cin == 6 && a.c1 == 32) launch_pdl(stem_kernel<6, 32>, dim3(grid_for(n, 128)), dim3(128), 0, st, a);
+    else if (a.cin == 3 && a.c1 == 32) launch_pdl(stem_kernel<3, 32>, dim3(grid_for(n, 128)), dim3(128), 0, st, a);
+    else if (a.cin == 6 && a.c1 == 16) launch_pdl(stem_kernel<6, 16>, dim3(grid_for(n, 128)), dim3(128), 0, st, a);
     else return -2;
     return launch_status();
 }
@@ -544,22 +611,22 @@ int head_launch(const HeadArgs &a, cudaStream_t st) {
     const long long n = a.is_dr ? (long long)a.img.w * a.img.h : (long long)a.H * a.W;
     const int g = grid_for(n, 128);
     if (!a.is_dr) {
-        if (a.cin == 3 && a.c1 == 16) head_kernel<3, 16, false><<<g, 128, 0, st>>>(a);
-        else if (a.cin == 3 && a.c1 == 32) head_kernel<3, 32, false><<<g, 128, 0, st>>>(a);
+        if (a.cin == 3 && a.c1 == 16) launch_pdl(head_kernel<3, 16, false>, dim3(g), dim3(128), 0, st, a);
+        else if (a.cin == 3 && a.c1 == 32) launch_pdl(head_kernel<3, 32, false>, dim3(g), dim3(128), 0, st, a);
         else return -2;
     } else {
-        if (a.cin == 6 && a.c1 == 32) head_kernel<6, 32, true><<<g, 128, 0, st>>>(a);
-        else if (a.cin == 6 && a.c1 == 16) head_kernel<6, 16, true><<<g, 128, 0, st>>>(a);
+        if (a.cin == 6 && a.c1 == 32) launch_pdl(head_kernel<6, 32, true>, dim3(g), dim3(128), 0, st, a);
+        else if (a.cin == 6 && a.c1 == 16) launch_pdl(head_kernel<6, 16, true>, dim3(g), dim3(128), 0, st, a);
         else return -2;
     }
     return launch_status();
 }
 
-int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *w, const float *b, const ShiftSpec &s,
+int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *wt, const float *b, const ShiftSpec &s,
                          __half *out, cudaStream_t st) {
     if (C % 8 || C > kDwMaxC) return -2;
-    const long long n = (long long)H * W * (C / 8);
-    dw_gelu_shift_kernel<<<grid_for(n, 256), 256, 0, st>>>(in, H, W, C, w, b, s, out);
+    launch_pdl(dw_gelu_shift_kernel, dim3(grid_for((long long)((W + 1) / 2) * (C / 8), 256), H), dim3(256), 0, st, in, H,
+               W, C, wt, b, s, out);
     return launch_status();
 }
 
@@ -567,12 +634,11 @@ int up_add_launch(const UpAddArgs &a, cudaStream_t st) {
     const int C = a.out.C;
     if (!a.tokens) {
         if (C % 8) return -2;
-        const long long n = (long long)a.out.H * a.out.W * (C / 8);
-        up_add_pad_kernel<<<grid_for(n, 256), 256, 0, st>>>(a);
+        launch_pdl(up_add_pad_kernel, dim3(grid_for((long long)a.out.W * (C / 8), 256), a.out.H), dim3(256), 0, st, a);
     } else {
         if (C % 2 || C > 512) return -2;
         const long long n = (long long)a.out.H * a.out.W * 32;
-        up_add_tok_kernel<<<grid_for(n, 256), 256, 0, st>>>(a);
+        launch_pdl(up_add_tok_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
     }
     return launch_status();
 }
@@ -580,7 +646,7 @@ int up_add_launch(const UpAddArgs &a, cudaStream_t st) {
 int ln_finalize_launch(const LnFinalizeArgs &a, cudaStream_t st) {
     if (a.N % 2 || a.N > 512 || a.ksplit < 1) return -2;
     const long long n = (long long)a.H * a.W * 32;
-    ln_finalize_kernel<<<grid_for(n, 256), 256, 0, st>>>(a);
+    launch_pdl(ln_finalize_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
     return launch_status();
 }
 

@@ -58,8 +58,9 @@ const char *last_launch_error();
 void pack_stem_conv(const float *w, int c1, int cin, __half *out);
 
 // Depthwise 3x3 (zero pad 1) + bias -> exact GELU -> W-shift scatter
-// (gc#85-95 with ChannelShift along W).  w is [C][9] (ONNX [C][1][3][3]).
-int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *w, const float *b, const ShiftSpec &s,
+// (gc#85-95 with ChannelShift along W).  wt is tap-major [9][C] fp32 (ONNX
+// [C][1][3][3] transposed at upload), b [C]; both 16-byte aligned.
+int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *wt, const float *b, const ShiftSpec &s,
                          __half *out, cudaStream_t st);
 
 // Decoder join: out = relu(bilinear2x(d)) + skip  (gc#236-240, 444-446).

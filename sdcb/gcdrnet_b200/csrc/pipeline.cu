@@ -97,7 +97,14 @@ void pack_net(Packer &pk, const NetW &n, DevNet &d) {
         o.C = b.norm2.c;
         pk.h16(pack_fc(b.fc1_w, o.C), &o.fc1); pk.f32(b.fc1_b, &o.fc1_b);
         pk.h16(pack_fc(b.fc2_w, o.C), &o.fc2); pk.f32(b.fc2_b, &o.fc2_b);
-        pk.f32(b.dw.w, &o.dw_w); pk.f32(b.dw.b, &o.dw_b);
+        {
+            // depthwise weights tap-major [9][C] (ONNX [C][1][3][3])
+            std::vector<float> wt((size_t)9 * o.C);
+            for (int c = 0; c < o.C; c++)
+                for (int tap = 0; tap < 9; tap++) wt[(size_t)tap * o.C + c] = b.dw.w[(size_t)c * 9 + tap];
+            pk.f32(wt, &o.dw_w);
+        }
+        pk.f32(b.dw.b, &o.dw_b);
         pk.f32(b.norm2.g, &o.n2_g); pk.f32(b.norm2.b, &o.n2_b); o.n2_eps = b.norm2.eps;
         pk.f32(b.norm_out.g, &o.no_g); pk.f32(b.norm_out.b, &o.no_b); o.no_eps = b.norm_out.eps;
         o.sa = shift_spec(b.shift_a);

@@ -24,7 +24,7 @@ namespace gcdr {
 struct DevBlock {
     const __half *fc1 = nullptr, *fc2 = nullptr;   // [N][K] (Gemm B transposed)
     const float *fc1_b = nullptr, *fc2_b = nullptr;
-    const float *dw_w = nullptr, *dw_b = nullptr;   // [C][9]
+    const float *dw_w = nullptr, *dw_b = nullptr;   // [9][C] tap-major, [C]
     const float *n2_g = nullptr, *n2_b = nullptr, *no_g = nullptr, *no_b = nullptr;
     float n2_eps = 1e-5f, no_eps = 1e-5f;
     ShiftSpec sa, sb;
