@@ -267,22 +267,33 @@ __device__ void epilogue_head(const EpiParams &ep, const TileGeom &tg, int y, in
     const int xa = min(max(x0, 0), Wh - 1), xb = min(max(x0 + 1, 0), Wh - 1);
     const __half *p00 = hp.dec5 + ((size_t)ya * Wh + xa) * C1, *p01 = hp.dec5 + ((size_t)ya * Wh + xb) * C1;
     const __half *p10 = hp.dec5 + ((size_t)yb * Wh + xa) * C1, *p11 = hp.dec5 + ((size_t)yb * Wh + xb) * C1;
+    // the x2 bilinear weights (products of 0.25 / 0.75, or 0 / 1 at the clamped edges) are exact
+    // in fp16: the interpolation of the fp16 dec5 runs on channel pairs (HFMA2), the rest in fp32
+    const __half2 w00 = __float2half2_rn((1.0f - dx) * (1.0f - dy)), w01 = __float2half2_rn(dx * (1.0f - dy));
+    const __half2 w10 = __float2half2_rn((1.0f - dx) * dy), w11 = __float2half2_rn(dx * dy);
     float o0 = hp.fb[0], o1 = hp.fb[1], o2 = hp.fb[2];
 #pragma unroll
-    for (int c0 = 0; c0 < C1; c0 += 16) {
-        float q00[16], q01[16], q10[16], q11[16];
-        load16h(p00 + c0, q00);
-        load16h(p01 + c0, q01);
-        load16h(p10 + c0, q10);
-        load16h(p11 + c0, q11);
+    for (int c0 = 0; c0 < C1; c0 += 8) {
+        const uint4 u00 = *reinterpret_cast<const uint4 *>(p00 + c0), u01 = *reinterpret_cast<const uint4 *>(p01 + c0);
+        const uint4 u10 = *reinterpret_cast<const uint4 *>(p10 + c0), u11 = *reinterpret_cast<const uint4 *>(p11 + c0);
+        const __half2 *a00 = reinterpret_cast<const __half2 *>(&u00), *a01 = reinterpret_cast<const __half2 *>(&u01);
+        const __half2 *a10 = reinterpret_cast<const __half2 *>(&u10), *a11 = reinterpret_cast<const __half2 *>(&u11);
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-            const float top = q00[k] + (q01[k] - q00[k]) * dx, bot = q10[k] + (q11[k] - q10[k]) * dx;
-            const float up = fmaxf(top + (bot - top) * dy, 0.0f);
-            const float sv = up + fmaxf(c1[c0 + k] + hp.b1[c0 + k], 0.0f);
-            o0 = fmaf(sv, hp.fw[c0 + k], o0);
-            o1 = fmaf(sv, hp.fw[C1 + c0 + k], o1);
-            o2 = fmaf(sv, hp.fw[2 * C1 + c0 + k], o2);
+        for (int k2 = 0; k2 < 4; k2++) {
+            __half2 up = __hmul2(a00[k2], w00);
+            up = __hfma2(a01[k2], w01, up);
+            up = __hfma2(a10[k2], w10, up);
+            up = __hfma2(a11[k2], w11, up);
+            const float2 uf = __half22float2(up);
+            const int c = c0 + 2 * k2;
+            const float s0 = fmaxf(uf.x, 0.0f) + fmaxf(c1[c] + hp.b1[c], 0.0f);
+            const float s1 = fmaxf(uf.y, 0.0f) + fmaxf(c1[c + 1] + hp.b1[c + 1], 0.0f);
+            o0 = fmaf(s0, hp.fw[c], o0);
+            o1 = fmaf(s0, hp.fw[C1 + c], o1);
+            o2 = fmaf(s0, hp.fw[2 * C1 + c], o2);
+            o0 = fmaf(s1, hp.fw[c + 1], o0);
+            o1 = fmaf(s1, hp.fw[C1 + c + 1], o1);
+            o2 = fmaf(s1, hp.fw[2 * C1 + c + 1], o2);
         }
     }
     const float o[3] = {1.0f / (1.0f + expf(-o0)), 1.0f / (1.0f + expf(-o1)), 1.0f / (1.0f + expf(-o2))};
