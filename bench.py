@@ -41,6 +41,23 @@ W_IMG, H_IMG = 1600, 1152
 WORKLOAD = "enhance 1600x1152 Bgr24 synthetic documents (config-0 generator), one image per GPU per step"
 
 
+TRAFFIC_TABLE = os.path.join(ROOT, "profiles", "ncu_traffic_1600x1152.md")
+
+
+def ncu_traffic(op: str):
+    """DRAM bytes (read + write) of one launch of `op` from the committed ncu summary
+    (a table row `| op | kernel | read MB | write MB | ... |`), or None."""
+    try:
+        with open(TRAFFIC_TABLE) as fh:
+            for line in fh:
+                cells = [c.strip() for c in line.strip().strip("|").split("|")]
+                if len(cells) >= 4 and cells[0] == op:
+                    return (float(cells[2]) + float(cells[3])) * 1e6
+    except (OSError, ValueError):
+        return None
+    return None
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -310,7 +327,8 @@ def main():
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": nbytes,
                     "d2h_bytes_per_step": nbytes, "api": "GcdrEnhancer.enhance (host numpy buffers)"},
             "roofline": {"kernel": name, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                         "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                         "frac": achieved / peak, "traffic": ncu_traffic(name),
+                         "traffic_source": os.path.relpath(TRAFFIC_TABLE, ROOT), "peak_source": peak_src,
                          "algorithmic_bytes": kbytes, "algorithmic_flops": kflops, "launch_ms": kms},
             "tensor_core": {"ms": tc_ms, "tflops": tc_flops / (tc_ms * 1e-3) / 1e12 if tc_ms else None,
                             "frac_of_peak": (tc_flops / (tc_ms * 1e-3) / 1e12) / tflops if tc_ms else None,

@@ -406,6 +406,7 @@ int conv_args_from_desc(const gcdr_conv_desc *d, ConvArgs &a, int &mode, std::st
     a.ksplit = d->ksplit > 0 ? d->ksplit : 1;
     if (mode == EPI_PARTIAL) a.ep.partial = static_cast<float *>(d->out);
     else if (a.ksplit != 1) { err = "k splits need the partial-sum epilogue"; return -1; }
+    if (fill_bias_consts(a)) { err = "bias copy failed (N <= 512)"; return -1; }
     return 0;
 }
 

@@ -40,6 +40,10 @@ struct RwConfig {
     int acc_cols = 32, acc_bufs = 1, tmem_cols = 32;
 };
 
+// Copies the layer's bias (device, N floats) into a.ep.bias_c (synchronous; at op
+// build time, never inside a stream capture).  0, or -1 if N exceeds kMaxBiasConst.
+int fill_bias_consts(ConvArgs &a);
+
 int tc_pick_bk(int C);
 bool tma_encode_2d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint32_t box_inner,
                    uint32_t box_outer, int bk, std::string &err);

@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(kRwThreads, 1)
                 for (int it = part; it < R * nch; it += 2) {
                     const int jj = it / nch, ch = it - jj * nch;
                     TmemLoader ld{acc0 + (uint32_t)(jj * cfg.acc_cols)};
-                    epilogue_plain_yx(args.ep, tg, y0 + jj, x, 0, N, ld, ch, nch, args.ep.bias);
+                    epilogue_plain_yx(args.ep, tg, y0 + jj, x, 0, N, ld, ch, nch, args.ep.bias_c);
                 }
             }
             tc_fence_before();

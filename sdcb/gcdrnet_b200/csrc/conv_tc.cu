@@ -334,6 +334,12 @@ int launch_bk(const ConvArgs &a, int mode, const TcConfig &cfg, const CUtensorMa
 
 int tc_pick_bk(int C) { return C % 64 == 0 ? 64 : C % 32 == 0 ? 32 : C % 16 == 0 ? 16 : 0; }
 
+int fill_bias_consts(ConvArgs &a) {
+    if (!a.ep.bias) return 0;
+    if (a.N > kMaxBiasConst) return -1;
+    return cudaMemcpy(a.ep.bias_c, a.ep.bias, (size_t)a.N * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
+}
+
 bool tma_encode_2d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint32_t box_inner,
                    uint32_t box_outer, int bk, std::string &err) {
     return encode_2d(m, base, inner, outer, box_inner, box_outer, bk, err);

@@ -55,8 +55,13 @@ struct HeadParams {
     int is_dr = 0;
 };
 
+constexpr int kMaxBiasConst = 512;
+
 struct EpiParams {
     const float *bias = nullptr;     // [N] (indexed with the slice offset)
+    // the same bias by value (kernel-parameter constant bank): the epilogues read
+    // these, a per-element global load being a full cache round trip per column
+    float bias_c[kMaxBiasConst];
     int relu = 0;                    // EPI_PLAIN: relu after the bias
     Act out;                         // primary output (logical dims = conv or pooled output)
     // LN modes
@@ -104,7 +109,7 @@ __device__ __forceinline__ void row_vals(L &ld, const EpiParams &ep, int N, long
     }
 #pragma unroll
     for (int k = 0; k < 32; k++)
-        if (k < w) v[k] += ep.bias[c0 + k] + (use_res ? r[k] : 0.0f);
+        if (k < w) v[k] += ep.bias_c[c0 + k] + (use_res ? r[k] : 0.0f);
 }
 
 // PLAIN epilogue of output pixel (y, x): bias [+ relu] -> fp16 store of the
@@ -143,7 +148,7 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     const bool valid = y < tg.conv_h && x < tg.conv_w;
     const long long tok = valid ? (long long)y * tg.conv_w + x : 0;
     if (MODE == EPI_PLAIN) {
-        epilogue_plain_yx(ep, tg, y, x, n0, Nsub, ld, part, nparts, ep.bias);
+        epilogue_plain_yx(ep, tg, y, x, n0, Nsub, ld, part, nparts, ep.bias_c);
         return;
     }
     if (MODE == EPI_PARTIAL) {
@@ -241,7 +246,7 @@ __device__ void epilogue_pool(const EpiParams &ep, const TileGeom &tg, int y2, i
         for (int k = 0; k < 32; k++) {
             if (k < cw) {
                 float v = fmaxf(a[k], b[k]);
-                v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1)) + ep.bias[n0 + c0 + k];
+                v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1)) + ep.bias_c[n0 + c0 + k];
                 h[k] = __float2half_rn(fmaxf(v, 0.0f));
             }
         }

@@ -397,6 +397,7 @@ int Worker::plan_arena() {
 }
 
 int Worker::build_ops() {
+    bias_fail_ = false;
     ops_.clear();
     launches_ = 0;
     const DevWeights &wt = *weights_;
@@ -405,6 +406,7 @@ int Worker::build_ops() {
     auto conv_op = [this, nsm, errp](ConvArgs a, int mode, const std::string &name, double flops_override = -1,
                                       double bytes_override = -1) {
         a.err = errp;
+        if (fill_bias_consts(a)) bias_fail_ = true;
         const bool partial = uses_partial(a, mode, nsm);
         int run_mode = mode;
         if (mode == EPI_PLAIN || partial) {
@@ -628,6 +630,7 @@ int Worker::build_ops() {
             conv_op(a, EPI_HEAD, pre + "head", head_flops, head_bytes);
         }
     }
+    if (bias_fail_) return fail(GCDR_ERR_DEVICE, "conv bias copy failed");
     return info_.size() == ops_.size() ? GCDR_OK : fail(GCDR_ERR_DEVICE, "op metadata mismatch");
 }
 

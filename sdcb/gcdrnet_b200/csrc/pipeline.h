@@ -122,6 +122,7 @@ private:
     cudaGraph_t graph_ = nullptr;
     cudaGraphExec_t exec_ = nullptr;
     int launches_ = 0;
+    bool bias_fail_ = false;
     std::string err_;
 };
 
