@@ -68,18 +68,45 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled during the timed region:
+    NVML polled every ~2 ms from a thread (the timed region can be a few tens of
+    ms), with nvidia-smi at 200 ms as the fallback.  Reads only."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, uuid: str | None = None):
         self.index = index
+        self.uuid = uuid
         self.proc = None
         self.lines = []
+        self.sm, self.mx, self.reasons = [], None, set()
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
 
     def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = None
+            if self.uuid:
+                try:
+                    h = pynvml.nvmlDeviceGetHandleByUUID(self.uuid)
+                except pynvml.NVMLError:
+                    h = None
+            if h is None:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self._nvml = (pynvml, h)
+            self.mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self._thread = threading.Thread(target=self._poll_nvml, daemon=True)
+            self._thread.start()
+            return self
+        except Exception:
+            self._nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-lms", "200", "-i", str(self.index)],
@@ -89,11 +116,27 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _poll_nvml(self):
+        pynvml, h = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.sm.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                mask = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for n, bit in self.REASONS:
+                    if mask & bit:
+                        self.reasons.add(n)
+            except Exception:
+                return
+            time.sleep(0.002)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=2)
         if self.proc:
             self.proc.terminate()
             try:
@@ -102,7 +145,7 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons = list(self.sm), self.mx, set(self.reasons)
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
@@ -117,7 +160,7 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvml" if self._nvml else "nvidia-smi"}
 
 
 def physical_index(local: int) -> int:
@@ -149,12 +192,20 @@ def whole_job_rate(world: int, steps: int, seconds: float) -> float:
     return world * steps / seconds
 
 
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def cpu_baseline_oracle(w: int, h: int, seconds: float = 30.0):
     """Times the CPU oracle's full enhancement on one image (all host threads)."""
     import numpy as np
     from oracle import gcdr_oracle as O
     from sdcb.gcdrnet_b200 import synth
     O.build()
+    O.set_threads(host_threads())
     orc = O.Oracle(GC, DR)
     img = synth.document(w, h, seed=0)
     dst = np.empty_like(img)
@@ -177,6 +228,7 @@ def run_reference(args):
     from oracle import gcdr_oracle as O
     from sdcb.gcdrnet_b200 import synth
     O.build()
+    O.set_threads(host_threads())      # torchrun exports OMP_NUM_THREADS=1; the baseline uses every core
     orc = O.Oracle(GC, DR)
     imgs = [synth.document(W_IMG, H_IMG, seed=s) for s in range(2)]
     dst = np.empty_like(imgs[0])
@@ -259,7 +311,11 @@ def main():
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize(dev)
-    with ClockSampler(physical_index(local)) as clk:
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        uuid = None
+    with ClockSampler(physical_index(local), uuid) as clk:
         for i in range(args.steps):
             flush.zero_()
             ev[i][0].record(stream)
