@@ -4,6 +4,13 @@
   run [--width W --height H --iters N]  device-resident throughput of one worker
   prof [--width W --height H]           per-op profile (the GCDRNET_PROF analogue,
                                         bench/Sdcb.SimdGcdrNet.Benchmark/Program.cs:993-1010)
+  microbench [--iters N]                isolated 3x3 conv + bias + relu layers of the GC/DR
+                                        pyramid at 1600x1152 through the layer entry gcdr_k_conv
+  batch [--count N]                     64 (N) Bgra32 1600x1152 documents enhanced in place with
+                                        row stride width*4+64 through GcdrEnhancer (host buffers)
+  stress [--count N] [--check]          odd-size Rgba32 documents (w 2000-4096, h 1500-3072,
+                                        seed 7): first pass (plan + graph capture per shape) and
+                                        a second pass; --check compares two with the CPU oracle
 Models default to the copies under tests/golden/models.
 """
 from __future__ import annotations
@@ -81,10 +88,151 @@ def cmd_prof(a):
     wk.close()
 
 
+def _peaks():
+    import json
+    p = os.path.join(_ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as fh:
+            d = json.load(fh)
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0)
+    except OSError:
+        return 6650.0, 1590.0
+
+
+# (label, kind, H, W, Cin, N): kind 3 = 3x3 zero-pad stride 1, kind 2 = 1x1.  Channel
+# counts below 16 are zero-padded to 16 for the tensor cores; FLOPs and bytes count the
+# real channels.
+_MICRO = [
+    ("6->32 3x3 @1152x1600", 3, 1152, 1600, 6, 32),
+    ("32->64 3x3 @576x800", 3, 576, 800, 32, 64),
+    ("64->128 3x3 @288x400", 3, 288, 400, 64, 128),
+    ("128->256 3x3 @144x200", 3, 144, 200, 128, 256),
+    ("256->256 3x3 @72x100", 3, 72, 100, 256, 256),
+    ("1x1 256->3 @1152x1600", 2, 1152, 1600, 256, 3),
+]
+
+
+def cmd_microbench(a):
+    import ctypes
+    import torch
+    from . import lib
+    L = lib()
+
+    class Desc(ctypes.Structure):
+        _fields_ = [("kind", ctypes.c_int), ("H", ctypes.c_int), ("W", ctypes.c_int), ("C", ctypes.c_int),
+                    ("N", ctypes.c_int), ("inp", ctypes.c_void_p), ("weight", ctypes.c_void_p),
+                    ("bias", ctypes.c_void_p), ("epilogue", ctypes.c_int), ("out", ctypes.c_void_p),
+                    ("scratch", ctypes.c_void_p), ("nsplit", ctypes.c_int), ("ksplit", ctypes.c_int)]
+
+    torch.cuda.set_device(a.device)
+    dev = torch.device("cuda", a.device)
+    hbm, tf = _peaks()
+    g = torch.Generator(device="cpu").manual_seed(1)
+    st = torch.cuda.Stream(dev)
+    print(f"{'layer':24s} {'us':>8s} {'TFLOP/s':>8s} {'%bf16':>6s} {'GB/s':>8s} {'%HBM':>6s}")
+    for label, kind, H, W, cin, n in _MICRO:
+        C, N = max(16, (cin + 15) // 16 * 16), max(16, (n + 15) // 16 * 16)
+        taps = 9 if kind == 3 else 1
+        x = torch.zeros(H, W, C, dtype=torch.float16)
+        x[:, :, :cin] = torch.randn(H, W, cin, generator=g)
+        w = torch.zeros(N, taps, C)
+        w[:n, :, :cin] = torch.randn(n, taps, cin, generator=g) * (2.0 / (cin * taps)) ** 0.5   # Kaiming normal
+        xt = x.to(dev)
+        wt = w.reshape(N, taps * C).to(dev, torch.float16)
+        bt = torch.zeros(N, device=dev)
+        if kind == 2:
+            inp = xt
+        else:
+            cnt = L.gcdr_k_to_layout(None, H, W, C, 3, None, None)
+            inp = torch.empty(cnt, dtype=torch.float16, device=dev)
+            L.gcdr_k_to_layout(xt.data_ptr(), H, W, C, 3, inp.data_ptr(), None)
+        out = torch.empty(H * W * N, dtype=torch.float16, device=dev)
+        d = Desc(kind, H, W, C, N, inp.data_ptr(), wt.data_ptr(), bt.data_ptr(), 2, out.data_ptr(), None, 1, 1)
+        for _ in range(3):
+            assert L.gcdr_k_conv(ctypes.byref(d), 0, ctypes.c_void_p(st.cuda_stream)) == 0
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(a.iters):
+            L.gcdr_k_conv(ctypes.byref(d), 0, ctypes.c_void_p(st.cuda_stream))
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1000 / a.iters
+        flops = 2.0 * H * W * n * taps * cin
+        byts = 2.0 * H * W * (cin + n) + 2.0 * n * taps * cin
+        tfs, gbs = flops / (us * 1e-6) / 1e12, byts / (us * 1e-6) / 1e9
+        print(f"{label:24s} {us:8.1f} {tfs:8.1f} {100 * tfs / tf:5.1f}% {gbs:8.1f} {100 * gbs / hbm:5.1f}%")
+
+
+def cmd_batch(a):
+    import numpy as np
+    from . import GcdrEnhancer, GcdrPixelFormat, synth
+    w, h = a.width, a.height
+    stride = w * 4 + 64
+    imgs = []
+    for seed in range(a.count):
+        px = synth.document(w, h, seed=seed, fmt=int(GcdrPixelFormat.Bgra32))
+        buf = np.zeros(stride * h, np.uint8)
+        buf.reshape(h, stride)[:, :w * 4] = px.reshape(h, w * 4)
+        imgs.append(buf)
+    alphas = [b.reshape(h, stride)[:, 3:w * 4:4].copy() for b in imgs]
+    with GcdrEnhancer.from_files(*_models(a), device=a.device) as enh:
+        warm = imgs[0].copy()
+        enh.enhance(warm, w, h, stride, warm, stride, GcdrPixelFormat.Bgra32)
+        lat = []
+        t0 = time.perf_counter()
+        for b in imgs:
+            t = time.perf_counter()
+            enh.enhance(b, w, h, stride, b, stride, GcdrPixelFormat.Bgra32)
+            lat.append(time.perf_counter() - t)
+        total = time.perf_counter() - t0
+    ok = all(np.array_equal(b.reshape(h, stride)[:, 3:w * 4:4], al) for b, al in zip(imgs, alphas))
+    lat.sort()
+    print(f"{a.count} x {w}x{h} Bgra32 in place, stride {stride}: {a.count / total:.1f} images/s, "
+          f"e2e median {1000 * lat[len(lat) // 2]:.2f} ms, max {1000 * lat[-1]:.2f} ms, alpha bit-exact: {ok}")
+
+
+def cmd_stress(a):
+    import numpy as np
+    from . import GcdrEnhancer, GcdrPixelFormat, synth
+    rng = np.random.default_rng(7)
+    shapes = [(int(rng.integers(2000, 4097)), int(rng.integers(1500, 3073))) for _ in range(a.count)]
+    fmt = int(GcdrPixelFormat.Rgba32)
+    imgs = [synth.document(w, h, seed=100 + i, fmt=fmt, strokes=int(200 * w * h / (1600 * 1152)))
+            for i, (w, h) in enumerate(shapes)]
+    with GcdrEnhancer.from_files(*_models(a), device=a.device) as enh:
+        outs = []
+        for rep in range(2):
+            lat = []
+            t0 = time.perf_counter()
+            for (w, h), im in zip(shapes, imgs):
+                dst = np.empty_like(im)
+                t = time.perf_counter()
+                enh.enhance(im, w, h, w * 4, dst, w * 4, fmt)
+                lat.append(time.perf_counter() - t)
+                if rep == 0:
+                    outs.append(dst)
+            total = time.perf_counter() - t0
+            mp = sum(w * h for w, h in shapes) / 1e6
+            print(f"pass {rep + 1}: {len(shapes)} Rgba32 images ({mp:.1f} MP), {len(shapes) / total:.1f} images/s, "
+                  f"{mp / total:.1f} MP/s, per image ms: " + " ".join(f"{1000 * t:.1f}" for t in lat))
+    if a.check:
+        sys.path.insert(0, _ROOT)
+        from oracle import gcdr_oracle as O
+        O.build()
+        orc = O.Oracle(*_models(a))
+        for i in (0, 1):
+            (w, h), im = shapes[i], imgs[i]
+            want = np.empty_like(im)
+            orc.enhance(im, w, h, w * 4, want, w * 4, fmt)
+            d = np.abs(outs[i].astype(np.int32) - want.astype(np.int32))
+            print(f"check {w}x{h}: max |u8 diff| {d.max()}, within 2: {(d <= 2).mean():.6f}")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(prog="python -m sdcb.gcdrnet_b200")
     sub = ap.add_subparsers(dest="cmd", required=True)
-    for name in ("enhance", "run", "prof"):
+    for name in ("enhance", "run", "prof", "microbench", "batch", "stress"):
         p = sub.add_parser(name)
         p.add_argument("--gc")
         p.add_argument("--dr")
@@ -92,13 +240,21 @@ def main(argv=None):
         if name == "enhance":
             p.add_argument("input")
             p.add_argument("output")
+        elif name == "microbench":
+            p.add_argument("--iters", type=int, default=20)
+        elif name in ("batch", "stress"):
+            p.add_argument("--count", type=int, default=64 if name == "batch" else 16)
+            p.add_argument("--width", type=int, default=1600)
+            p.add_argument("--height", type=int, default=1152)
+            p.add_argument("--check", action="store_true")
         else:
             p.add_argument("--width", type=int, default=1600)
             p.add_argument("--height", type=int, default=1152)
             p.add_argument("--format", type=int, default=0)
             p.add_argument("--iters", type=int, default=10)
     a = ap.parse_args(argv)
-    {"enhance": cmd_enhance, "run": cmd_run, "prof": cmd_prof}[a.cmd](a)
+    {"enhance": cmd_enhance, "run": cmd_run, "prof": cmd_prof, "microbench": cmd_microbench, "batch": cmd_batch,
+     "stress": cmd_stress}[a.cmd](a)
     return 0
 
 
