@@ -94,30 +94,42 @@ struct Act {
 __host__ __device__ inline int refl_lo(int n) { return n > 1 ? 1 : 0; }      // source of padded index 0
 __host__ __device__ inline int refl_hi(int n) { return n > 1 ? n - 2 : 0; }  // source of padded index n+1
 
+// Calls put(r) for the row r of pixel (y, x) and, for LAY_PADREFL, for each
+// border copy that mirrors it (no arrays: interior pixels return after one put).
+template <class F>
+__device__ __forceinline__ void act_rows(const Act &a, int y, int x, F &&put) {
+    put(a.row(y, x));
+    if (a.kind != LAY_PADREFL) return;
+    const bool ylo = y == refl_lo(a.H), yhi = y == refl_hi(a.H);
+    const bool xlo = x == refl_lo(a.W), xhi = x == refl_hi(a.W);
+    if (!(ylo || yhi || xlo || xhi)) return;
+    const long long P = a.W + 2, top = 0, bot = (long long)(a.H + 1) * P, row = (long long)(y + 1) * P;
+    if (ylo) put(top + x + 1);
+    if (yhi) put(bot + x + 1);
+    if (xlo) put(row);
+    if (xhi) put(row + a.W + 1);
+    if (ylo && xlo) put(top);
+    if (ylo && xhi) put(top + a.W + 1);
+    if (yhi && xlo) put(bot);
+    if (yhi && xhi) put(bot + a.W + 1);
+}
+
 // Stores `n` halves (n multiple of 2, 4-byte aligned) at channel c0 of pixel
 // (y, x), plus the reflect-border copies for LAY_PADREFL.
-__device__ inline void act_store(const Act &a, int y, int x, int c0, const __half *v, int n) {
-    auto put = [&](long long r) {
+__device__ __forceinline__ void act_store(const Act &a, int y, int x, int c0, const __half *v, int n) {
+    act_rows(a, y, x, [&](long long r) {
         __half *d = a.p + r * a.C + c0;
         if ((n & 7) == 0 && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
             for (int k = 0; k < n; k += 8) *reinterpret_cast<uint4 *>(d + k) = *reinterpret_cast<const uint4 *>(v + k);
         } else {
             for (int k = 0; k < n; k += 2) *reinterpret_cast<__half2 *>(d + k) = *reinterpret_cast<const __half2 *>(v + k);
         }
-    };
-    put(a.row(y, x));
-    if (a.kind == LAY_PADREFL) {
-        int ys[2], xs[2], ny = 0, nx = 0;
-        if (y == refl_lo(a.H)) ys[ny++] = 0;
-        if (y == refl_hi(a.H)) ys[ny++] = a.H + 1;
-        if (x == refl_lo(a.W)) xs[nx++] = 0;
-        if (x == refl_hi(a.W)) xs[nx++] = a.W + 1;
-        const int P = a.W + 2;
-        for (int i = 0; i < ny; i++) put((long long)ys[i] * P + (x + 1));
-        for (int j = 0; j < nx; j++) put((long long)(y + 1) * P + xs[j]);
-        for (int i = 0; i < ny; i++)
-            for (int j = 0; j < nx; j++) put((long long)ys[i] * P + xs[j]);
-    }
+    });
+}
+
+// Two channels (c even) by value.
+__device__ __forceinline__ void act_store2(const Act &a, int y, int x, int c, __half2 v) {
+    act_rows(a, y, x, [&](long long r) { *reinterpret_cast<__half2 *>(a.p + r * a.C + c) = v; });
 }
 
 __device__ inline const __half *act_ptr(const Act &a, int y, int x) { return a.p + a.row(y, x) * a.C; }
@@ -131,9 +143,14 @@ struct ShiftSpec {
     int ngroups = 0;
     int ends[5] = {0, 0, 0, 0, 0};
     int offs[5] = {0, 0, 0, 0, 0};
+    // > 0 when group g covers [g*gs, min((g+1)*gs, C)) (ONNX Split into equal
+    // ceil-sized chunks): the group of a channel is one division
+    int gs = 0;
 };
 
+// Group of channel c (-1 past the last group).
 __device__ inline int shift_group(const ShiftSpec &s, int c) {
+    if (s.gs > 0) return c < s.ends[s.ngroups - 1] ? c / s.gs : -1;
     int g = 0;
     while (g < s.ngroups - 1 && c >= s.ends[g]) g++;
     return c < s.ends[s.ngroups - 1] ? g : -1;
@@ -151,34 +168,38 @@ __device__ inline int shift_dest(int s, int off, int L, bool *zero) {
     return d;
 }
 
-// Stores the channels [c0, c0+n) (n even, c0 even) of token pixel (y, x) of a
-// LAY_PLAIN [H][W][C] tensor with the group shift along `axis` (2 = H, 3 = W)
-// applied as a scatter; channel pairs in one group go out as one 4-byte store.
+// Stores channels c, c+1 (c even) of token pixel (y, x) of a LAY_PLAIN [H][W][C]
+// tensor with the group shift along `axis` (2 = H, 3 = W) applied as a scatter;
+// a pair in one group goes out as one 4-byte store.
+__device__ __forceinline__ void shift_store2(const Act &a, const ShiftSpec &s, int axis, int y, int x, int c, float v0,
+                                             float v1) {
+    const int g0 = shift_group(s, c), g1 = shift_group(s, c + 1);
+    int dy = y, dx = x;
+    bool z = false;
+    if (g0 >= 0) {
+        if (axis == 2) dy = shift_dest(y, s.offs[g0], a.H, &z);
+        else dx = shift_dest(x, s.offs[g0], a.W, &z);
+    }
+    __half *d = a.p + ((size_t)dy * a.W + dx) * a.C + c;
+    if (g0 == g1) {
+        *reinterpret_cast<__half2 *>(d) = z ? __float2half2_rn(0.0f) : __floats2half2_rn(v0, v1);
+    } else {
+        d[0] = __float2half_rn(z ? 0.0f : v0);
+        int ey = y, ex = x;
+        bool z1 = false;
+        if (g1 >= 0) {
+            if (axis == 2) ey = shift_dest(y, s.offs[g1], a.H, &z1);
+            else ex = shift_dest(x, s.offs[g1], a.W, &z1);
+        }
+        a.p[((size_t)ey * a.W + ex) * a.C + c + 1] = __float2half_rn(z1 ? 0.0f : v1);
+    }
+}
+
+// Stores the channels [c0, c0+n) (n even, c0 even) of token pixel (y, x) with
+// the group shift (shift_store2 per pair).
 __device__ inline void shift_store(const Act &a, const ShiftSpec &s, int axis, int y, int x, int c0,
                                    const float *v, int n) {
-    for (int k = 0; k < n; k += 2) {
-        const int c = c0 + k;
-        const int g0 = shift_group(s, c), g1 = shift_group(s, c + 1);
-        int dy = y, dx = x;
-        bool z = false;
-        if (g0 >= 0) {
-            if (axis == 2) dy = shift_dest(y, s.offs[g0], a.H, &z);
-            else dx = shift_dest(x, s.offs[g0], a.W, &z);
-        }
-        __half *d = a.p + ((size_t)dy * a.W + dx) * a.C + c;
-        if (g0 == g1) {
-            *reinterpret_cast<__half2 *>(d) = z ? __float2half2_rn(0.0f) : __floats2half2_rn(v[k], v[k + 1]);
-        } else {
-            d[0] = __float2half_rn(z ? 0.0f : v[k]);
-            int ey = y, ex = x;
-            bool z1 = false;
-            if (g1 >= 0) {
-                if (axis == 2) ey = shift_dest(y, s.offs[g1], a.H, &z1);
-                else ex = shift_dest(x, s.offs[g1], a.W, &z1);
-            }
-            a.p[((size_t)ey * a.W + ex) * a.C + c + 1] = __float2half_rn(z1 ? 0.0f : v[k + 1]);
-        }
-    }
+    for (int k = 0; k < n; k += 2) shift_store2(a, s, axis, y, x, c0 + k, v[k], v[k + 1]);
 }
 
 // Loads 16 consecutive halves (16-byte aligned) as floats.

@@ -385,8 +385,8 @@ __global__ void up_add_tok_kernel(const UpAddArgs a) {
         const int pi = lane + 32 * j;
         if (pi >= pairs) break;
         const int c = 2 * pi;
-        float t[2] = {(v[2 * j] - mean) * rstd * a.g[c] + a.b[c], (v[2 * j + 1] - mean) * rstd * a.g[c + 1] + a.b[c + 1]};
-        shift_store(a.h, a.shift, 2, Y, X, c, t, 2);
+        shift_store2(a.h, a.shift, 2, Y, X, c, (v[2 * j] - mean) * rstd * a.g[c] + a.b[c],
+                     (v[2 * j + 1] - mean) * rstd * a.g[c + 1] + a.b[c + 1]);
     }
     pdl_trigger();
 }
@@ -459,8 +459,7 @@ __global__ void ln_finalize_kernel(const LnFinalizeArgs a) {
         const int c = 2 * pi;
         const float y0 = (v[2 * j] - mean) * rstd * a.g1[c] + a.b1[c];
         const float y1 = (v[2 * j + 1] - mean) * rstd * a.g1[c + 1] + a.b1[c + 1];
-        __align__(4) __half h[2] = {__float2half_rn(y0), __float2half_rn(y1)};
-        act_store(a.out, y, x, c, h, 2);
+        act_store2(a.out, y, x, c, __floats2half2_rn(y0, y1));
         v[2 * j] = y0;
         v[2 * j + 1] = y1;
         s2 += y0 + y1;
@@ -482,8 +481,8 @@ __global__ void ln_finalize_kernel(const LnFinalizeArgs a) {
         const int pi = lane + 32 * j;
         if (pi >= pairs) break;
         const int c = 2 * pi;
-        float o[2] = {(v[2 * j] - mean2) * rstd2 * a.g2[c] + a.b2[c], (v[2 * j + 1] - mean2) * rstd2 * a.g2[c + 1] + a.b2[c + 1]};
-        shift_store(a.out2, a.shift, 2, y, x, c, o, 2);
+        shift_store2(a.out2, a.shift, 2, y, x, c, (v[2 * j] - mean2) * rstd2 * a.g2[c] + a.b2[c],
+                     (v[2 * j + 1] - mean2) * rstd2 * a.g2[c + 1] + a.b2[c + 1]);
     }
     pdl_trigger();
 }

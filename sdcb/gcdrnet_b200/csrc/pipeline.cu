@@ -72,6 +72,14 @@ ShiftSpec shift_spec(const ShiftW &s) {
         o.ends[i] = s.ends[i];
         o.offs[i] = s.offs[i];
     }
+    // equal ceil-sized chunks (the last one shorter): channel group = c / gs
+    if (o.ngroups > 0) {
+        const int gs = o.ends[0];
+        bool uniform = gs > 0;
+        for (int i = 0; i < o.ngroups - 1; i++) uniform = uniform && o.ends[i] == (i + 1) * gs;
+        uniform = uniform && o.ends[o.ngroups - 1] > (o.ngroups - 1) * gs && o.ends[o.ngroups - 1] <= o.ngroups * gs;
+        o.gs = uniform ? gs : 0;
+    }
     return o;
 }
 
