@@ -202,6 +202,18 @@ __device__ inline void shift_store(const Act &a, const ShiftSpec &s, int axis, i
     for (int k = 0; k < n; k += 2) shift_store2(a, s, axis, y, x, c0 + k, v[k], v[k + 1]);
 }
 
+// Loads 8 consecutive halves (16-byte aligned) as floats.
+__device__ inline void load16h8(const __half *p, float *v) {
+    const uint4 a = *reinterpret_cast<const uint4 *>(p);
+    const __half2 *ha = reinterpret_cast<const __half2 *>(&a);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float2 f = __half22float2(ha[k]);
+        v[2 * k] = f.x;
+        v[2 * k + 1] = f.y;
+    }
+}
+
 // Loads 16 consecutive halves (16-byte aligned) as floats.
 __device__ inline void load16h(const __half *p, float *v) {
     const uint4 a = *reinterpret_cast<const uint4 *>(p), b = *reinterpret_cast<const uint4 *>(p + 8);

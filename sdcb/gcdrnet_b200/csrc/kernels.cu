@@ -325,164 +325,220 @@ __global__ void up_add_pad_kernel(const UpAddArgs a) {
     pdl_trigger();
 }
 
-// One warp per output pixel: out = relu(up(d)) + skip as tokens, then
-// LN2(out) scattered with the H shift.  Lanes own channel pairs.
-__global__ void up_add_tok_kernel(const UpAddArgs a) {
+// Lane groups for the per-pixel LayerNorm kernels: LP lanes (16 or 32) share a
+// pixel (token), each lane owning NCH chunks of 8 channels (16-byte accesses).
+template <int LP>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int m = LP / 2; m; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+
+__device__ __forceinline__ void load8f(const float *p, float *v) {
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(p)), b = __ldg(reinterpret_cast<const float4 *>(p + 4));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ uint4 pack8h(const float *v) {
+    uint4 u;
+    __half2 *h = reinterpret_cast<__half2 *>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; k++) h[k] = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+    return u;
+}
+
+// H-shift scatter of channels [c0, c0+8) of token pixel (y, x) of a LAY_PLAIN
+// tensor: one 16-byte store when the chunk lies in one channel group.
+__device__ __forceinline__ void shift_store8(const Act &a, const ShiftSpec &s, int y, int x, int c0, const float *v) {
+    const int g0 = shift_group(s, c0), g7 = shift_group(s, c0 + 7);
+    if (g0 == g7) {
+        int dy = y;
+        bool z = false;
+        if (g0 >= 0) dy = shift_dest(y, s.offs[g0], a.H, &z);
+        *reinterpret_cast<uint4 *>(a.p + ((size_t)dy * a.W + x) * a.C + c0) = z ? make_uint4(0, 0, 0, 0) : pack8h(v);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; k++) shift_store2(a, s, 2, y, x, c0 + 2 * k, v[2 * k], v[2 * k + 1]);
+    }
+}
+
+// out = relu(up(d)) + skip as tokens, then LN2(out) scattered with the H shift;
+// LP lanes per output pixel, 8 channels per lane and chunk.
+template <int LP, int NCH>
+__global__ void __launch_bounds__(256) up_add_tok_kernel(const UpAddArgs a) {
     pdl_wait();
-    const int C = a.out.C, H = a.out.H, W = a.out.W;
-    const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (p >= H * W) return;
-    const int Y = p / W, X = p - Y * W;
+    const int C = a.out.C, H = a.out.H, W = a.out.W, nchunk = C >> 3;
+    const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+    const int p = gid / LP, l = gid - p * LP;
+    const bool valid = p < H * W;              // invalid groups still join the shuffles
+    const int pp = valid ? p : 0;
+    const int Y = pp / W, X = pp - Y * W;
     const int h = H / 2, w = W / 2;
     int ya, yb, xa, xb;
     float dy, dx;
     bilin_coords(Y, h, ya, yb, dy);
     bilin_coords(X, w, xa, xb, dx);
-    const __half *s = act_ptr(a.skip, Y, X);
-    __half *o = a.out.p + a.out.row(Y, X) * C;
     const __half *d00 = a.d + ((size_t)ya * w + xa) * C, *d01 = a.d + ((size_t)ya * w + xb) * C;
     const __half *d10 = a.d + ((size_t)yb * w + xa) * C, *d11 = a.d + ((size_t)yb * w + xb) * C;
-    const int pairs = C / 2;   // C even, at most 512
-    float v[16];
+    const __half *sk = act_ptr(a.skip, Y, X);
+    float v[NCH][8];
     float sum = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int pi = lane + 32 * j;
-        if (pi >= pairs) break;
-        const int c = 2 * pi;
-        const float2 a00 = __half22float2(*reinterpret_cast<const __half2 *>(d00 + c));
-        const float2 a01 = __half22float2(*reinterpret_cast<const __half2 *>(d01 + c));
-        const float2 a10 = __half22float2(*reinterpret_cast<const __half2 *>(d10 + c));
-        const float2 a11 = __half22float2(*reinterpret_cast<const __half2 *>(d11 + c));
-        const float2 sk = __half22float2(*reinterpret_cast<const __half2 *>(s + c));
-        float t[2];
-        const float q00[2] = {a00.x, a00.y}, q01[2] = {a01.x, a01.y}, q10[2] = {a10.x, a10.y}, q11[2] = {a11.x, a11.y};
-        const float sq[2] = {sk.x, sk.y};
+    for (int k = 0; k < NCH; k++) {
+        const int ch = l + LP * k;
 #pragma unroll
-        for (int e = 0; e < 2; e++) {
-            const float top = q00[e] + (q01[e] - q00[e]) * dx, bot = q10[e] + (q11[e] - q10[e]) * dx;
-            t[e] = fmaxf(top + (bot - top) * dy, 0.0f) + sq[e];
+        for (int e = 0; e < 8; e++) v[k][e] = 0.f;
+        if (ch < nchunk) {
+            const int c0 = ch * 8;
+            float q00[8], q01[8], q10[8], q11[8], qs[8];
+            load16h8(d00 + c0, q00);
+            load16h8(d01 + c0, q01);
+            load16h8(d10 + c0, q10);
+            load16h8(d11 + c0, q11);
+            load16h8(sk + c0, qs);
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const float top = q00[e] + (q01[e] - q00[e]) * dx, bot = q10[e] + (q11[e] - q10[e]) * dx;
+                v[k][e] = fmaxf(top + (bot - top) * dy, 0.0f) + qs[e];
+                sum += v[k][e];
+            }
+            if (valid)
+                *reinterpret_cast<uint4 *>(a.out.p + a.out.row(Y, X) * C + c0) = pack8h(v[k]);
         }
-        *reinterpret_cast<__half2 *>(o + c) = __floats2half2_rn(t[0], t[1]);
-        v[2 * j] = t[0];
-        v[2 * j + 1] = t[1];
-        sum += t[0] + t[1];
     }
-    for (int m = 16; m; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
-    const float mean = sum / C;
+    const float mean = group_sum<LP>(sum) / C;
     float q = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        if (lane + 32 * j >= pairs) break;
-        const float d0 = v[2 * j] - mean, d1 = v[2 * j + 1] - mean;
-        q += d0 * d0 + d1 * d1;
-    }
-    for (int m = 16; m; m >>= 1) q += __shfl_xor_sync(0xffffffffu, q, m);
-    const float rstd = rsqrtf(q / C + a.eps);
+    for (int k = 0; k < NCH; k++)
+        if (l + LP * k < nchunk)
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int pi = lane + 32 * j;
-        if (pi >= pairs) break;
-        const int c = 2 * pi;
-        shift_store2(a.h, a.shift, 2, Y, X, c, (v[2 * j] - mean) * rstd * a.g[c] + a.b[c],
-                     (v[2 * j + 1] - mean) * rstd * a.g[c + 1] + a.b[c + 1]);
+            for (int e = 0; e < 8; e++) {
+                const float dd = v[k][e] - mean;
+                q += dd * dd;
+            }
+    const float rstd = rsqrtf(group_sum<LP>(q) / C + a.eps);
+#pragma unroll
+    for (int k = 0; k < NCH; k++) {
+        const int ch = l + LP * k;
+        if (ch < nchunk && valid) {
+            const int c0 = ch * 8;
+            float g[8], bb[8], o[8];
+            load8f(a.g + c0, g);
+            load8f(a.b + c0, bb);
+#pragma unroll
+            for (int e = 0; e < 8; e++) o[e] = (v[k][e] - mean) * rstd * g[e] + bb[e];
+            shift_store8(a.h, a.shift, Y, X, c0, o);
+        }
     }
     pdl_trigger();
 }
 
-// One warp per token; lanes own channel pairs (N even, N <= 512).  The k-split
-// partials are summed in order (k ascending); all pairs of one k are loaded together.
-__global__ void ln_finalize_kernel(const LnFinalizeArgs a) {
+// Split-K finish, LP lanes per token, 8 channels per lane and chunk: the k-split
+// partials summed in order (k ascending), + bias (+ residual), LN1 -> out,
+// [LN2 -> out2 with the H shift].
+template <int LP, int NCH>
+__global__ void __launch_bounds__(256) ln_finalize_kernel(const LnFinalizeArgs a) {
     pdl_wait();
-    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
+    const int N = a.N, nchunk = N >> 3;
     const int T = a.H * a.W;
-    if (t >= T) return;
-    const int y = t / a.W, x = t - y * a.W;
-    const int N = a.N, pairs = N / 2;
-    float v[16];
+    const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+    const int t = gid / LP, l = gid - t * LP;
+    const bool valid = t < T;                  // invalid groups still join the shuffles
+    const int tt = valid ? t : 0;
+    const int y = tt / a.W, x = tt - y * a.W;
+    float v[NCH][8];
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int c = 2 * (lane + 32 * j);
-        if (c < N) {
-            const float2 bb = *reinterpret_cast<const float2 *>(a.bias + c);
-            v[2 * j] = bb.x;
-            v[2 * j + 1] = bb.y;
-        }
+    for (int k = 0; k < NCH; k++) {
+        const int ch = l + LP * k;
+        if (ch < nchunk) load8f(a.bias + ch * 8, v[k]);
+        else
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[k][e] = 0.f;
     }
-    for (int k = 0; k < a.ksplit; k++) {
-        const float *pk = a.partial + ((size_t)k * T + t) * N;
-        float2 pv[8];
+    for (int ks = 0; ks < a.ksplit; ks++) {
+        const float *pk = a.partial + ((size_t)ks * T + tt) * N;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int c = 2 * (lane + 32 * j);
-            if (c < N) pv[j] = *reinterpret_cast<const float2 *>(pk + c);
-        }
+        for (int k = 0; k < NCH; k++) {
+            const int ch = l + LP * k;
+            if (ch < nchunk) {
+                float pv[8];
+                load8f(pk + ch * 8, pv);
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            if (2 * (lane + 32 * j) < N) {
-                v[2 * j] += pv[j].x;
-                v[2 * j + 1] += pv[j].y;
+                for (int e = 0; e < 8; e++) v[k][e] += pv[e];
             }
         }
     }
     float sum = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int pi = lane + 32 * j;
-        if (pi >= pairs) break;
-        const int c = 2 * pi;
-        if (a.res) {
-            const float2 r = __half22float2(*reinterpret_cast<const __half2 *>(a.res + (size_t)t * N + c));
-            v[2 * j] += r.x;
-            v[2 * j + 1] += r.y;
+    for (int k = 0; k < NCH; k++) {
+        const int ch = l + LP * k;
+        if (ch < nchunk) {
+            if (a.res) {
+                float r[8];
+                load16h8(a.res + (size_t)tt * N + ch * 8, r);
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[k][e] += r[e];
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e++) sum += v[k][e];
         }
-        sum += v[2 * j] + v[2 * j + 1];
     }
-    for (int m = 16; m; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
-    const float mean = sum / N;
+    const float mean = group_sum<LP>(sum) / N;
     float q = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        if (lane + 32 * j >= pairs) break;
-        const float d0 = v[2 * j] - mean, d1 = v[2 * j + 1] - mean;
-        q += d0 * d0 + d1 * d1;
-    }
-    for (int m = 16; m; m >>= 1) q += __shfl_xor_sync(0xffffffffu, q, m);
-    const float rstd = rsqrtf(q / N + a.eps1);
+    for (int k = 0; k < NCH; k++)
+        if (l + LP * k < nchunk)
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const float dd = v[k][e] - mean;
+                q += dd * dd;
+            }
+    const float rstd = rsqrtf(group_sum<LP>(q) / N + a.eps1);
     float s2 = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int pi = lane + 32 * j;
-        if (pi >= pairs) break;
-        const int c = 2 * pi;
-        const float y0 = (v[2 * j] - mean) * rstd * a.g1[c] + a.b1[c];
-        const float y1 = (v[2 * j + 1] - mean) * rstd * a.g1[c + 1] + a.b1[c + 1];
-        act_store2(a.out, y, x, c, __floats2half2_rn(y0, y1));
-        v[2 * j] = y0;
-        v[2 * j + 1] = y1;
-        s2 += y0 + y1;
-    }
-    if (!a.ln2) return;
-    for (int m = 16; m; m >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, m);
-    const float mean2 = s2 / N;
-    float q2 = 0.f;
+    for (int k = 0; k < NCH; k++) {
+        const int ch = l + LP * k;
+        if (ch < nchunk) {
+            const int c0 = ch * 8;
+            float g[8], bb[8];
+            load8f(a.g1 + c0, g);
+            load8f(a.b1 + c0, bb);
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        if (lane + 32 * j >= pairs) break;
-        const float d0 = v[2 * j] - mean2, d1 = v[2 * j + 1] - mean2;
-        q2 += d0 * d0 + d1 * d1;
+            for (int e = 0; e < 8; e++) {
+                v[k][e] = (v[k][e] - mean) * rstd * g[e] + bb[e];
+                s2 += v[k][e];
+            }
+            if (valid) {
+                const uint4 u = pack8h(v[k]);
+                act_store(a.out, y, x, c0, reinterpret_cast<const __half *>(&u), 8);
+            }
+        }
     }
-    for (int m = 16; m; m >>= 1) q2 += __shfl_xor_sync(0xffffffffu, q2, m);
-    const float rstd2 = rsqrtf(q2 / N + a.eps2);
+    if (a.ln2) {
+        const float mean2 = group_sum<LP>(s2) / N;
+        float q2 = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int pi = lane + 32 * j;
-        if (pi >= pairs) break;
-        const int c = 2 * pi;
-        shift_store2(a.out2, a.shift, 2, y, x, c, (v[2 * j] - mean2) * rstd2 * a.g2[c] + a.b2[c],
-                     (v[2 * j + 1] - mean2) * rstd2 * a.g2[c + 1] + a.b2[c + 1]);
+        for (int k = 0; k < NCH; k++)
+            if (l + LP * k < nchunk)
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const float dd = v[k][e] - mean2;
+                    q2 += dd * dd;
+                }
+        const float rstd2 = rsqrtf(group_sum<LP>(q2) / N + a.eps2);
+#pragma unroll
+        for (int k = 0; k < NCH; k++) {
+            const int ch = l + LP * k;
+            if (ch < nchunk && valid) {
+                const int c0 = ch * 8;
+                float g[8], bb[8], o[8];
+                load8f(a.g2 + c0, g);
+                load8f(a.b2 + c0, bb);
+#pragma unroll
+                for (int e = 0; e < 8; e++) o[e] = (v[k][e] - mean2) * rstd2 * g[e] + bb[e];
+                shift_store8(a.out2, a.shift, y, x, c0, o);
+            }
+        }
     }
     pdl_trigger();
 }
@@ -635,17 +691,25 @@ int up_add_launch(const UpAddArgs &a, cudaStream_t st) {
         if (C % 8) return -2;
         launch_pdl(up_add_pad_kernel, dim3(grid_for((long long)a.out.W * (C / 8), 256), a.out.H), dim3(256), 0, st, a);
     } else {
-        if (C % 2 || C > 512) return -2;
-        const long long n = (long long)a.out.H * a.out.W * 32;
-        launch_pdl(up_add_tok_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
+        if (C % 8 || C > 512) return -2;
+        const int nchunk = C / 8;
+        const int LP = nchunk <= 16 ? 16 : 32;
+        const long long n = (long long)a.out.H * a.out.W * LP;
+        if (LP == 16) launch_pdl(up_add_tok_kernel<16, 1>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
+        else if (nchunk <= 32) launch_pdl(up_add_tok_kernel<32, 1>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
+        else launch_pdl(up_add_tok_kernel<32, 2>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
     }
     return launch_status();
 }
 
 int ln_finalize_launch(const LnFinalizeArgs &a, cudaStream_t st) {
-    if (a.N % 2 || a.N > 512 || a.ksplit < 1) return -2;
-    const long long n = (long long)a.H * a.W * 32;
-    launch_pdl(ln_finalize_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
+    if (a.N % 8 || a.N > 512 || a.ksplit < 1) return -2;
+    const int nchunk = a.N / 8;
+    const int LP = nchunk <= 16 ? 16 : 32;
+    const long long n = (long long)a.H * a.W * LP;
+    if (LP == 16) launch_pdl(ln_finalize_kernel<16, 1>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
+    else if (nchunk <= 32) launch_pdl(ln_finalize_kernel<32, 1>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
+    else launch_pdl(ln_finalize_kernel<32, 2>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
     return launch_status();
 }
 
