@@ -43,6 +43,7 @@ constexpr int kProducer2Warp = 1 + kMmaWarps + kEpiWarps;     // the second TMA 
 
 struct TcShared {
     uint64_t full[kMaxStages], empty[kMaxStages], tfull[2], tempty[2];
+    float xchg[4][64];                 // LayerNorm row halves: partial sums per lane quadrant
     uint32_t tmem_base;
     int abort_flag;
     int issued[2], consumed;
@@ -222,14 +223,20 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                     TmemLoader bot{acc0 + (uint32_t)((cfg.rt + i) * cfg.acc_cols)};
                     epilogue_pool(args.ep, tg, y2, x0 + 128 * i + row, ni * Ns, Ns, top, bot, part, 2);
                 }
-            } else if (MODE == EPI_PLAIN || MODE == EPI_PARTIAL || part == 0) {
-                // LayerNorm modes need whole rows: the first four warps finish them
-                const int nparts = (MODE == EPI_PLAIN || MODE == EPI_PARTIAL) ? 2 : 1;
+            } else if (MODE == EPI_LN2 || MODE == EPI_RESLN) {
+                // whole LayerNorm rows: the two warps of a lane quadrant take half of the columns each
                 for (int i = 0; i < cfg.rt; i++) {
                     const int tile = mu * cfg.rt + i;
                     if (tile >= tg.ntiles) break;
                     TmemLoader ld{acc0 + (uint32_t)(i * cfg.acc_cols)};
-                    epilogue_tile<MODE>(args.ep, tg, tile, row, ni * Ns, Ns, N, ki, ld, part, nparts);
+                    epilogue_ln_split<MODE>(args.ep, tg, tile, row, N, ld, part, lane, sh->xchg[quad], 3 + quad);
+                }
+            } else {
+                for (int i = 0; i < cfg.rt; i++) {
+                    const int tile = mu * cfg.rt + i;
+                    if (tile >= tg.ntiles) break;
+                    TmemLoader ld{acc0 + (uint32_t)(i * cfg.acc_cols)};
+                    epilogue_tile<MODE>(args.ep, tg, tile, row, ni * Ns, Ns, N, ki, ld, part, 2);
                 }
             }
             tc_fence_before();
@@ -398,6 +405,10 @@ int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, st
     if (!flat_only || mode == EPI_HEAD) {   // the head epilogue exists only in the row-window kernel
         RwConfig rc;
         if (rw_plan(a, mode, num_sms, rc) == 0) return rw_conv_launch(a, mode, rc, num_sms, st, err);
+    }
+    if ((mode == EPI_LN2 || mode == EPI_RESLN) && (a.nsplit != 1 || a.N % 32)) {
+        err = "LayerNorm layers need whole rows with N % 32 == 0";
+        return -1;
     }
     TcConfig cfg;
     if (tc_plan(a, num_sms, cfg, err)) return -1;

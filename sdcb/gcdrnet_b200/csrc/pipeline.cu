@@ -329,6 +329,11 @@ Split split_policy(const ConvArgs &a, bool ln_mode, int nsm) {
 
 bool uses_partial(const ConvArgs &a, int mode, int nsm) {
     if (mode != EPI_LN2 && mode != EPI_RESLN) return false;
+    static const bool no_split = [] { const char *v = std::getenv("GCDR_CUDA_LN_SPLIT"); return v && v[0] == '0'; }();
+    if (no_split) return false;
+    // small K with enough tiles: one kernel with the LayerNorm epilogue beats split-K + finalize
+    // (measured: 1x1 fc2, K = 160, 57 tiles at 1600x1152)
+    if (a.ntaps * a.C <= 192 && a.tg.ntiles >= 32) return false;
     Split s = split_policy(a, true, nsm);
     return s.nsplit > 1 || s.ksplit > 1;
 }
