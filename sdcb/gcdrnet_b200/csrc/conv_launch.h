@@ -38,6 +38,7 @@ struct RwConfig {
     int b_block = 0;       // one (k-block, tap) weight block: N rows x bk, 1 KB aligned
     int b_bytes = 0;       // all weights: 9 * C/bk blocks
     int acc_cols = 32, acc_bufs = 1, tmem_cols = 32;
+    int win_tx = 0;        // head: bytes of the dec5 window box per stage (0 otherwise)
 };
 
 // Copies the layer's bias (device, N floats) into a.ep.bias_c (synchronous; at op
@@ -45,6 +46,8 @@ struct RwConfig {
 int fill_bias_consts(ConvArgs &a);
 
 int tc_pick_bk(int C);
+bool tma_encode_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1,
+                   uint32_t b2, std::string &err);
 bool tma_encode_2d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint32_t box_inner,
                    uint32_t box_outer, int bk, std::string &err);
 // 0 and a plan when the layer suits the row-window kernel, -1 otherwise.

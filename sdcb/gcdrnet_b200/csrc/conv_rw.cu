@@ -15,7 +15,10 @@
 //     memory for the whole persistent CTA.
 // Roles: warp 0 (and warp 13) TMA producers taking alternate stages, warps 1..R
 // MMA issuers (one accumulator = one output row each), warps 5-12 epilogue
-// (bias [+ relu], or the 2x2 max-pool + relu of two accumulators).
+// (bias [+ relu], the 2x2 max-pool + relu of two accumulators, or the head).
+// Head units also carry their dec5 window in the ring stage (a third TMA box, read
+// by the epilogue), so a head stage is released by the MMA commits and the epilogue
+// warps together.
 // Every mbarrier wait is bounded; on expiry the CTA raises the abort flag and the
 // global error word, drains its copies in flight and its last commit, and frees TMEM.
 #include <cuda.h>
@@ -50,10 +53,13 @@ struct RwShared {
 
 __host__ __device__ inline int round1k(int b) { return (b + 1023) & ~1023; }
 
-template <int BK, int MODE>
+// HC: the head's stem channels (16 or 32; a separate instantiation each: one register
+// allocation per width), 0 for the other modes
+template <int BK, int MODE, int HC>
 __global__ void __launch_bounds__(kRwThreads, 1)
     rw_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ ConvArgs args, const __grid_constant__ RwConfig cfg) {
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ ConvArgs args,
+                   const __grid_constant__ RwConfig cfg) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *bres = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = bres + cfg.b_bytes;
@@ -68,7 +74,7 @@ __global__ void __launch_bounds__(kRwThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < cfg.stages; s++) {
             mbar_init(&sh->full[s], 1);
-            mbar_init(&sh->empty[s], (uint32_t)R);
+            mbar_init(&sh->empty[s], (uint32_t)(MODE == EPI_HEAD ? R + kRwEpiWarps : R));
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&sh->tfull[b], (uint32_t)R);
@@ -127,9 +133,12 @@ __global__ void __launch_bounds__(kRwThreads, 1)
                     if ((g & 1) == p) {
                         if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err)) { ok = false; break; }
                         uint8_t *stage = ring + (size_t)s * cfg.stage_bytes;
-                        mbar_expect_tx(&sh->full[s], (uint32_t)((R + 2) * kSegRows * BK * 2));
+                        mbar_expect_tx(&sh->full[s], (uint32_t)((R + 2) * kSegRows * BK * 2 + cfg.win_tx));
                         for (int r = 0; r < R + 2; r++)
                             tma_load_2d(stage + (size_t)r * cfg.seg_bytes, &tmA, kb * BK, (y0 + r) * pitch + x0, &sh->full[s]);
+                        if (MODE == EPI_HEAD)   // dec5 rows y0/2 - 1.., columns x0/2 - 1.. (edge: zero fill, never read)
+                            tma_load_3d(stage + (size_t)(R + 2) * cfg.seg_bytes, &tmC, 0, x0 / 2 - 1, y0 / 2 - 1,
+                                        &sh->full[s]);
                         issued++;
                     }
                     if (++s == cfg.stages) { s = 0; ph ^= 1u; }
@@ -217,12 +226,21 @@ __global__ void __launch_bounds__(kRwThreads, 1)
                     epilogue_pool(args.ep, tg, y0 / 2 + q, x, 0, N, top, bot, ch, nch);
                 }
             } else if (MODE == EPI_HEAD) {
-                // a whole channel row per pixel (the 1x1 over C1): rows alternate between the warps
-                for (int jj = part; jj < R; jj += 2) {
-                    TmemLoader ld{acc0 + (uint32_t)(jj * cfg.acc_cols)};
-                    if (N == 32) epilogue_head<32>(args.ep, tg, y0 + jj, x, ld);
-                    else epilogue_head<16>(args.ep, tg, y0 + jj, x, ld);
+                // pixel pairs (rows 2q, 2q + 1: one shared dec5 row) alternate between the warps;
+                // one head unit = one ring stage (C = BK), whose dec5 window the MMA commit left
+                // in place: the full barrier's phase has completed (wait for visibility only)
+                const int hs = t % cfg.stages;
+                const uint8_t *win = ring + (size_t)hs * cfg.stage_bytes + (size_t)(R + 2) * cfg.seg_bytes;
+                // (after an abort it is skipped: the next unit's vote ends all epilogue warps together)
+                if (mbar_wait(&sh->full[hs], (uint32_t)((t / cfg.stages) & 1), abort_flag, args.err)) {
+                    for (int q = part; q < R / 2; q += 2) {
+                        TmemLoader l0{acc0 + (uint32_t)(2 * q * cfg.acc_cols)};
+                        TmemLoader l1{acc0 + (uint32_t)((2 * q + 1) * cfg.acc_cols)};
+                        epilogue_head_pair<HC>(args.ep, tg, y0 + 2 * q, x, l0, l1, win, y0 / 2 - 1, x0 / 2 - 1);
+                    }
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh->empty[hs]);    // the window may be overwritten
             } else {
                 for (int it = part; it < R * nch; it += 2) {
                     const int jj = it / nch, ch = it - jj * nch;
@@ -271,17 +289,17 @@ size_t rw_smem(const RwConfig &cfg) {
     return 1024 + (size_t)cfg.b_bytes + (size_t)cfg.stages * cfg.stage_bytes + sizeof(RwShared);
 }
 
-template <int BK, int MODE>
-int rw_launch_bk_mode(const ConvArgs &a, const RwConfig &cfg, const CUtensorMap &ta, const CUtensorMap &tb, int grid,
-                      cudaStream_t st, std::string &err) {
-    auto k = rw_conv_kernel<BK, MODE>;
+template <int BK, int MODE, int HC = 0>
+int rw_launch_bk_mode(const ConvArgs &a, const RwConfig &cfg, const CUtensorMap &ta, const CUtensorMap &tb,
+                      const CUtensorMap &tc, int grid, cudaStream_t st, std::string &err) {
+    auto k = rw_conv_kernel<BK, MODE, HC>;
     const size_t smem = rw_smem(cfg);
     // the attribute is per kernel, shared by every layer (and every thread) launching it:
     // always the same cap, never a layer's own size, so concurrent workers cannot lower it
     // under one another's launches
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kRwSmemCap);
     if (e != cudaSuccess) { err = std::string("rw smem attribute: ") + cudaGetErrorString(e); return -1; }
-    e = launch_pdl(k, dim3(grid), dim3(kRwThreads), smem, st, ta, tb, a, cfg);
+    e = launch_pdl(k, dim3(grid), dim3(kRwThreads), smem, st, ta, tb, tc, a, cfg);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { err = std::string("rw_conv launch: ") + cudaGetErrorString(e); return -1; }
     return 0;
@@ -299,7 +317,9 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
     int cols = 32;
     while (cols < a.N) cols <<= 1;
     const int segs_x = (tg.conv_w + 127) / 128;
-    const int r_min = tg.pool ? 2 : 1;
+    // pool: conv row pairs; head: pixel pairs of rows 2q, 2q + 1
+    const int r_min = (tg.pool || mode == EPI_HEAD) ? 2 : 1;
+    if (mode == EPI_HEAD && (tg.conv_h % 2 || tg.conv_w % 2)) return -1;
     // (k-block, rows per unit): the most rows that fit TMEM (two buffers), keep >= 3
     // ring stages and still fill the GPU in one wave; narrower k-blocks when the
     // widest leave too few stages.  Weights must stay resident.
@@ -309,6 +329,7 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
     for (int pass = 0; pass < 2 && !found; pass++) {
         for (int bk = tc_pick_bk(a.C); bk >= 16 && !found; bk >>= 1) {
             if (a.C % bk) continue;
+            if (mode == EPI_HEAD && bk != a.C) continue;   // one ring stage (and dec5 window) per head unit
             const int b_block = round1k(a.N * bk * 2);
             const int b_bytes = 9 * (a.C / bk) * b_block;
             if (b_bytes > 96 * 1024) continue;
@@ -318,7 +339,10 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
                 const int R = pass == 0 ? (i == 0 ? 4 : i == 1 ? 2 : 0) : (r_min << i);
                 if (R < r_min || R > 4) continue;
                 const int units = ((tg.conv_h + R - 1) / R) * segs_x;
-                const int stages = avail / ((R + 2) * seg_bytes);
+                // head: the unit's dec5 window (R/2 + 2 rows of kHeadWinCols columns x N channels)
+                const int win_tx = mode == EPI_HEAD ? (R / 2 + 2) * kHeadWinCols * a.N * 2 : 0;
+                const int stage_bytes = (R + 2) * seg_bytes + round1k(win_tx);
+                const int stages = avail / stage_bytes;
                 if (2 * R * cols > 512 || stages < 3) continue;
                 if (pass == 0 && units < num_sms && !(tg.pool && R == 2)) continue;
                 cfg.bk = bk;
@@ -328,7 +352,8 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
                 cfg.seg_bytes = seg_bytes;
                 cfg.segs_x = segs_x;
                 cfg.units = units;
-                cfg.stage_bytes = (R + 2) * seg_bytes;
+                cfg.stage_bytes = stage_bytes;
+                cfg.win_tx = win_tx;
                 cfg.stages = stages > kMaxStages ? kMaxStages : stages;
                 found = true;
             }
@@ -351,6 +376,14 @@ int rw_conv_launch(const ConvArgs &a, int mode, const RwConfig &cfg, int num_sms
         return -1;
     if (!tma_encode_2d(&tb, a.B, (uint64_t)a.C * 9, (uint64_t)a.N, (uint32_t)cfg.bk, (uint32_t)a.N, cfg.bk, err))
         return -1;
+    CUtensorMap tc = tb;   // the head's dec5 window map (other modes: unused)
+    if (mode == EPI_HEAD) {
+        const __half *d5 = a.ep.head.dec5;
+        if (!d5 || (reinterpret_cast<uintptr_t>(d5) & 15)) { err = "head: dec5 missing or misaligned"; return -1; }
+        if (!tma_encode_3d(&tc, d5, (uint64_t)a.N, (uint64_t)(a.tg.conv_w / 2), (uint64_t)(a.tg.conv_h / 2),
+                           (uint32_t)a.N, (uint32_t)kHeadWinCols, (uint32_t)(cfg.R / 2 + 2), err))
+            return -1;
+    }
     const int grid = cfg.units < num_sms ? cfg.units : num_sms;
     static const bool verbose = [] { const char *v = std::getenv("GCDR_CUDA_VERBOSE"); return v && v[0] == '1'; }();
     if (verbose)
@@ -361,13 +394,15 @@ int rw_conv_launch(const ConvArgs &a, int mode, const RwConfig &cfg, int num_sms
     if (grid < 1) return 0;
     if (rw_smem(cfg) > (size_t)kRwSmemCap) { err = "rw_conv: shared memory plan over the cap"; return -1; }
     switch (cfg.bk * 8 + mode) {
-        case 64 * 8 + EPI_PLAIN: return rw_launch_bk_mode<64, EPI_PLAIN>(a, cfg, ta, tb, grid, st, err);
-        case 64 * 8 + EPI_POOL: return rw_launch_bk_mode<64, EPI_POOL>(a, cfg, ta, tb, grid, st, err);
-        case 32 * 8 + EPI_PLAIN: return rw_launch_bk_mode<32, EPI_PLAIN>(a, cfg, ta, tb, grid, st, err);
-        case 32 * 8 + EPI_POOL: return rw_launch_bk_mode<32, EPI_POOL>(a, cfg, ta, tb, grid, st, err);
-        case 16 * 8 + EPI_PLAIN: return rw_launch_bk_mode<16, EPI_PLAIN>(a, cfg, ta, tb, grid, st, err);
-        case 16 * 8 + EPI_POOL: return rw_launch_bk_mode<16, EPI_POOL>(a, cfg, ta, tb, grid, st, err);
-        case 16 * 8 + EPI_HEAD: return rw_launch_bk_mode<16, EPI_HEAD>(a, cfg, ta, tb, grid, st, err);
+        case 64 * 8 + EPI_PLAIN: return rw_launch_bk_mode<64, EPI_PLAIN>(a, cfg, ta, tb, tc, grid, st, err);
+        case 64 * 8 + EPI_POOL: return rw_launch_bk_mode<64, EPI_POOL>(a, cfg, ta, tb, tc, grid, st, err);
+        case 32 * 8 + EPI_PLAIN: return rw_launch_bk_mode<32, EPI_PLAIN>(a, cfg, ta, tb, tc, grid, st, err);
+        case 32 * 8 + EPI_POOL: return rw_launch_bk_mode<32, EPI_POOL>(a, cfg, ta, tb, tc, grid, st, err);
+        case 16 * 8 + EPI_PLAIN: return rw_launch_bk_mode<16, EPI_PLAIN>(a, cfg, ta, tb, tc, grid, st, err);
+        case 16 * 8 + EPI_POOL: return rw_launch_bk_mode<16, EPI_POOL>(a, cfg, ta, tb, tc, grid, st, err);
+        case 16 * 8 + EPI_HEAD:
+            return a.N == 32 ? rw_launch_bk_mode<16, EPI_HEAD, 32>(a, cfg, ta, tb, tc, grid, st, err)
+                             : rw_launch_bk_mode<16, EPI_HEAD, 16>(a, cfg, ta, tb, tc, grid, st, err);
     }
     err = "rw_conv: bad k-block / mode";
     return -1;

@@ -347,6 +347,26 @@ int fill_bias_consts(ConvArgs &a) {
     return cudaMemcpy(a.ep.bias_c, a.ep.bias, (size_t)a.N * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
 }
 
+// [d2][d1][d0] fp16 (d0 contiguous, 32 or 64 bytes: the swizzle of that width), a box
+// of (b0, b1, b2); out-of-range elements of a box read as zero
+bool tma_encode_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1,
+                   uint32_t b2, std::string &err) {
+    if (!get_encoder(err)) return false;
+    if (d0 * 2 != 32 && d0 * 2 != 64) { err = "tma 3d: inner extent must be 32 or 64 bytes"; return false; }
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+    cuuint32_t box[3] = {b0, b1, b2};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, d0 * 2 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        err = "cuTensorMapEncodeTiled (3d) failed (" + std::to_string((int)r) + ")";
+        return false;
+    }
+    return true;
+}
+
 bool tma_encode_2d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint32_t box_inner,
                    uint32_t box_outer, int bk, std::string &err) {
     return encode_2d(m, base, inner, outer, box_inner, box_outer, bk, err);

@@ -342,54 +342,23 @@ __device__ void epilogue_pool(const EpiParams &ep, const TileGeom &tg, int y2, i
     }
 }
 
-// EPI_HEAD for padded-image pixel (y, x): the accumulator row holds the stem conv
-// (C1 = 16 or 32 columns).  Warp-collective (the TMEM load); stores are masked.
-template <int C1, class L>
-__device__ void epilogue_head(const EpiParams &ep, const TileGeom &tg, int y, int x, L &ld) {
-    const HeadParams &hp = ep.head;
-    float c1[C1];
-    if (C1 == 32) ld.load32(0, c1);
-    else ld.load16(0, c1);
-    if (y >= tg.conv_h || x >= tg.conv_w) return;
-    const int H = tg.conv_h, W = tg.conv_w, Hh = H / 2, Wh = W / 2;
-    // bilinear x2 of dec5, half_pixel, edge clamp (ONNX Resize linear)
-    const float fy = ((float)y + 0.5f) * 0.5f - 0.5f, fx = ((float)x + 0.5f) * 0.5f - 0.5f;
-    const int y0 = (int)floorf(fy), x0 = (int)floorf(fx);
-    const float dy = fy - (float)y0, dx = fx - (float)x0;
-    const int ya = min(max(y0, 0), Hh - 1), yb = min(max(y0 + 1, 0), Hh - 1);
-    const int xa = min(max(x0, 0), Wh - 1), xb = min(max(x0 + 1, 0), Wh - 1);
-    const __half *p00 = hp.dec5 + ((size_t)ya * Wh + xa) * C1, *p01 = hp.dec5 + ((size_t)ya * Wh + xb) * C1;
-    const __half *p10 = hp.dec5 + ((size_t)yb * Wh + xa) * C1, *p11 = hp.dec5 + ((size_t)yb * Wh + xb) * C1;
-    // the x2 bilinear weights (products of 0.25 / 0.75, or 0 / 1 at the clamped edges) are exact
-    // in fp16: the interpolation of the fp16 dec5 runs on channel pairs (HFMA2), the rest in fp32
-    const __half2 w00 = __float2half2_rn((1.0f - dx) * (1.0f - dy)), w01 = __float2half2_rn(dx * (1.0f - dy));
-    const __half2 w10 = __float2half2_rn((1.0f - dx) * dy), w11 = __float2half2_rn(dx * dy);
-    float o0 = hp.fb[0], o1 = hp.fb[1], o2 = hp.fb[2];
-#pragma unroll
-    for (int c0 = 0; c0 < C1; c0 += 8) {
-        const uint4 u00 = *reinterpret_cast<const uint4 *>(p00 + c0), u01 = *reinterpret_cast<const uint4 *>(p01 + c0);
-        const uint4 u10 = *reinterpret_cast<const uint4 *>(p10 + c0), u11 = *reinterpret_cast<const uint4 *>(p11 + c0);
-        const __half2 *a00 = reinterpret_cast<const __half2 *>(&u00), *a01 = reinterpret_cast<const __half2 *>(&u01);
-        const __half2 *a10 = reinterpret_cast<const __half2 *>(&u10), *a11 = reinterpret_cast<const __half2 *>(&u11);
-#pragma unroll
-        for (int k2 = 0; k2 < 4; k2++) {
-            __half2 up = __hmul2(a00[k2], w00);
-            up = __hfma2(a01[k2], w01, up);
-            up = __hfma2(a10[k2], w10, up);
-            up = __hfma2(a11[k2], w11, up);
-            const float2 uf = __half22float2(up);
-            const int c = c0 + 2 * k2;
-            const float s0 = fmaxf(uf.x, 0.0f) + fmaxf(c1[c] + hp.b1[c], 0.0f);
-            const float s1 = fmaxf(uf.y, 0.0f) + fmaxf(c1[c + 1] + hp.b1[c + 1], 0.0f);
-            o0 = fmaf(s0, hp.fw[c], o0);
-            o1 = fmaf(s0, hp.fw[C1 + c], o1);
-            o2 = fmaf(s0, hp.fw[2 * C1 + c], o2);
-            o0 = fmaf(s1, hp.fw[c + 1], o0);
-            o1 = fmaf(s1, hp.fw[C1 + c + 1], o1);
-            o2 = fmaf(s1, hp.fw[2 * C1 + c + 1], o2);
-        }
-    }
-    const float o[3] = {1.0f / (1.0f + expf(-o0)), 1.0f / (1.0f + expf(-o1)), 1.0f / (1.0f + expf(-o2))};
+// dec5 window of one row-window unit in shared memory: a TMA box of C1 channels x
+// kHeadWinCols dec5 columns x (R/2 + 2) dec5 rows, rows of C1 * 2 bytes under the
+// matching swizzle (32B for 16 channels, 64B for 32: 16-byte chunk bits [5:4] XOR
+// address bits [8:7]), so that the two-column gathers of a warp hit distinct banks.
+constexpr int kHeadWinCols = 66;   // 128 pixels -> 64 dec5 columns + the clamp/interpolation halo
+
+template <int C1>
+__device__ __forceinline__ uint4 head_win_ld(const uint8_t *win, int r, int c, int k) {
+    uint32_t off = (uint32_t)((r * kHeadWinCols + c) * (C1 * 2) + k * 16);
+    off ^= ((off >> 7) & (C1 == 32 ? 3u : 1u)) << 4;
+    return *reinterpret_cast<const uint4 *>(win + off);
+}
+
+__device__ __forceinline__ float sigmoid_fast(float v) { return __fdividef(1.0f, 1.0f + __expf(-v)); }
+
+// The per-pixel tail of the head: div6 into the DR stem input (GC) or the u8 output (DR).
+__device__ __forceinline__ void head_store(const HeadParams &hp, int W, int y, int x, const float *o) {
     const size_t pix = (size_t)y * W + x;
     if (!hp.is_dr) {
         // div6: r = clamp(x / max(I_sm, 1e-6), 0, 1) with x = u8 / 255, written as the DR stem input
@@ -399,9 +368,8 @@ __device__ void epilogue_head(const EpiParams &ep, const TileGeom &tg, int y, in
 #pragma unroll
         for (int c = 0; c < 3; c++) {
             const __half u = xu[c];
-            const float xv = __half2float(u) / 255.0f;
             const float d = o[c] > 1e-6f ? o[c] : 1e-6f;
-            float r = xv / d;
+            float r = __fdividef(__half2float(u) * (1.0f / 255.0f), d);
             r = r < 0.0f ? 0.0f : (r > 1.0f ? 1.0f : r);
             const __half rh = __float2half_rn(r);
             const __half rl = __float2half_rn(r - __half2float(rh));
@@ -442,6 +410,88 @@ __device__ void epilogue_head(const EpiParams &ep, const TileGeom &tg, int y, in
             d[1] = q[1];
             d[2 - ob] = q[2];
         }
+    }
+}
+
+// EPI_HEAD for the padded-image pixels (y, x) and (y + 1, x), y even: accumulator rows
+// ld0 / ld1 hold their stem conv (C1 = 16 or 32 columns).  The two rows share the
+// middle dec5 row of their x2 bilinear (half_pixel, edge clamp: ONNX Resize linear),
+// so six window columns serve both pixels.  win holds dec5 rows wy0.. and columns
+// wx0.. (window origin, may be -1).  Warp-collective (the TMEM loads); stores are masked.
+template <int C1, class L>
+__device__ void epilogue_head_pair(const EpiParams &ep, const TileGeom &tg, int y, int x, L &ld0, L &ld1,
+                                   const uint8_t *win, int wy0, int wx0) {
+    const HeadParams &hp = ep.head;
+    // the TMEM loads below are warp-collective: a warp leaves only as a whole; lanes past
+    // the image edge compute on in-window data and store nothing
+    const bool valid = y < tg.conv_h && x < tg.conv_w;
+    if (!__any_sync(0xffffffffu, valid)) return;
+    const int Hh = tg.conv_h >> 1, Wh = tg.conv_w >> 1;
+    const int M = y >> 1, n = x >> 1;
+    const bool xodd = x & 1;
+    // even output row y: dec5 rows M-1 (1/4), M (3/4); odd row y+1: rows M (3/4), M+1 (1/4)
+    const int r0 = max(M - 1, 0) - wy0, r1 = M - wy0, r2 = min(M + 1, Hh - 1) - wy0;
+    // even x: columns n-1 (1/4), n (3/4); odd x: n (3/4), n+1 (1/4)
+    const int cA = (xodd ? n : max(n - 1, 0)) - wx0, cB = (xodd ? min(n + 1, Wh - 1) : n) - wx0;
+    // the products of 1/4 and 3/4 are exact in fp16: the interpolation of the fp16 dec5
+    // runs on channel pairs (HFMA2), the rest in fp32
+    const float wa = xodd ? 0.75f : 0.25f, wb = 1.0f - wa;
+    const __half2 q_a = __float2half2_rn(0.25f * wa), q_b = __float2half2_rn(0.25f * wb);
+    const __half2 t_a = __float2half2_rn(0.75f * wa), t_b = __float2half2_rn(0.75f * wb);
+    float oa0 = hp.fb[0], oa1 = hp.fb[1], oa2 = hp.fb[2];
+    float ob0 = hp.fb[0], ob1 = hp.fb[1], ob2 = hp.fb[2];
+    uint32_t ca[16], cb[16];   // the stem conv of both pixels, 16 channels at a time
+#pragma unroll
+    for (int k = 0; k < C1 / 8; k++) {
+        if (k % 2 == 0) {
+            // a phase boundary for the scheduler: the next phase's window loads stay below
+            // this phase's arithmetic (hoisting them all would spill at 128 registers)
+            if (k) asm volatile("" ::: "memory");
+            ld0.load16_nw(ca, 8 * k);
+            ld1.load16_nw(cb, 8 * k);
+            L::wait_ld();
+        }
+        const uint4 u0a = head_win_ld<C1>(win, r0, cA, k), u0b = head_win_ld<C1>(win, r0, cB, k);
+        const uint4 u1a = head_win_ld<C1>(win, r1, cA, k), u1b = head_win_ld<C1>(win, r1, cB, k);
+        const uint4 u2a = head_win_ld<C1>(win, r2, cA, k), u2b = head_win_ld<C1>(win, r2, cB, k);
+        const __half2 *h0a = reinterpret_cast<const __half2 *>(&u0a), *h0b = reinterpret_cast<const __half2 *>(&u0b);
+        const __half2 *h1a = reinterpret_cast<const __half2 *>(&u1a), *h1b = reinterpret_cast<const __half2 *>(&u1b);
+        const __half2 *h2a = reinterpret_cast<const __half2 *>(&u2a), *h2b = reinterpret_cast<const __half2 *>(&u2b);
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            __half2 ue = __hmul2(h0a[p], q_a);
+            ue = __hfma2(h0b[p], q_b, ue);
+            ue = __hfma2(h1a[p], t_a, ue);
+            ue = __hfma2(h1b[p], t_b, ue);
+            __half2 uo = __hmul2(h1a[p], t_a);
+            uo = __hfma2(h1b[p], t_b, uo);
+            uo = __hfma2(h2a[p], q_a, uo);
+            uo = __hfma2(h2b[p], q_b, uo);
+            const float2 fe = __half22float2(ue), fo = __half22float2(uo);
+            const int c = 8 * k + 2 * p, cl = c % 16;
+            const float sa0 = fmaxf(fe.x, 0.0f) + fmaxf(__uint_as_float(ca[cl]) + hp.b1[c], 0.0f);
+            const float sa1 = fmaxf(fe.y, 0.0f) + fmaxf(__uint_as_float(ca[cl + 1]) + hp.b1[c + 1], 0.0f);
+            const float sb0 = fmaxf(fo.x, 0.0f) + fmaxf(__uint_as_float(cb[cl]) + hp.b1[c], 0.0f);
+            const float sb1 = fmaxf(fo.y, 0.0f) + fmaxf(__uint_as_float(cb[cl + 1]) + hp.b1[c + 1], 0.0f);
+            oa0 = fmaf(sa0, hp.fw[c], oa0);
+            oa1 = fmaf(sa0, hp.fw[C1 + c], oa1);
+            oa2 = fmaf(sa0, hp.fw[2 * C1 + c], oa2);
+            ob0 = fmaf(sb0, hp.fw[c], ob0);
+            ob1 = fmaf(sb0, hp.fw[C1 + c], ob1);
+            ob2 = fmaf(sb0, hp.fw[2 * C1 + c], ob2);
+            oa0 = fmaf(sa1, hp.fw[c + 1], oa0);
+            oa1 = fmaf(sa1, hp.fw[C1 + c + 1], oa1);
+            oa2 = fmaf(sa1, hp.fw[2 * C1 + c + 1], oa2);
+            ob0 = fmaf(sb1, hp.fw[c + 1], ob0);
+            ob1 = fmaf(sb1, hp.fw[C1 + c + 1], ob1);
+            ob2 = fmaf(sb1, hp.fw[2 * C1 + c + 1], ob2);
+        }
+    }
+    const float oa[3] = {sigmoid_fast(oa0), sigmoid_fast(oa1), sigmoid_fast(oa2)};
+    const float ob[3] = {sigmoid_fast(ob0), sigmoid_fast(ob1), sigmoid_fast(ob2)};
+    if (valid) {
+        head_store(hp, tg.conv_w, y, x, oa);
+        head_store(hp, tg.conv_w, y + 1, x, ob);
     }
 }
 
