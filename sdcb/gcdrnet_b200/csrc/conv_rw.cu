@@ -36,10 +36,19 @@ namespace gcdr {
 
 namespace {
 
-constexpr int kRwMmaWarps = 4;
-constexpr int kRwEpiWarps = 8;
-constexpr int kRwThreads = (2 + kRwMmaWarps + kRwEpiWarps) * 32;
-constexpr int kRwProducer2 = 1 + kRwMmaWarps + kRwEpiWarps;
+// Warp roles: producer 0 = warp 0, MMA issuers = warps 1..mma, epilogue = the next epi
+// warps (a multiple of 4: each TMEM lane quadrant alike, `parts` warps per quadrant),
+// producer 1 (when there are two) = the last warp.  The head's epilogue is long and
+// latency-bound (one pixel pair per thread and unit), so its CTA trades a producer and an
+// MMA warp for four more epilogue warps: 16 warps at the 128 registers a thread may keep.
+template <int MODE>
+struct RwRoles {
+    static constexpr int prod = MODE == EPI_HEAD ? 1 : 2;
+    static constexpr int mma = MODE == EPI_HEAD ? 3 : 4;
+    static constexpr int epi = MODE == EPI_HEAD ? 12 : 8;
+    static constexpr int parts = epi / 4;
+    static constexpr int threads = (prod + mma + epi) * 32;
+};
 constexpr int kSegRows = 136;          // 128 outputs + 2 halo, rounded up to 8 rows
 constexpr int kRwSmemCap = 210 * 1024;
 
@@ -56,7 +65,7 @@ __host__ __device__ inline int round1k(int b) { return (b + 1023) & ~1023; }
 // HC: the head's stem channels (16 or 32; a separate instantiation each: one register
 // allocation per width), 0 for the other modes
 template <int BK, int MODE, int HC>
-__global__ void __launch_bounds__(kRwThreads, 1)
+__global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
     rw_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ ConvArgs args,
                    const __grid_constant__ RwConfig cfg) {
@@ -70,15 +79,17 @@ __global__ void __launch_bounds__(kRwThreads, 1)
     const int N = args.N, C = args.C, R = cfg.R;
     const int kbs = C / BK;                     // k-blocks (ring stages) per unit
     const int pitch = tg.pitch;
+    using Roles = RwRoles<MODE>;
+    const int issuers = min(Roles::mma, R);     // MMA warps with rows (each commits once per stage / unit)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < cfg.stages; s++) {
             mbar_init(&sh->full[s], 1);
-            mbar_init(&sh->empty[s], (uint32_t)(MODE == EPI_HEAD ? R + kRwEpiWarps : R));
+            mbar_init(&sh->empty[s], (uint32_t)(MODE == EPI_HEAD ? issuers + Roles::epi : issuers));
         }
         for (int b = 0; b < 2; b++) {
-            mbar_init(&sh->tfull[b], (uint32_t)R);
-            mbar_init(&sh->tempty[b], kRwEpiWarps);
+            mbar_init(&sh->tfull[b], (uint32_t)issuers);
+            mbar_init(&sh->tempty[b], Roles::epi);
         }
         mbar_init(&sh->bfull, 1);
         sh->abort_flag = 0;
@@ -110,7 +121,7 @@ __global__ void __launch_bounds__(kRwThreads, 1)
         x0 = (u - yb * cfg.segs_x) * 128;
     };
 
-    if (warp == 0 || warp == kRwProducer2) {
+    if (warp == 0 || (Roles::prod == 2 && warp == Roles::mma + Roles::epi + 1)) {
         const int p = warp == 0 ? 0 : 1;
         if (lane == 0) {
             if (p == 0) {
@@ -130,7 +141,7 @@ __global__ void __launch_bounds__(kRwThreads, 1)
                 int y0, x0;
                 unit_origin(u, y0, x0);
                 for (int kb = 0; kb < kbs; kb++, g++) {
-                    if ((g & 1) == p) {
+                    if (g % Roles::prod == p) {
                         if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err)) { ok = false; break; }
                         uint8_t *stage = ring + (size_t)s * cfg.stage_bytes;
                         mbar_expect_tx(&sh->full[s], (uint32_t)((R + 2) * kSegRows * BK * 2 + cfg.win_tx));
@@ -146,8 +157,8 @@ __global__ void __launch_bounds__(kRwThreads, 1)
             }
             sh->issued[p] = issued;
         }
-    } else if (warp <= kRwMmaWarps) {
-        const int j = warp - 1;                    // output row of the unit = accumulator
+    } else if (warp <= Roles::mma) {
+        const int j = warp - 1;                    // output rows j, j + mma, ... of the unit (one accumulator each)
         if (lane == 0 && j < R) {
             constexpr uint32_t layout = BK == 64 ? 2u : BK == 32 ? 4u : 6u;
             constexpr uint32_t sbo = 8u * BK * 2u;
@@ -163,22 +174,31 @@ __global__ void __launch_bounds__(kRwThreads, 1)
                 const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
                 if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err)) break;
                 tc_fence_after();
-                const uint32_t dcol = tmem_base + (uint32_t)((ab * R + j) * cfg.acc_cols);
+                const uint32_t dcol0 = tmem_base + (uint32_t)(ab * R * cfg.acc_cols);
                 for (int kb = 0; kb < kbs; kb++) {
                     if (!mbar_wait(&sh->full[s], ph, abort_flag, args.err)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t stage = smem_u32(ring + (size_t)s * cfg.stage_bytes);
+                    // taps outer, this warp's rows inner (head: rows j and j + mma, R <= 2 * mma):
+                    // consecutive MMAs go to different accumulators.  The row count is a compile-time
+                    // bound, the issue loop stays fully unrolled (it bounds the thin layers).
+                    constexpr int kRows = MODE == EPI_HEAD ? 2 : 1;
 #pragma unroll
                     for (int ky = 0; ky < 3; ky++) {
-                        const uint32_t seg = stage + (uint32_t)((j + ky) * cfg.seg_bytes);
 #pragma unroll
                         for (int kx = 0; kx < 3; kx++) {
-                            const uint64_t ad = desc0 | (uint64_t)(((seg + (uint32_t)(kx * BK * 2)) & 0x3FFFFu) >> 4);
                             const uint64_t bd = desc0 | (uint64_t)(((b_s + (uint32_t)((kb * 9 + ky * 3 + kx) * cfg.b_block)) & 0x3FFFFu) >> 4);
 #pragma unroll
                             for (int kk = 0; kk < BK / 16; kk++)
-                                mma_f16(dcol, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                                        (kb | ky | kx | kk) ? 1u : 0u);
+#pragma unroll
+                                for (int i = 0; i < kRows; i++) {
+                                    const int jr = j + i * Roles::mma;
+                                    if (kRows > 1 && jr >= R) break;
+                                    const uint32_t seg = stage + (uint32_t)((jr + ky) * cfg.seg_bytes);
+                                    const uint64_t ad = desc0 | (uint64_t)(((seg + (uint32_t)(kx * BK * 2)) & 0x3FFFFu) >> 4);
+                                    mma_f16(dcol0 + (uint32_t)(jr * cfg.acc_cols), ad + (uint64_t)(kk * 2),
+                                            bd + (uint64_t)(kk * 2), idesc, (kb | ky | kx | kk) ? 1u : 0u);
+                                }
                         }
                     }
                     mma_commit(&sh->empty[s]);
@@ -190,9 +210,9 @@ __global__ void __launch_bounds__(kRwThreads, 1)
             if (j == 0) sh->consumed = consumed;
         }
     } else {
-        const int e = warp - 1 - kRwMmaWarps;       // epilogue warp 0..7
-        const int quad = warp & 3;
-        const int part = e >> 2;
+        const int e = warp - 1 - Roles::mma;        // epilogue warp 0..epi-1
+        const int quad = warp & 3;                  // the TMEM lane quadrant this warp may read
+        const int part = e >> 2;                    // 0..parts-1
         const int row = quad * 32 + lane;           // pixel within the unit's 128
         const uint32_t lane_base = tmem_base + ((uint32_t)(quad * 32) << 16);
         int t = 0;
@@ -209,31 +229,31 @@ __global__ void __launch_bounds__(kRwThreads, 1)
                 "bar.red.or.pred q, 2, %2, p;\n\t"
                 "selp.u32 %0, 1, 0, q;\n\t}"
                 : "=r"(bad)
-                : "r"((uint32_t)ok), "n"(kRwEpiWarps * 32));
+                : "r"((uint32_t)ok), "n"(Roles::epi * 32));
             if (bad) break;
             tc_fence_after();
             const uint32_t acc0 = lane_base + (uint32_t)(ab * R * cfg.acc_cols);
             const int x = x0 + row;
-            // work items (output row or pooled row, 32/16-column chunk), alternating
-            // between the two warps of each TMEM lane quadrant
+            // work items (output row or pooled row, 32/16-column chunk) taken in turn by the
+            // warps of each TMEM lane quadrant
             const int cw = (N % 32 == 0) ? 32 : 16, nch = N / cw;
             if (MODE == EPI_POOL) {
                 const int rows2 = min(R / 2, tg.conv_h / 2 - y0 / 2);   // uniform over the CTA
-                for (int it = part; it < rows2 * nch; it += 2) {
+                for (int it = part; it < rows2 * nch; it += Roles::parts) {
                     const int q = it / nch, ch = it - q * nch;
                     TmemLoader top{acc0 + (uint32_t)(2 * q * cfg.acc_cols)};
                     TmemLoader bot{acc0 + (uint32_t)((2 * q + 1) * cfg.acc_cols)};
                     epilogue_pool(args.ep, tg, y0 / 2 + q, x, 0, N, top, bot, ch, nch);
                 }
             } else if (MODE == EPI_HEAD) {
-                // pixel pairs (rows 2q, 2q + 1: one shared dec5 row) alternate between the warps;
+                // pixel pairs (rows 2q, 2q + 1: one shared dec5 row) taken in turn by the warps;
                 // one head unit = one ring stage (C = BK), whose dec5 window the MMA commit left
                 // in place: the full barrier's phase has completed (wait for visibility only)
                 const int hs = t % cfg.stages;
                 const uint8_t *win = ring + (size_t)hs * cfg.stage_bytes + (size_t)(R + 2) * cfg.seg_bytes;
                 // (after an abort it is skipped: the next unit's vote ends all epilogue warps together)
                 if (mbar_wait(&sh->full[hs], (uint32_t)((t / cfg.stages) & 1), abort_flag, args.err)) {
-                    for (int q = part; q < R / 2; q += 2) {
+                    for (int q = part; q < R / 2; q += Roles::parts) {
                         TmemLoader l0{acc0 + (uint32_t)(2 * q * cfg.acc_cols)};
                         TmemLoader l1{acc0 + (uint32_t)((2 * q + 1) * cfg.acc_cols)};
                         epilogue_head_pair<HC>(args.ep, tg, y0 + 2 * q, x, l0, l1, win, y0 / 2 - 1, x0 / 2 - 1);
@@ -242,7 +262,7 @@ __global__ void __launch_bounds__(kRwThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sh->empty[hs]);    // the window may be overwritten
             } else {
-                for (int it = part; it < R * nch; it += 2) {
+                for (int it = part; it < R * nch; it += Roles::parts) {
                     const int jj = it / nch, ch = it - jj * nch;
                     TmemLoader ld{acc0 + (uint32_t)(jj * cfg.acc_cols)};
                     epilogue_plain_yx(args.ep, tg, y0 + jj, x, 0, N, ld, ch, nch, args.ep.bias_c);
@@ -257,9 +277,10 @@ __global__ void __launch_bounds__(kRwThreads, 1)
     __syncthreads();
     if (threadIdx.x == 0) {
         // drain: unconsumed TMA stages (after an abort only), the weights, the last commit
-        const int issued_end = max(2 * sh->issued[0], 2 * sh->issued[1] + 1);
+        // producer p issued the stages g = p, p + prod, ... (issued[p] of them)
+        const int issued_end = max(Roles::prod * sh->issued[0], Roles::prod * sh->issued[1] + 1);
         for (int g = sh->consumed; g < issued_end; g++) {
-            if (g / 2 >= sh->issued[g & 1]) continue;
+            if (g / Roles::prod >= sh->issued[g % Roles::prod]) continue;
             const int s = g % cfg.stages;
             const uint32_t ph = (uint32_t)((g / cfg.stages) & 1);
             long long t0 = clock64();
@@ -299,7 +320,7 @@ int rw_launch_bk_mode(const ConvArgs &a, const RwConfig &cfg, const CUtensorMap 
     // under one another's launches
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kRwSmemCap);
     if (e != cudaSuccess) { err = std::string("rw smem attribute: ") + cudaGetErrorString(e); return -1; }
-    e = launch_pdl(k, dim3(grid), dim3(kRwThreads), smem, st, ta, tb, tc, a, cfg);
+    e = launch_pdl(k, dim3(grid), dim3(RwRoles<MODE>::threads), smem, st, ta, tb, tc, a, cfg);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { err = std::string("rw_conv launch: ") + cudaGetErrorString(e); return -1; }
     return 0;
@@ -324,7 +345,8 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
     // ring stages and still fill the GPU in one wave; narrower k-blocks when the
     // widest leave too few stages.  Weights must stay resident.
     bool found = false;
-    // pass 0: R = 4 or 2 with a full wave of units (pool: R = 2 always qualifies);
+    // pass 0: R = 4 or 2 (head: 6, 4 or 2: three epilogue warps per lane quadrant, one
+    // pixel pair each) with a full wave of units (pool: R = 2 always qualifies);
     // pass 1 (small layers): the fewest rows per unit that fit, for the most units
     for (int pass = 0; pass < 2 && !found; pass++) {
         for (int bk = tc_pick_bk(a.C); bk >= 16 && !found; bk >>= 1) {
@@ -336,8 +358,10 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
             const int seg_bytes = round1k(kSegRows * bk * 2);
             const int avail = kRwSmemCap - 1024 - b_bytes - (int)sizeof(RwShared);
             for (int i = 0; i < 3 && !found; i++) {
-                const int R = pass == 0 ? (i == 0 ? 4 : i == 1 ? 2 : 0) : (r_min << i);
-                if (R < r_min || R > 4) continue;
+                // (head R <= 6: two rows per MMA warp at most)
+                const int R = mode == EPI_HEAD ? (pass == 0 ? 6 - 2 * i : 2 + 2 * i)
+                                               : pass == 0 ? (i == 0 ? 4 : i == 1 ? 2 : 0) : (r_min << i);
+                if (R < r_min || R > (mode == EPI_HEAD ? 6 : 4)) continue;
                 const int units = ((tg.conv_h + R - 1) / R) * segs_x;
                 // head: the unit's dec5 window (R/2 + 2 rows of kHeadWinCols columns x N channels)
                 const int win_tx = mode == EPI_HEAD ? (R / 2 + 2) * kHeadWinCols * a.N * 2 : 0;
@@ -362,7 +386,8 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
     if (!found) return -1;
     cfg.acc_cols = cols;
     cfg.acc_bufs = 2;
-    cfg.tmem_cols = cols * cfg.R * 2;
+    cfg.tmem_cols = 32;   // an allocation is a power of two columns
+    while (cfg.tmem_cols < cols * cfg.R * 2) cfg.tmem_cols <<= 1;
     return 0;
 }
 
