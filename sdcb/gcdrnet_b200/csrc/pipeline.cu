@@ -304,27 +304,52 @@ struct Split {
     int nsplit = 1, ksplit = 1;
 };
 
-Split split_policy(const ConvArgs &a, bool ln_mode, int nsm) {
-    Split s;
-    if (a.tg.ntiles >= nsm) return s;
-    auto units = [&] { return a.tg.ntiles * s.nsplit * s.ksplit; };
-    for (int ns = 1; ns <= a.N / 32; ns++) {
-        if (a.N % ns) continue;
+// The split of a layer with fewer 128-pixel tiles than SMs.
+//   Plain layers: N slices only, the most that keep the units within one wave (a
+//   slice at least 32 wide).
+//   LayerNorm layers: N slices x K ranges, the fp32 partials summed and normalised by
+//   ln_finalize, chosen by an estimate fitted to measured layer times on B200
+//   (1600x1152, both nets): waves of units, each an MMA chain into one accumulator at
+//   ~250 cycles per 16-deep k-step (x1.6 for 512-wide slices: two MMAs per step),
+//   ~1000 cycles of fill and its partials stored at ~8 B/cycle; plus the finalize at
+//   ~8 us + the partials read back at ~2.5 TB/s.  (The LayerNorm epilogue of the conv
+//   itself, on one tile per CTA, measured several times slower than any split.)
+Split split_policy(const ConvArgs &a, int mode, int nsm) {
+    Split best;
+    if (a.tg.ntiles >= nsm) return best;
+    auto valid_slice = [&](int ns) {
+        if (a.N % ns) return false;
         const int Ns = a.N / ns;
-        if (Ns % 16 || (Ns > 256 && Ns % 256)) continue;
-        s.nsplit = ns;
-        if (units() >= nsm) break;
+        return Ns % 16 == 0 && Ns <= 512 && !(Ns > 256 && Ns % 256);
+    };
+    if (mode == EPI_PLAIN) {
+        for (int ns = 1; ns <= a.N / 32; ns++)
+            if (valid_slice(ns) && (long long)a.tg.ntiles * ns <= nsm) best.nsplit = ns;
+        return best;
     }
-    if (ln_mode) {
-        const int bk = tc_pick_bk(a.C);
-        const int kblocks = a.ntaps * (a.C / bk);
-        for (int ks = 1; ks <= 9; ks++) {
-            if (kblocks % ks) continue;
-            s.ksplit = ks;
-            if (units() >= 2 * nsm) break;
+    const int bk = tc_pick_bk(a.C);
+    if (!bk) return best;
+    const int kblocks = a.ntaps * (a.C / bk);
+    const double T = (double)a.tg.conv_h * a.tg.conv_w;
+    double best_us = 1e30;
+    for (int ns = 1; ns <= a.N / 16; ns++) {
+        if (!valid_slice(ns)) continue;
+        const int Ns = a.N / ns;
+        for (int ks = 1; ks <= kblocks; ks++) {
+            if (kblocks % ks || (ns == 1 && ks == 1)) continue;
+            const long long units = (long long)a.tg.ntiles * ns * ks;
+            const long long waves = (units + nsm - 1) / nsm;
+            const double ksteps = (double)(kblocks / ks) * (bk / 16);
+            const double conv = waves * (ksteps * 250.0 * (Ns > 256 ? 1.6 : 1.0) + 1000.0 + 128.0 * Ns * 4 / 8) / 1900.0;
+            const double fin = 8.0 + (double)ks * T * a.N * 4 / 2.5e6;
+            if (conv + fin < best_us) {
+                best_us = conv + fin;
+                best.nsplit = ns;
+                best.ksplit = ks;
+            }
         }
     }
-    return s;
+    return best;
 }
 
 bool uses_partial(const ConvArgs &a, int mode, int nsm) {
@@ -334,7 +359,7 @@ bool uses_partial(const ConvArgs &a, int mode, int nsm) {
     // small K with enough tiles: one kernel with the LayerNorm epilogue beats split-K + finalize
     // (measured: 1x1 fc2, K = 160, 57 tiles at 1600x1152)
     if (a.ntaps * a.C <= 192 && a.tg.ntiles >= 32) return false;
-    Split s = split_policy(a, true, nsm);
+    Split s = split_policy(a, mode, nsm);
     return s.nsplit > 1 || s.ksplit > 1;
 }
 
@@ -353,7 +378,7 @@ size_t partial_floats(const DevNet &n, int H, int W, int nsm) {
     size_t need = 0;
     for (auto &l : layers) {
         if (!uses_partial(l.first, l.second, nsm)) continue;
-        Split s = split_policy(l.first, true, nsm);
+        Split s = split_policy(l.first, l.second, nsm);
         need = std::max(need, (size_t)s.ksplit * l.first.tg.conv_h * l.first.tg.conv_w * l.first.N);
     }
     return need;
@@ -423,7 +448,7 @@ int Worker::build_ops() {
         const bool partial = uses_partial(a, mode, nsm);
         int run_mode = mode;
         if (mode == EPI_PLAIN || partial) {
-            Split sp = split_policy(a, mode != EPI_PLAIN, nsm);
+            Split sp = split_policy(a, mode, nsm);
             a.nsplit = sp.nsplit;
             if (partial) {
                 a.ksplit = sp.ksplit;
