@@ -187,10 +187,21 @@ __global__ void __launch_bounds__(128) head_kernel(const HeadArgs a) {
     pdl_trigger();
 }
 
+// gc#88-92: x * (0.5 * (erf(x / 1.4142135381698608) + 1)).  erf by Abramowitz &
+// Stegun, Handbook of Mathematical Functions, formula 7.1.26: for z >= 0,
+// erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2), t = 1 / (1 + p z),
+// |error| <= 1.5e-7 (two orders below the fp16 rounding of the stored activation).
+// For x < 0 the factor 1 + erf(z) = e(z) = poly * exp(-z^2) is formed directly, so the
+// small negative tail carries no cancellation.
 __device__ __forceinline__ float gelu_exact(float v) {
-    // gc#88-92: x * (0.5 * (erf(x / 1.4142135381698608) + 1)); the division by
-    // sqrt(2) as a product with its reciprocal (within 1 ulp of the quotient)
-    return v * (0.5f * (erff(v * 0.70710678118654752f) + 1.0f));
+    const float z = fabsf(v) * 0.70710678118654752f;
+    const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+    float poly = fmaf(t, 1.061405429f, -1.453152027f);
+    poly = fmaf(poly, t, 1.421413741f);
+    poly = fmaf(poly, t, -0.284496736f);
+    poly = fmaf(poly, t, 0.254829592f);
+    const float e = poly * t * __expf(-z * z);        // 1 - erf(z)
+    return 0.5f * v * (v >= 0.0f ? 2.0f - e : e);
 }
 
 // out = shiftW(gelu(dw(in))): depthwise 3x3 (zero pad 1) + bias + exact GELU,
@@ -198,80 +209,96 @@ __device__ __forceinline__ float gelu_exact(float v) {
 // of pixel x goes to column x - off_g, and a source whose destination falls
 // outside the row writes the zero that its wrapped column must receive (each
 // output element is written exactly once).  A thread computes one 8-channel
-// chunk of two neighbouring pixels (x, x+1) from a shared 3 x 4 input window;
-// only the stores of chunks that straddle a group boundary split.  Grid (row
-// segments, y); the tap-major weights ([9][C] fp32) are staged in shared memory.
+// chunk of PX consecutive pixels (x..x+PX-1) from a 3 x (PX+2) input window; each
+// tap's eight weights are read once from shared memory (tap-major [9][C] fp32)
+// and serve all PX pixels (PX = 2 for the small layers, where parallelism counts,
+// 4 for the large ones, where one wave of 128-thread blocks must hold the layer).  Only the stores of chunks that straddle a group
+// boundary split.  A flat grid of 128-thread blocks over (row, quad, chunk): no
+// partly empty block per row, and seven blocks per SM hold a /8 layer in one wave.
 constexpr int kDwMaxC = 512;
 
-__device__ __forceinline__ void dw_acc8(float *acc, const uint4 raw, const float *wp) {
-    const float4 w0 = *reinterpret_cast<const float4 *>(wp), w1 = *reinterpret_cast<const float4 *>(wp + 4);
+__device__ __forceinline__ void unpack8f(const uint4 raw, float *f) {
     const __half2 *hv = reinterpret_cast<const __half2 *>(&raw);
-    const float2 f0 = __half22float2(hv[0]), f1 = __half22float2(hv[1]), f2 = __half22float2(hv[2]),
-                 f3 = __half22float2(hv[3]);
-    acc[0] = fmaf(w0.x, f0.x, acc[0]);
-    acc[1] = fmaf(w0.y, f0.y, acc[1]);
-    acc[2] = fmaf(w0.z, f1.x, acc[2]);
-    acc[3] = fmaf(w0.w, f1.y, acc[3]);
-    acc[4] = fmaf(w1.x, f2.x, acc[4]);
-    acc[5] = fmaf(w1.y, f2.y, acc[5]);
-    acc[6] = fmaf(w1.z, f3.x, acc[6]);
-    acc[7] = fmaf(w1.w, f3.y, acc[7]);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float2 t = __half22float2(hv[i]);
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
 }
 
-__global__ void __launch_bounds__(256) dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *wt,
+template <int PX>
+__global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *wt,
                                                             const float *b, const ShiftSpec s, __half *out) {
     pdl_wait();
-    __shared__ __align__(16) float ws[9 * kDwMaxC];
+    extern __shared__ __align__(16) float ws[];   // [9][C]
     for (int i = threadIdx.x * 4; i < 9 * C; i += blockDim.x * 4)
         *reinterpret_cast<float4 *>(ws + i) = __ldg(reinterpret_cast<const float4 *>(wt + i));
     __syncthreads();
     const int chunks = C >> 3;
-    const int Wp = (W + 1) >> 1;                       // pixel pairs per row
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    const int y = blockIdx.y;
-    if (t < Wp * chunks) {
-        const int xp = t / chunks, ch = t - xp * chunks;
-        const int x = 2 * xp, c0 = ch * 8;
-        float acc[2][8];
+    const int Wq = (W + PX - 1) / PX;                  // pixel groups per row
+    const int per_row = Wq * chunks;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int y = i / per_row, t = i - y * per_row;
+    if (y < H) {
+        const int xq = t / chunks, ch = t - xq * chunks;
+        const int x = PX * xq, c0 = ch * 8;
+        float acc[PX][8];
         {
             const float4 b0 = __ldg(reinterpret_cast<const float4 *>(b + c0));
             const float4 b1 = __ldg(reinterpret_cast<const float4 *>(b + c0 + 4));
             const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-            for (int k = 0; k < 8; k++) acc[0][k] = acc[1][k] = bv[k];
+            for (int p = 0; p < PX; p++)
+#pragma unroll
+                for (int k = 0; k < 8; k++) acc[p][k] = bv[k];
         }
         const __half *col = in + c0;
 #pragma unroll
         for (int ky = 0; ky < 3; ky++) {
             const int yy = y + ky - 1;
             if (yy < 0 || yy >= H) continue;
+            float w[3][8];
+#pragma unroll
+            for (int kx = 0; kx < 3; kx++) {
+                const float4 w0 = *reinterpret_cast<const float4 *>(ws + (ky * 3 + kx) * C + c0);
+                const float4 w1 = *reinterpret_cast<const float4 *>(ws + (ky * 3 + kx) * C + c0 + 4);
+                w[kx][0] = w0.x; w[kx][1] = w0.y; w[kx][2] = w0.z; w[kx][3] = w0.w;
+                w[kx][4] = w1.x; w[kx][5] = w1.y; w[kx][6] = w1.z; w[kx][7] = w1.w;
+            }
             const __half *rowp = col + (size_t)yy * W * C;
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int xx = x - 1 + j;             // pixel x uses columns x-1..x+1, pixel x+1 x..x+2
+            for (int j = 0; j < PX + 2; j++) {
+                const int xx = x - 1 + j;             // pixel x + p uses columns x + p - 1 .. x + p + 1
                 if (xx < 0 || xx >= W) continue;
-                const uint4 raw = *reinterpret_cast<const uint4 *>(rowp + (size_t)xx * C);
-                if (j < 3) dw_acc8(acc[0], raw, ws + (ky * 3 + j) * C + c0);
-                if (j > 0) dw_acc8(acc[1], raw, ws + (ky * 3 + j - 1) * C + c0);
+                float f[8];
+                unpack8f(*reinterpret_cast<const uint4 *>(rowp + (size_t)xx * C), f);
+#pragma unroll
+                for (int p = 0; p < PX; p++) {
+                    const int kx = j - p;
+                    if (kx < 0 || kx > 2) continue;
+#pragma unroll
+                    for (int k = 0; k < 8; k++) acc[p][k] = fmaf(w[kx][k], f[k], acc[p][k]);
+                }
             }
         }
         const int ga = shift_group(s, c0), gb = shift_group(s, c0 + 7);
         const int offa = ga >= 0 ? s.offs[ga] : 0, offb = gb >= 0 ? s.offs[gb] : 0;
         const int split = ga == gb ? 8 : s.ends[ga] - c0;   // channels [0, split) shift by offa, the rest offb
+        __half *rowo = out + (size_t)y * W * C + c0;
 #pragma unroll
-        for (int px = 0; px < 2; px++) {
-            if (x + px >= W) break;
+        for (int p = 0; p < PX; p++) {
+            if (x + p >= W) break;
             __align__(16) __half o[8];
 #pragma unroll
-            for (int k = 0; k < 8; k++) o[k] = __float2half_rn(gelu_exact(acc[px][k]));
+            for (int k = 0; k < 8; k++) o[k] = __float2half_rn(gelu_exact(acc[p][k]));
             bool za, zb;
-            const int da = shift_dest(x + px, offa, W, &za);
-            __half *rowo = out + (size_t)y * W * C + c0;
+            const int da = shift_dest(x + p, offa, W, &za);
             if (split == 8) {
                 if (za) *reinterpret_cast<uint4 *>(rowo + (size_t)da * C) = make_uint4(0, 0, 0, 0);
                 else *reinterpret_cast<uint4 *>(rowo + (size_t)da * C) = *reinterpret_cast<const uint4 *>(o);
             } else {
-                const int db = shift_dest(x + px, offb, W, &zb);
+                const int db = shift_dest(x + p, offb, W, &zb);
                 const __half zero = __float2half_rn(0.0f);
                 for (int k = 0; k < 8; k++) {
                     if (k < split) rowo[(size_t)da * C + k] = za ? zero : o[k];
@@ -680,8 +707,18 @@ int head_launch(const HeadArgs &a, cudaStream_t st) {
 int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *wt, const float *b, const ShiftSpec &s,
                          __half *out, cudaStream_t st) {
     if (C % 8 || C > kDwMaxC) return -2;
-    launch_pdl(dw_gelu_shift_kernel, dim3(grid_for((long long)((W + 1) / 2) * (C / 8), 256), H), dim3(256), 0, st, in, H,
-               W, C, wt, b, s, out);
+    static const int nsm = [] {
+        int d = 0, n = 148;
+        if (cudaGetDevice(&d) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+        return n;
+    }();
+    const int blocks2 = grid_for((long long)((W + 1) / 2) * (C / 8) * H, 128);
+    const size_t smem = (size_t)9 * C * sizeof(float);
+    if (blocks2 <= 7 * nsm)
+        launch_pdl(dw_gelu_shift_kernel<2>, dim3(blocks2), dim3(128), smem, st, in, H, W, C, wt, b, s, out);
+    else
+        launch_pdl(dw_gelu_shift_kernel<4>, dim3(grid_for((long long)((W + 3) / 4) * (C / 8) * H, 128)), dim3(128), smem,
+                   st, in, H, W, C, wt, b, s, out);
     return launch_status();
 }
 
