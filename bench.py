@@ -10,7 +10,9 @@ scaling "weak").  Prints ONE JSON line on rank 0:
             between steps, max over ranks;
   e2e       the same metric through the public API (GcdrEnhancer.enhance on
             host numpy buffers: strided copy to pinned staging, H2D, graph,
-            D2H, copy out), wall clock around synchronous calls, max over ranks;
+            D2H, copy out), called from E2E_THREADS host threads sharing one
+            enhancer (its worker pool), wall clock, max over ranks; plus the
+            single-thread milliseconds per image (the API's latency);
   roofline  of the dominant kernel from a live per-op profile (CUDA events),
             against MEASURED_PEAKS.json;
   cpu_baseline  the CPU oracle (C restatement of the reference's CPU path) on
@@ -42,6 +44,7 @@ WORKLOAD = "enhance 1600x1152 Bgr24 synthetic documents (config-0 generator), on
 
 
 TRAFFIC_TABLE = os.path.join(ROOT, "profiles", "ncu_traffic_1600x1152.md")
+E2E_THREADS = 3   # concurrent GcdrEnhancer.enhance callers of the end-to-end measurement
 
 
 def ncu_traffic(op: str):
@@ -328,20 +331,38 @@ def main():
     value = whole_job_rate(world, args.steps, total_ms / 1000.0)
     clocks = clk.summary()
 
-    # end to end through the public API (host buffers, synchronous calls)
+    # end to end through the public API (host buffers): E2E_THREADS host threads call
+    # GcdrEnhancer.enhance concurrently, as a server shares one enhancer (its worker pool
+    # rents each caller a worker: one image's host copies overlap another's kernels);
+    # step i is image i, taken by thread i % E2E_THREADS
     enh = GcdrEnhancer.from_files(GC, DR, device=local)
-    host_dst = np.empty(nbytes, np.uint8)
-    for i in range(args.warmup):
-        enh.enhance(imgs[i % n_img], W_IMG, H_IMG, W_IMG * 3, host_dst, W_IMG * 3, 0)
+    host_dst = [np.empty(nbytes, np.uint8) for _ in range(E2E_THREADS)]
+
+    def e2e_part(k: int, steps: int):
+        for i in range(k, steps, E2E_THREADS):
+            enh.enhance(imgs[i % n_img], W_IMG, H_IMG, W_IMG * 3, host_dst[k], W_IMG * 3, 0)
+
+    def e2e_run(steps: int):
+        th = [threading.Thread(target=e2e_part, args=(k, steps)) for k in range(E2E_THREADS)]
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+
+    e2e_run(max(args.warmup, E2E_THREADS))    # every thread's worker is created and its graph captured
     barrier()
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
-    for i in range(args.steps):
-        enh.enhance(imgs[i % n_img], W_IMG, H_IMG, W_IMG * 3, host_dst, W_IMG * 3, 0)
+    e2e_run(args.steps)
     torch.cuda.synchronize(dev)
     e2e_s = max_over_ranks(time.perf_counter() - t0, dist, dev)
     barrier()
     e2e_value = whole_job_rate(world, args.steps, e2e_s)
+    # the same calls from one thread: the single-image latency of the API
+    t0 = time.perf_counter()
+    for i in range(min(args.steps, 10)):
+        enh.enhance(imgs[i % n_img], W_IMG, H_IMG, W_IMG * 3, host_dst[0], W_IMG * 3, 0)
+    e2e_single_ms = (time.perf_counter() - t0) * 1000.0 / min(args.steps, 10)
 
     # live per-op profile -> dominant kernel roofline
     prof = worker.profile(reps=3)
@@ -381,7 +402,8 @@ def main():
                        "l2": "256 MB flush between timed steps (outside the events)",
                        "precision": "fp16 tensor-core layers (fp32 accumulate), fp32 stem/head/div6"},
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": nbytes,
-                    "d2h_bytes_per_step": nbytes, "api": "GcdrEnhancer.enhance (host numpy buffers)"},
+                    "d2h_bytes_per_step": nbytes, "api": "GcdrEnhancer.enhance (host numpy buffers)",
+                    "host_threads": E2E_THREADS, "single_thread_ms_per_image": e2e_single_ms},
             "roofline": {"kernel": name, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak, "traffic": ncu_traffic(name),
                          "traffic_source": os.path.relpath(TRAFFIC_TABLE, ROOT), "peak_source": peak_src,
