@@ -43,7 +43,6 @@ constexpr int kProducer2Warp = 1 + kMmaWarps + kEpiWarps;     // the second TMA 
 
 struct TcShared {
     uint64_t full[kMaxStages], empty[kMaxStages], tfull[2], tempty[2];
-    float xchg[4][64];                 // LayerNorm row halves: partial sums per lane quadrant
     uint32_t tmem_base;
     int abort_flag;
     int issued[2], consumed;
@@ -59,6 +58,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     TcShared *sh = reinterpret_cast<TcShared *>(ring + (size_t)cfg.stages * cfg.stage_bytes);
+    constexpr bool kLnUnits = MODE == EPI_LN2 || MODE == EPI_RESLN;   // whole rows, units split by buffer
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const TileGeom &tg = args.tg;
@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&sh->tfull[b], (uint32_t)nacc);
-            mbar_init(&sh->tempty[b], kEpiWarps);
+            mbar_init(&sh->tempty[b], kLnUnits ? kEpiWarps / 2 : kEpiWarps);
         }
         sh->abort_flag = 0;
         sh->issued[0] = sh->issued[1] = 0;
@@ -199,20 +199,32 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const uint32_t lane_base = tmem_base + ((uint32_t)(quad * 32) << 16);
         int t = 0;
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, t++) {
+            // LayerNorm modes: each set of four warps (one per lane quadrant) takes the units
+            // of one accumulator buffer, one whole row per thread
+            if (kLnUnits && (cfg.acc_bufs == 2 ? (t & 1) : 0) != part) continue;
             int mu, ni, ki;
             unit_coords(args, u, mu, ni, ki);
             const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
             const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
             bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err);
-            // all epilogue warps leave together (bar.red.or over their threads)
+            // the warps sharing this unit leave together (bar.red.or over their threads)
             uint32_t bad;
-            asm volatile(
-                "{\n\t.reg .pred p, q;\n\t"
-                "setp.eq.u32 p, %1, 0;\n\t"
-                "bar.red.or.pred q, 2, %2, p;\n\t"
-                "selp.u32 %0, 1, 0, q;\n\t}"
-                : "=r"(bad)
-                : "r"((uint32_t)ok), "n"(kEpiWarps * 32));
+            if (kLnUnits)
+                asm volatile(
+                    "{\n\t.reg .pred p, q;\n\t"
+                    "setp.eq.u32 p, %1, 0;\n\t"
+                    "bar.red.or.pred q, %2, %3, p;\n\t"
+                    "selp.u32 %0, 1, 0, q;\n\t}"
+                    : "=r"(bad)
+                    : "r"((uint32_t)ok), "r"(3 + part), "n"(kEpiWarps / 2 * 32));
+            else
+                asm volatile(
+                    "{\n\t.reg .pred p, q;\n\t"
+                    "setp.eq.u32 p, %1, 0;\n\t"
+                    "bar.red.or.pred q, 2, %2, p;\n\t"
+                    "selp.u32 %0, 1, 0, q;\n\t}"
+                    : "=r"(bad)
+                    : "r"((uint32_t)ok), "n"(kEpiWarps * 32));
             if (bad) break;
             tc_fence_after();
             const uint32_t acc0 = lane_base + (uint32_t)(ab * nst * cfg.acc_cols);
@@ -223,13 +235,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                     TmemLoader bot{acc0 + (uint32_t)((cfg.rt + i) * cfg.acc_cols)};
                     epilogue_pool(args.ep, tg, y2, x0 + 128 * i + row, ni * Ns, Ns, top, bot, part, 2);
                 }
-            } else if (MODE == EPI_LN2 || MODE == EPI_RESLN) {
-                // whole LayerNorm rows: the two warps of a lane quadrant take half of the columns each
+            } else if (kLnUnits) {
                 for (int i = 0; i < cfg.rt; i++) {
                     const int tile = mu * cfg.rt + i;
                     if (tile >= tg.ntiles) break;
                     TmemLoader ld{acc0 + (uint32_t)(i * cfg.acc_cols)};
-                    epilogue_ln_split<MODE>(args.ep, tg, tile, row, N, ld, part, lane, sh->xchg[quad], 3 + quad);
+                    epilogue_ln_row<MODE>(args.ep, tg, tile, row, N, ld);
                 }
             } else {
                 for (int i = 0; i < cfg.rt; i++) {

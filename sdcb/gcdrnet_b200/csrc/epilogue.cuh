@@ -230,90 +230,72 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     }
 }
 
-// Sum of the two halves of a row held by a pair of warps (same lanes, parts 0/1):
-// exchanged through `xchg` (64 floats) under the pair's named barrier; both sides
-// add in the same order (part 0's half first).
-__device__ __forceinline__ float pair_sum(float v, float *xchg, int part, int lane, int bar_id) {
-    xchg[part * 32 + lane] = v;
-    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-    const float o = xchg[(part ^ 1) * 32 + lane];
-    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-    return part == 0 ? v + o : o + v;
-}
-
-// LayerNorm modes (EPI_LN2, EPI_RESLN) with the row split between two warps of a
-// TMEM lane quadrant (`part` 0/1 own column chunks [part*N/2, (part+1)*N/2)):
-// exact two-pass statistics, each pass's partial sums exchanged by pair_sum.
+// LayerNorm modes (EPI_LN2, EPI_RESLN) with one whole row per thread (the four warps
+// of one set of TMEM lane quadrants own the unit).  Exact two-pass statistics without a
+// second read of the residual: the first pass writes t = acc + bias (+ res) back into
+// the row's TMEM columns, and LN2 runs its two passes over the LN1 output, written back
+// the same way.  Warp-collective (TMEM); stores are masked.
 template <int MODE, class L>
-__device__ void epilogue_ln_split(const EpiParams &ep, const TileGeom &tg, int tile, int row, int N, L &ld, int part,
-                                  int lane, float *xchg, int bar_id) {
+__device__ void epilogue_ln_row(const EpiParams &ep, const TileGeom &tg, int tile, int row, int N, L &ld) {
     float v[32];
-    const int cw = ((N / 2) % 32 == 0) ? 32 : 16;
-    const int cbeg = part * (N / 2), cend = cbeg + N / 2;
     const long long q = (long long)tile * 128 + row;
     const int y = (int)(q / tg.pitch), x = (int)(q - (long long)y * tg.pitch);
     const bool valid = y < tg.conv_h && x < tg.conv_w;
     const long long tok = valid ? (long long)y * tg.conv_w + x : 0;
-    const bool use_res = MODE == EPI_RESLN;
     float s = 0.f;
-    for (int c0 = cbeg; c0 < cend; c0 += cw) {
-        row_vals(ld, ep, N, tok, use_res, c0, cw, v);
+    for (int c0 = 0; c0 < N; c0 += 32) {
+        row_vals(ld, ep, N, tok, MODE == EPI_RESLN, c0, 32, v);
 #pragma unroll
-        for (int k = 0; k < 32; k++)
-            if (k < cw) s += v[k];
+        for (int k = 0; k < 32; k++) s += v[k];
+        ld.store32(c0, v);
     }
-    const float mean = pair_sum(s, xchg, part, lane, bar_id) / N;
+    L::wait_st();
+    const float mean = s / N;
     float sq = 0.f;
-    for (int c0 = cbeg; c0 < cend; c0 += cw) {
-        row_vals(ld, ep, N, tok, use_res, c0, cw, v);
+    for (int c0 = 0; c0 < N; c0 += 32) {
+        ld.load32(c0, v);
 #pragma unroll
-        for (int k = 0; k < 32; k++)
-            if (k < cw) {
-                const float d = v[k] - mean;
-                sq += d * d;
-            }
+        for (int k = 0; k < 32; k++) {
+            const float d = v[k] - mean;
+            sq += d * d;
+        }
     }
-    const float rstd = rsqrtf(pair_sum(sq, xchg, part, lane, bar_id) / N + ep.eps1);
+    const float rstd = rsqrtf(sq / N + ep.eps1);
     float s2 = 0.f;
-    for (int c0 = cbeg; c0 < cend; c0 += cw) {
-        row_vals(ld, ep, N, tok, use_res, c0, cw, v);
+    for (int c0 = 0; c0 < N; c0 += 32) {
+        ld.load32(c0, v);
         __align__(16) __half h[32];
 #pragma unroll
-        for (int k = 0; k < 32; k++)
-            if (k < cw) {
-                const float t = (v[k] - mean) * rstd * ep.g1[c0 + k] + ep.b1[c0 + k];
-                s2 += t;
-                h[k] = __float2half_rn(t);
-            }
-        if (valid) act_store(ep.out, y, x, c0, h, cw);
+        for (int k = 0; k < 32; k++) {
+            const float t = (v[k] - mean) * rstd * ep.g1[c0 + k] + ep.b1[c0 + k];
+            s2 += t;
+            h[k] = __float2half_rn(t);
+            v[k] = t;
+        }
+        if (valid) act_store(ep.out, y, x, c0, h, 32);
+        if (MODE == EPI_LN2) ld.store32(c0, v);
     }
     if (MODE == EPI_RESLN) return;
     // EPI_LN2: LN2 over the fp32 LN1 outputs, then the H-shift scatter
-    const float mean2 = pair_sum(s2, xchg, part, lane, bar_id) / N;
+    L::wait_st();
+    const float mean2 = s2 / N;
     float q2 = 0.f;
-    for (int c0 = cbeg; c0 < cend; c0 += cw) {
-        row_vals(ld, ep, N, tok, false, c0, cw, v);
+    for (int c0 = 0; c0 < N; c0 += 32) {
+        ld.load32(c0, v);
 #pragma unroll
-        for (int k = 0; k < 32; k++)
-            if (k < cw) {
-                const float d = (v[k] - mean) * rstd * ep.g1[c0 + k] + ep.b1[c0 + k] - mean2;
-                q2 += d * d;
-            }
+        for (int k = 0; k < 32; k++) {
+            const float d = v[k] - mean2;
+            q2 += d * d;
+        }
     }
-    const float rstd2 = rsqrtf(pair_sum(q2, xchg, part, lane, bar_id) / N + ep.eps2);
-    for (int c0 = cbeg; c0 < cend; c0 += cw) {
-        row_vals(ld, ep, N, tok, false, c0, cw, v);
+    const float rstd2 = rsqrtf(q2 / N + ep.eps2);
+    for (int c0 = 0; c0 < N; c0 += 32) {
+        ld.load32(c0, v);
         if (valid) {
-            float o[32];
-#pragma unroll
-            for (int k = 0; k < 32; k++)
-                if (k < cw) {
-                    const float t = (v[k] - mean) * rstd * ep.g1[c0 + k] + ep.b1[c0 + k];
-                    o[k] = (t - mean2) * rstd2 * ep.g2[c0 + k] + ep.b2[c0 + k];
-                }
 #pragma unroll
             for (int k = 0; k < 32; k += 2)
-                if (k < cw) shift_store2(ep.out2, ep.shift, 2, y, x, c0 + k, o[k], o[k + 1]);
+                shift_store2(ep.out2, ep.shift, 2, y, x, c0 + k, (v[k] - mean2) * rstd2 * ep.g2[c0 + k] + ep.b2[c0 + k],
+                             (v[k + 1] - mean2) * rstd2 * ep.g2[c0 + k + 1] + ep.b2[c0 + k + 1]);
         }
     }
 }
