@@ -285,31 +285,30 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-
-bool get_encoder(std::string &err) {
-    if (g_encode) return true;
-    cudaDriverEntryPointQueryResult q;
-    void *fn = nullptr;
-    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
-        err = "cuTensorMapEncodeTiled not available";
-        return false;
-    }
-    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    return true;
+// The driver entry point, looked up once (thread-safe: workers plan concurrently).
+PFN_cuTensorMapEncodeTiled_v12000 get_encoder(std::string &err) {
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        cudaDriverEntryPointQueryResult q;
+        void *f = nullptr;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q);
+        return (e == cudaSuccess && q == cudaDriverEntryPointSuccess) ? reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f)
+                                                                        : nullptr;
+    }();
+    if (!fn) err = "cuTensorMapEncodeTiled not available";
+    return fn;
 }
 
 bool encode_2d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint32_t box_inner,
                uint32_t box_outer, int bk, std::string &err) {
-    if (!get_encoder(err)) return false;
+    const auto encode = get_encoder(err);
+    if (!encode) return false;
     cuuint64_t dims[2] = {inner, outer};
     cuuint64_t strides[1] = {inner * 2};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t es[2] = {1, 1};
     CUtensorMapSwizzle sw = bk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : bk == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
                                                                              : CU_TENSOR_MAP_SWIZZLE_32B;
-    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+    CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
@@ -362,13 +361,14 @@ int fill_bias_consts(ConvArgs &a) {
 // of (b0, b1, b2); out-of-range elements of a box read as zero
 bool tma_encode_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1,
                    uint32_t b2, std::string &err) {
-    if (!get_encoder(err)) return false;
+    const auto encode = get_encoder(err);
+    if (!encode) return false;
     if (d0 * 2 != 32 && d0 * 2 != 64) { err = "tma 3d: inner extent must be 32 or 64 bytes"; return false; }
     cuuint64_t dims[3] = {d0, d1, d2};
     cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
     cuuint32_t box[3] = {b0, b1, b2};
     cuuint32_t es[3] = {1, 1, 1};
-    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+    CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, d0 * 2 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
