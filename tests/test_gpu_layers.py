@@ -36,6 +36,9 @@ CASES = [
     (0, 256, 320, 16, 16, 0),   # dec5-like, 4 tiles per work unit
     (0, 128, 200, 32, 32, 0),   # 2 tiles per work unit
     (0, 96, 150, 64, 64, 2),    # thin layer + relu
+    # 256-wide plain slices over several tiles
+    (3, 24, 30, 128, 256, 2),   # 6 tiles, zero pad + relu (microbench form)
+    (0, 10, 37, 64, 256, 0),    # odd tile count
     # row-window kernel edges: 4 rows per unit with a ragged last unit (rows past the
     # image), odd pooled-row count, segments past the right edge, zero padding
     (0, 150, 1100, 16, 32, 1),
