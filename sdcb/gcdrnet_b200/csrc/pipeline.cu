@@ -2,6 +2,7 @@
 // DR-Net, CUDA-graph capture and the worker's enhance entry points.
 #include "pipeline.h"
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 
@@ -158,6 +159,10 @@ Worker::~Worker() {
     if (h_src_) cudaFreeHost(h_src_);
     if (h_dst_) cudaFreeHost(h_dst_);
     if (h_err_) cudaFreeHost(h_err_);
+    pool_.reset();
+    if (flag_ev_) cudaEventDestroy(flag_ev_);
+    for (auto &e : band_ev_)
+        if (e) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -174,6 +179,10 @@ int Worker::init(std::string &err) {
     num_sms_ = prop.multiProcessorCount;
     if (cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking) != cudaSuccess) { err = "stream"; return GCDR_ERR_DEVICE; }
     if (cudaMallocHost(&h_err_, sizeof(int)) != cudaSuccess) { err = "pinned alloc"; return GCDR_ERR_OOM; }
+    if (cudaEventCreateWithFlags(&flag_ev_, cudaEventDisableTiming) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
+    for (auto &e : band_ev_)
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
+    pool_ = std::make_unique<HostPool>(kHostBands - 1, device_);
     const char *g = std::getenv("GCDR_CUDA_GRAPH");
     use_graph_ = !(g && g[0] == '0');
     const char *sv = std::getenv("GCDR_CUDA_STEM");   // "simt": fp32 SIMT stem/head kernels
@@ -754,23 +763,65 @@ int Worker::enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8
     int rc = bind(w, h, fmt);
     if (rc) return rc;
     const size_t row = (size_t)w * bpp_, img = row * h;
-    if ((size_t)src_stride == row) std::memcpy(h_src_, src, img);
-    else
-        for (int y = 0; y < h; y++) std::memcpy(h_src_ + y * row, src + (size_t)y * src_stride, row);
-    cudaError_t e = cudaMemcpyAsync(d_src_, h_src_, img, cudaMemcpyHostToDevice, stream_);
-    if (e == cudaSuccess) {
-        if (exec_) {
-            if (cudaGraphLaunch(exec_, stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "graph launch failed");
-        } else if ((rc = run_ops(stream_))) return rc;
-        e = cudaMemcpyAsync(h_dst_, d_dst_, img, cudaMemcpyDeviceToHost, stream_);
+    auto band = [&](int b, int &y0, int &y1) {
+        y0 = (int)((long long)h * b / kHostBands);
+        y1 = (int)((long long)h * (b + 1) / kHostBands);
+    };
+    // stage and upload: band b's H2D is enqueued by whichever thread staged it (the bands are
+    // disjoint, so their order on the stream does not matter); the graph follows them all
+    std::atomic<int> up_fail{0};
+    pool_->run(kHostBands, [&](int b) {
+        int y0, y1;
+        band(b, y0, y1);
+        uint8_t *stage = h_src_ + (size_t)y0 * row;
+        if ((size_t)src_stride == row) std::memcpy(stage, src + (size_t)y0 * row, (size_t)(y1 - y0) * row);
+        else
+            for (int y = y0; y < y1; y++) std::memcpy(h_src_ + (size_t)y * row, src + (size_t)y * src_stride, row);
+        if (cudaMemcpyAsync(d_src_ + (size_t)y0 * row, stage, (size_t)(y1 - y0) * row, cudaMemcpyHostToDevice, stream_) !=
+            cudaSuccess)
+            up_fail = 1;
+    });
+    if (up_fail) return fail(GCDR_ERR_DEVICE, "H2D copy failed");
+    if (exec_) {
+        if (cudaGraphLaunch(exec_, stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "graph launch failed");
+    } else if ((rc = run_ops(stream_))) return rc;
+    cudaError_t e = cudaMemcpyAsync(h_err_, d_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_);
+    if (e == cudaSuccess) e = cudaEventRecord(flag_ev_, stream_);
+    for (int b = 0; b < kHostBands && e == cudaSuccess; b++) {
+        int y0, y1;
+        band(b, y0, y1);
+        e = cudaMemcpyAsync(h_dst_ + (size_t)y0 * row, d_dst_ + (size_t)y0 * row, (size_t)(y1 - y0) * row,
+                            cudaMemcpyDeviceToHost, stream_);
+        if (e == cudaSuccess) e = cudaEventRecord(band_ev_[b], stream_);
     }
-    if (e == cudaSuccess) e = cudaMemcpyAsync(h_err_, d_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
-    if (e != cudaSuccess) return fail(GCDR_ERR_DEVICE, std::string("CUDA error: ") + cudaGetErrorString(e));
-    if ((rc = check_err_flag())) return rc;
-    if ((size_t)dst_stride == row) std::memcpy(dst, h_dst_, img);
-    else
-        for (int y = 0; y < h; y++) std::memcpy(dst + (size_t)y * dst_stride, h_dst_ + y * row, row);
+    if (e == cudaSuccess) e = cudaEventSynchronize(flag_ev_);
+    if (e != cudaSuccess) {
+        cudaStreamSynchronize(stream_);
+        return fail(GCDR_ERR_DEVICE, std::string("CUDA error: ") + cudaGetErrorString(e));
+    }
+    // the caller's buffer is written only after a clean device flag: dst may alias src, and a
+    // device error is retried on a fresh worker from the same src
+    if ((rc = check_err_flag())) {
+        cudaStreamSynchronize(stream_);
+        return rc;
+    }
+    std::atomic<int> down_fail{0};
+    pool_->run(kHostBands, [&](int b) {
+        int y0, y1;
+        band(b, y0, y1);
+        if (cudaEventSynchronize(band_ev_[b]) != cudaSuccess) {
+            down_fail = 1;
+            return;
+        }
+        const uint8_t *stage = h_dst_ + (size_t)y0 * row;
+        if ((size_t)dst_stride == row) std::memcpy(dst + (size_t)y0 * row, stage, (size_t)(y1 - y0) * row);
+        else
+            for (int y = y0; y < y1; y++) std::memcpy(dst + (size_t)y * dst_stride, h_dst_ + (size_t)y * row, row);
+    });
+    if (down_fail) {
+        cudaStreamSynchronize(stream_);
+        return fail(GCDR_ERR_DEVICE, "D2H copy failed");
+    }
     return GCDR_OK;
 }
 

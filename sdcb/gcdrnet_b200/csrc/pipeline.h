@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "host_pool.h"
 #include "model.h"
 
 namespace gcdr {
@@ -112,10 +113,15 @@ private:
     float *ws_ = nullptr;   // split-K partial sums (EPI_PARTIAL), shared by both nets
     uint8_t *d_src_ = nullptr, *d_dst_ = nullptr;
     int *d_err_ = nullptr;
-    // pinned staging
+    // pinned staging, copied in kHostBands row bands by the caller and pool_'s helpers: each
+    // band's H2D is issued as soon as it is staged; after the graph, the error flag comes back
+    // first (flag_ev_), then each band (band_ev_) is copied out as soon as its D2H lands
+    static constexpr int kHostBands = 4;
     uint8_t *h_src_ = nullptr, *h_dst_ = nullptr;
     int *h_err_ = nullptr;
     size_t pin_bytes_ = 0;
+    std::unique_ptr<HostPool> pool_;
+    cudaEvent_t flag_ev_ = nullptr, band_ev_[kHostBands] = {};
     // ops and graph
     std::vector<std::function<int(cudaStream_t)>> ops_;
     std::vector<OpInfo> info_;
