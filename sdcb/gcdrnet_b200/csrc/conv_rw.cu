@@ -256,7 +256,10 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
                     for (int q = part; q < R / 2; q += Roles::parts) {
                         TmemLoader l0{acc0 + (uint32_t)(2 * q * cfg.acc_cols)};
                         TmemLoader l1{acc0 + (uint32_t)((2 * q + 1) * cfg.acc_cols)};
-                        epilogue_head_pair<HC>(args.ep, tg, y0 + 2 * q, x, l0, l1, win, y0 / 2 - 1, x0 / 2 - 1);
+                        const uint8_t *segs = ring + (size_t)hs * cfg.stage_bytes;
+                        epilogue_head_pair<HC>(args.ep, tg, y0 + 2 * q, x, l0, l1, win, y0 / 2 - 1, x0 / 2 - 1,
+                                               segs + (size_t)(2 * q + 1) * cfg.seg_bytes,
+                                               segs + (size_t)(2 * q + 2) * cfg.seg_bytes, row + 1);
                     }
                 }
                 __syncwarp();

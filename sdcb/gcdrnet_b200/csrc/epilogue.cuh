@@ -340,11 +340,11 @@ __device__ __forceinline__ uint4 head_win_ld(const uint8_t *win, int r, int c, i
 __device__ __forceinline__ float sigmoid_fast(float v) { return __fdividef(1.0f, 1.0f + __expf(-v)); }
 
 // The per-pixel tail of the head: div6 into the DR stem input (GC) or the u8 output (DR).
-__device__ __forceinline__ void head_store(const HeadParams &hp, int W, int y, int x, const float *o) {
+// xin: the pixel's first 8 stem-input channels (GC: the u8 image in channels 0-2).
+__device__ __forceinline__ void head_store(const HeadParams &hp, int W, int y, int x, const float *o, const uint4 xin) {
     const size_t pix = (size_t)y * W + x;
     if (!hp.is_dr) {
         // div6: r = clamp(x / max(I_sm, 1e-6), 0, 1) with x = u8 / 255, written as the DR stem input
-        const uint4 xin = *reinterpret_cast<const uint4 *>(hp.si_in.p + hp.si_in.row(y, x) * kStemInC);
         const __half *xu = reinterpret_cast<const __half *>(&xin);
         __align__(16) __half v[kStemInC];
 #pragma unroll
@@ -400,9 +400,13 @@ __device__ __forceinline__ void head_store(const HeadParams &hp, int W, int y, i
 // middle dec5 row of their x2 bilinear (half_pixel, edge clamp: ONNX Resize linear),
 // so six window columns serve both pixels.  win holds dec5 rows wy0.. and columns
 // wx0.. (window origin, may be -1).  Warp-collective (the TMEM loads); stores are masked.
+// segs: the unit's stem-input row segments in the same ring stage (segment r = padded row
+// y0 + r, pixel slot p = padded column x0 + p, 32-byte rows under the 32B swizzle), where the
+// GC tail finds its pixels' u8 values (segments jj + 1, jj + 2, slot x - x0 + 1).
 template <int C1, class L>
 __device__ void epilogue_head_pair(const EpiParams &ep, const TileGeom &tg, int y, int x, L &ld0, L &ld1,
-                                   const uint8_t *win, int wy0, int wx0) {
+                                   const uint8_t *win, int wy0, int wx0, const uint8_t *seg0, const uint8_t *seg1,
+                                   int slot) {
     const HeadParams &hp = ep.head;
     // the TMEM loads below are warp-collective: a warp leaves only as a whole; lanes past
     // the image edge compute on in-window data and store nothing
@@ -472,8 +476,16 @@ __device__ void epilogue_head_pair(const EpiParams &ep, const TileGeom &tg, int 
     const float oa[3] = {sigmoid_fast(oa0), sigmoid_fast(oa1), sigmoid_fast(oa2)};
     const float ob[3] = {sigmoid_fast(ob0), sigmoid_fast(ob1), sigmoid_fast(ob2)};
     if (valid) {
-        head_store(hp, tg.conv_w, y, x, oa);
-        head_store(hp, tg.conv_w, y + 1, x, ob);
+        uint4 xa = make_uint4(0, 0, 0, 0), xb = xa;
+        if (!hp.is_dr) {
+            // channels 0-7 of the pixel: 16-byte chunk 0 of its 32-byte row, at chunk 0 ^ address bit 7
+            const uint32_t off = (uint32_t)slot * 32u;
+            const uint32_t sw = ((off >> 7) & 1u) << 4;
+            xa = *reinterpret_cast<const uint4 *>(seg0 + (off ^ sw));
+            xb = *reinterpret_cast<const uint4 *>(seg1 + (off ^ sw));
+        }
+        head_store(hp, tg.conv_w, y, x, oa, xa);
+        head_store(hp, tg.conv_w, y + 1, x, ob, xb);
     }
 }
 
