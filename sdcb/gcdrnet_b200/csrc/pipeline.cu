@@ -762,7 +762,7 @@ int Worker::enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8
     if (cudaSetDevice(device_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "cudaSetDevice");
     int rc = bind(w, h, fmt);
     if (rc) return rc;
-    const size_t row = (size_t)w * bpp_, img = row * h;
+    const size_t row = (size_t)w * bpp_;
     auto band = [&](int b, int &y0, int &y1) {
         y0 = (int)((long long)h * b / kHostBands);
         y1 = (int)((long long)h * (b + 1) / kHostBands);
