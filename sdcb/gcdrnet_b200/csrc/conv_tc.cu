@@ -37,7 +37,7 @@ namespace {
 
 constexpr int kMmaWarps = 4;
 constexpr int kEpiWarps = 8;
-constexpr int kTcSmemCap = 176 * 1024;   // the ring budget below plus the barriers and alignment
+constexpr int kTcSmemCap = 200 * 1024;   // the ring budget below plus the barriers and alignment
 constexpr int kConvThreads = (2 + kMmaWarps + kEpiWarps) * 32;
 constexpr int kProducer2Warp = 1 + kMmaWarps + kEpiWarps;     // the second TMA producer
 
@@ -411,9 +411,9 @@ int tc_plan(const ConvArgs &a, int num_sms, TcConfig &cfg, std::string &err) {
     }
     const int nst = a.tg.pool ? 2 * cfg.rt : cfg.rt;
     cfg.sub_bytes = (128 * nst * bk * 2 + Ns * bk * 2 + 1023) & ~1023;
-    // at most ~176 KB per CTA: deep enough for every layer here, with room to spare
-    // below the 227 KB limit (a profiler attached to the process may claim some)
-    const int budget = 176 * 1024 - (int)sizeof(TcShared) - 1024;
+    // at most ~200 KB per CTA (below the 227 KB limit): one stage more than 176 KB for the
+    // 256-wide layers, which measured ~1.5 % faster over the whole enhancement
+    const int budget = kTcSmemCap - (int)sizeof(TcShared) - 1024;
     // several k-blocks per stage when they are small (few channels per tap): one
     // barrier round trip and one commit per stage instead of per k-block
     const int kb_unit = a.ntaps * (a.C / bk) / a.ksplit;
