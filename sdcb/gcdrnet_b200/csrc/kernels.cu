@@ -614,9 +614,10 @@ __global__ void nhwc2bgr_kernel(const float *y, int W, int ph, int pw, uint8_t *
     if (bpp == 4) d[3] = al;
 }
 
-__global__ void stem_in_kernel(const ImgSpec im, Act si) {
+__global__ void stem_in_kernel(const ImgSpec im, Act si, int *err) {
     pdl_wait();
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx == 0 && err) *err = 0;   // the enhancement's first kernel clears the device error word
     if (idx >= (long long)si.H * si.W) return;
     const int y = (int)(idx / si.W), x = (int)(idx - (long long)y * si.W);
     const int sy = max(y - im.ph, 0), sx = max(x - im.pw, 0);
@@ -650,9 +651,9 @@ bool pdl_enabled() {
     return on;
 }
 
-int stem_in_launch(const ImgSpec &im, const Act &si, cudaStream_t st) {
+int stem_in_launch(const ImgSpec &im, const Act &si, int *err, cudaStream_t st) {
     if (si.C != 16 || si.kind != LAY_PADREFL) return -2;
-    if (launch_pdl(stem_in_kernel, dim3(grid_for((long long)si.H * si.W, 256)), dim3(256), 0, st, im, si) != cudaSuccess)
+    if (launch_pdl(stem_in_kernel, dim3(grid_for((long long)si.H * si.W, 256)), dim3(256), 0, st, im, si, err) != cudaSuccess)
         return launch_status();
     return launch_status();
 }

@@ -49,7 +49,8 @@ int head_launch(const HeadArgs &a, cudaStream_t st);
 // The GC stem input (the stem-input layout of epilogue.cuh, LAY_PADREFL
 // [H+2][W+2][16] fp16): [x, x, 0] with x the u8 pixel of the top/left
 // replicate-padded source in B,G,R order (GcdrEnhancer.cs:242-243 pads and reads it).
-int stem_in_launch(const ImgSpec &im, const Act &si, cudaStream_t st);
+// err (may be null): the device error word, cleared by the kernel (the enhancement's first)
+int stem_in_launch(const ImgSpec &im, const Act &si, int *err, cudaStream_t st);
 // CUDA error string of this thread's last failed launch of the kernels above.
 const char *last_launch_error();
 // Stem conv weights for that layout: ONNX [C1][Cin][3][3] -> [C1][9 taps][16]

@@ -508,9 +508,12 @@ int Worker::build_ops() {
                                    0});
         }
     };
-    ops_.push_back([errp](cudaStream_t st) { return cudaMemsetAsync(errp, 0, sizeof(int), st) == cudaSuccess ? 0 : GCDR_ERR_DEVICE; });
     info_.clear();
-    info_.push_back(OpInfo{"reset_error_flag", 0, 4, 0});
+    if (simt_stem_) {
+        // the first kernel of the tensor-core path (stem_in) clears the device error word itself
+        ops_.push_back([errp](cudaStream_t st) { return cudaMemsetAsync(errp, 0, sizeof(int), st) == cudaSuccess ? 0 : GCDR_ERR_DEVICE; });
+        info_.push_back(OpInfo{"reset_error_flag", 0, 4, 0});
+    }
     auto simt = [this](const std::string &name, double flops, double bytes) { info_.push_back(OpInfo{name, flops, bytes, 0}); };
 
     ImgSpec img;
@@ -547,8 +550,8 @@ int Worker::build_ops() {
             // DR: written by the GC head)
             if (!which) {
                 const Act si = si_gc_;
-                ops_.push_back([img, si, this](cudaStream_t st) {
-                    return stem_in_launch(img, si, st) ? fail(GCDR_ERR_DEVICE, std::string("stem input launch: ") + last_launch_error()) : 0;
+                ops_.push_back([img, si, errp, this](cudaStream_t st) {
+                    return stem_in_launch(img, si, errp, st) ? fail(GCDR_ERR_DEVICE, std::string("stem input launch: ") + last_launch_error()) : 0;
                 });
                 launches_++;
                 simt(pre + "stem_in", 0, (double)h_ * w_ * bpp_ + (double)(H_ + 2) * (W_ + 2) * kStemInC * 2);
