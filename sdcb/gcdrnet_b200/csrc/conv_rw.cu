@@ -13,8 +13,9 @@
 //     swizzled tile (base offset 0);
 //   * the weights (9 taps x C/bk k-blocks of N x bk) stay resident in shared
 //     memory for the whole persistent CTA.
-// Roles: warp 0 (and warp 13) TMA producers taking alternate stages, warps 1..R
-// MMA issuers (one accumulator = one output row each), warps 5-12 epilogue
+// Roles: warp 0 (and warp 13) TMA producers taking alternate stages, warps 1..4
+// MMA issuers (one accumulator = one output row each; the rows j and j + 4 of
+// 8-row pool units), warps 5-12 epilogue
 // (bias [+ relu], the 2x2 max-pool + relu of two accumulators, or the head).
 // Head units also carry their dec5 window in the ring stage (a third TMA box, read
 // by the epilogue), so a head stage is released by the MMA commits and the epilogue
@@ -63,8 +64,9 @@ struct RwShared {
 __host__ __device__ inline int round1k(int b) { return (b + 1023) & ~1023; }
 
 // HC: the head's stem channels (16 or 32; a separate instantiation each: one register
-// allocation per width), 0 for the other modes
-template <int BK, int MODE, int HC>
+// allocation per width), 0 for the other modes.  ROWS: output rows per MMA warp (2 for the
+// head and the 8-row pool units; a compile-time bound keeps the issue loop unrolled)
+template <int BK, int MODE, int HC, int ROWS>
 __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
     rw_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ ConvArgs args,
@@ -179,10 +181,10 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
                     if (!mbar_wait(&sh->full[s], ph, abort_flag, args.err)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t stage = smem_u32(ring + (size_t)s * cfg.stage_bytes);
-                    // taps outer, this warp's rows inner (head: rows j and j + mma, R <= 2 * mma):
+                    // taps outer, this warp's rows inner (rows j and j + mma when ROWS = 2):
                     // consecutive MMAs go to different accumulators.  The row count is a compile-time
                     // bound, the issue loop stays fully unrolled (it bounds the thin layers).
-                    constexpr int kRows = MODE == EPI_HEAD ? 2 : 1;
+                    constexpr int kRows = ROWS;
 #pragma unroll
                     for (int ky = 0; ky < 3; ky++) {
 #pragma unroll
@@ -313,10 +315,10 @@ size_t rw_smem(const RwConfig &cfg) {
     return 1024 + (size_t)cfg.b_bytes + (size_t)cfg.stages * cfg.stage_bytes + sizeof(RwShared);
 }
 
-template <int BK, int MODE, int HC = 0>
+template <int BK, int MODE, int HC = 0, int ROWS = 1>
 int rw_launch_bk_mode(const ConvArgs &a, const RwConfig &cfg, const CUtensorMap &ta, const CUtensorMap &tb,
                       const CUtensorMap &tc, int grid, cudaStream_t st, std::string &err) {
-    auto k = rw_conv_kernel<BK, MODE, HC>;
+    auto k = rw_conv_kernel<BK, MODE, HC, ROWS>;
     const size_t smem = rw_smem(cfg);
     // the attribute is per kernel, shared by every layer (and every thread) launching it:
     // always the same cap, never a layer's own size, so concurrent workers cannot lower it
@@ -349,7 +351,9 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
     // widest leave too few stages.  Weights must stay resident.
     bool found = false;
     // pass 0: R = 4 or 2 (head: 6, 4 or 2: three epilogue warps per lane quadrant, one
-    // pixel pair each) with a full wave of units (pool: R = 2 always qualifies);
+    // pixel pair each; pool: 8 first, two rows per MMA warp, when that still leaves eight
+    // units per SM: fewer handshakes and halo rows per output row) with a full wave of
+    // units (pool: R = 2 always qualifies);
     // pass 1 (small layers): the fewest rows per unit that fit, for the most units
     for (int pass = 0; pass < 2 && !found; pass++) {
         for (int bk = tc_pick_bk(a.C); bk >= 16 && !found; bk >>= 1) {
@@ -363,8 +367,8 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
             for (int i = 0; i < 3 && !found; i++) {
                 // (head R <= 6: two rows per MMA warp at most)
                 const int R = mode == EPI_HEAD ? (pass == 0 ? 6 - 2 * i : 2 + 2 * i)
-                                               : pass == 0 ? (i == 0 ? 4 : i == 1 ? 2 : 0) : (r_min << i);
-                if (R < r_min || R > (mode == EPI_HEAD ? 6 : 4)) continue;
+                              : pass == 0 ? (i == 0 ? (mode == EPI_POOL ? 8 : 4) : i == 1 ? 4 : 2) : (r_min << i);
+                if (R < r_min || R > (mode == EPI_HEAD ? 6 : mode == EPI_POOL ? 8 : 4)) continue;
                 const int units = ((tg.conv_h + R - 1) / R) * segs_x;
                 // head: the unit's dec5 window (R/2 + 2 rows of kHeadWinCols columns x N channels)
                 const int win_tx = mode == EPI_HEAD ? (R / 2 + 2) * kHeadWinCols * a.N * 2 : 0;
@@ -372,6 +376,8 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
                 const int stages = avail / stage_bytes;
                 if (2 * R * cols > 512 || stages < 3) continue;
                 if (pass == 0 && units < num_sms && !(tg.pool && R == 2)) continue;
+                // (8-row units: instantiated for 16-channel k-blocks, the stems)
+                if (R == 8 && (bk != 16 || (pass == 0 && units < 8 * num_sms))) continue;
                 cfg.bk = bk;
                 cfg.R = R;
                 cfg.b_block = b_block;
@@ -427,10 +433,12 @@ int rw_conv_launch(const ConvArgs &a, int mode, const RwConfig &cfg, int num_sms
         case 32 * 8 + EPI_PLAIN: return rw_launch_bk_mode<32, EPI_PLAIN>(a, cfg, ta, tb, tc, grid, st, err);
         case 32 * 8 + EPI_POOL: return rw_launch_bk_mode<32, EPI_POOL>(a, cfg, ta, tb, tc, grid, st, err);
         case 16 * 8 + EPI_PLAIN: return rw_launch_bk_mode<16, EPI_PLAIN>(a, cfg, ta, tb, tc, grid, st, err);
-        case 16 * 8 + EPI_POOL: return rw_launch_bk_mode<16, EPI_POOL>(a, cfg, ta, tb, tc, grid, st, err);
+        case 16 * 8 + EPI_POOL:
+            return cfg.R > 4 ? rw_launch_bk_mode<16, EPI_POOL, 0, 2>(a, cfg, ta, tb, tc, grid, st, err)
+                             : rw_launch_bk_mode<16, EPI_POOL>(a, cfg, ta, tb, tc, grid, st, err);
         case 16 * 8 + EPI_HEAD:
-            return a.N == 32 ? rw_launch_bk_mode<16, EPI_HEAD, 32>(a, cfg, ta, tb, tc, grid, st, err)
-                             : rw_launch_bk_mode<16, EPI_HEAD, 16>(a, cfg, ta, tb, tc, grid, st, err);
+            return a.N == 32 ? rw_launch_bk_mode<16, EPI_HEAD, 32, 2>(a, cfg, ta, tb, tc, grid, st, err)
+                             : rw_launch_bk_mode<16, EPI_HEAD, 16, 2>(a, cfg, ta, tb, tc, grid, st, err);
     }
     err = "rw_conv: bad k-block / mode";
     return -1;
