@@ -264,7 +264,7 @@ def main(argv=None):
         elif name in ("batch", "stress"):
             p.add_argument("--count", type=int, default=64 if name == "batch" else 16)
             if name == "batch":
-                p.add_argument("--threads", type=int, default=3)
+                p.add_argument("--threads", type=int, default=4)
             p.add_argument("--width", type=int, default=1600)
             p.add_argument("--height", type=int, default=1152)
             p.add_argument("--check", action="store_true")
