@@ -424,8 +424,11 @@ __device__ void epilogue_head_pair(const EpiParams &ep, const TileGeom &tg, int 
     const float wa = xodd ? 0.75f : 0.25f, wb = 1.0f - wa;
     const __half2 q_a = __float2half2_rn(0.25f * wa), q_b = __float2half2_rn(0.25f * wb);
     const __half2 t_a = __float2half2_rn(0.75f * wa), t_b = __float2half2_rn(0.75f * wb);
-    float oa0 = hp.fb[0], oa1 = hp.fb[1], oa2 = hp.fb[2];
-    float ob0 = hp.fb[0], ob1 = hp.fb[1], ob2 = hp.fb[2];
+    // the 1x1 on packed fp32 pairs (FFMA2: even channels in .x, odd in .y, one chain each,
+    // added at the end), the relu-add of the bias likewise
+    float2 oa[3], ob[3];
+#pragma unroll
+    for (int o = 0; o < 3; o++) oa[o] = ob[o] = make_float2(hp.fb[o], 0.0f);
     uint32_t ca[16], cb[16];   // the stem conv of both pixels, 16 channels at a time
 #pragma unroll
     for (int k = 0; k < C1 / 8; k++) {
@@ -455,26 +458,23 @@ __device__ void epilogue_head_pair(const EpiParams &ep, const TileGeom &tg, int 
             uo = __hfma2(h2b[p], q_b, uo);
             const float2 fe = __half22float2(ue), fo = __half22float2(uo);
             const int c = 8 * k + 2 * p, cl = c % 16;
-            const float sa0 = fmaxf(fe.x, 0.0f) + fmaxf(__uint_as_float(ca[cl]) + hp.b1[c], 0.0f);
-            const float sa1 = fmaxf(fe.y, 0.0f) + fmaxf(__uint_as_float(ca[cl + 1]) + hp.b1[c + 1], 0.0f);
-            const float sb0 = fmaxf(fo.x, 0.0f) + fmaxf(__uint_as_float(cb[cl]) + hp.b1[c], 0.0f);
-            const float sb1 = fmaxf(fo.y, 0.0f) + fmaxf(__uint_as_float(cb[cl + 1]) + hp.b1[c + 1], 0.0f);
-            oa0 = fmaf(sa0, hp.fw[c], oa0);
-            oa1 = fmaf(sa0, hp.fw[C1 + c], oa1);
-            oa2 = fmaf(sa0, hp.fw[2 * C1 + c], oa2);
-            ob0 = fmaf(sb0, hp.fw[c], ob0);
-            ob1 = fmaf(sb0, hp.fw[C1 + c], ob1);
-            ob2 = fmaf(sb0, hp.fw[2 * C1 + c], ob2);
-            oa0 = fmaf(sa1, hp.fw[c + 1], oa0);
-            oa1 = fmaf(sa1, hp.fw[C1 + c + 1], oa1);
-            oa2 = fmaf(sa1, hp.fw[2 * C1 + c + 1], oa2);
-            ob0 = fmaf(sb1, hp.fw[c + 1], ob0);
-            ob1 = fmaf(sb1, hp.fw[C1 + c + 1], ob1);
-            ob2 = fmaf(sb1, hp.fw[2 * C1 + c + 1], ob2);
+            const float2 bias = make_float2(hp.b1[c], hp.b1[c + 1]);
+            const float2 ta = __fadd2_rn(make_float2(__uint_as_float(ca[cl]), __uint_as_float(ca[cl + 1])), bias);
+            const float2 tb = __fadd2_rn(make_float2(__uint_as_float(cb[cl]), __uint_as_float(cb[cl + 1])), bias);
+            const float2 sa = __fadd2_rn(make_float2(fmaxf(fe.x, 0.0f), fmaxf(fe.y, 0.0f)),
+                                         make_float2(fmaxf(ta.x, 0.0f), fmaxf(ta.y, 0.0f)));
+            const float2 sb = __fadd2_rn(make_float2(fmaxf(fo.x, 0.0f), fmaxf(fo.y, 0.0f)),
+                                         make_float2(fmaxf(tb.x, 0.0f), fmaxf(tb.y, 0.0f)));
+#pragma unroll
+            for (int o = 0; o < 3; o++) {
+                const float2 w = make_float2(hp.fw[o * C1 + c], hp.fw[o * C1 + c + 1]);
+                oa[o] = __ffma2_rn(sa, w, oa[o]);
+                ob[o] = __ffma2_rn(sb, w, ob[o]);
+            }
         }
     }
-    const float oa[3] = {sigmoid_fast(oa0), sigmoid_fast(oa1), sigmoid_fast(oa2)};
-    const float ob[3] = {sigmoid_fast(ob0), sigmoid_fast(ob1), sigmoid_fast(ob2)};
+    const float ya[3] = {sigmoid_fast(oa[0].x + oa[0].y), sigmoid_fast(oa[1].x + oa[1].y), sigmoid_fast(oa[2].x + oa[2].y)};
+    const float yb[3] = {sigmoid_fast(ob[0].x + ob[0].y), sigmoid_fast(ob[1].x + ob[1].y), sigmoid_fast(ob[2].x + ob[2].y)};
     if (valid) {
         uint4 xa = make_uint4(0, 0, 0, 0), xb = xa;
         if (!hp.is_dr) {
@@ -484,8 +484,8 @@ __device__ void epilogue_head_pair(const EpiParams &ep, const TileGeom &tg, int 
             xa = *reinterpret_cast<const uint4 *>(seg0 + (off ^ sw));
             xb = *reinterpret_cast<const uint4 *>(seg1 + (off ^ sw));
         }
-        head_store(hp, tg.conv_w, y, x, oa, xa);
-        head_store(hp, tg.conv_w, y + 1, x, ob, xb);
+        head_store(hp, tg.conv_w, y, x, ya, xa);
+        head_store(hp, tg.conv_w, y + 1, x, yb, xb);
     }
 }
 

@@ -192,16 +192,21 @@ __global__ void __launch_bounds__(128) head_kernel(const HeadArgs a) {
 // erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2), t = 1 / (1 + p z),
 // |error| <= 1.5e-7 (two orders below the fp16 rounding of the stored activation).
 // For x < 0 the factor 1 + erf(z) = e(z) = poly * exp(-z^2) is formed directly, so the
-// small negative tail carries no cancellation.
-__device__ __forceinline__ float gelu_exact(float v) {
-    const float z = fabsf(v) * 0.70710678118654752f;
-    const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
-    float poly = fmaf(t, 1.061405429f, -1.453152027f);
-    poly = fmaf(poly, t, 1.421413741f);
-    poly = fmaf(poly, t, -0.284496736f);
-    poly = fmaf(poly, t, 0.254829592f);
-    const float e = poly * t * __expf(-z * z);        // 1 - erf(z)
-    return 0.5f * v * (v >= 0.0f ? 2.0f - e : e);
+// small negative tail carries no cancellation.  Two values at a time: the multiplies and
+// fused multiply-adds on packed fp32 pairs (FMUL2 / FFMA2, each lane rounded as its scalar
+// form), the reciprocal, exponential and selects per lane.
+__device__ __forceinline__ float2 gelu_exact2(float2 v) {
+    const float2 z = __fmul2_rn(make_float2(fabsf(v.x), fabsf(v.y)), make_float2(0.70710678118654752f, 0.70710678118654752f));
+    const float2 d = __ffma2_rn(make_float2(0.3275911f, 0.3275911f), z, make_float2(1.0f, 1.0f));
+    const float2 t = make_float2(__fdividef(1.0f, d.x), __fdividef(1.0f, d.y));
+    float2 poly = __ffma2_rn(t, make_float2(1.061405429f, 1.061405429f), make_float2(-1.453152027f, -1.453152027f));
+    poly = __ffma2_rn(poly, t, make_float2(1.421413741f, 1.421413741f));
+    poly = __ffma2_rn(poly, t, make_float2(-0.284496736f, -0.284496736f));
+    poly = __ffma2_rn(poly, t, make_float2(0.254829592f, 0.254829592f));
+    const float2 zz = __fmul2_rn(z, z);
+    const float2 e = __fmul2_rn(__fmul2_rn(poly, t), make_float2(__expf(-zz.x), __expf(-zz.y)));   // 1 - erf(z)
+    const float2 h = __fmul2_rn(make_float2(0.5f, 0.5f), v);
+    return __fmul2_rn(h, make_float2(v.x >= 0.0f ? 2.0f - e.x : e.x, v.y >= 0.0f ? 2.0f - e.y : e.y));
 }
 
 // out = shiftW(gelu(dw(in))): depthwise 3x3 (zero pad 1) + bias + exact GELU,
@@ -215,17 +220,8 @@ __device__ __forceinline__ float gelu_exact(float v) {
 // 4 for the large ones, where one wave of 128-thread blocks must hold the layer).  Only the stores of chunks that straddle a group
 // boundary split.  A flat grid of 128-thread blocks over (row, quad, chunk): no
 // partly empty block per row, and seven blocks per SM hold a /8 layer in one wave.
+// The tap sums and the GELU run on packed channel pairs (FFMA2), lane by lane as fmaf.
 constexpr int kDwMaxC = 512;
-
-__device__ __forceinline__ void unpack8f(const uint4 raw, float *f) {
-    const __half2 *hv = reinterpret_cast<const __half2 *>(&raw);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const float2 t = __half22float2(hv[i]);
-        f[2 * i] = t.x;
-        f[2 * i + 1] = t.y;
-    }
-}
 
 template <int PX>
 __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *wt,
@@ -243,42 +239,49 @@ __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in,
     if (y < H) {
         const int xq = t / chunks, ch = t - xq * chunks;
         const int x = PX * xq, c0 = ch * 8;
-        float acc[PX][8];
+        float2 acc[PX][4];   // channel pairs (c0 + 2i, c0 + 2i + 1): packed FFMA2, per lane as fmaf
         {
             const float4 b0 = __ldg(reinterpret_cast<const float4 *>(b + c0));
             const float4 b1 = __ldg(reinterpret_cast<const float4 *>(b + c0 + 4));
-            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-            for (int p = 0; p < PX; p++)
-#pragma unroll
-                for (int k = 0; k < 8; k++) acc[p][k] = bv[k];
+            for (int p = 0; p < PX; p++) {
+                acc[p][0] = make_float2(b0.x, b0.y);
+                acc[p][1] = make_float2(b0.z, b0.w);
+                acc[p][2] = make_float2(b1.x, b1.y);
+                acc[p][3] = make_float2(b1.z, b1.w);
+            }
         }
         const __half *col = in + c0;
 #pragma unroll
         for (int ky = 0; ky < 3; ky++) {
             const int yy = y + ky - 1;
             if (yy < 0 || yy >= H) continue;
-            float w[3][8];
+            float2 w[3][4];
 #pragma unroll
             for (int kx = 0; kx < 3; kx++) {
                 const float4 w0 = *reinterpret_cast<const float4 *>(ws + (ky * 3 + kx) * C + c0);
                 const float4 w1 = *reinterpret_cast<const float4 *>(ws + (ky * 3 + kx) * C + c0 + 4);
-                w[kx][0] = w0.x; w[kx][1] = w0.y; w[kx][2] = w0.z; w[kx][3] = w0.w;
-                w[kx][4] = w1.x; w[kx][5] = w1.y; w[kx][6] = w1.z; w[kx][7] = w1.w;
+                w[kx][0] = make_float2(w0.x, w0.y);
+                w[kx][1] = make_float2(w0.z, w0.w);
+                w[kx][2] = make_float2(w1.x, w1.y);
+                w[kx][3] = make_float2(w1.z, w1.w);
             }
             const __half *rowp = col + (size_t)yy * W * C;
 #pragma unroll
             for (int j = 0; j < PX + 2; j++) {
                 const int xx = x - 1 + j;             // pixel x + p uses columns x + p - 1 .. x + p + 1
                 if (xx < 0 || xx >= W) continue;
-                float f[8];
-                unpack8f(*reinterpret_cast<const uint4 *>(rowp + (size_t)xx * C), f);
+                const uint4 raw = *reinterpret_cast<const uint4 *>(rowp + (size_t)xx * C);
+                const __half2 *hv = reinterpret_cast<const __half2 *>(&raw);
+                float2 f[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) f[i] = __half22float2(hv[i]);
 #pragma unroll
                 for (int p = 0; p < PX; p++) {
                     const int kx = j - p;
                     if (kx < 0 || kx > 2) continue;
 #pragma unroll
-                    for (int k = 0; k < 8; k++) acc[p][k] = fmaf(w[kx][k], f[k], acc[p][k]);
+                    for (int i = 0; i < 4; i++) acc[p][i] = __ffma2_rn(w[kx][i], f[i], acc[p][i]);
                 }
             }
         }
@@ -291,7 +294,11 @@ __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in,
             if (x + p >= W) break;
             __align__(16) __half o[8];
 #pragma unroll
-            for (int k = 0; k < 8; k++) o[k] = __float2half_rn(gelu_exact(acc[p][k]));
+            for (int i = 0; i < 4; i++) {
+                const float2 g = gelu_exact2(acc[p][i]);
+                o[2 * i] = __float2half_rn(g.x);
+                o[2 * i + 1] = __float2half_rn(g.y);
+            }
             bool za, zb;
             const int da = shift_dest(x + p, offa, W, &za);
             if (split == 8) {
