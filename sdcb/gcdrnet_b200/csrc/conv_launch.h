@@ -53,7 +53,7 @@ bool tma_encode_2d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t ou
 // 0 and a plan when the layer suits the row-window kernel, -1 otherwise.
 int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg);
 int rw_conv_launch(const ConvArgs &a, int mode, const RwConfig &cfg, int num_sms, cudaStream_t st, std::string &err);
-int tc_plan(const ConvArgs &a, int num_sms, TcConfig &cfg, std::string &err);
+int tc_plan(const ConvArgs &a, int mode, int num_sms, TcConfig &cfg, std::string &err);
 // tcgen05 path (sm_100a).  mode = EpiMode.
 int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, std::string &err);
 // SIMT reference path: same math and epilogue, fp32 FMA, accumulators staged in
