@@ -325,9 +325,12 @@ __device__ __forceinline__ void bilin_coords(int Y, int n, int &a0, int &a1, flo
     a1 = min(max(y0 + 1, 0), n - 1);
 }
 
-__global__ void up_add_pad_kernel(const UpAddArgs a) {
+// CH: 8-channel chunks per pixel when fixed at compile time (0: from the layout); the
+// interpolation and the skip add run on packed fp32 pairs (FMUL2 / FFMA2 / FADD2)
+template <int CH>
+__global__ void __launch_bounds__(256) up_add_pad_kernel(const UpAddArgs a) {
     pdl_wait();
-    const int C = a.out.C, H = a.out.H, W = a.out.W, chunks = C / 8;
+    const int C = CH ? CH * 8 : a.out.C, H = a.out.H, W = a.out.W, chunks = CH ? CH : C / 8;
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     const int Y = blockIdx.y;
     if (t < W * chunks) {
@@ -345,14 +348,15 @@ __global__ void up_add_pad_kernel(const UpAddArgs a) {
         const __half2 *h00 = reinterpret_cast<const __half2 *>(&r00), *h01 = reinterpret_cast<const __half2 *>(&r01);
         const __half2 *h10 = reinterpret_cast<const __half2 *>(&r10), *h11 = reinterpret_cast<const __half2 *>(&r11);
         const __half2 *hs = reinterpret_cast<const __half2 *>(&rs);
+        const float2 wx0 = make_float2(1.0f - dx, 1.0f - dx), wx1 = make_float2(dx, dx);
+        const float2 wy0 = make_float2(1.0f - dy, 1.0f - dy), wy1 = make_float2(dy, dy);
         __align__(16) __half2 o[4];
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            const float2 v00 = __half22float2(h00[k]), v01 = __half22float2(h01[k]);
-            const float2 v10 = __half22float2(h10[k]), v11 = __half22float2(h11[k]), sk = __half22float2(hs[k]);
-            const float t0 = v00.x + (v01.x - v00.x) * dx, b0 = v10.x + (v11.x - v10.x) * dx;
-            const float t1 = v00.y + (v01.y - v00.y) * dx, b1 = v10.y + (v11.y - v10.y) * dx;
-            o[k] = __floats2half2_rn(fmaxf(t0 + (b0 - t0) * dy, 0.0f) + sk.x, fmaxf(t1 + (b1 - t1) * dy, 0.0f) + sk.y);
+            const float2 top = __ffma2_rn(__half22float2(h01[k]), wx1, __fmul2_rn(__half22float2(h00[k]), wx0));
+            const float2 bot = __ffma2_rn(__half22float2(h11[k]), wx1, __fmul2_rn(__half22float2(h10[k]), wx0));
+            const float2 up = __ffma2_rn(bot, wy1, __fmul2_rn(top, wy0));
+            o[k] = __float22half2_rn(__fadd2_rn(make_float2(fmaxf(up.x, 0.0f), fmaxf(up.y, 0.0f)), __half22float2(hs[k])));
         }
         act_store(a.out, Y, X, c0, reinterpret_cast<const __half *>(o), 8);
     }
@@ -415,6 +419,8 @@ __global__ void __launch_bounds__(256) up_add_tok_kernel(const UpAddArgs a) {
     const __half *d00 = a.d + ((size_t)ya * w + xa) * C, *d01 = a.d + ((size_t)ya * w + xb) * C;
     const __half *d10 = a.d + ((size_t)yb * w + xa) * C, *d11 = a.d + ((size_t)yb * w + xb) * C;
     const __half *sk = act_ptr(a.skip, Y, X);
+    const float2 wx0 = make_float2(1.0f - dx, 1.0f - dx), wx1 = make_float2(dx, dx);
+    const float2 wy0 = make_float2(1.0f - dy, 1.0f - dy), wy1 = make_float2(dy, dy);
     float v[NCH][8];
     float sum = 0.f;
 #pragma unroll
@@ -424,17 +430,22 @@ __global__ void __launch_bounds__(256) up_add_tok_kernel(const UpAddArgs a) {
         for (int e = 0; e < 8; e++) v[k][e] = 0.f;
         if (ch < nchunk) {
             const int c0 = ch * 8;
-            float q00[8], q01[8], q10[8], q11[8], qs[8];
-            load16h8(d00 + c0, q00);
-            load16h8(d01 + c0, q01);
-            load16h8(d10 + c0, q10);
-            load16h8(d11 + c0, q11);
-            load16h8(sk + c0, qs);
+            const uint4 r00 = *reinterpret_cast<const uint4 *>(d00 + c0), r01 = *reinterpret_cast<const uint4 *>(d01 + c0);
+            const uint4 r10 = *reinterpret_cast<const uint4 *>(d10 + c0), r11 = *reinterpret_cast<const uint4 *>(d11 + c0);
+            const uint4 rs = *reinterpret_cast<const uint4 *>(sk + c0);
+            const __half2 *h00 = reinterpret_cast<const __half2 *>(&r00), *h01 = reinterpret_cast<const __half2 *>(&r01);
+            const __half2 *h10 = reinterpret_cast<const __half2 *>(&r10), *h11 = reinterpret_cast<const __half2 *>(&r11);
+            const __half2 *hs = reinterpret_cast<const __half2 *>(&rs);
+            // the interpolation and the skip add on packed fp32 pairs
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-                const float top = q00[e] + (q01[e] - q00[e]) * dx, bot = q10[e] + (q11[e] - q10[e]) * dx;
-                v[k][e] = fmaxf(top + (bot - top) * dy, 0.0f) + qs[e];
-                sum += v[k][e];
+            for (int e = 0; e < 4; e++) {
+                const float2 top = __ffma2_rn(__half22float2(h01[e]), wx1, __fmul2_rn(__half22float2(h00[e]), wx0));
+                const float2 bot = __ffma2_rn(__half22float2(h11[e]), wx1, __fmul2_rn(__half22float2(h10[e]), wx0));
+                const float2 up = __ffma2_rn(bot, wy1, __fmul2_rn(top, wy0));
+                const float2 r = __fadd2_rn(make_float2(fmaxf(up.x, 0.0f), fmaxf(up.y, 0.0f)), __half22float2(hs[e]));
+                v[k][2 * e] = r.x;
+                v[k][2 * e + 1] = r.y;
+                sum += r.x + r.y;
             }
             if (valid)
                 *reinterpret_cast<uint4 *>(a.out.p + a.out.row(Y, X) * C + c0) = pack8h(v[k]);
@@ -734,7 +745,13 @@ int up_add_launch(const UpAddArgs &a, cudaStream_t st) {
     const int C = a.out.C;
     if (!a.tokens) {
         if (C % 8) return -2;
-        launch_pdl(up_add_pad_kernel, dim3(grid_for((long long)a.out.W * (C / 8), 256), a.out.H), dim3(256), 0, st, a);
+        const dim3 grid(grid_for((long long)a.out.W * (C / 8), 256), a.out.H);
+        switch (C) {
+            case 16: launch_pdl(up_add_pad_kernel<2>, grid, dim3(256), 0, st, a); break;
+            case 32: launch_pdl(up_add_pad_kernel<4>, grid, dim3(256), 0, st, a); break;
+            case 64: launch_pdl(up_add_pad_kernel<8>, grid, dim3(256), 0, st, a); break;
+            default: launch_pdl(up_add_pad_kernel<0>, grid, dim3(256), 0, st, a); break;
+        }
     } else {
         if (C % 8 || C > 512) return -2;
         const int nchunk = C / 8;
