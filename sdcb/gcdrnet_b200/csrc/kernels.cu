@@ -226,11 +226,12 @@ constexpr int kDwMaxC = 512;
 template <int PX>
 __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *wt,
                                                             const float *b, const ShiftSpec s, __half *out) {
-    pdl_wait();
     extern __shared__ __align__(16) float ws[];   // [9][C]
+    // the weights are constant: staged before the wait on the previous kernel
     for (int i = threadIdx.x * 4; i < 9 * C; i += blockDim.x * 4)
         *reinterpret_cast<float4 *>(ws + i) = __ldg(reinterpret_cast<const float4 *>(wt + i));
     __syncthreads();
+    pdl_wait();
     const int chunks = C >> 3;
     const int Wq = (W + PX - 1) / PX;                  // pixel groups per row
     const int per_row = Wq * chunks;
@@ -483,7 +484,6 @@ __global__ void __launch_bounds__(256) up_add_tok_kernel(const UpAddArgs a) {
 // [LN2 -> out2 with the H shift].
 template <int LP, int NCH>
 __global__ void __launch_bounds__(256) ln_finalize_kernel(const LnFinalizeArgs a) {
-    pdl_wait();
     const int N = a.N, nchunk = N >> 3;
     const int T = a.H * a.W;
     const int gid = blockIdx.x * blockDim.x + threadIdx.x;
@@ -500,6 +500,9 @@ __global__ void __launch_bounds__(256) ln_finalize_kernel(const LnFinalizeArgs a
 #pragma unroll
             for (int e = 0; e < 8; e++) v[k][e] = 0.f;
     }
+    pdl_wait();   // (the bias is constant: read before the wait on the partials' producer)
+    // (unrolled: the loads of several partials in flight at once; the sum stays in k order)
+#pragma unroll 4
     for (int ks = 0; ks < a.ksplit; ks++) {
         const float *pk = a.partial + ((size_t)ks * T + tt) * N;
 #pragma unroll
