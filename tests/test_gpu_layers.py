@@ -44,6 +44,9 @@ CASES = [
     (0, 150, 1100, 16, 32, 1),
     (0, 150, 1100, 32, 32, 0),
     (3, 150, 600, 16, 16, 2),
+    # flat plain layers with between one and two waves of single tiles: two tiles per unit
+    (0, 144, 200, 128, 64, 0),    # DR dec3
+    (3, 144, 200, 128, 256, 2),   # the 128 -> 256 microbench conv
     # 8-row pool units (stem shapes: at least eight units per SM), one with a ragged last unit
     (0, 1100, 1500, 16, 16, 1),
     (0, 1152, 1600, 16, 32, 1),
