@@ -1,8 +1,8 @@
 #!/usr/bin/env python
 """Benchmark: 1600x1152 Bgr24 document enhancement (GC-Net -> div6 -> DR-Net).
 
-One step = STREAMS synthetic 1600x1152 documents (the seeded config-0
-generator) enhanced by each GPU at once, one per worker and CUDA stream, as a
+One step = STREAMS synthetic 1600x1152 documents (the seeded document
+generator: paper level, smooth shading, dark strokes, noise) enhanced by each GPU at once, one per worker and CUDA stream, as a
 server keeps several images in flight (per-image data parallelism, no
 inter-GPU traffic: scaling "weak").  Prints ONE JSON line on rank 0:
 
@@ -44,7 +44,7 @@ DR = os.path.join(MODELS, "gcdrnet_drnet_sim.onnx")
 METRIC = "1600x1152 images/sec"
 W_IMG, H_IMG = 1600, 1152
 STREAMS = 4       # images in flight per GPU and step: one worker (graph, arena) and stream each
-WORKLOAD = (f"enhance 1600x1152 Bgr24 synthetic documents (config-0 generator), {STREAMS} images per GPU "
+WORKLOAD = (f"enhance 1600x1152 Bgr24 synthetic documents (seeded paper/shading/strokes/noise generator), {STREAMS} images per GPU "
             "per step on concurrent worker streams")
 
 
