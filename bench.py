@@ -2,8 +2,9 @@
 """Benchmark: 1600x1152 Bgr24 document enhancement (GC-Net -> div6 -> DR-Net).
 
 One step = STREAMS synthetic 1600x1152 documents (the seeded document
-generator: paper level, smooth shading, dark strokes, noise) enhanced by each GPU at once, one per worker and CUDA stream, as a
-server keeps several images in flight (per-image data parallelism, no
+generator: paper level, smooth shading, dark strokes, noise) enhanced by each
+GPU at once, one per worker and CUDA stream, as a server keeps several images
+in flight (per-image data parallelism, no
 inter-GPU traffic: scaling "weak").  Prints ONE JSON line on rank 0:
 
   value     images/s over all ranks, inputs resident in HBM, per-step CUDA
