@@ -208,15 +208,14 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_baseline_oracle(w: int, h: int, seconds: float = 30.0):
-    """Times the CPU oracle's full enhancement on one image (all host threads)."""
+def cpu_baseline_oracle(img, w: int, h: int, seconds: float = 30.0):
+    """Times the CPU oracle's full enhancement of `img` (Bgr24) with all host threads;
+    returns (images/s, threads, images timed, the oracle's output)."""
     import numpy as np
     from oracle import gcdr_oracle as O
-    from sdcb.gcdrnet_b200 import synth
     O.build()
     O.set_threads(host_threads())
     orc = O.Oracle(GC, DR)
-    img = synth.document(w, h, seed=0)
     dst = np.empty_like(img)
     t0 = time.perf_counter()
     orc.enhance(img, w, h, w * 3, dst, w * 3, 0)
@@ -226,7 +225,16 @@ def cpu_baseline_oracle(w: int, h: int, seconds: float = 30.0):
         orc.enhance(img, w, h, w * 3, dst, w * 3, 0)
         n += 1
     total = time.perf_counter() - t0
-    return n / total, O.num_threads(), n
+    return n / total, O.num_threads(), n, dst
+
+
+def parity_u8(got, want) -> dict:
+    """u8 agreement of the backend's output with the oracle's (the parity gate:
+    within 2 LSB on >= 99.9 % of the values, never more than 8 off)."""
+    import numpy as np
+    d = np.abs(got.astype(np.int32) - want.astype(np.int32))
+    frac = float((d <= 2).mean())
+    return {"max_abs_u8": int(d.max()), "frac_within_2": frac, "pass": bool(d.max() <= 8 and frac >= 0.999)}
 
 
 def run_reference(args):
@@ -414,10 +422,16 @@ def main():
     tc_flops = sum(p[2] for p in kern if p[4])
 
     cpu = None
+    parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, n = cpu_baseline_oracle(W_IMG, H_IMG)
+        v, cores, n, want = cpu_baseline_oracle(imgs[0], W_IMG, H_IMG)
         cpu = {"value": v, "unit": "images/s", "cores": cores, "kind": "port",
                "sample": f"{n} full 1600x1152 Bgr24 image(s), CPU oracle (OpenMP C restatement)"}
+        # the benchmark's own output (public API, first document) against the oracle's, untimed
+        got = np.empty(nbytes, np.uint8)
+        enh.enhance(imgs[0], W_IMG, H_IMG, W_IMG * 3, got, W_IMG * 3, 0)
+        parity = dict(parity_u8(got, want.reshape(-1)), image=f"seed {rank_seeds(0, 1)[0]} 1600x1152 Bgr24",
+                      vs="CPU oracle")
 
     if rank == 0:
         line = {
@@ -444,6 +458,7 @@ def main():
             "gpu_launches": launches * args.steps * STREAMS,
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "parity": parity,
             "profile_top": sorted([(p[0], round(p[1], 4)) for p in kern], key=lambda t: -t[1])[:12],
         }
         print(json.dumps(line), flush=True)

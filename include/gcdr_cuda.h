@@ -202,7 +202,17 @@ GCDR_API int gcdr_k_nhwc2bgr(const float *y, int H, int W, int ph, int pw, uint8
  * out: fp16 [Ho][Wo][N] (epilogue 0-2).  nsplit: N slices per 128-row tile
  * (N/nsplit a multiple of 16); ksplit: k splits (epilogue 3 only; must divide
  * 9*C/BK).  0 means 1.  reference != 0 runs the SIMT reference kernels instead
- * of tcgen05 (nsplit = ksplit = 1; scratch: ceil(Ho*pitch/128)*128*N floats). */
+ * of tcgen05 (nsplit = ksplit = 1; scratch: ceil(Ho*pitch/128)*128*N floats).
+ * bias_host: optional HOST copy of the bias (N floats).  The epilogues take the
+ *   bias as kernel parameters, so without it gcdr_k_conv reads the device bias
+ *   back first (a blocking copy); with it (or with epilogue 3, which adds no
+ *   bias) the call only enqueues work on `stream`.
+ * wait_cycles: bound of every device-side wait of the tensor-core kernel in SM
+ *   cycles (0: the default, about 2 s).  A wait that runs out makes the kernel
+ *   give up, drain its own copies and return; gcdr_k_status then reports
+ *   GCDR_ERR_TIMEOUT.
+ * timeout_probe: test hook; nonzero makes the kernel issue no copies and no
+ *   MMAs, so its first waits run out after wait_cycles and nothing is written. */
 typedef struct {
     int kind;
     int H, W, C, N;
@@ -214,14 +224,60 @@ typedef struct {
     float *scratch;
     int nsplit;
     int ksplit;
+    const float *bias_host;
+    long long wait_cycles;
+    int timeout_probe;
 } gcdr_conv_desc;
+/* Enqueues one layer on `stream` (see bias_host for the one blocking case).
+ * Device-side waits report through the current device's layer error word,
+ * read by gcdr_k_status. */
 GCDR_API int gcdr_k_conv(const gcdr_conv_desc *d, int reference, void *stream);
+/* Waits for `stream`, then reads and clears the current device's layer error
+ * word: GCDR_ERR_TIMEOUT if a gcdr_k_conv kernel gave up on a wait since the
+ * last gcdr_k_status, else GCDR_OK (GCDR_ERR_DEVICE if the stream failed). */
+GCDR_API int gcdr_k_status(void *stream);
 /* Repacks fp16 NHWC [H][W][C] into a layer input layout:
  *   kind 1  [H+2][W+2][C] with a reflect border
  *   kind 2  four zero-bordered phase planes [(H+2)/2][(W+2)/2][C] (H, W even)
  *   kind 3  [H+2][W+2][C] with a zero border
  * Returns the element count of the layout when dst is NULL. */
 GCDR_API int64_t gcdr_k_to_layout(const void *src, int H, int W, int C, int kind, void *dst, void *stream);
+/* The token-stage kernels of the shifted-MLP blocks and decoder joins, for
+ * kernel-level parity tests.  DEVICE pointers, fp16 activations, fp32
+ * parameters (16-byte aligned), asynchronous on `stream`.
+ *
+ * gcdr_act: an activation in one of the layer layouts (kind 0 tokens
+ * [H][W][C]; 1, 2, 3 as gcdr_k_to_layout).  gcdr_shift: a channel shift
+ * (ChannelShiftOp, Extensions/ChannelShiftOp.cs:70-188): `ngroups` (<= 5)
+ * cumulative channel-group ends; group g is shifted by offs[g]
+ * (out[y] = in[y + off], zero fill), channels past the last end unshifted. */
+typedef struct {
+    void *p;
+    int H, W, C;
+    int kind;
+} gcdr_act;
+typedef struct {
+    int ngroups;
+    int ends[5];
+    int offs[5];
+} gcdr_shift;
+/* Depthwise 3x3 (zero pad 1) + bias -> exact GELU -> shift along W
+ * (gc#85-95): in, out tokens [H][W][C]; wt tap-major [9][C], b [C]. */
+GCDR_API int gcdr_k_dw_gelu_shift(const void *in, int H, int W, int C, const float *wt, const float *b,
+                                  const gcdr_shift *shift, void *out, void *stream);
+/* Decoder join (gc#236-240): out = relu(bilinear2x(d)) + skip, d tokens
+ * [H/2][W/2][C].  With g != NULL (token form, gc#240-250) out must be tokens
+ * and h (tokens) gets LayerNorm(out; g, b, eps) shifted along H. */
+GCDR_API int gcdr_k_up_add(const void *d, const gcdr_act *skip, const gcdr_act *out, const float *g,
+                           const float *b, float eps, const gcdr_shift *shift, void *h, void *stream);
+/* Finishes a split-K layer: per token, the ksplit fp32 partials
+ * [ksplit][H*W][N] summed in order + bias (+ res tokens), then
+ * out = LayerNorm(v; g1, b1, eps1) in out's layout; with g2 != NULL also
+ * out2 (tokens) = LayerNorm(out; g2, b2, eps2) shifted along H. */
+GCDR_API int gcdr_k_ln_finalize(const float *partial, int ksplit, int H, int W, int N, const float *bias,
+                                const void *res, const float *g1, const float *b1, float eps1,
+                                const float *g2, const float *b2, float eps2, const gcdr_shift *shift,
+                                const gcdr_act *out, void *out2, void *stream);
 /* Scratch floats gcdr_k_conv needs with reference != 0. */
 GCDR_API int64_t gcdr_k_conv_scratch(const gcdr_conv_desc *d);
 /* Number of SMs the tcgen05 kernels use on the current device. */
@@ -240,9 +296,10 @@ GCDR_API int gcdr_device_sms(void);
  *     else GCDR_ERR_RANGE (nothing is launched, a message goes to stderr).
  *   - The first call on a device loads the workspace's address with
  *     cudaGetSymbolAddress (the driver reserves the workspace then): make it
- *     before any stream capture.
- *   - Returns after the layer has finished on `stream` (GCDR_ERR_TIMEOUT if a
- *     device-side wait expired).
+ *     before any stream capture.  Every call looks the address up again.
+ *   - Synchronous: returns after the layer has finished on `stream`
+ *     (GCDR_ERR_TIMEOUT if a device-side wait expired).  d->bias stays on the
+ *     device (bias_host is not needed).
  *   - One workspace per device: calls that overlap in time race on it. */
 #define GCDR_STATIC_WS_BYTES (16 * 1024 * 1024)
 GCDR_API int gcdr_k_conv_static(const gcdr_conv_desc *d, void *stream);

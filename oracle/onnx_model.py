@@ -8,7 +8,7 @@ each shift Split and the per-group shift offsets/axes encoded by its
 ``Mod``/``Slice`` roll pattern.
 
 The shift recovery follows the reference's pattern pass
-``Extensions/ChannelShiftOp.cs:344-467`` (FuseShiftPass): a roll by ``cut``
+``Extensions/ChannelShiftOp.cs:64-188`` (FuseShiftPass): a roll by ``cut``
 of a tensor zero-padded by ``pad`` and sliced back is a shift by
 ``((pad + cut) % L) - pad``; for the exported ``cut = c mod L`` with
 ``|c| <= pad`` this is ``c`` itself (offsets 2, 1, 0, -1, -2).
@@ -218,7 +218,7 @@ class OnnxGraph:
                     raise ValueError("roll cut is not a Mod")
                 c = int(self.inits[mod.inputs[0]].reshape(-1)[0])
                 p = int(pads[ax])
-                # ChannelShiftOp.cs:440 offset = ((pad + cut) % L) - pad, cut = c mod L
+                # ChannelShiftOp.cs:158-161 offset = ((pad + cut) % L) - pad, cut = c mod L
                 # with L = n + 2*pad > 2*pad >= |c| this is exactly c.
                 if abs(c) > p:
                     raise ValueError("shift larger than its zero pad")

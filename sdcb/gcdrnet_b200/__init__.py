@@ -21,7 +21,7 @@ import io
 import os
 import threading
 
-__all__ = ["GcdrBackend", "GcdrPixelFormat", "GcdrEnhancer", "CudaWorker", "lib", "library_path",
+__all__ = ["GcdrBackend", "GcdrPixelFormat", "GcdrEnhancer", "CudaWorker", "ConvDesc", "lib", "library_path",
            "GcdrError", "ArgumentError", "ArgumentOutOfRangeError", "NotSupportedError",
            "DeviceLostError", "DeviceTimeoutError", "ModelError", "OutOfMemoryError",
            "bytes_per_pixel"]
@@ -97,6 +97,15 @@ def _raise(rc: int, msg: str = ""):
         raise _ERRORS.get(rc, GcdrError)(msg or f"gcdr status {rc}")
 
 
+class ConvDesc(ctypes.Structure):
+    """gcdr_conv_desc of include/gcdr_cuda.h (the layer entries gcdr_k_conv / gcdr_k_conv_static)."""
+    _fields_ = [("kind", ctypes.c_int), ("H", ctypes.c_int), ("W", ctypes.c_int), ("C", ctypes.c_int),
+                ("N", ctypes.c_int), ("inp", ctypes.c_void_p), ("weight", ctypes.c_void_p),
+                ("bias", ctypes.c_void_p), ("epilogue", ctypes.c_int), ("out", ctypes.c_void_p),
+                ("scratch", ctypes.c_void_p), ("nsplit", ctypes.c_int), ("ksplit", ctypes.c_int),
+                ("bias_host", ctypes.c_void_p), ("wait_cycles", ctypes.c_longlong), ("timeout_probe", ctypes.c_int)]
+
+
 _lib = None
 _lib_lock = threading.Lock()
 
@@ -144,6 +153,11 @@ def lib():
         L.gcdr_k_to_layout.restype = i64
         L.gcdr_device_sms.restype = i
         L.gcdr_k_conv_static.argtypes = [vp, vp]
+        L.gcdr_k_status.argtypes = [vp]
+        f = ctypes.c_float
+        L.gcdr_k_dw_gelu_shift.argtypes = [vp, i, i, i, vp, vp, vp, vp, vp]
+        L.gcdr_k_up_add.argtypes = [vp, vp, vp, vp, vp, f, vp, vp, vp]
+        L.gcdr_k_ln_finalize.argtypes = [vp, i, i, i, i, vp, vp, vp, vp, f, vp, vp, f, vp, vp, vp, vp]
         _lib = L
         return L
 

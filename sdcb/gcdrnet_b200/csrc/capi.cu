@@ -406,7 +406,14 @@ int conv_args_from_desc(const gcdr_conv_desc *d, ConvArgs &a, int &mode, std::st
     a.ksplit = d->ksplit > 0 ? d->ksplit : 1;
     if (mode == EPI_PARTIAL) a.ep.partial = static_cast<float *>(d->out);
     else if (a.ksplit != 1) { err = "k splits need the partial-sum epilogue"; return -1; }
-    if (fill_bias_consts(a)) { err = "bias copy failed (N <= 512)"; return -1; }
+    a.wait_cycles = d->wait_cycles > 0 ? d->wait_cycles : 0;
+    a.timeout_probe = d->timeout_probe != 0;
+    // the epilogues take the bias as kernel parameters; the partial sums add none
+    if (mode != EPI_PARTIAL) {
+        if (a.N > kMaxBiasConst) { err = "N > 512"; return -1; }
+        if (d->bias_host) std::memcpy(a.ep.bias_c, d->bias_host, (size_t)a.N * sizeof(float));
+        else if (fill_bias_consts(a)) { err = "bias copy failed"; return -1; }
+    }
     return 0;
 }
 
@@ -423,27 +430,161 @@ __global__ void to_layout_kernel(const __half *src, int H, int W, int C, Act dst
 
 }  // namespace
 
+namespace {
+
+// One layer error word per device (the kernels' timeout flag of gcdr_k_conv), allocated and
+// zeroed on the device's first layer call; gcdr_k_status reads and clears it.
+constexpr int kMaxLayerDevices = 64;
+std::mutex g_layer_err_mu;
+int *g_layer_err[kMaxLayerDevices] = {};
+
+int *layer_err_word(int dev) {
+    if (dev < 0 || dev >= kMaxLayerDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(g_layer_err_mu);
+    if (!g_layer_err[dev]) {
+        int *p = nullptr;
+        if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) {
+            cudaFree(p);
+            return nullptr;
+        }
+        g_layer_err[dev] = p;
+    }
+    return g_layer_err[dev];
+}
+
+}  // namespace
+
 extern "C" int gcdr_k_conv(const gcdr_conv_desc *d, int reference, void *stream) {
     ConvArgs a;
     int mode = 0;
     std::string err;
     if (conv_args_from_desc(d, a, mode, err)) return GCDR_ERR_ARG;
-    static thread_local int *d_err = nullptr;
-    if (!d_err && cudaMalloc(&d_err, sizeof(int)) != cudaSuccess) return GCDR_ERR_OOM;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess) return GCDR_ERR_DEVICE;
+    int *d_err = layer_err_word(dev);
+    if (!d_err) return GCDR_ERR_OOM;
     a.err = d_err;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (reference) {
         if (!d->scratch) return GCDR_ERR_ARG;
         return ref_conv_launch(a, mode, d->scratch, st, err) ? GCDR_ERR_DEVICE : GCDR_OK;
     }
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (tc_conv_launch(a, mode, sms, st, err)) {
         std::fprintf(stderr, "gcdr_k_conv: %s\n", err.c_str());
         return GCDR_ERR_DEVICE;
     }
     return GCDR_OK;
+}
+
+extern "C" int gcdr_k_status(void *stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return GCDR_ERR_DEVICE;
+    if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return GCDR_ERR_DEVICE;
+    int *d_err = layer_err_word(dev);
+    if (!d_err) return GCDR_ERR_OOM;
+    int h = 0;
+    if (cudaMemcpy(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemset(d_err, 0, sizeof(int)) != cudaSuccess)
+        return GCDR_ERR_DEVICE;
+    return (h & GCDR_ERR_FLAG_TIMEOUT) ? GCDR_ERR_TIMEOUT : h ? GCDR_ERR_DEVICE : GCDR_OK;
+}
+
+namespace {
+
+bool act_from(const gcdr_act *g, Act &a) {
+    if (!g || !g->p || g->H < 1 || g->W < 1 || g->C < 1 || g->kind < 0 || g->kind > 3) return false;
+    a.p = static_cast<__half *>(g->p);
+    a.H = g->H;
+    a.W = g->W;
+    a.C = g->C;
+    a.kind = g->kind == 0 ? LAY_PLAIN : g->kind == 1 ? LAY_PADREFL : g->kind == 2 ? LAY_PHASE : LAY_PADZERO;
+    return !(a.kind == LAY_PHASE && (a.H % 2 || a.W % 2));
+}
+
+ShiftSpec shift_from(const gcdr_shift *s) {
+    if (!s) return ShiftSpec{};
+    return make_shift(s->ngroups, s->ends, s->offs);
+}
+
+bool shift_ok(const gcdr_shift *s, int C) {
+    if (!s) return true;
+    if (s->ngroups < 0 || s->ngroups > 5) return false;
+    int prev = 0;
+    for (int g = 0; g < s->ngroups; g++) {
+        if (s->ends[g] < prev || s->ends[g] > C) return false;
+        prev = s->ends[g];
+    }
+    return true;
+}
+
+}  // namespace
+
+extern "C" int gcdr_k_dw_gelu_shift(const void *in, int H, int W, int C, const float *wt, const float *b,
+                                    const gcdr_shift *shift, void *out, void *stream) {
+    if (!in || !wt || !b || !out || H < 1 || W < 1 || !shift_ok(shift, C)) return GCDR_ERR_ARG;
+    const int rc = dw_gelu_shift_launch(static_cast<const __half *>(in), H, W, C, wt, b, shift_from(shift),
+                                        static_cast<__half *>(out), static_cast<cudaStream_t>(stream));
+    return rc == -2 ? GCDR_ERR_ARG : rc ? GCDR_ERR_DEVICE : GCDR_OK;
+}
+
+extern "C" int gcdr_k_up_add(const void *d, const gcdr_act *skip, const gcdr_act *out, const float *g,
+                             const float *b, float eps, const gcdr_shift *shift, void *h, void *stream) {
+    UpAddArgs u;
+    if (!d || !act_from(skip, u.skip) || !act_from(out, u.out)) return GCDR_ERR_ARG;
+    if (u.skip.H != u.out.H || u.skip.W != u.out.W || u.skip.C != u.out.C || u.out.H % 2 || u.out.W % 2)
+        return GCDR_ERR_ARG;
+    u.d = static_cast<const __half *>(d);
+    if (g) {
+        if (!b || !h || u.out.kind != LAY_PLAIN || !shift_ok(shift, u.out.C)) return GCDR_ERR_ARG;
+        u.tokens = 1;
+        u.g = g;
+        u.b = b;
+        u.eps = eps;
+        u.h.p = static_cast<__half *>(h);
+        u.h.H = u.out.H;
+        u.h.W = u.out.W;
+        u.h.C = u.out.C;
+        u.h.kind = LAY_PLAIN;
+        u.shift = shift_from(shift);
+    }
+    const int rc = up_add_launch(u, static_cast<cudaStream_t>(stream));
+    return rc == -2 ? GCDR_ERR_ARG : rc ? GCDR_ERR_DEVICE : GCDR_OK;
+}
+
+extern "C" int gcdr_k_ln_finalize(const float *partial, int ksplit, int H, int W, int N, const float *bias,
+                                  const void *res, const float *g1, const float *b1, float eps1,
+                                  const float *g2, const float *b2, float eps2, const gcdr_shift *shift,
+                                  const gcdr_act *out, void *out2, void *stream) {
+    LnFinalizeArgs f;
+    if (!partial || !bias || !g1 || !b1 || ksplit < 1 || H < 1 || W < 1 || !act_from(out, f.out)) return GCDR_ERR_ARG;
+    if (f.out.H != H || f.out.W != W || f.out.C != N) return GCDR_ERR_ARG;
+    f.partial = partial;
+    f.ksplit = ksplit;
+    f.H = H;
+    f.W = W;
+    f.N = N;
+    f.bias = bias;
+    f.res = static_cast<const __half *>(res);
+    f.g1 = g1;
+    f.b1 = b1;
+    f.eps1 = eps1;
+    if (g2) {
+        if (!b2 || !out2 || !shift_ok(shift, N)) return GCDR_ERR_ARG;
+        f.ln2 = 1;
+        f.g2 = g2;
+        f.b2 = b2;
+        f.eps2 = eps2;
+        f.shift = shift_from(shift);
+        f.out2.p = static_cast<__half *>(out2);
+        f.out2.H = H;
+        f.out2.W = W;
+        f.out2.C = N;
+        f.out2.kind = LAY_PLAIN;
+    }
+    const int rc = ln_finalize_launch(f, static_cast<cudaStream_t>(stream));
+    return rc == -2 ? GCDR_ERR_ARG : rc ? GCDR_ERR_DEVICE : GCDR_OK;
 }
 
 extern "C" int64_t gcdr_k_conv_scratch(const gcdr_conv_desc *d) {

@@ -228,4 +228,7 @@ __device__ inline void load16h(const __half *p, float *v) {
 #define GCDR_ERR_FLAG_TIMEOUT 1
 #define GCDR_ERR_FLAG_BOUNDS 2
 
+// Default bound of a device-side wait: ~2 s of SM clock at 1.9 GHz.
+constexpr long long kWaitCycles = 4000000000LL;
+
 }  // namespace gcdr

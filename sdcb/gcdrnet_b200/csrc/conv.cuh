@@ -29,7 +29,14 @@ struct ConvArgs {
     TileGeom tg;
     EpiParams ep;
     int *err = nullptr;        // device error flag (GCDR_ERR_FLAG_*)
+    long long wait_cycles = 0; // bound of each mbarrier wait in SM cycles (0: the default, ~2 s)
+    int timeout_probe = 0;     // test hook: issue no copies and no MMAs, so every wait runs out
 };
+
+// The wait bound a launch uses.
+__host__ __device__ inline long long wait_budget(const ConvArgs &a) {
+    return a.wait_cycles > 0 ? a.wait_cycles : kWaitCycles;
+}
 
 // Work unit u -> (m unit, n slice, k split).
 __host__ __device__ inline void unit_coords(const ConvArgs &a, int u, int &tile, int &ni, int &ki) {

@@ -54,7 +54,7 @@ constexpr int kSegRows = 136;          // 128 outputs + 2 halo, rounded up to 8 
 constexpr int kRwSmemCap = 210 * 1024;
 
 struct RwShared {
-    uint64_t full[kMaxStages], empty[kMaxStages], tfull[2], tempty[2], bfull;
+    uint64_t full[kMaxStages], empty[kMaxStages], tfull[2], tempty[2], bfull, mdone[4];
     uint32_t tmem_base;
     int abort_flag;
     int issued[2], consumed;
@@ -94,6 +94,7 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
             mbar_init(&sh->tempty[b], Roles::epi);
         }
         mbar_init(&sh->bfull, 1);
+        for (int m = 0; m < 4; m++) mbar_init(&sh->mdone[m], 1);
         sh->abort_flag = 0;
         sh->issued[0] = sh->issued[1] = 0;
         sh->consumed = 0;
@@ -112,6 +113,7 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
     tc_fence_after();
     const uint32_t tmem_base = sh->tmem_base;
     volatile int *abort_flag = &sh->abort_flag;
+    const long long budget = wait_budget(args);
     pdl_trigger();                          // all CTAs are resident: the next kernel may start launching
     const bool b_loader = (warp == 0 && lane == 0);
     if (!b_loader) pdl_wait();              // activations of the previous kernels
@@ -126,25 +128,26 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
     if (warp == 0 || (Roles::prod == 2 && warp == Roles::mma + Roles::epi + 1)) {
         const int p = warp == 0 ? 0 : 1;
         if (lane == 0) {
-            if (p == 0) {
+            if (p == 0 && !args.timeout_probe) {
                 // resident weights: block (kb, tap) = rows [0, N) x columns tap*C + kb*BK
                 mbar_expect_tx(&sh->bfull, (uint32_t)(9 * kbs * N * BK * 2));
                 for (int kb = 0; kb < kbs; kb++)
                     for (int tap = 0; tap < 9; tap++)
                         tma_load_2d(bres + (size_t)(kb * 9 + tap) * cfg.b_block, &tmB, tap * C + kb * BK, 0, &sh->bfull);
                 sh->b_issued = 1;
-                pdl_wait();                 // the weights are constant; the activations are not
             }
+            if (p == 0) pdl_wait();         // the weights are constant; the activations are not
             int s = 0;
             uint32_t ph = 0;
             int g = 0, issued = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < cfg.units && ok; u += gridDim.x) {
+            // (the timeout probe issues nothing: every consumer's wait runs out)
+            for (int u = blockIdx.x; u < cfg.units && ok && !args.timeout_probe; u += gridDim.x) {
                 int y0, x0;
                 unit_origin(u, y0, x0);
                 for (int kb = 0; kb < kbs; kb++, g++) {
                     if (g % Roles::prod == p) {
-                        if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err)) { ok = false; break; }
+                        if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err, budget)) { ok = false; break; }
                         uint8_t *stage = ring + (size_t)s * cfg.stage_bytes;
                         mbar_expect_tx(&sh->full[s], (uint32_t)((R + 2) * kSegRows * BK * 2 + cfg.win_tx));
                         for (int r = 0; r < R + 2; r++)
@@ -170,15 +173,15 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
             int s = 0;
             uint32_t ph = 0;
             int t = 0, consumed = 0;
-            bool ok = mbar_wait(&sh->bfull, 0, abort_flag, args.err);
+            bool ok = mbar_wait(&sh->bfull, 0, abort_flag, args.err, budget);
             for (int u = blockIdx.x; u < cfg.units && ok; u += gridDim.x, t++) {
                 const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
                 const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
-                if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err)) break;
+                if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err, budget)) break;
                 tc_fence_after();
                 const uint32_t dcol0 = tmem_base + (uint32_t)(ab * R * cfg.acc_cols);
                 for (int kb = 0; kb < kbs; kb++) {
-                    if (!mbar_wait(&sh->full[s], ph, abort_flag, args.err)) { ok = false; break; }
+                    if (!mbar_wait(&sh->full[s], ph, abort_flag, args.err, budget)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t stage = smem_u32(ring + (size_t)s * cfg.stage_bytes);
                     // taps outer, this warp's rows inner (rows j and j + mma when ROWS = 2):
@@ -210,6 +213,13 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
                 if (ok) mma_commit(&sh->tfull[ab]);
             }
             if (j == 0) sh->consumed = consumed;
+            if (*abort_flag) {
+                // after an abort the issuers stop at different stages: each waits (bounded)
+                // for the completion of every MMA it issued before TMEM is freed
+                mma_commit(&sh->mdone[j]);
+                long long t0 = clock64();
+                while (!mbar_try(&sh->mdone[j], 0) && clock64() - t0 < kWaitCycles) {}
+            }
         }
     } else {
         const int e = warp - 1 - Roles::mma;        // epilogue warp 0..epi-1
@@ -223,7 +233,7 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
             unit_origin(u, y0, x0);
             const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
             const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
-            bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err);
+            bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err, budget);
             uint32_t bad;
             asm volatile(
                 "{\n\t.reg .pred p, q;\n\t"
@@ -254,7 +264,7 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
                 const int hs = t % cfg.stages;
                 const uint8_t *win = ring + (size_t)hs * cfg.stage_bytes + (size_t)(R + 2) * cfg.seg_bytes;
                 // (after an abort it is skipped: the next unit's vote ends all epilogue warps together)
-                if (mbar_wait(&sh->full[hs], (uint32_t)((t / cfg.stages) & 1), abort_flag, args.err)) {
+                if (mbar_wait(&sh->full[hs], (uint32_t)((t / cfg.stages) & 1), abort_flag, args.err, budget)) {
                     for (int q = part; q < R / 2; q += Roles::parts) {
                         TmemLoader l0{acc0 + (uint32_t)(2 * q * cfg.acc_cols)};
                         TmemLoader l1{acc0 + (uint32_t)((2 * q + 1) * cfg.acc_cols)};

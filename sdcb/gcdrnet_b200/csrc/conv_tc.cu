@@ -42,7 +42,7 @@ constexpr int kConvThreads = (2 + kMmaWarps + kEpiWarps) * 32;
 constexpr int kProducer2Warp = 1 + kMmaWarps + kEpiWarps;     // the second TMA producer
 
 struct TcShared {
-    uint64_t full[kMaxStages], empty[kMaxStages], tfull[2], tempty[2];
+    uint64_t full[kMaxStages], empty[kMaxStages], tfull[2], tempty[2], mdone[kMmaWarps];
     uint32_t tmem_base;
     int abort_flag;
     int issued[2], consumed;
@@ -84,6 +84,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             mbar_init(&sh->tfull[b], (uint32_t)nacc);
             mbar_init(&sh->tempty[b], kLnUnits ? kEpiWarps / 2 : kEpiWarps);
         }
+        for (int m = 0; m < kMmaWarps; m++) mbar_init(&sh->mdone[m], 1);
         sh->abort_flag = 0;
         sh->issued[0] = sh->issued[1] = 0;
         sh->consumed = 0;
@@ -101,6 +102,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = sh->tmem_base;
     volatile int *abort_flag = &sh->abort_flag;
+    const long long budget = wait_budget(args);
     pdl_trigger();                          // all CTAs are resident: the next kernel may start launching
     pdl_wait();                             // activations of the previous kernels
 
@@ -113,7 +115,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             uint32_t ph = 0;
             int g = 0, issued = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+            // (the timeout probe issues nothing: every consumer's wait runs out)
+            for (int u = blockIdx.x; u < nunits && ok && !args.timeout_probe; u += gridDim.x) {
                 int mu, ni, ki;
                 unit_coords(args, u, mu, ni, ki);
                 long long r0, r1;
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                 }
                 for (int st = 0; st < kblocks / cfg.kps; st++, g++) {
                     if ((g & 1) == p) {
-                        if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err)) { ok = false; break; }
+                        if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err, budget)) { ok = false; break; }
                         uint8_t *stage = ring + (size_t)s * cfg.stage_bytes;
                         mbar_expect_tx(&sh->full[s], (uint32_t)cfg.kps * (a_bytes + b_bytes));
                         for (int j = 0; j < cfg.kps; j++) {
@@ -167,11 +170,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, t++) {
                 const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
                 const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
-                if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err)) break;
+                if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err, budget)) break;
                 tc_fence_after();
                 const uint32_t dcol = tmem_base + (uint32_t)((ab * nst + i) * cfg.acc_cols + h * 256);
                 for (int st = 0; st < kblocks / cfg.kps; st++) {
-                    if (!mbar_wait(&sh->full[s], ph, abort_flag, args.err)) { ok = false; break; }
+                    if (!mbar_wait(&sh->full[s], ph, abort_flag, args.err, budget)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t stage = smem_u32(ring + (size_t)s * cfg.stage_bytes);
                     for (int j = 0; j < cfg.kps; j++) {
@@ -190,6 +193,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                 if (ok) mma_commit(&sh->tfull[ab]);
             }
             if (m == 0) sh->consumed = consumed;
+            if (*abort_flag) {
+                // after an abort the issuers stop at different stages: each waits (bounded)
+                // for the completion of every MMA it issued before TMEM is freed
+                mma_commit(&sh->mdone[m]);
+                long long t0 = clock64();
+                while (!mbar_try(&sh->mdone[m], 0) && clock64() - t0 < kWaitCycles) {}
+            }
         }
     } else {
         const int e = warp - 1 - kMmaWarps;         // epilogue warp 0..7
@@ -206,7 +216,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             unit_coords(args, u, mu, ni, ki);
             const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
             const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
-            bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err);
+            bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err, budget);
             // the warps sharing this unit leave together (bar.red.or over their threads)
             uint32_t bad;
             if (kLnUnits)

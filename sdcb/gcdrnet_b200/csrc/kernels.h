@@ -101,6 +101,9 @@ struct LnFinalizeArgs {
 };
 int ln_finalize_launch(const LnFinalizeArgs &a, cudaStream_t st);
 
+// Channel-shift groups (cumulative ends, offsets; at most 5) -> ShiftSpec (pipeline.cu).
+ShiftSpec make_shift(int ngroups, const int *ends, const int *offs);
+
 // Standalone glue kernels (the C ABI's gcdr_k_*).
 int k_bgr2nhwc(const uint8_t *src, int w, int h, int stride, int fmt, float *x, int ph, int pw, cudaStream_t st);
 int k_div6(const float *x, const float *s, size_t npx, float *out6, cudaStream_t st);

@@ -11,7 +11,7 @@
 // encoder/decoder convs (gc#22-23), the LayerNorm epsilons, the Gemm B
 // operands (transB=0), the Resize mode (linear, half_pixel, x2), and the
 // shift-MLP groups/offsets exactly as FuseShiftPass derives them
-// (Extensions/ChannelShiftOp.cs:344-467, offset formula :440).
+// (Extensions/ChannelShiftOp.cs:64-188, offset formula :158-161).
 #include "model.h"
 
 #include <cmath>

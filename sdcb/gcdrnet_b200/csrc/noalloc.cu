@@ -9,15 +9,17 @@
 // device, code running where cudaMalloc is not allowed) can still run the
 // layer.  The array is part of this file's device image: the driver reserves
 // it on a device when the module is loaded there, which the first call on that
-// device does through cudaGetSymbolAddress.  That first call should therefore
-// come before any stream capture.  Every call shares the one workspace per
-// device, so calls that overlap in time (two host threads, or two streams
-// without ordering between them) race on it.
+// device does through cudaGetSymbolAddress (every call looks the address up
+// again).  That first call should therefore come before any stream capture.
+// The call is synchronous: it reads the kernels' error word back before it
+// returns.  Every call shares the one workspace per device, so calls that
+// overlap in time (two host threads, or two streams without ordering between
+// them) race on it.  The partial sums add no bias (the sum kernel adds it from
+// the device bias), so no bias is read back to the host.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
-#include <mutex>
 #include <string>
 
 #include "../../../include/gcdr_cuda.h"
@@ -36,9 +38,6 @@ constexpr long long kHeaderFloats = 64;
 constexpr long long kStaticWsFloats = GCDR_STATIC_WS_BYTES / 4;
 static __device__ __align__(256) float g_static_ws[kHeaderFloats + kStaticWsFloats];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_setup_mu;
-float *g_ws_addr[kMaxDevices] = {};
 
 // out[t][n] = act(sum_k partial[k][t][n] + bias[n]), k summed in order; 8 channels a thread.
 __global__ void splitk_sum_kernel(const float *__restrict__ partial, int ksplit, long long T, int N,
@@ -66,19 +65,17 @@ __global__ void splitk_sum_kernel(const float *__restrict__ partial, int ksplit,
     *reinterpret_cast<uint4 *>(out + t * N + c0) = *reinterpret_cast<const uint4 *>(h);
 }
 
-// Address of this device's static workspace (looked up once per device).
-float *static_ws(int dev) {
-    std::lock_guard<std::mutex> lock(g_setup_mu);
-    if (!g_ws_addr[dev]) {
-        void *p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_static_ws);
-        if (e != cudaSuccess || !p) {
-            std::fprintf(stderr, "gcdr_k_conv_static: cudaGetSymbolAddress failed: %s\n", cudaGetErrorString(e));
-            return nullptr;
-        }
-        g_ws_addr[dev] = static_cast<float *>(p);
+// Device address of the current device's static workspace.  Looked up on every call (cheap
+// once the module is loaded), so the address stays right after a device reset reloads the
+// module at another address.
+float *static_ws() {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_ws);
+    if (e != cudaSuccess || !p) {
+        std::fprintf(stderr, "gcdr_k_conv_static: cudaGetSymbolAddress failed: %s\n", cudaGetErrorString(e));
+        return nullptr;
     }
-    return g_ws_addr[dev];
+    return static_cast<float *>(p);
 }
 
 }  // namespace
@@ -106,8 +103,8 @@ extern "C" int gcdr_k_conv_static(const gcdr_conv_desc *d, void *stream) {
         return GCDR_ERR_RANGE;
     }
     int dev = 0, sms = 148;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GCDR_ERR_DEVICE;
-    float *ws = static_ws(dev);
+    if (cudaGetDevice(&dev) != cudaSuccess) return GCDR_ERR_DEVICE;
+    float *ws = static_ws();
     if (!ws) return GCDR_ERR_DEVICE;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     int *err_word = reinterpret_cast<int *>(ws);

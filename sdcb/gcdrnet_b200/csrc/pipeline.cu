@@ -24,6 +24,25 @@ DevWeights::~DevWeights() {
     }
 }
 
+// Channel-shift groups (ends, offsets) -> ShiftSpec, with the equal-chunk shortcut.
+ShiftSpec make_shift(int ngroups, const int *ends, const int *offs) {
+    ShiftSpec o;
+    o.ngroups = ngroups < 0 ? 0 : ngroups > 5 ? 5 : ngroups;
+    for (int i = 0; i < o.ngroups; i++) {
+        o.ends[i] = ends[i];
+        o.offs[i] = offs[i];
+    }
+    // equal ceil-sized chunks (the last one shorter): channel group = c / gs
+    if (o.ngroups > 0) {
+        const int gs = o.ends[0];
+        bool uniform = gs > 0;
+        for (int i = 0; i < o.ngroups - 1; i++) uniform = uniform && o.ends[i] == (i + 1) * gs;
+        uniform = uniform && o.ends[o.ngroups - 1] > (o.ngroups - 1) * gs && o.ends[o.ngroups - 1] <= o.ngroups * gs;
+        o.gs = uniform ? gs : 0;
+    }
+    return o;
+}
+
 namespace {
 
 struct Packer {
@@ -67,21 +86,8 @@ std::vector<__half> pack_fc(const std::vector<float> &b, int C) {
 }
 
 ShiftSpec shift_spec(const ShiftW &s) {
-    ShiftSpec o;
-    o.ngroups = (int)s.ends.size();
-    for (int i = 0; i < o.ngroups && i < 5; i++) {
-        o.ends[i] = s.ends[i];
-        o.offs[i] = s.offs[i];
-    }
-    // equal ceil-sized chunks (the last one shorter): channel group = c / gs
-    if (o.ngroups > 0) {
-        const int gs = o.ends[0];
-        bool uniform = gs > 0;
-        for (int i = 0; i < o.ngroups - 1; i++) uniform = uniform && o.ends[i] == (i + 1) * gs;
-        uniform = uniform && o.ends[o.ngroups - 1] > (o.ngroups - 1) * gs && o.ends[o.ngroups - 1] <= o.ngroups * gs;
-        o.gs = uniform ? gs : 0;
-    }
-    return o;
+    const int n = (int)std::min(s.ends.size(), s.offs.size());
+    return make_shift(n, s.ends.data(), s.offs.data());
 }
 
 void pack_net(Packer &pk, const NetW &n, DevNet &d) {
@@ -855,10 +861,11 @@ int Worker::debug_intermediates(float *gc_in, float *gc_out, float *dr_in, float
     int rc = k_bgr2nhwc(d_src_, w_, h_, w_ * bpp_, fmt_, dx, ph_, pw_, stream_);
     cudaMemcpyAsync(x.data(), dx, n3 * 4, cudaMemcpyDeviceToHost, stream_);
     std::vector<__half> si;
-    if (simt_stem_ || debug_) {
+    if (simt_stem_) {
         cudaMemcpyAsync(r.data(), r_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
     } else {
-        // r = r_hi + r_lo from the DR stem input (interior rows of [H+2][W+2][16])
+        // r = r_hi + r_lo from the DR stem input (interior rows of [H+2][W+2][16]): the
+        // division-corrected image exactly as the DR stem reads it, debug mode or not
         si.resize((size_t)si_dr_.rows() * kStemInC);
         cudaMemcpyAsync(si.data(), si_dr_.p, si.size() * 2, cudaMemcpyDeviceToHost, stream_);
     }

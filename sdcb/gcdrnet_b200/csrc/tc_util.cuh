@@ -11,8 +11,6 @@
 namespace gcdr {
 namespace {
 
-constexpr long long kWaitCycles = 4000000000LL;   // ~2 s at 1.9 GHz
-
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -33,14 +31,16 @@ __device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait; false when the budget ran out or another role aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err) {
+// Bounded wait of at most `budget` SM cycles; false when the budget ran out or
+// another role aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err,
+                                          long long budget) {
     if (mbar_try(b, parity)) return true;
     long long t0 = clock64();
     while (true) {
         if (mbar_try(b, parity)) return true;
         if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > budget) {
             *abort_flag = 1;
             atomicOr(err, GCDR_ERR_FLAG_TIMEOUT);
             return false;

@@ -1,8 +1,8 @@
 """Builds the committed golden fixtures from the reference checkout.
 
-Run once in a container that has the reference mounted:
+Run once where the reference checkout is available, giving its root:
 
-    python tests/golden/make_fixtures.py /root/reference
+    python tests/golden/make_fixtures.py <reference checkout>
 
 It copies, unchanged, the reference's onnxruntime golden fixtures
 (tests/testdata/{small,pad,mid}_{src.png,shadow.f32,output.f32},
@@ -31,4 +31,6 @@ def main(ref: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_fixtures.py <reference checkout root>")
+    main(sys.argv[1])

@@ -7,11 +7,55 @@ import ctypes
 import numpy as np
 
 
-class ConvDesc(ctypes.Structure):
-    _fields_ = [("kind", ctypes.c_int), ("H", ctypes.c_int), ("W", ctypes.c_int), ("C", ctypes.c_int),
-                ("N", ctypes.c_int), ("inp", ctypes.c_void_p), ("weight", ctypes.c_void_p),
-                ("bias", ctypes.c_void_p), ("epilogue", ctypes.c_int), ("out", ctypes.c_void_p),
-                ("scratch", ctypes.c_void_p), ("nsplit", ctypes.c_int), ("ksplit", ctypes.c_int)]
+from sdcb.gcdrnet_b200 import ConvDesc  # noqa: F401  (gcdr_conv_desc)
+
+
+class Act(ctypes.Structure):
+    """gcdr_act: kind 0 tokens, 1 reflect-padded, 2 phase planes, 3 zero-padded."""
+    _fields_ = [("p", ctypes.c_void_p), ("H", ctypes.c_int), ("W", ctypes.c_int), ("C", ctypes.c_int),
+                ("kind", ctypes.c_int)]
+
+
+class Shift(ctypes.Structure):
+    """gcdr_shift: cumulative channel-group ends and offsets (at most 5 groups)."""
+    _fields_ = [("ngroups", ctypes.c_int), ("ends", ctypes.c_int * 5), ("offs", ctypes.c_int * 5)]
+
+    @classmethod
+    def of(cls, ends, offs):
+        s = cls()
+        s.ngroups = len(ends)
+        for g, (e, o) in enumerate(zip(ends, offs)):
+            s.ends[g] = e
+            s.offs[g] = o
+        return s
+
+
+def to_device_layout(lib, x_hwc_f16, kind):
+    """fp16 torch tensor [H][W][C] on the device -> the flat buffer of layout `kind` (1, 2, 3)."""
+    import torch
+    H, W, C = x_hwc_f16.shape
+    n = lib.gcdr_k_to_layout(None, H, W, C, kind, None, None)
+    assert n > 0
+    buf = torch.empty(n, dtype=torch.float16, device=x_hwc_f16.device)
+    assert lib.gcdr_k_to_layout(x_hwc_f16.data_ptr(), H, W, C, kind, buf.data_ptr(), None) == n
+    return buf
+
+
+def from_device_layout(buf, H, W, C, kind):
+    """Interior [H][W][C] (fp32 numpy) of a layout buffer (kind 0 tokens, 1/3 padded, 2 phase)."""
+    a = buf.float().cpu().numpy()
+    if kind == 0:
+        return a.reshape(H, W, C)
+    if kind in (1, 3):
+        return a.reshape(H + 2, W + 2, C)[1:H + 1, 1:W + 1]
+    P, Q = (H + 2) // 2, (W + 2) // 2
+    planes = a.reshape(2, 2, P, Q, C)
+    out = np.empty((H, W, C), np.float32)
+    for y in range(H):
+        for x in range(W):
+            yy, xx = y + 1, x + 1
+            out[y, x] = planes[yy & 1, xx & 1, yy >> 1, xx >> 1]
+    return out
 
 
 def pack_weights(w_onnx: np.ndarray) -> np.ndarray:
@@ -66,12 +110,17 @@ def run_conv(lib, kind, x_hwc, w_onnx, bias, epilogue=0, reference=False, nsplit
     return out.float().cpu().numpy()
 
 
-def torch_conv(kind, x_hwc, w_onnx, bias, epilogue=0):
-    """fp32 torch reference of one layer (input rounded to fp16 like the kernel's)."""
+def torch_conv(kind, x_hwc, w_onnx, bias, epilogue=0, round_operands=True):
+    """fp32 torch reference of one layer.  round_operands: input and weights
+    rounded to fp16 first, like the kernel's operands (the check then measures the
+    accumulation and output rounding only); False keeps them fp32, so the check
+    also covers the operand quantisation."""
     import torch
     import torch.nn.functional as F
-    x = torch.from_numpy(np.ascontiguousarray(x_hwc)).half().float().permute(2, 0, 1)[None]
-    w = torch.from_numpy(w_onnx).half().float()
+    x = torch.from_numpy(np.ascontiguousarray(x_hwc)).permute(2, 0, 1)[None]
+    w = torch.from_numpy(w_onnx)
+    if round_operands:
+        x, w = x.half().float(), w.half().float()
     b = torch.from_numpy(np.ascontiguousarray(bias, np.float32))
     if kind == 0:
         y = F.conv2d(F.pad(x, (1, 1, 1, 1), mode="reflect"), w, b)

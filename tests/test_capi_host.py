@@ -40,7 +40,7 @@ def test_model_topology_recognised():
         for b in blocks:
             a, w = b["shifts"]
             assert a["axis"] == 2 and w["axis"] == 3            # shift along H, then W (gc#48, gc#99)
-            assert a["offs"] == [2, 1, 0, -1, -2] == w["offs"]  # ChannelShiftOp.cs:440
+            assert a["offs"] == [2, 1, 0, -1, -2] == w["offs"]  # ChannelShiftOp.cs:158-161
         assert blocks[0]["shifts"][0]["ends"] == ends[0]
         assert blocks[1]["shifts"][0]["ends"] == ends[2]
 

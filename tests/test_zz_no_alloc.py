@@ -47,10 +47,15 @@ def _out_dims(kind, H, W):
 
 
 # (kind, H, W, C, N, epilogue, nsplit, ksplit, seed): GC pe3 at /8 of a small page
-# (stride 2, 18 k-blocks in 3 splits) and a DR fc2-like 1x1 token Gemm with relu.
+# (stride 2, 18 k-blocks in 3 splits), a DR fc2-like 1x1 token Gemm with relu, and the
+# two padded-pitch layouts (reflect border, zero border) at widths that are not a
+# multiple of 128: their grid rows carry two pitch columns per image row that the
+# partial-sum epilogue drops, packing the partials by pixel index.
 CALLS = [
     (1, 16, 20, 128, 160, 0, 1, 3, 11),
     (2, 18, 25, 256, 256, 2, 2, 4, 12),
+    (0, 20, 150, 64, 64, 0, 1, 3, 13),
+    (3, 16, 200, 32, 128, 2, 2, 9, 14),
 ]
 
 
@@ -59,6 +64,8 @@ def test_static_workspace_conv_matches_allocating_entry():
     from sdcb.gcdrnet_b200 import lib
     L = lib()
     for kind, H, W, C, N, ep, ns, ks, seed in CALLS:
+        Ho, Wo = _out_dims(kind, H, W)
+        assert ks * Ho * Wo * N <= STATIC_WS_FLOATS
         inp, wt, bt = _layer(L, kind, H, W, C, N, seed)
         Ho, Wo = _out_dims(kind, H, W)
         want = torch.full((Ho, Wo, N), float("nan"), dtype=torch.float16, device="cuda:0")
