@@ -50,7 +50,8 @@ WORKLOAD = (f"enhance 1600x1152 Bgr24 synthetic documents (seeded paper/shading/
 
 
 TRAFFIC_TABLE = os.path.join(ROOT, "profiles", "ncu_traffic_1600x1152.md")
-E2E_THREADS = 4   # concurrent GcdrEnhancer.enhance callers of the end-to-end measurement
+E2E_THREADS = 4   # concurrent GcdrEnhancer.enhance callers per GPU process in the end-to-end measurement
+C3_IMAGES = 512   # the end-to-end workload: documents drained from the shared host queue
 
 
 def ncu_traffic(op: str):
@@ -186,19 +187,58 @@ def rank_seeds(rank: int, n: int) -> list:
     return [rank * 1000 + s for s in range(n)]
 
 
-def max_over_ranks(x: float, dist=None, device=None) -> float:
-    """The largest `x` over all ranks (the slowest rank sets a multi-GPU time)."""
+def max_over_ranks(x: float, dist=None) -> float:
+    """The largest `x` over all ranks (the slowest rank sets a multi-GPU time).  The
+    ranks talk over the host (gloo): no NCCL and no GPU memory is involved."""
     if dist is None:
         return x
     import torch
-    t = torch.tensor([x], dtype=torch.float64, device=device)
+    t = torch.tensor([x], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def min_over_ranks(x: float, dist=None) -> float:
+    return -max_over_ranks(-x, dist)
+
+
+def gather_ints(x: int, dist=None, world: int = 1) -> list:
+    """x from every rank, in rank order (gloo)."""
+    if dist is None:
+        return [int(x)]
+    import torch
+    out = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(out, torch.tensor([int(x)], dtype=torch.int64))
+    return [int(t.item()) for t in out]
 
 
 def whole_job_rate(world: int, steps: int, seconds: float) -> float:
     """Images per second over the whole job: every rank enhances one image per step."""
     return world * steps / seconds
+
+
+def c3_pools(rank: int, world: int, barrier, nbytes: int):
+    """The c3 input pool (C3_IMAGES seeded Bgr24 documents, seed = index) and an output pool
+    of the same shape, as files every rank maps.  Rank 0 creates them; each rank generates
+    the images i = rank (mod world) with its share of the host cores."""
+    import tempfile
+    from sdcb.gcdrnet_b200 import dp, synth
+    tag = os.environ.get("TORCHELASTIC_RUN_ID", "") + "_" + os.environ.get("MASTER_PORT", str(os.getpid()))
+    base = os.path.join(tempfile.gettempdir(), f"gcdr_c3_{tag}")
+    if rank == 0:
+        dp.HostImagePool(base + ".in", C3_IMAGES, nbytes, create=True).close(remove=False)
+        dp.HostImagePool(base + ".out", C3_IMAGES, nbytes, create=True).close(remove=False)
+    barrier()
+    pin = dp.HostImagePool(base + ".in", C3_IMAGES, nbytes, create=False)
+    pout = dp.HostImagePool(base + ".out", C3_IMAGES, nbytes, create=False)
+    procs = max(1, min(32, host_threads() // world))
+    dp.fill_pool(pin, range(rank, C3_IMAGES, world), synth.DocumentMaker(W_IMG, H_IMG, 0), procs)
+    barrier()
+    # map every page into this process before the timed drain (a server's buffers are resident)
+    pin.arr.sum(dtype="uint64")
+    pout.arr[rank::world] = 0
+    barrier()
+    return pin, pout
 
 
 def host_threads() -> int:
@@ -301,13 +341,19 @@ def main():
     dev = torch.device("cuda", local)
     dist = None
     if world > 1:
+        # images are independent: the ranks only meet on the host (gloo barrier and timings,
+        # and the rendezvous store that carries the shared image queue); no NCCL anywhere
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
 
     def barrier():
         if dist is not None:
             dist.barrier()
+
+    # the c3 pool: C3_IMAGES seeded documents in one host file every rank maps, generated by
+    # all ranks together (spawned helper processes)
+    pool_in, pool_out = c3_pools(rank, world, barrier, W_IMG * H_IMG * 3)
 
     n_img = 4
     imgs = [synth.document(W_IMG, H_IMG, seed=sd) for sd in rank_seeds(rank, n_img)]
@@ -359,45 +405,70 @@ def main():
     with ClockSampler(physical_index(local), uuid) as clk:
         total_ms = timed(STREAMS)
     barrier()
-    total_ms = max_over_ranks(total_ms, dist, dev)
+    total_ms = max_over_ranks(total_ms, dist)
     value = whole_job_rate(world, args.steps * STREAMS, total_ms / 1000.0)
     clocks = clk.summary()
     barrier()
-    single_ms = max_over_ranks(timed(1), dist, dev)
+    single_ms = max_over_ranks(timed(1), dist)
     single_value = whole_job_rate(world, args.steps, single_ms / 1000.0)
 
-    # end to end through the public API (host buffers): E2E_THREADS host threads call
-    # GcdrEnhancer.enhance concurrently, as a server shares one enhancer (its worker pool
-    # rents each caller a worker: one image's host copies overlap another's kernels);
-    # step i is image i, taken by thread i % E2E_THREADS
+    # end to end through the public API (host buffers), the c3 workload: C3_IMAGES documents
+    # drained from one shared host queue by every rank (one process per GPU), each rank with
+    # E2E_THREADS host threads calling GcdrEnhancer.enhance on one shared enhancer (its worker
+    # pool rents each caller a worker: one image's host copies overlap another's kernels);
+    # results go back into a shared host pool.  Wall clock from the common start (a barrier)
+    # to the last rank's finish, on the host's monotonic clock (one clock for all ranks).
     enh = GcdrEnhancer.from_files(GC, DR, device=local)
     host_dst = [np.empty(nbytes, np.uint8) for _ in range(E2E_THREADS)]
 
-    def e2e_part(k: int, steps: int):
-        for i in range(k, steps, E2E_THREADS):
+    def warm(k: int):
+        for i in range(2):
             enh.enhance(imgs[i % n_img], W_IMG, H_IMG, W_IMG * 3, host_dst[k], W_IMG * 3, 0)
 
-    def e2e_run(steps: int):
-        th = [threading.Thread(target=e2e_part, args=(k, steps)) for k in range(E2E_THREADS)]
-        for t in th:
-            t.start()
-        for t in th:
-            t.join()
+    th = [threading.Thread(target=warm, args=(k,)) for k in range(E2E_THREADS)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
 
-    e2e_run(max(args.warmup, E2E_THREADS))    # every thread's worker is created and its graph captured
+    def work(i: int):
+        enh.enhance(pool_in.image(i), W_IMG, H_IMG, W_IMG * 3, pool_out.image(i), W_IMG * 3, 0)
+
+    from sdcb.gcdrnet_b200 import dp
+    if dist is not None:
+        store = dist.distributed_c10d._get_default_store()
+    else:
+        from torch.distributed import HashStore
+        store = HashStore()
+    queue = dp.SharedQueue(store, C3_IMAGES, rank, world, prefix="c3")
+    store.add("c3/ranks_seen", 1)
     barrier()
     torch.cuda.synchronize(dev)
-    t0 = time.perf_counter()
-    e2e_run(args.steps)
-    torch.cuda.synchronize(dev)
-    e2e_s = max_over_ranks(time.perf_counter() - t0, dist, dev)
+    t0 = time.monotonic()
+    did = dp.drain(queue, work, E2E_THREADS)
+    t1 = time.monotonic()
     barrier()
-    e2e_value = whole_job_rate(world, args.steps, e2e_s)
+    e2e_s = max_over_ranks(t1, dist) - min_over_ranks(t0, dist)
+    per_rank = gather_ints(did, dist, world)
+    ranks_seen = int(store.add("c3/ranks_seen", 0))
+    ndone, requeued = queue.counts()
+    e2e_value = C3_IMAGES / e2e_s
     # the same calls from one thread: the single-image latency of the API
     t0 = time.perf_counter()
     for i in range(min(args.steps, 10)):
         enh.enhance(imgs[i % n_img], W_IMG, H_IMG, W_IMG * 3, host_dst[0], W_IMG * 3, 0)
     e2e_single_ms = (time.perf_counter() - t0) * 1000.0 / min(args.steps, 10)
+
+    c3_check = None
+    if rank == 0:
+        # the drained results are the enhancements of their own images (spot check, untimed)
+        ref = np.empty(nbytes, np.uint8)
+        ids = sorted({0, C3_IMAGES // 2, C3_IMAGES - 1})
+        same = 0
+        for i in ids:
+            enh.enhance(pool_in.image(i), W_IMG, H_IMG, W_IMG * 3, ref, W_IMG * 3, 0)
+            same += int(np.array_equal(ref, pool_out.image(i)))
+        c3_check = {"images_checked": ids, "identical_to_a_direct_call": same == len(ids)}
 
     # live per-op profile -> dominant kernel roofline
     prof = worker.profile(reps=3)
@@ -445,7 +516,12 @@ def main():
                        "l2": "256 MB flush between timed steps (outside the events)",
                        "precision": "fp16 tensor-core layers (fp32 accumulate), fp32 stem/head/div6"},
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": nbytes,
-                    "d2h_bytes_per_step": nbytes, "api": "GcdrEnhancer.enhance (host numpy buffers)",
+                    "d2h_bytes_per_step": nbytes, "step": "one image",
+                    "api": "GcdrEnhancer.enhance (host buffers: shared host pool in, shared host pool out)",
+                    "workload": f"{C3_IMAGES} 1600x1152 Bgr24 documents (seeds 0-{C3_IMAGES - 1}) drained from one "
+                                f"shared host queue by {world} GPU process(es), {E2E_THREADS} calling threads each",
+                    "seconds": e2e_s, "per_rank_images": per_rank, "ranks_seen": ranks_seen,
+                    "images_done": ndone, "requeued": requeued, "check": c3_check,
                     "host_threads": E2E_THREADS, "single_thread_ms_per_image": e2e_single_ms},
             "roofline": {"kernel": name, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak, "traffic": ncu_traffic(name),
@@ -465,6 +541,9 @@ def main():
     for w in workers:
         w.close()
     enh.dispose()
+    barrier()
+    pool_in.close(remove=rank == 0)
+    pool_out.close(remove=rank == 0)
     if dist is not None:
         dist.destroy_process_group()
     return 0

@@ -16,13 +16,23 @@ from __future__ import annotations
 import numpy as np
 
 
+def _cubic_weights(n: int, cells: int) -> np.ndarray:
+    """[n][cells] weights of bicubic (Keys, a = -0.5) interpolation of `cells` grid nodes
+    spread over n pixels (node k at pixel (k + 0.5) * n / cells - 0.5), edge-clamped."""
+    t = (np.arange(n, dtype=np.float64) + 0.5) * cells / n - 0.5
+    i0 = np.floor(t).astype(np.int64)
+    wts = np.zeros((n, cells))
+    for k in range(-1, 3):
+        d = np.abs(t - (i0 + k))
+        kw = np.where(d <= 1, (1.5 * d - 2.5) * d * d + 1,
+                      np.where(d < 2, ((-0.5 * d + 2.5) * d - 4) * d + 2, 0.0))
+        np.add.at(wts, (np.arange(n), np.clip(i0 + k, 0, cells - 1)), kw)
+    return wts
+
+
 def _bicubic_field(gains: np.ndarray, h: int, w: int) -> np.ndarray:
-    from scipy.ndimage import zoom
-    g = np.pad(gains, 1, mode="edge")
-    z = zoom(g, ((h + 2 * h / 4) / g.shape[0], (w + 2 * w / 4) / g.shape[1]), order=3, mode="nearest")
-    y0 = (z.shape[0] - h) // 2
-    x0 = (z.shape[1] - w) // 2
-    return z[y0:y0 + h, x0:x0 + w]
+    """The 4x4 gain grid bicubically upsampled to h x w (separable: two small matrix products)."""
+    return _cubic_weights(h, gains.shape[0]) @ gains @ _cubic_weights(w, gains.shape[1]).T
 
 
 def document(width: int = 1600, height: int = 1152, seed: int = 0, fmt: int = 0, strokes: int = 200) -> np.ndarray:
@@ -55,7 +65,7 @@ def document(width: int = 1600, height: int = 1152, seed: int = 0, fmt: int = 0,
     if ys_all:
         ys, xs, vs = np.concatenate(ys_all), np.concatenate(xs_all), np.concatenate(vs_all)
         img[ys, xs, :] = vs[:, None] * shade[ys, xs][:, None]
-    img += rng.normal(0, 3, img.shape).astype(np.float32)
+    img += rng.standard_normal(img.shape, dtype=np.float32) * np.float32(3.0)
     bgr = np.clip(np.rint(img), 0, 255).astype(np.uint8)
     if fmt in (1, 3):
         bgr = bgr[:, :, ::-1]
@@ -63,3 +73,13 @@ def document(width: int = 1600, height: int = 1152, seed: int = 0, fmt: int = 0,
         a = rng.integers(0, 256, (height, width, 1), dtype=np.uint8)
         bgr = np.concatenate([bgr, a], axis=2)
     return np.ascontiguousarray(bgr)
+
+
+class DocumentMaker:
+    """document(width, height, seed=i, fmt) as a picklable callable of i (worker processes)."""
+
+    def __init__(self, width: int = 1600, height: int = 1152, fmt: int = 0):
+        self.width, self.height, self.fmt = width, height, fmt
+
+    def __call__(self, i: int) -> np.ndarray:
+        return document(self.width, self.height, seed=int(i), fmt=self.fmt)
