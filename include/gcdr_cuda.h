@@ -128,6 +128,13 @@ GCDR_API int gcdr_cuda_debug_intermediates(gcdr_cuda *w, float *gc_in, float *gc
 /* Debug: kernel launches per enhance in the captured graph, and the padded
  * shape the worker is bound to. */
 GCDR_API int gcdr_cuda_launch_count(const gcdr_cuda *w);
+/* Shape plans: a worker keeps the arena, op sequence and CUDA graph of up to 8
+ * image shapes (width, height, format, debug mode), least recently used
+ * evicted first and the cached arenas kept within a 12 GB budget (the
+ * reference caches 8 sizes, GcdrEnhancer.cs:45-46, 128-136, within the arena
+ * budget of VkPipeline2.cs:104-117).  captures: graphs captured so far (one
+ * per shape seen while not cached); plans: shapes held now. */
+GCDR_API int gcdr_cuda_plan_stats(const gcdr_cuda *w, int *captures, int *plans);
 /* Debug mode: the heads also write the shading map I_sm and the DR output as
  * fp32 planes, returned by gcdr_cuda_debug_intermediates (gc_out) and
  * gcdr_cuda_debug_output.  Re-captures the graph on the next enhance. */

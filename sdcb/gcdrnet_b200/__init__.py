@@ -134,6 +134,7 @@ def lib():
         L.gcdr_cuda_debug_output.argtypes = [vp, vp]
         L.gcdr_cuda_set_debug.argtypes = [vp, i]
         L.gcdr_cuda_launch_count.argtypes = [vp]
+        L.gcdr_cuda_plan_stats.argtypes = [vp, ctypes.POINTER(i), ctypes.POINTER(i)]
         L.gcdr_cuda_profile.argtypes = [vp, i, vp, i]
         L.gcdr_cuda_last_error.argtypes = [vp]
         L.gcdr_cuda_last_error.restype = cp
@@ -361,6 +362,13 @@ class CudaWorker:
     @property
     def launch_count(self) -> int:
         return lib().gcdr_cuda_launch_count(self._h)
+
+    @property
+    def plan_stats(self) -> tuple:
+        """(graph captures so far, shape plans held): one capture per shape not cached."""
+        c, p = ctypes.c_int(), ctypes.c_int()
+        self._check(lib().gcdr_cuda_plan_stats(self._h, ctypes.byref(c), ctypes.byref(p)))
+        return c.value, p.value
 
     def close(self):
         if self._h is not None:

@@ -152,6 +152,13 @@ extern "C" int gcdr_cuda_set_debug(gcdr_cuda *w, int on) {
 
 extern "C" int gcdr_cuda_launch_count(const gcdr_cuda *w) { return w ? w->w->launches() : 0; }
 
+extern "C" int gcdr_cuda_plan_stats(const gcdr_cuda *w, int *captures, int *plans) {
+    if (!w) return GCDR_ERR_ARG;
+    if (captures) *captures = w->w->captures();
+    if (plans) *plans = w->w->plans();
+    return GCDR_OK;
+}
+
 extern "C" int gcdr_cuda_profile(gcdr_cuda *w, int reps, gcdr_op_profile *out, int cap) {
     if (!w || reps < 1) return -GCDR_ERR_ARG;
     std::vector<double> ms;
@@ -186,9 +193,13 @@ struct gcdr_enhancer {
     std::atomic<int64_t> pools{0}, workers{0}, evicted{0};
     std::atomic<int> inject{0};
     static constexpr int kMaxIdle = 4;                 // GcdrEnhancer.cs:45 MaxPerSize
-    static constexpr int64_t kIdleBudget = 3LL << 30;  // VkPipeline2.cs:137-138
+    // device bytes of the idle workers beyond the first (VkPipeline2.cs:137-138 keeps 3 GB for
+    // one arena; here a worker holds several shape plans, Worker::kPlanBudget each at most)
+    static constexpr int64_t kIdleBudget = 32LL << 30;
 
-    int rent(std::unique_ptr<Worker> &w, uint64_t &gen, std::string &err) {
+    // An idle worker, preferring one that holds a plan (arena + graph) for this image shape,
+    // else a new one.
+    int rent(std::unique_ptr<Worker> &w, uint64_t &gen, std::string &err, int width, int height, int fmt) {
         {
             std::lock_guard<std::mutex> g(mu);
             gen = generation;
@@ -198,8 +209,11 @@ struct gcdr_enhancer {
                 pools++;
             }
             if (!idle.empty()) {
-                w = std::move(idle.front());
-                idle.pop_front();
+                auto it = idle.begin();
+                for (auto j = idle.begin(); j != idle.end(); ++j)
+                    if ((*j)->has_plan(width, height, fmt)) { it = j; break; }
+                w = std::move(*it);
+                idle.erase(it);
                 idle_bytes -= w->device_bytes();
                 return GCDR_OK;
             }
@@ -271,7 +285,7 @@ extern "C" int gcdr_enhancer_enhance(gcdr_enhancer *e, const uint8_t *src, size_
         std::unique_ptr<Worker> w;
         uint64_t gen = 0;
         std::string msg;
-        int rc = e->rent(w, gen, msg);
+        int rc = e->rent(w, gen, msg, width, height, pixel_format);
         if (rc) { put_err(err, err_cap, msg); return rc; }
         if (e->inject.load() > 0 && e->inject.fetch_sub(1) > 0) w->inject_device_loss = 1;
         rc = w->enhance_host(src, width, height, src_stride, dst, dst_stride, pixel_format);

@@ -2,6 +2,7 @@
 // DR-Net, CUDA-graph capture and the worker's enhance entry points.
 #include "pipeline.h"
 
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
@@ -156,12 +157,24 @@ int upload_weights(const Model &m, int device, std::shared_ptr<DevWeights> &out,
 
 Worker::Worker(int device, std::shared_ptr<DevWeights> w) : device_(device), weights_(std::move(w)) {}
 
+void ShapePlan::release() {
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (arena) cudaFree(arena);   // waits for the device: no launch of this plan is in flight after it
+    exec = nullptr;
+    graph = nullptr;
+    arena = nullptr;
+    arena_bytes = 0;
+    ops.clear();
+    info.clear();
+}
+
 Worker::~Worker() {
     cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
-    if (exec_) cudaGraphExecDestroy(exec_);
-    if (graph_) cudaGraphDestroy(graph_);
-    if (arena_) cudaFree(arena_);
+    release_current();
+    for (auto &p : cache_) p.release();
+    cache_.clear();
     if (h_src_) cudaFreeHost(h_src_);
     if (h_dst_) cudaFreeHost(h_dst_);
     if (h_err_) cudaFreeHost(h_err_);
@@ -197,10 +210,68 @@ int Worker::init(std::string &err) {
 }
 
 void Worker::set_debug(bool on) {
-    if (on != debug_) {
-        debug_ = on;
-        bound_ = false;   // re-plan: the head kernels write the debug planes
-    }
+    debug_ = on;   // the next bind finds or builds a plan in this mode (the heads write the debug planes)
+}
+
+int64_t Worker::device_bytes() const {
+    int64_t b = (int64_t)arena_bytes_;
+    for (const auto &p : cache_) b += (int64_t)p.arena_bytes;
+    return b;
+}
+
+bool Worker::has_plan(int w, int h, int fmt) const {
+    if (bound_ && w == w_ && h == h_ && fmt == fmt_ && plan_debug_ == debug_) return true;
+    for (const auto &p : cache_)
+        if (p.w == w && p.h == h && p.fmt == fmt && p.debug == debug_) return true;
+    return false;
+}
+
+void Worker::stash() {
+    ShapePlan p;
+    p.w = w_; p.h = h_; p.fmt = fmt_; p.H = H_; p.W = W_; p.ph = ph_; p.pw = pw_; p.bpp = bpp_;
+    p.debug = plan_debug_;
+    p.arena = arena_; p.arena_bytes = arena_bytes_;
+    p.gcb = gcb_; p.drb = drb_;
+    p.r = r_; p.ism = ism_; p.ydbg = ydbg_;
+    p.si_gc = si_gc_; p.si_dr = si_dr_;
+    p.ws = ws_;
+    p.d_src = d_src_; p.d_dst = d_dst_; p.d_err = d_err_;
+    p.ops = std::move(ops_);
+    p.info = std::move(info_);
+    p.graph = graph_; p.exec = exec_;
+    p.launches = launches_;
+    p.last_use = tick_;
+    cache_.push_back(std::move(p));
+    arena_ = nullptr; arena_bytes_ = 0;
+    graph_ = nullptr; exec_ = nullptr;
+    ops_.clear(); info_.clear();
+    bound_ = false;
+}
+
+void Worker::restore(ShapePlan &&p) {
+    w_ = p.w; h_ = p.h; fmt_ = p.fmt; H_ = p.H; W_ = p.W; ph_ = p.ph; pw_ = p.pw; bpp_ = p.bpp;
+    plan_debug_ = p.debug;
+    arena_ = p.arena; arena_bytes_ = p.arena_bytes;
+    gcb_ = p.gcb; drb_ = p.drb;
+    r_ = p.r; ism_ = p.ism; ydbg_ = p.ydbg;
+    si_gc_ = p.si_gc; si_dr_ = p.si_dr;
+    ws_ = p.ws;
+    d_src_ = p.d_src; d_dst_ = p.d_dst; d_err_ = p.d_err;
+    ops_ = std::move(p.ops);
+    info_ = std::move(p.info);
+    graph_ = p.graph; exec_ = p.exec;
+    launches_ = p.launches;
+    p.arena = nullptr; p.graph = nullptr; p.exec = nullptr;   // owned by the worker now
+}
+
+void Worker::release_current() {
+    if (exec_) cudaGraphExecDestroy(exec_);
+    if (graph_) cudaGraphDestroy(graph_);
+    if (arena_) cudaFree(arena_);
+    exec_ = nullptr; graph_ = nullptr; arena_ = nullptr; arena_bytes_ = 0;
+    ops_.clear(); info_.clear();
+    launches_ = 0;
+    bound_ = false;
 }
 
 namespace {
@@ -406,11 +477,11 @@ int Worker::plan_arena() {
     Alloc al;
     plan_net(al, gcb_, w.gc, H_, W_);
     plan_net(al, drb_, w.dr, H_, W_);
-    al.take(reinterpret_cast<void **>(&r_), simt_stem_ || debug_ ? (size_t)H_ * W_ * 3 * 4 : 256);
+    al.take(reinterpret_cast<void **>(&r_), simt_stem_ || plan_debug_ ? (size_t)H_ * W_ * 3 * 4 : 256);
     al.act(si_gc_, H_, W_, kStemInC, LAY_PADREFL);
     al.act(si_dr_, H_, W_, kStemInC, LAY_PADREFL);
-    al.take(reinterpret_cast<void **>(&ism_), debug_ ? (size_t)H_ * W_ * 3 * 4 : 256);
-    al.take(reinterpret_cast<void **>(&ydbg_), debug_ ? (size_t)H_ * W_ * 3 * 4 : 256);
+    al.take(reinterpret_cast<void **>(&ism_), plan_debug_ ? (size_t)H_ * W_ * 3 * 4 : 256);
+    al.take(reinterpret_cast<void **>(&ydbg_), plan_debug_ ? (size_t)H_ * W_ * 3 * 4 : 256);
     const size_t img = (size_t)h_ * w_ * bpp_;
     al.take(reinterpret_cast<void **>(&d_src_), img + 16);
     al.take(reinterpret_cast<void **>(&d_dst_), img + 16);
@@ -418,19 +489,24 @@ int Worker::plan_arena() {
     const size_t wsf = std::max(partial_floats(w.gc, H_, W_, num_sms_), partial_floats(w.dr, H_, W_, num_sms_));
     al.take(reinterpret_cast<void **>(&ws_), std::max(wsf, (size_t)64) * 4);
     const size_t need = al.off;
-    // grow-only within the budget (VkPipeline2.cs:104-117): 1/8 headroom first, 1/4 on regrowth
-    const size_t budget = size_t(3) << 30;
-    bool shrink = arena_ && arena_bytes_ > budget && need <= budget;
-    if (!arena_ || arena_bytes_ < need || shrink) {
-        if (arena_) { cudaFree(arena_); arena_ = nullptr; arena_bytes_ = 0; }
-        size_t div = arena_bytes_ ? 4 : 8;
-        size_t cap = need / div * (div + 1) <= budget ? need / div * (div + 1) : need;
-        if (cudaMalloc(&arena_, cap) != cudaSuccess) {
-            cudaGetLastError();
-            return fail(GCDR_ERR_OOM, "arena: cudaMalloc failed");
-        }
-        arena_bytes_ = cap;
+    // one arena per shape plan, sized exactly; the plan cache keeps the sum of the cached
+    // plans' arenas within kPlanBudget (the reference's arena budget, VkPipeline2.cs:104-117),
+    // evicting the least recently used shapes first
+    size_t cached = 0;
+    for (const auto &p : cache_) cached += p.arena_bytes;
+    while (!cache_.empty() && ((int)cache_.size() >= kMaxPlans || cached + need > kPlanBudget)) {
+        auto lru = std::min_element(cache_.begin(), cache_.end(),
+                                    [](const ShapePlan &a, const ShapePlan &b) { return a.last_use < b.last_use; });
+        cached -= lru->arena_bytes;
+        lru->release();
+        cache_.erase(lru);
     }
+    if (cudaMalloc(&arena_, need) != cudaSuccess) {
+        cudaGetLastError();
+        arena_ = nullptr;
+        return fail(GCDR_ERR_OOM, "arena: cudaMalloc failed");
+    }
+    arena_bytes_ = need;
     for (auto &it : al.items) *it.first = arena_ + it.second;
     // zero borders of the stride-2 inputs (LAY_PHASE) and everything else once per plan
     if (cudaMemsetAsync(arena_, 0, need, stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "arena memset failed");
@@ -657,10 +733,10 @@ int Worker::build_ops() {
             ha.is_dr = which;
             if (!which) {
                 ha.r_out = r_;
-                ha.ism_out = debug_ ? ism_ : nullptr;
+                ha.ism_out = plan_debug_ ? ism_ : nullptr;
             } else {
                 ha.dst = d_dst_;
-                ha.y_out = debug_ ? ydbg_ : nullptr;
+                ha.y_out = plan_debug_ ? ydbg_ : nullptr;
             }
             ops_.push_back([ha, this](cudaStream_t st) { return head_launch(ha, st) ? fail(GCDR_ERR_DEVICE, std::string("head launch: ") + last_launch_error()) : 0; });
             launches_++;
@@ -676,12 +752,12 @@ int Worker::build_ops() {
             hp.is_dr = which;
             if (!which) {
                 hp.si_out = si_dr_;
-                hp.r_out = debug_ ? r_ : nullptr;
-                hp.ism_out = debug_ ? ism_ : nullptr;
+                hp.r_out = plan_debug_ ? r_ : nullptr;
+                hp.ism_out = plan_debug_ ? ism_ : nullptr;
             } else {
                 hp.img = img;
                 hp.dst = d_dst_;
-                hp.y_out = debug_ ? ydbg_ : nullptr;
+                hp.y_out = plan_debug_ ? ydbg_ : nullptr;
             }
             conv_op(a, EPI_HEAD, pre + "head", head_flops, head_bytes);
         }
@@ -739,20 +815,37 @@ int Worker::capture() {
 }
 
 int Worker::bind(int w, int h, int fmt) {
-    if (bound_ && w == w_ && h == h_ && fmt == fmt_) return GCDR_OK;
-    bound_ = false;
+    ++tick_;
+    if (bound_ && w == w_ && h == h_ && fmt == fmt_ && plan_debug_ == debug_) return GCDR_OK;
+    if (cudaSetDevice(device_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "cudaSetDevice");
+    if (cudaStreamSynchronize(stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "stream sync");
+    // the shape's plan may be cached: swap it in, graph and all
+    for (size_t i = 0; i < cache_.size(); i++) {
+        ShapePlan &p = cache_[i];
+        if (p.w != w || p.h != h || p.fmt != fmt || p.debug != debug_) continue;
+        ShapePlan hit = std::move(p);
+        cache_.erase(cache_.begin() + (long)i);
+        if (bound_) stash();
+        else release_current();
+        restore(std::move(hit));
+        bound_ = true;
+        return GCDR_OK;
+    }
+    // a new shape: plan its arena, build its ops, capture its graph
+    if (bound_) stash();
+    else release_current();   // the leftovers of a plan that failed part way
     w_ = w; h_ = h; fmt_ = fmt;
     bpp_ = fmt >= 2 ? 4 : 3;
     ph_ = (-h) & 31; pw_ = (-w) & 31;
     H_ = h + ph_; W_ = w + pw_;
-    if (cudaSetDevice(device_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "cudaSetDevice");
-    if (cudaStreamSynchronize(stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "stream sync");
+    plan_debug_ = debug_;
     int rc = plan_arena();
     if (rc) return rc;
     rc = build_ops();
     if (rc) return rc;
     rc = capture();
     if (rc) return rc;
+    captures_++;
     bound_ = true;
     return GCDR_OK;
 }
@@ -869,12 +962,12 @@ int Worker::debug_intermediates(float *gc_in, float *gc_out, float *dr_in, float
         si.resize((size_t)si_dr_.rows() * kStemInC);
         cudaMemcpyAsync(si.data(), si_dr_.p, si.size() * 2, cudaMemcpyDeviceToHost, stream_);
     }
-    if (gc_out && debug_) cudaMemcpyAsync(gc_out, ism_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
-    if (dr_out && debug_) cudaMemcpyAsync(dr_out, ydbg_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
+    if (gc_out && plan_debug_) cudaMemcpyAsync(gc_out, ism_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
+    if (dr_out && plan_debug_) cudaMemcpyAsync(dr_out, ydbg_, n3 * 4, cudaMemcpyDeviceToHost, stream_);
     cudaError_t e = cudaStreamSynchronize(stream_);
     cudaFree(dx);
     if (rc || e != cudaSuccess) return fail(GCDR_ERR_DEVICE, "debug copy failed");
-    if ((gc_out || dr_out) && !debug_) return fail(GCDR_ERR_ARG, "shading map / output need debug mode (gcdr_cuda_set_debug)");
+    if ((gc_out || dr_out) && !plan_debug_) return fail(GCDR_ERR_ARG, "shading map / output need debug mode (gcdr_cuda_set_debug)");
     if (!si.empty())
         for (int yy = 0; yy < H_; yy++)
             for (int xx = 0; xx < W_; xx++) {

@@ -69,6 +69,31 @@ struct OpInfo {
     int tensor = 0;      // 1: tcgen05 kernel
 };
 
+// Everything that depends on the bound shape (width, height, pixel format, debug mode): the
+// shape's own device arena and the buffers planned in it, the op sequence over those buffers
+// and its CUDA graph.  A worker keeps up to Worker::kMaxPlans of them, least recently used
+// evicted first (the reference caches up to 8 sizes per enhancer, GcdrEnhancer.cs:45-46,
+// 128-136), so alternating sizes re-use their graphs instead of re-planning.
+struct ShapePlan {
+    int w = 0, h = 0, fmt = -1, H = 0, W = 0, ph = 0, pw = 0, bpp = 3;
+    bool debug = false;
+    uint8_t *arena = nullptr;
+    size_t arena_bytes = 0;
+    NetBufs gcb, drb;
+    float *r = nullptr, *ism = nullptr, *ydbg = nullptr;
+    Act si_gc, si_dr;
+    float *ws = nullptr;
+    uint8_t *d_src = nullptr, *d_dst = nullptr;
+    int *d_err = nullptr;
+    std::vector<std::function<int(cudaStream_t)>> ops;
+    std::vector<OpInfo> info;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int launches = 0;
+    uint64_t last_use = 0;
+    void release();   // frees the arena and the graph
+};
+
 class Worker {
 public:
     Worker(int device, std::shared_ptr<DevWeights> w);
@@ -78,8 +103,19 @@ public:
     int enhance_device(const uint8_t *d_src, int w, int h, uint8_t *d_dst, int fmt, cudaStream_t st);
     int debug_intermediates(float *gc_in, float *gc_out, float *dr_in, float *dr_out);
     void set_debug(bool on);
-    int64_t device_bytes() const { return (int64_t)arena_bytes_; }
+    // device bytes of every cached shape's arena (VkPipeline2.cs:141's DeviceBytes)
+    int64_t device_bytes() const;
     int launches() const { return launches_; }
+    // graph captures so far (one per new shape), shapes held (bound + cached)
+    int captures() const { return captures_; }
+    int plans() const { return (int)cache_.size() + (bound_ ? 1 : 0); }
+    // whether the worker holds a plan for this image shape (the pool's rent preference)
+    bool has_plan(int w, int h, int fmt) const;
+    static constexpr int kMaxPlans = 8;                     // GcdrEnhancer.cs:45-46
+    // arena bytes over all of a worker's plans: a 4096 x 3072 shape's arena is 2.9 GB (1600 x 1152:
+    // 0.43 GB, measured), so a
+    // budget of a few such shapes (of the B200's 180 GB)
+    static constexpr size_t kPlanBudget = size_t(12) << 30;
     const std::vector<OpInfo> &op_info() const { return info_; }
     // Runs the bound op sequence `reps` times eagerly with CUDA events around each
     // op; ms[i] = mean duration of op i.
@@ -90,6 +126,9 @@ public:
 
 private:
     int bind(int w, int h, int fmt);
+    void stash();                   // current plan -> cache_
+    void restore(ShapePlan &&p);    // cache entry -> current plan
+    void release_current();
     int plan_arena();
     int build_ops();
     int run_ops(cudaStream_t st);
@@ -130,6 +169,10 @@ private:
     cudaGraph_t graph_ = nullptr;
     cudaGraphExec_t exec_ = nullptr;
     int launches_ = 0;
+    bool plan_debug_ = false;       // debug mode the current plan was built in
+    std::vector<ShapePlan> cache_;  // plans not bound right now
+    uint64_t tick_ = 0;
+    int captures_ = 0;
     bool bias_fail_ = false;
     std::string err_;
 };
