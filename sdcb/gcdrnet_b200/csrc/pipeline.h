@@ -113,8 +113,7 @@ public:
     bool has_plan(int w, int h, int fmt) const;
     static constexpr int kMaxPlans = 8;                     // GcdrEnhancer.cs:45-46
     // arena bytes over all of a worker's plans: a 4096 x 3072 shape's arena is 2.9 GB (1600 x 1152:
-    // 0.43 GB, measured), so a
-    // budget of a few such shapes (of the B200's 180 GB)
+    // 0.43 GB, measured), so the budget holds a few of the largest shapes (of the B200's 180 GB)
     static constexpr size_t kPlanBudget = size_t(12) << 30;
     const std::vector<OpInfo> &op_info() const { return info_; }
     // Runs the bound op sequence `reps` times eagerly with CUDA events around each
