@@ -234,9 +234,11 @@ def c3_pools(rank: int, world: int, barrier, nbytes: int):
     procs = max(1, min(32, host_threads() // world))
     dp.fill_pool(pin, range(rank, C3_IMAGES, world), synth.DocumentMaker(W_IMG, H_IMG, 0), procs)
     barrier()
-    # map every page into this process before the timed drain (a server's buffers are resident)
-    pin.arr.sum(dtype="uint64")
-    pout.arr[rank::world] = 0
+    # map every page of both pools into this process before the timed drain (a server's
+    # buffers are resident): one read per input page, one write per output page
+    flat_in, flat_out = pin.arr.reshape(-1), pout.arr.reshape(-1)
+    int(flat_in[::4096].sum(dtype="uint64"))
+    flat_out[::4096] = 0
     barrier()
     return pin, pout
 
@@ -450,6 +452,7 @@ def main():
     barrier()
     e2e_s = max_over_ranks(t1, dist) - min_over_ranks(t0, dist)
     per_rank = gather_ints(did, dist, world)
+    per_rank_ms = gather_ints(int(1000 * (t1 - t0)), dist, world)
     ranks_seen = int(store.add("c3/ranks_seen", 0))
     ndone, requeued = queue.counts()
     e2e_value = C3_IMAGES / e2e_s
@@ -520,7 +523,8 @@ def main():
                     "api": "GcdrEnhancer.enhance (host buffers: shared host pool in, shared host pool out)",
                     "workload": f"{C3_IMAGES} 1600x1152 Bgr24 documents (seeds 0-{C3_IMAGES - 1}) drained from one "
                                 f"shared host queue by {world} GPU process(es), {E2E_THREADS} calling threads each",
-                    "seconds": e2e_s, "per_rank_images": per_rank, "ranks_seen": ranks_seen,
+                    "seconds": e2e_s, "per_rank_images": per_rank, "per_rank_ms": per_rank_ms,
+                    "ranks_seen": ranks_seen, "host_cpus": host_threads(),
                     "images_done": ndone, "requeued": requeued, "check": c3_check,
                     "host_threads": E2E_THREADS, "single_thread_ms_per_image": e2e_single_ms},
             "roofline": {"kernel": name, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,

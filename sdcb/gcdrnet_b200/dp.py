@@ -69,17 +69,19 @@ class SharedQueue:
 
     def take(self, poll_s: float = 0.005):
         """The next index to work on, or None when every index is done."""
+        self.heartbeat(force=False)
+        n = int(self.store.add(self._k("next"), 1)) - 1
+        if n < self.total:
+            return self._claim(n)       # two store round trips per fresh index
+        # fresh indices exhausted: requeued ones (a dead worker's, put back by reap()), until
+        # every index is done
         while True:
             self.heartbeat(force=False)
-            # requeued indices first (those of a dead worker); one store round trip when there are none
             rq_len = self._count("rq_len")
             if rq_len and self._count("rq_taken") < rq_len:
                 slot = int(self.store.add(self._k("rq_taken"), 1)) - 1
                 if slot < rq_len:
                     return self._claim(int(self.store.get(self._k("rq", slot))))
-            n = int(self.store.add(self._k("next"), 1)) - 1
-            if n < self.total:
-                return self._claim(n)
             if self._count("ndone") >= self.total:
                 return None
             self.reap()
