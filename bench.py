@@ -312,7 +312,8 @@ def run_reference(args):
         "config": {"workload": WORKLOAD, "image_hw": [H_IMG, W_IMG],
                    "impl_note": "CPU oracle restating the reference CPU path, all host threads, rank 0"},
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": cores, "kind": "port",
-                         "sample": f"{len(times)} full 1600x1152 images (of {args.steps} asked; time budget {budget:.0f}s)"},
+                         "sample": f"{len(times)} full 1600x1152 images (of {args.steps} asked; time budget {budget:.0f}s)",
+                         "isa": O.isa(), "cpu_model": O.cpu_model()},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -499,8 +500,10 @@ def main():
     parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, cores, n, want = cpu_baseline_oracle(imgs[0], W_IMG, H_IMG)
+        from oracle import gcdr_oracle as O
         cpu = {"value": v, "unit": "images/s", "cores": cores, "kind": "port",
-               "sample": f"{n} full 1600x1152 Bgr24 image(s), CPU oracle (OpenMP C restatement)"}
+               "sample": f"{n} full 1600x1152 Bgr24 image(s), CPU oracle (OpenMP C restatement)",
+               "isa": O.isa(), "cpu_model": O.cpu_model()}
         # the benchmark's own output (public API, first document) against the oracle's, untimed
         got = np.empty(nbytes, np.uint8)
         enh.enhance(imgs[0], W_IMG, H_IMG, W_IMG * 3, got, W_IMG * 3, 0)

@@ -27,7 +27,9 @@ import numpy as np
 from .onnx_model import OnnxGraph, split_sizes
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "_build", "libgcdr_oracle.so")
+LIB_PATH = os.path.join(_HERE, "_build", "libgcdr_oracle.so")            # AVX2 + FMA
+LIB512_PATH = os.path.join(_HERE, "_build", "libgcdr_oracle_avx512.so")  # x86-64-v4 (AVX-512)
+_V4_FLAGS = ("avx512f", "avx512bw", "avx512vl", "avx512dq", "avx512cd")
 
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
@@ -36,28 +38,58 @@ _lib = None
 
 
 def build(force: bool = False) -> str:
-    """Compile gcdr_oracle.c into oracle/_build/libgcdr_oracle.so (gcc, OpenMP)."""
+    """Compile gcdr_oracle.c (gcc, OpenMP) twice: oracle/_build/libgcdr_oracle.so for AVX2 +
+    FMA hosts and libgcdr_oracle_avx512.so for AVX-512 (x86-64-v4) hosts.  The libraries
+    are built once and may run on another x86 host; lib() loads the widest one the host
+    runs.  Both give bit-identical results on the golden and benchmark images."""
     src = os.path.join(_HERE, "gcdr_oracle.c")
-    if not force and os.path.exists(LIB_PATH) and os.path.getmtime(LIB_PATH) >= os.path.getmtime(src):
-        return LIB_PATH
     import subprocess
     os.makedirs(os.path.dirname(LIB_PATH), exist_ok=True)
-    tmp = LIB_PATH + ".tmp%d" % os.getpid()
-    # AVX2+FMA only: the library is built once and may run on another x86 host.
-    cmd = ["gcc", "-O3", "-mavx2", "-mfma", "-fopenmp", "-fPIC", "-shared",
-           "-fvisibility=hidden", "-o", tmp, src, "-lm"]
-    subprocess.check_call(cmd)
-    os.replace(tmp, LIB_PATH)
+    for path, isa in ((LIB_PATH, ["-mavx2", "-mfma"]), (LIB512_PATH, ["-march=x86-64-v4", "-mprefer-vector-width=512"])):
+        if not force and os.path.exists(path) and os.path.getmtime(path) >= os.path.getmtime(src):
+            continue
+        tmp = path + ".tmp%d" % os.getpid()
+        subprocess.check_call(["gcc", "-O3"] + isa + ["-fopenmp", "-fPIC", "-shared", "-fvisibility=hidden",
+                                                      "-o", tmp, src, "-lm"])
+        os.replace(tmp, path)
     return LIB_PATH
+
+
+def _host_flags() -> set:
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("flags"):
+                    return set(line.split(":", 1)[1].split())
+    except OSError:
+        pass
+    return set()
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def isa() -> str:
+    """The instruction set of the oracle library lib() loads on this host."""
+    return "avx512 (x86-64-v4)" if all(f in _host_flags() for f in _V4_FLAGS) else "avx2+fma"
 
 
 def lib():
     global _lib
     if _lib is not None:
         return _lib
-    if not os.path.exists(LIB_PATH):
+    path = LIB512_PATH if isa().startswith("avx512") else LIB_PATH
+    if not os.path.exists(path):
         build()
-    L = ctypes.CDLL(LIB_PATH)
+    L = ctypes.CDLL(path)
     i, sz, f = ctypes.c_int, ctypes.c_size_t, ctypes.c_float
     L.orc_conv2d.argtypes = [_f32p, i, i, i, _f32p, ctypes.c_void_p, i, i, i, i, i, _f32p]
     L.orc_maxpool2_relu.argtypes = [_f32p, i, i, i, _f32p]

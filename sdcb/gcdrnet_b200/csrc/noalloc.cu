@@ -38,7 +38,6 @@ constexpr long long kHeaderFloats = 64;
 constexpr long long kStaticWsFloats = GCDR_STATIC_WS_BYTES / 4;
 static __device__ __align__(256) float g_static_ws[kHeaderFloats + kStaticWsFloats];
 
-
 // out[t][n] = act(sum_k partial[k][t][n] + bias[n]), k summed in order; 8 channels a thread.
 __global__ void splitk_sum_kernel(const float *__restrict__ partial, int ksplit, long long T, int N,
                                   const float *__restrict__ bias, int relu, __half *__restrict__ out) {

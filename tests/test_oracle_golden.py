@@ -93,3 +93,27 @@ def test_post_rounds_crops_and_copies_alpha():
         if bpp == 4:
             assert np.array_equal(px[:, :, 3], src.reshape(h, stride)[:, : w * 4].reshape(h, w, 4)[:, :, 3])
         assert np.all(rows[:, w * bpp:] == 0xA5)
+
+
+def test_oracle_builds_agree_bit_for_bit():
+    """The AVX2 and AVX-512 builds of the oracle give identical results (the CPU
+    baseline uses the widest one the host runs)."""
+    import ctypes
+    import numpy as np
+    from oracle import gcdr_oracle as O
+    O.build()
+    if not O.isa().startswith("avx512"):
+        pytest.skip("host without AVX-512")
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((20, 30, 32)).astype(np.float32)
+    w = rng.standard_normal((48, 32, 3, 3)).astype(np.float32)
+    b = rng.standard_normal(48).astype(np.float32)
+    outs = []
+    for path in (O.LIB_PATH, O.LIB512_PATH):
+        L = ctypes.CDLL(path)
+        vp, i = ctypes.c_void_p, ctypes.c_int
+        L.orc_conv2d.argtypes = [vp, i, i, i, vp, vp, i, i, i, i, i, vp]
+        out = np.empty((20, 30, 48), np.float32)
+        L.orc_conv2d(x.ctypes.data, 20, 30, 32, w.ctypes.data, b.ctypes.data, 48, 3, 1, 1, 1, out.ctypes.data)
+        outs.append(out)
+    assert np.array_equal(outs[0], outs[1])
