@@ -177,6 +177,17 @@ GCDR_API void gcdr_enhancer_pool_stats(const gcdr_enhancer *e, int64_t *pools,
  * touching the GPU (host-side fault injection, the analogue of setting
  * Dev.Lost in VulkanDeviceLossTests.cs:14-33). */
 GCDR_API void gcdr_enhancer_inject_device_loss(gcdr_enhancer *e, int count);
+/* Page-locks the caller's host buffer [p, p + bytes) for every device
+ * (cudaHostRegister, portable), or releases it (before the memory is freed).
+ * Enhance calls whose source or destination lies wholly in page-locked memory
+ * (registered here, or allocated pinned) copy it by DMA directly, in any row
+ * stride, instead of through the worker's pinned staging: the host then moves
+ * each image once instead of three times.  A destination apart from the
+ * source is written by DMA right behind the graph; after a device error its
+ * contents are unspecified (the source is untouched, so the retry is exact).
+ * No counterpart in the reference (its buffers are managed Spans). */
+GCDR_API int gcdr_host_register(void *p, size_t bytes);
+GCDR_API int gcdr_host_unregister(void *p);
 /* GcdrEnhancer.Dispose (GcdrEnhancer.cs:325-331). */
 GCDR_API void gcdr_enhancer_destroy(gcdr_enhancer *e);
 

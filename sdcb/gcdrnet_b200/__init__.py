@@ -22,7 +22,7 @@ import os
 import threading
 
 __all__ = ["GcdrBackend", "GcdrPixelFormat", "GcdrEnhancer", "CudaWorker", "ConvDesc", "lib", "library_path",
-           "GcdrError", "ArgumentError", "ArgumentOutOfRangeError", "NotSupportedError",
+           "register_host", "unregister_host", "GcdrError", "ArgumentError", "ArgumentOutOfRangeError", "NotSupportedError",
            "DeviceLostError", "DeviceTimeoutError", "ModelError", "OutOfMemoryError",
            "bytes_per_pixel"]
 
@@ -155,12 +155,27 @@ def lib():
         L.gcdr_device_sms.restype = i
         L.gcdr_k_conv_static.argtypes = [vp, vp]
         L.gcdr_k_status.argtypes = [vp]
+        L.gcdr_host_register.argtypes = [vp, sz]
+        L.gcdr_host_unregister.argtypes = [vp]
         f = ctypes.c_float
         L.gcdr_k_dw_gelu_shift.argtypes = [vp, i, i, i, vp, vp, vp, vp, vp]
         L.gcdr_k_up_add.argtypes = [vp, vp, vp, vp, vp, f, vp, vp, vp]
         L.gcdr_k_ln_finalize.argtypes = [vp, i, i, i, i, vp, vp, vp, vp, f, vp, vp, f, vp, vp, vp, vp]
         _lib = L
         return L
+
+
+def register_host(buf) -> None:
+    """Page-locks a C-contiguous numpy array (or other buffer) for direct DMA: enhance calls
+    whose source or destination lies in it skip the staging copies.  Call unregister_host
+    before the memory goes away."""
+    b = _Buf(buf, writable=False)
+    _raise(lib().gcdr_host_register(b.ptr, b.len), "host register failed")
+
+
+def unregister_host(buf) -> None:
+    b = _Buf(buf, writable=False)
+    _raise(lib().gcdr_host_unregister(b.ptr), "host unregister failed")
 
 
 class _Buf:

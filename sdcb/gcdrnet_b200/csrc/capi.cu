@@ -319,6 +319,24 @@ extern "C" void gcdr_enhancer_inject_device_loss(gcdr_enhancer *e, int count) {
 
 extern "C" void gcdr_enhancer_destroy(gcdr_enhancer *e) { delete e; }
 
+extern "C" int gcdr_host_register(void *p, size_t bytes) {
+    if (!p || !bytes) return GCDR_ERR_ARG;
+    cudaError_t e = cudaHostRegister(p, bytes, cudaHostRegisterPortable);
+    if (e == cudaSuccess) return GCDR_OK;
+    std::fprintf(stderr, "gcdr_host_register: %s\n", cudaGetErrorString(e));
+    cudaGetLastError();
+    return e == cudaErrorMemoryAllocation ? GCDR_ERR_OOM : e == cudaErrorHostMemoryAlreadyRegistered ? GCDR_ERR_ARG
+                                                                                                     : GCDR_ERR_DEVICE;
+}
+
+extern "C" int gcdr_host_unregister(void *p) {
+    if (!p) return GCDR_ERR_ARG;
+    cudaError_t e = cudaHostUnregister(p);
+    if (e == cudaSuccess) return GCDR_OK;
+    cudaGetLastError();
+    return e == cudaErrorHostMemoryNotRegistered ? GCDR_ERR_ARG : GCDR_ERR_DEVICE;
+}
+
 // ------------------------------------------------------- standalone kernels
 
 extern "C" int gcdr_k_bgr2nhwc(const uint8_t *src, int w, int h, int stride, int fmt, float *x, int ph, int pw,

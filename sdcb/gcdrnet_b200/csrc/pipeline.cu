@@ -856,6 +856,24 @@ int Worker::check_err_flag() {
     return GCDR_OK;
 }
 
+namespace {
+
+// Whether host address p lies in page-locked memory (cudaMallocHost / cudaHostAlloc, or a
+// range the caller registered with cudaHostRegister): the copy engines then read or write it
+// directly, with no staging copy.
+bool pinned(const void *p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeHost;
+}
+
+bool pinned_range(const uint8_t *p, size_t n) { return pinned(p) && pinned(p + n - 1); }
+
+}  // namespace
+
 int Worker::enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8_t *dst, int dst_stride, int fmt) {
     if (inject_device_loss > 0) {
         inject_device_loss--;
@@ -869,32 +887,57 @@ int Worker::enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8
         y0 = (int)((long long)h * b / kHostBands);
         y1 = (int)((long long)h * (b + 1) / kHostBands);
     };
-    // stage and upload: band b's H2D is enqueued by whichever thread staged it (the bands are
-    // disjoint, so their order on the stream does not matter); the graph follows them all
-    std::atomic<int> up_fail{0};
-    pool_->run(kHostBands, [&](int b) {
-        int y0, y1;
-        band(b, y0, y1);
-        uint8_t *stage = h_src_ + (size_t)y0 * row;
-        if ((size_t)src_stride == row) std::memcpy(stage, src + (size_t)y0 * row, (size_t)(y1 - y0) * row);
-        else
-            for (int y = y0; y < y1; y++) std::memcpy(h_src_ + (size_t)y * row, src + (size_t)y * src_stride, row);
-        if (cudaMemcpyAsync(d_src_ + (size_t)y0 * row, stage, (size_t)(y1 - y0) * row, cudaMemcpyHostToDevice, stream_) !=
-            cudaSuccess)
-            up_fail = 1;
-    });
-    if (up_fail) return fail(GCDR_ERR_DEVICE, "H2D copy failed");
+    // page-locked caller buffers are copied by DMA directly (any row stride); pageable ones go
+    // through the worker's pinned staging, copied by the host in row bands
+    const size_t src_len = (size_t)(h - 1) * src_stride + row, dst_len = (size_t)(h - 1) * dst_stride + row;
+    const bool direct_in = pinned_range(src, src_len);
+    const bool direct_out = pinned_range(dst, dst_len);
+    const bool overlap = dst < src + src_len && src < dst + dst_len;
+    if (direct_in) {
+        if (cudaMemcpy2DAsync(d_src_, row, src, src_stride, row, h, cudaMemcpyHostToDevice, stream_) != cudaSuccess)
+            return fail(GCDR_ERR_DEVICE, "H2D copy failed");
+    } else {
+        // stage and upload: band b's H2D is enqueued by whichever thread staged it (the bands
+        // are disjoint, so their order on the stream does not matter); the graph follows them all
+        std::atomic<int> up_fail{0};
+        pool_->run(kHostBands, [&](int b) {
+            int y0, y1;
+            band(b, y0, y1);
+            uint8_t *stage = h_src_ + (size_t)y0 * row;
+            if ((size_t)src_stride == row) std::memcpy(stage, src + (size_t)y0 * row, (size_t)(y1 - y0) * row);
+            else
+                for (int y = y0; y < y1; y++) std::memcpy(h_src_ + (size_t)y * row, src + (size_t)y * src_stride, row);
+            if (cudaMemcpyAsync(d_src_ + (size_t)y0 * row, stage, (size_t)(y1 - y0) * row, cudaMemcpyHostToDevice,
+                                stream_) != cudaSuccess)
+                up_fail = 1;
+        });
+        if (up_fail) return fail(GCDR_ERR_DEVICE, "H2D copy failed");
+    }
     if (exec_) {
         if (cudaGraphLaunch(exec_, stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "graph launch failed");
     } else if ((rc = run_ops(stream_))) return rc;
     cudaError_t e = cudaMemcpyAsync(h_err_, d_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_);
     if (e == cudaSuccess) e = cudaEventRecord(flag_ev_, stream_);
-    for (int b = 0; b < kHostBands && e == cudaSuccess; b++) {
-        int y0, y1;
-        band(b, y0, y1);
-        e = cudaMemcpyAsync(h_dst_ + (size_t)y0 * row, d_dst_ + (size_t)y0 * row, (size_t)(y1 - y0) * row,
-                            cudaMemcpyDeviceToHost, stream_);
-        if (e == cudaSuccess) e = cudaEventRecord(band_ev_[b], stream_);
+    if (direct_out && !overlap) {
+        // a destination apart from the source is written by DMA right behind the graph (after a
+        // device error its contents are unspecified; the retry reads the untouched source)
+        if (e == cudaSuccess)
+            e = cudaMemcpy2DAsync(dst, dst_stride, d_dst_, row, row, h, cudaMemcpyDeviceToHost, stream_);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+        if (e != cudaSuccess) {
+            cudaStreamSynchronize(stream_);
+            return fail(GCDR_ERR_DEVICE, std::string("CUDA error: ") + cudaGetErrorString(e));
+        }
+        return check_err_flag();
+    }
+    if (!direct_out) {
+        for (int b = 0; b < kHostBands && e == cudaSuccess; b++) {
+            int y0, y1;
+            band(b, y0, y1);
+            e = cudaMemcpyAsync(h_dst_ + (size_t)y0 * row, d_dst_ + (size_t)y0 * row, (size_t)(y1 - y0) * row,
+                                cudaMemcpyDeviceToHost, stream_);
+            if (e == cudaSuccess) e = cudaEventRecord(band_ev_[b], stream_);
+        }
     }
     if (e == cudaSuccess) e = cudaEventSynchronize(flag_ev_);
     if (e != cudaSuccess) {
@@ -906,6 +949,12 @@ int Worker::enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8
     if ((rc = check_err_flag())) {
         cudaStreamSynchronize(stream_);
         return rc;
+    }
+    if (direct_out) {
+        // page-locked destination overlapping the source (in place): DMA once the flag is clean
+        e = cudaMemcpy2DAsync(dst, dst_stride, d_dst_, row, row, h, cudaMemcpyDeviceToHost, stream_);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+        return e == cudaSuccess ? GCDR_OK : fail(GCDR_ERR_DEVICE, "D2H copy failed");
     }
     std::atomic<int> down_fail{0};
     pool_->run(kHostBands, [&](int b) {
