@@ -424,6 +424,40 @@ def main():
     single_ms = max_over_ranks(timed(1), dist)
     single_value = whole_job_rate(world, args.steps, single_ms / 1000.0)
 
+    # batched launches (several images per CUDA-graph launch, one worker): the four 1600x1152
+    # documents, and eight 640x480 ones against one at a time (small images leave most SMs idle)
+    def timed_batch(wk, srcs, dsts, w, h, per_launch):
+        for _ in range(2):
+            for j in range(0, len(srcs), per_launch):
+                wk.enhance_batch_device(srcs[j:j + per_launch], w, h, dsts[j:j + per_launch], 0, main.cuda_stream)
+        torch.cuda.synchronize(dev)
+        ms = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(main)
+            for j in range(0, len(srcs), per_launch):
+                wk.enhance_batch_device(srcs[j:j + per_launch], w, h, dsts[j:j + per_launch], 0, main.cuda_stream)
+            b.record(main)
+            torch.cuda.synchronize(dev)
+            ms += a.elapsed_time(b)
+        return max_over_ranks(ms, dist)
+
+    bw = workers[1]   # (workers[0] stays bound to the single-image plan the per-op profile below uses)
+    big_ms = timed_batch(bw, [t.data_ptr() for t in d_src], [t.data_ptr() for t in d_dst], W_IMG, H_IMG, STREAMS)
+    sw, sh_ = 640, 480
+    small = [torch.from_numpy(synth.document(sw, sh_, seed=900 + k).reshape(-1)).to(dev) for k in range(8)]
+    small_out = [torch.empty_like(t) for t in small]
+    sp, so = [t.data_ptr() for t in small], [t.data_ptr() for t in small_out]
+    small_one_ms = timed_batch(bw, sp, so, sw, sh_, 1)
+    small_bat_ms = timed_batch(bw, sp, so, sw, sh_, 8)
+    batching = {
+        "1600x1152_4_per_launch": whole_job_rate(world, args.steps * STREAMS, big_ms / 1000.0),
+        "640x480_one_per_launch": whole_job_rate(world, args.steps * 8, small_one_ms / 1000.0),
+        "640x480_8_per_launch": whole_job_rate(world, args.steps * 8, small_bat_ms / 1000.0),
+        "unit": "images/s", "note": "inputs in HBM, one worker, CUDA events, L2 flushed between steps",
+    }
+
     # end to end through the public API (host buffers), the c3 workload: C3_IMAGES documents
     # drained from one shared host queue by every rank (one process per GPU), each rank with
     # E2E_THREADS host threads calling GcdrEnhancer.enhance on one shared enhancer (its worker
@@ -563,6 +597,7 @@ def main():
                             "frac_of_peak": (tc_flops / (tc_ms * 1e-3) / 1e12) / tflops if tc_ms else None,
                             "share_of_step": tc_ms / total_prof_ms if total_prof_ms else None},
             "single_stream": {"value": single_value, "unit": "images/s", "ms_per_image": single_ms / args.steps},
+            "batched_launches": batching,
             "gpu_launches": launches * args.steps * STREAMS,
             "clocks": clocks,
             "cpu_baseline": cpu,

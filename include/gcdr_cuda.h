@@ -118,6 +118,19 @@ GCDR_API int gcdr_cuda_enhance(gcdr_cuda *w, const uint8_t *src, int width, int 
  * already in HBM. */
 GCDR_API int gcdr_cuda_enhance_device(gcdr_cuda *w, const uint8_t *d_src, int width, int height,
                                       uint8_t *d_dst, int pixel_format, void *stream);
+/* Batched images per launch: n (1..16) images of one shape and format in ONE
+ * CUDA-graph launch.  The worker's batch plan for (width, height, format, n)
+ * holds n image slices in its arena and its graph n concurrent branches, one
+ * per image: the low-resolution layers of one image occupy only part of the
+ * GPU, n branches fill it.  Host buffers as gcdr_cuda_enhance (dst[k] may
+ * alias src[k] at equal strides; page-locked sources are copied by DMA
+ * directly); the _device form takes tight device images and is asynchronous
+ * on `stream`.  No counterpart in the reference: its README lists batching as
+ * not covered (README.md:182). */
+GCDR_API int gcdr_cuda_enhance_batch(gcdr_cuda *w, const uint8_t *const *src, int n, int width, int height,
+                                     int src_stride, uint8_t *const *dst, int dst_stride, int pixel_format);
+GCDR_API int gcdr_cuda_enhance_batch_device(gcdr_cuda *w, const uint8_t *const *d_src, int n, int width,
+                                            int height, uint8_t *const *d_dst, int pixel_format, void *stream);
 /* Device bytes held by the worker (arena + staging): VkPipeline2.cs:141. */
 GCDR_API int64_t gcdr_cuda_device_bytes(const gcdr_cuda *w);
 /* Debug: padded NHWC fp32 intermediates of the last enhance -- the GC

@@ -128,6 +128,8 @@ def lib():
         L.gcdr_cuda_create_from_onnx.argtypes = [i, vp, sz, vp, sz, i, ctypes.POINTER(vp)]
         L.gcdr_cuda_enhance.argtypes = [vp, vp, i, i, i, vp, i, i]
         L.gcdr_cuda_enhance_device.argtypes = [vp, vp, i, i, vp, i, vp]
+        L.gcdr_cuda_enhance_batch.argtypes = [vp, vp, i, i, i, i, vp, i, i]
+        L.gcdr_cuda_enhance_batch_device.argtypes = [vp, vp, i, i, i, vp, i, vp]
         L.gcdr_cuda_device_bytes.argtypes = [vp]
         L.gcdr_cuda_device_bytes.restype = i64
         L.gcdr_cuda_debug_intermediates.argtypes = [vp, vp, vp, vp]
@@ -343,6 +345,28 @@ class CudaWorker:
     def enhance_device(self, d_src: int, width, height, d_dst: int, format=GcdrPixelFormat.Bgr24, stream: int = 0):
         self._check(lib().gcdr_cuda_enhance_device(self._h, d_src, int(width), int(height), d_dst, int(format),
                                                    stream or None))
+
+    def enhance_batch(self, srcs, width, height, src_stride, dsts, dst_stride, format=GcdrPixelFormat.Bgr24):
+        """n same-shape images (host buffers) in one CUDA-graph launch (gcdr_cuda_enhance_batch)."""
+        if len(srcs) != len(dsts):
+            raise ArgumentError("srcs and dsts differ in length")
+        s = [_Buf(b, False) for b in srcs]
+        d = [_Buf(b, True) for b in dsts]
+        n = len(s)
+        sp = (ctypes.c_void_p * n)(*[b.ptr for b in s])
+        dp_ = (ctypes.c_void_p * n)(*[b.ptr for b in d])
+        self._check(lib().gcdr_cuda_enhance_batch(self._h, sp, n, int(width), int(height), int(src_stride), dp_,
+                                                  int(dst_stride), int(format)))
+
+    def enhance_batch_device(self, d_srcs, width, height, d_dsts, format=GcdrPixelFormat.Bgr24, stream: int = 0):
+        """n same-shape device-resident tight images in one CUDA-graph launch, asynchronous on `stream`."""
+        n = len(d_srcs)
+        if n != len(d_dsts):
+            raise ArgumentError("d_srcs and d_dsts differ in length")
+        sp = (ctypes.c_void_p * n)(*d_srcs)
+        dp_ = (ctypes.c_void_p * n)(*d_dsts)
+        self._check(lib().gcdr_cuda_enhance_batch_device(self._h, sp, n, int(width), int(height), dp_, int(format),
+                                                         stream or None))
 
     def set_debug(self, on: bool = True):
         self._check(lib().gcdr_cuda_set_debug(self._h, 1 if on else 0))

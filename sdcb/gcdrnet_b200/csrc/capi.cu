@@ -132,6 +132,28 @@ extern "C" int gcdr_cuda_enhance_device(gcdr_cuda *w, const uint8_t *d_src, int 
     return w->w->enhance_device(d_src, width, height, d_dst, pixel_format, static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int gcdr_cuda_enhance_batch(gcdr_cuda *w, const uint8_t *const *src, int n, int width, int height,
+                                       int src_stride, uint8_t *const *dst, int dst_stride, int pixel_format) {
+    if (!w || !src || !dst || n < 1 || n > Worker::kMaxBatch) return GCDR_ERR_ARG;
+    for (int k = 0; k < n; k++)
+        if (!src[k] || !dst[k]) return GCDR_ERR_ARG;
+    int rc = check_image_args(width, height, pixel_format);
+    if (rc) return rc;
+    const int bpp = pixel_format >= 2 ? 4 : 3;
+    if (src_stride < width * bpp || dst_stride < width * bpp) return GCDR_ERR_RANGE;
+    return w->w->enhance_host_batch(src, n, width, height, src_stride, dst, dst_stride, pixel_format);
+}
+
+extern "C" int gcdr_cuda_enhance_batch_device(gcdr_cuda *w, const uint8_t *const *d_src, int n, int width, int height,
+                                              uint8_t *const *d_dst, int pixel_format, void *stream) {
+    if (!w || !d_src || !d_dst || n < 1 || n > Worker::kMaxBatch) return GCDR_ERR_ARG;
+    for (int k = 0; k < n; k++)
+        if (!d_src[k] || !d_dst[k]) return GCDR_ERR_ARG;
+    int rc = check_image_args(width, height, pixel_format);
+    if (rc) return rc;
+    return w->w->enhance_device_batch(d_src, n, width, height, d_dst, pixel_format, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int64_t gcdr_cuda_device_bytes(const gcdr_cuda *w) { return w ? w->w->device_bytes() : 0; }
 
 extern "C" int gcdr_cuda_debug_intermediates(gcdr_cuda *w, float *gc_in, float *gc_out, float *dr_in) {

@@ -178,6 +178,12 @@ Worker::~Worker() {
     if (h_src_) cudaFreeHost(h_src_);
     if (h_dst_) cudaFreeHost(h_dst_);
     if (h_err_) cudaFreeHost(h_err_);
+    if (h_errs_) cudaFreeHost(h_errs_);
+    for (int k = 0; k < kMaxBatch; k++) {
+        if (fork_[k]) cudaStreamDestroy(fork_[k]);
+        if (join_ev_[k]) cudaEventDestroy(join_ev_[k]);
+    }
+    if (fork_ev_) cudaEventDestroy(fork_ev_);
     pool_.reset();
     if (flag_ev_) cudaEventDestroy(flag_ev_);
     for (auto &e : band_ev_)
@@ -201,6 +207,8 @@ int Worker::init(std::string &err) {
     if (cudaEventCreateWithFlags(&flag_ev_, cudaEventDisableTiming) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
     for (auto &e : band_ev_)
         if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
+    if (cudaEventCreateWithFlags(&fork_ev_, cudaEventDisableTiming) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
+    if (cudaMallocHost(&h_errs_, sizeof(int) * kMaxBatch) != cudaSuccess) { err = "pinned alloc"; return GCDR_ERR_OOM; }
     pool_ = std::make_unique<HostPool>(kHostBands - 1, device_);
     const char *g = std::getenv("GCDR_CUDA_GRAPH");
     use_graph_ = !(g && g[0] == '0');
@@ -220,9 +228,9 @@ int64_t Worker::device_bytes() const {
 }
 
 bool Worker::has_plan(int w, int h, int fmt) const {
-    if (bound_ && w == w_ && h == h_ && fmt == fmt_ && plan_debug_ == debug_) return true;
+    if (bound_ && w == w_ && h == h_ && fmt == fmt_ && plan_debug_ == debug_ && nimg_ == 1) return true;
     for (const auto &p : cache_)
-        if (p.w == w && p.h == h && p.fmt == fmt && p.debug == debug_) return true;
+        if (p.w == w && p.h == h && p.fmt == fmt && p.debug == debug_ && p.nimg == 1) return true;
     return false;
 }
 
@@ -230,6 +238,9 @@ void Worker::stash() {
     ShapePlan p;
     p.w = w_; p.h = h_; p.fmt = fmt_; p.H = H_; p.W = W_; p.ph = ph_; p.pw = pw_; p.bpp = bpp_;
     p.debug = plan_debug_;
+    p.nimg = nimg_;
+    p.slices = std::move(slices_);
+    p.slice_begin = std::move(slice_begin_);
     p.arena = arena_; p.arena_bytes = arena_bytes_;
     p.gcb = gcb_; p.drb = drb_;
     p.r = r_; p.ism = ism_; p.ydbg = ydbg_;
@@ -245,12 +256,16 @@ void Worker::stash() {
     arena_ = nullptr; arena_bytes_ = 0;
     graph_ = nullptr; exec_ = nullptr;
     ops_.clear(); info_.clear();
+    slices_.clear(); slice_begin_.clear();
     bound_ = false;
 }
 
 void Worker::restore(ShapePlan &&p) {
     w_ = p.w; h_ = p.h; fmt_ = p.fmt; H_ = p.H; W_ = p.W; ph_ = p.ph; pw_ = p.pw; bpp_ = p.bpp;
     plan_debug_ = p.debug;
+    nimg_ = p.nimg;
+    slices_ = std::move(p.slices);
+    slice_begin_ = std::move(p.slice_begin);
     arena_ = p.arena; arena_bytes_ = p.arena_bytes;
     gcb_ = p.gcb; drb_ = p.drb;
     r_ = p.r; ism_ = p.ism; ydbg_ = p.ydbg;
@@ -270,6 +285,7 @@ void Worker::release_current() {
     if (arena_) cudaFree(arena_);
     exec_ = nullptr; graph_ = nullptr; arena_ = nullptr; arena_bytes_ = 0;
     ops_.clear(); info_.clear();
+    slices_.clear(); slice_begin_.clear();
     launches_ = 0;
     bound_ = false;
 }
@@ -488,7 +504,10 @@ int Worker::plan_arena() {
     al.take(reinterpret_cast<void **>(&d_err_), 256);
     const size_t wsf = std::max(partial_floats(w.gc, H_, W_, num_sms_), partial_floats(w.dr, H_, W_, num_sms_));
     al.take(reinterpret_cast<void **>(&ws_), std::max(wsf, (size_t)64) * 4);
-    const size_t need = al.off;
+    // a batch plan holds nimg_ such image slices, one after another
+    layout_ = al.items;
+    slice_bytes_ = al.off;
+    const size_t need = slice_bytes_ * (size_t)nimg_;
     // one arena per shape plan, sized exactly; the plan cache keeps the sum of the cached
     // plans' arenas within kPlanBudget (the reference's arena budget, VkPipeline2.cs:104-117),
     // evicting the least recently used shapes first
@@ -507,21 +526,53 @@ int Worker::plan_arena() {
         return fail(GCDR_ERR_OOM, "arena: cudaMalloc failed");
     }
     arena_bytes_ = need;
-    for (auto &it : al.items) *it.first = arena_ + it.second;
+    slices_.assign(nimg_, ImageSlice{});
+    for (int k = 0; k < nimg_; k++) {
+        use_slice(k);
+        slices_[k] = ImageSlice{d_src_, d_dst_, d_err_};
+    }
+    use_slice(0);
     // zero borders of the stride-2 inputs (LAY_PHASE) and everything else once per plan
     if (cudaMemsetAsync(arena_, 0, need, stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "arena memset failed");
-    // pinned staging (grow-only)
-    if (pin_bytes_ < img) {
+    // pinned staging (grow-only): one image per slice
+    const size_t stage = img * (size_t)nimg_;
+    if (pin_bytes_ < stage) {
         if (h_src_) cudaFreeHost(h_src_);
         if (h_dst_) cudaFreeHost(h_dst_);
         h_src_ = h_dst_ = nullptr;
-        size_t cap = img + img / 4 + 64;
+        size_t cap = stage + stage / 4 + 64;
         if (cudaMallocHost(&h_src_, cap) != cudaSuccess || cudaMallocHost(&h_dst_, cap) != cudaSuccess) {
             pin_bytes_ = 0;
             return fail(GCDR_ERR_OOM, "pinned staging alloc failed");
         }
         pin_bytes_ = cap;
     }
+    return GCDR_OK;
+}
+
+void Worker::use_slice(int k) {
+    for (auto &it : layout_) *it.first = arena_ + (size_t)k * slice_bytes_ + it.second;
+}
+
+int Worker::build_all_ops() {
+    std::vector<std::function<int(cudaStream_t)>> all;
+    std::vector<OpInfo> all_info;
+    slice_begin_.clear();
+    int launches = 0;
+    for (int k = 0; k < nimg_; k++) {
+        use_slice(k);
+        const int rc = build_ops();
+        if (rc) return rc;
+        slice_begin_.push_back(all.size());
+        for (auto &op : ops_) all.push_back(std::move(op));
+        for (auto &oi : info_) all_info.push_back(oi);
+        launches += launches_;
+    }
+    slice_begin_.push_back(all.size());
+    use_slice(0);
+    ops_ = std::move(all);
+    info_ = std::move(all_info);
+    launches_ = launches;
     return GCDR_OK;
 }
 
@@ -802,9 +853,32 @@ int Worker::capture() {
     if (exec_) { cudaGraphExecDestroy(exec_); exec_ = nullptr; }
     if (graph_) { cudaGraphDestroy(graph_); graph_ = nullptr; }
     if (!use_graph_) return GCDR_OK;
+    for (int k = 1; k < nimg_; k++) {   // batch plans: one capture branch (stream) per image
+        if (!fork_[k] && cudaStreamCreateWithFlags(&fork_[k], cudaStreamNonBlocking) != cudaSuccess)
+            return fail(GCDR_ERR_DEVICE, "stream");
+        if (!join_ev_[k] && cudaEventCreateWithFlags(&join_ev_[k], cudaEventDisableTiming) != cudaSuccess)
+            return fail(GCDR_ERR_DEVICE, "event");
+    }
     if (cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
         return fail(GCDR_ERR_DEVICE, "graph capture begin failed");
-    int rc = run_ops(stream_);
+    int rc = GCDR_OK;
+    if (nimg_ == 1) {
+        rc = run_ops(stream_);
+    } else {
+        // image k's ops on branch k (image 0 on the capturing stream), forked from and joined
+        // back into it: one graph whose branches run concurrently
+        cudaError_t ce = cudaEventRecord(fork_ev_, stream_);
+        for (int k = 1; k < nimg_ && ce == cudaSuccess; k++) ce = cudaStreamWaitEvent(fork_[k], fork_ev_, 0);
+        for (int k = 0; k < nimg_ && !rc && ce == cudaSuccess; k++) {
+            cudaStream_t bs = k ? fork_[k] : stream_;
+            for (size_t i = slice_begin_[k]; i < slice_begin_[k + 1] && !rc; i++) rc = ops_[i](bs);
+        }
+        for (int k = 1; k < nimg_ && !rc && ce == cudaSuccess; k++) {
+            ce = cudaEventRecord(join_ev_[k], fork_[k]);
+            if (ce == cudaSuccess) ce = cudaStreamWaitEvent(stream_, join_ev_[k], 0);
+        }
+        if (!rc && ce != cudaSuccess) rc = fail(GCDR_ERR_DEVICE, std::string("batch capture: ") + cudaGetErrorString(ce));
+    }
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(stream_, &g);
     if (rc) { if (g) cudaGraphDestroy(g); return rc; }
@@ -814,15 +888,15 @@ int Worker::capture() {
     return GCDR_OK;
 }
 
-int Worker::bind(int w, int h, int fmt) {
+int Worker::bind(int w, int h, int fmt, int nimg) {
     ++tick_;
-    if (bound_ && w == w_ && h == h_ && fmt == fmt_ && plan_debug_ == debug_) return GCDR_OK;
+    if (bound_ && w == w_ && h == h_ && fmt == fmt_ && plan_debug_ == debug_ && nimg_ == nimg) return GCDR_OK;
     if (cudaSetDevice(device_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "cudaSetDevice");
     if (cudaStreamSynchronize(stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "stream sync");
     // the shape's plan may be cached: swap it in, graph and all
     for (size_t i = 0; i < cache_.size(); i++) {
         ShapePlan &p = cache_[i];
-        if (p.w != w || p.h != h || p.fmt != fmt || p.debug != debug_) continue;
+        if (p.w != w || p.h != h || p.fmt != fmt || p.debug != debug_ || p.nimg != nimg) continue;
         ShapePlan hit = std::move(p);
         cache_.erase(cache_.begin() + (long)i);
         if (bound_) stash();
@@ -839,9 +913,10 @@ int Worker::bind(int w, int h, int fmt) {
     ph_ = (-h) & 31; pw_ = (-w) & 31;
     H_ = h + ph_; W_ = w + pw_;
     plan_debug_ = debug_;
+    nimg_ = nimg;
     int rc = plan_arena();
     if (rc) return rc;
-    rc = build_ops();
+    rc = build_all_ops();
     if (rc) return rc;
     rc = capture();
     if (rc) return rc;
@@ -993,8 +1068,81 @@ int Worker::enhance_device(const uint8_t *d_src, int w, int h, uint8_t *d_dst, i
     return GCDR_OK;
 }
 
+int Worker::enhance_host_batch(const uint8_t *const *src, int n, int w, int h, int src_stride, uint8_t *const *dst,
+                               int dst_stride, int fmt) {
+    if (n < 1 || n > kMaxBatch) return fail(GCDR_ERR_ARG, "batch size must be 1..16");
+    if (inject_device_loss > 0) {
+        inject_device_loss--;
+        return fail(GCDR_ERR_DEVICE, "injected device loss");
+    }
+    if (cudaSetDevice(device_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "cudaSetDevice");
+    int rc = bind(w, h, fmt, n);
+    if (rc) return rc;
+    const size_t row = (size_t)w * bpp_, img = row * h;
+    const size_t src_len = (size_t)(h - 1) * src_stride + row;
+    // upload: page-locked sources by DMA directly, pageable ones staged (one image per helper task)
+    std::atomic<int> up_fail{0};
+    pool_->run(n, [&](int k) {
+        uint8_t *dev = slices_[k].d_src;
+        cudaError_t e;
+        if (pinned_range(src[k], src_len)) {
+            e = cudaMemcpy2DAsync(dev, row, src[k], src_stride, row, h, cudaMemcpyHostToDevice, stream_);
+        } else {
+            uint8_t *stage = h_src_ + (size_t)k * img;
+            for (int y = 0; y < h; y++) std::memcpy(stage + (size_t)y * row, src[k] + (size_t)y * src_stride, row);
+            e = cudaMemcpyAsync(dev, stage, img, cudaMemcpyHostToDevice, stream_);
+        }
+        if (e != cudaSuccess) up_fail = 1;
+    });
+    if (up_fail) return fail(GCDR_ERR_DEVICE, "H2D copy failed");
+    if (exec_) {
+        if (cudaGraphLaunch(exec_, stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "graph launch failed");
+    } else if ((rc = run_ops(stream_))) return rc;
+    cudaError_t e = cudaSuccess;
+    for (int k = 0; k < n && e == cudaSuccess; k++)
+        e = cudaMemcpyAsync(h_errs_ + k, slices_[k].d_err, sizeof(int), cudaMemcpyDeviceToHost, stream_);
+    for (int k = 0; k < n && e == cudaSuccess; k++)
+        e = cudaMemcpyAsync(h_dst_ + (size_t)k * img, slices_[k].d_dst, img, cudaMemcpyDeviceToHost, stream_);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess) {
+        cudaStreamSynchronize(stream_);
+        return fail(GCDR_ERR_DEVICE, std::string("CUDA error: ") + cudaGetErrorString(e));
+    }
+    // the callers' buffers are written only after every image's device flag is clean
+    int flags = 0;
+    for (int k = 0; k < n; k++) flags |= h_errs_[k];
+    if (flags & GCDR_ERR_FLAG_TIMEOUT) return fail(GCDR_ERR_TIMEOUT, "a device-side wait timed out");
+    if (flags) return fail(GCDR_ERR_DEVICE, "device error flag set");
+    pool_->run(n, [&](int k) {
+        const uint8_t *stage = h_dst_ + (size_t)k * img;
+        for (int y = 0; y < h; y++) std::memcpy(dst[k] + (size_t)y * dst_stride, stage + (size_t)y * row, row);
+    });
+    return GCDR_OK;
+}
+
+int Worker::enhance_device_batch(const uint8_t *const *d_src, int n, int w, int h, uint8_t *const *d_dst, int fmt,
+                                 cudaStream_t st) {
+    if (n < 1 || n > kMaxBatch) return fail(GCDR_ERR_ARG, "batch size must be 1..16");
+    if (cudaSetDevice(device_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "cudaSetDevice");
+    int rc = bind(w, h, fmt, n);
+    if (rc) return rc;
+    cudaStream_t s = st ? st : stream_;
+    const size_t img = (size_t)w * h * bpp_;
+    for (int k = 0; k < n; k++)
+        if (cudaMemcpyAsync(slices_[k].d_src, d_src[k], img, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+            return fail(GCDR_ERR_DEVICE, "d2d copy");
+    if (exec_) {
+        if (cudaGraphLaunch(exec_, s) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "graph launch failed");
+    } else if ((rc = run_ops(s))) return rc;
+    for (int k = 0; k < n; k++)
+        if (cudaMemcpyAsync(d_dst[k], slices_[k].d_dst, img, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+            return fail(GCDR_ERR_DEVICE, "d2d copy");
+    return GCDR_OK;
+}
+
 int Worker::debug_intermediates(float *gc_in, float *gc_out, float *dr_in, float *dr_out) {
     if (!bound_) return fail(GCDR_ERR_ARG, "worker not bound to a size");
+    if (nimg_ != 1) return fail(GCDR_ERR_ARG, "debug intermediates need a single-image enhance");
     if (cudaStreamSynchronize(stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "sync");
     const size_t n3 = (size_t)H_ * W_ * 3;
     std::vector<float> x(n3), r(n3);

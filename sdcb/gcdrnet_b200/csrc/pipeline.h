@@ -74,9 +74,18 @@ struct OpInfo {
 // and its CUDA graph.  A worker keeps up to Worker::kMaxPlans of them, least recently used
 // evicted first (the reference caches up to 8 sizes per enhancer, GcdrEnhancer.cs:45-46,
 // 128-136), so alternating sizes re-use their graphs instead of re-planning.
+// One image's device buffers in a batch plan (the arena holds `nimg` such slices).
+struct ImageSlice {
+    uint8_t *d_src = nullptr, *d_dst = nullptr;
+    int *d_err = nullptr;
+};
+
 struct ShapePlan {
     int w = 0, h = 0, fmt = -1, H = 0, W = 0, ph = 0, pw = 0, bpp = 3;
     bool debug = false;
+    int nimg = 1;                       // images per launch (a batch plan: one graph branch each)
+    std::vector<ImageSlice> slices;
+    std::vector<size_t> slice_begin;    // first op of each image's branch
     uint8_t *arena = nullptr;
     size_t arena_bytes = 0;
     NetBufs gcb, drb;
@@ -101,6 +110,15 @@ public:
     int init(std::string &err);
     int enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8_t *dst, int dst_stride, int fmt);
     int enhance_device(const uint8_t *d_src, int w, int h, uint8_t *d_dst, int fmt, cudaStream_t st);
+    // n same-shape images in one CUDA-graph launch: a batch plan holds n image slices and its
+    // graph n concurrent branches (one per image).  Host buffers (staged, or by DMA when page-
+    // locked); dst[k] may alias src[k] at equal strides.
+    int enhance_host_batch(const uint8_t *const *src, int n, int w, int h, int src_stride, uint8_t *const *dst,
+                           int dst_stride, int fmt);
+    // The same with device-resident tight images, asynchronous on `st` (or the worker's stream).
+    int enhance_device_batch(const uint8_t *const *d_src, int n, int w, int h, uint8_t *const *d_dst, int fmt,
+                             cudaStream_t st);
+    static constexpr int kMaxBatch = 16;
     int debug_intermediates(float *gc_in, float *gc_out, float *dr_in, float *dr_out);
     void set_debug(bool on);
     // device bytes of every cached shape's arena (VkPipeline2.cs:141's DeviceBytes)
@@ -124,7 +142,9 @@ public:
     int inject_device_loss = 0;   // test hook: the next N enhances fail with GCDR_ERR_DEVICE
 
 private:
-    int bind(int w, int h, int fmt);
+    int bind(int w, int h, int fmt, int nimg = 1);
+    void use_slice(int k);          // points the buffer members at image slice k of the arena
+    int build_all_ops();            // build_ops for every image slice, concatenated
     void stash();                   // current plan -> cache_
     void restore(ShapePlan &&p);    // cache entry -> current plan
     void release_current();
@@ -169,6 +189,14 @@ private:
     cudaGraphExec_t exec_ = nullptr;
     int launches_ = 0;
     bool plan_debug_ = false;       // debug mode the current plan was built in
+    int nimg_ = 1;                  // images per launch of the current plan
+    std::vector<ImageSlice> slices_;
+    std::vector<size_t> slice_begin_;
+    std::vector<std::pair<void **, size_t>> layout_;   // buffer member -> offset in a slice
+    size_t slice_bytes_ = 0;
+    cudaStream_t fork_[kMaxBatch] = {};                // capture branches of a batch plan
+    cudaEvent_t fork_ev_ = nullptr, join_ev_[kMaxBatch] = {};
+    int *h_errs_ = nullptr;                            // pinned: one error word per image slice
     std::vector<ShapePlan> cache_;  // plans not bound right now
     uint64_t tick_ = 0;
     int captures_ = 0;

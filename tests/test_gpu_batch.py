@@ -1,0 +1,76 @@
+"""Batched images per launch: n same-shape images in one CUDA-graph launch
+(gcdr_cuda_enhance_batch / _batch_device) give the same bytes as n single
+enhancements, in every pixel format, strided and in place.  The reference does
+not batch (README.md:182); the per-image results are the contract it defines
+(GcdrEnhancer.cs:181-271)."""
+import numpy as np
+import pytest
+
+import golden_data as G
+
+pytestmark = pytest.mark.gpu
+
+
+def _docs(n, w, h, fmt, stride, seed0=40):
+    from sdcb.gcdrnet_b200 import synth
+    bpp = 4 if fmt >= 2 else 3
+    out = []
+    for k in range(n):
+        px = synth.document(w, h, seed=seed0 + k, fmt=fmt, strokes=25)
+        buf = np.full((h, stride), 0x5A, np.uint8)
+        buf[:, :w * bpp] = px.reshape(h, w * bpp)
+        out.append(buf.reshape(-1))
+    return out
+
+
+@pytest.mark.parametrize("n,w,h,fmt,pad", [(3, 217, 150, 0, 0), (4, 160, 96, 2, 64), (2, 301, 203, 3, 5)])
+def test_batch_matches_single_images(n, w, h, fmt, pad):
+    from sdcb.gcdrnet_b200 import CudaWorker
+    bpp = 4 if fmt >= 2 else 3
+    stride = w * bpp + pad
+    srcs = _docs(n, w, h, fmt, stride)
+    with CudaWorker.from_files(G.GC_PATH, G.DR_PATH) as wk:
+        want = []
+        for s in srcs:
+            d = np.full_like(s, 0x5A)
+            wk.enhance(s, w, h, stride, d, stride, fmt)
+            want.append(d)
+        dsts = [np.full_like(s, 0x5A) for s in srcs]
+        wk.enhance_batch(srcs, w, h, stride, dsts, stride, fmt)
+        for k in range(n):
+            assert np.array_equal(dsts[k], want[k]), f"image {k} of the batch"
+        caps = wk.plan_stats[0]
+        # in place, a second time: the batch plan is cached (no capture)
+        io = [s.copy() for s in srcs]
+        wk.enhance_batch(io, w, h, stride, io, stride, fmt)
+        for k in range(n):
+            assert np.array_equal(io[k], want[k]), f"in place, image {k}"
+        assert wk.plan_stats[0] == caps
+
+
+def test_batch_device_matches_single():
+    import torch
+    from sdcb.gcdrnet_b200 import CudaWorker
+    n, w, h = 4, 640, 480
+    srcs = _docs(n, w, h, 0, w * 3, seed0=70)
+    dev = torch.device("cuda:0")
+    d_src = [torch.from_numpy(s).to(dev) for s in srcs]
+    d_one = [torch.empty_like(t) for t in d_src]
+    d_bat = [torch.empty_like(t) for t in d_src]
+    with CudaWorker.from_files(G.GC_PATH, G.DR_PATH) as wk:
+        for k in range(n):
+            wk.enhance_device(d_src[k].data_ptr(), w, h, d_one[k].data_ptr(), 0)
+        torch.cuda.synchronize()
+        wk.enhance_batch_device([t.data_ptr() for t in d_src], w, h, [t.data_ptr() for t in d_bat], 0)
+        torch.cuda.synchronize()
+        assert wk.plan_stats == (2, 2), "a single-image plan and a batch plan"
+    for k in range(n):
+        assert torch.equal(d_one[k], d_bat[k]), f"image {k}"
+
+
+def test_batch_rejects_bad_sizes():
+    from sdcb.gcdrnet_b200 import ArgumentError, CudaWorker
+    with CudaWorker.from_files(G.GC_PATH, G.DR_PATH) as wk:
+        srcs = _docs(17, 32, 32, 0, 96)
+        with pytest.raises(ArgumentError):
+            wk.enhance_batch(srcs, 32, 32, 96, [s.copy() for s in srcs], 96, 0)
