@@ -12,11 +12,15 @@ inter-GPU traffic: scaling "weak").  Prints ONE JSON line on rank 0:
             back into, with an L2 flush (256 MB write) between steps, max over
             ranks; the same loop with one image per step (one stream) is
             reported beside it as single_stream;
-  e2e       the same metric through the public API (GcdrEnhancer.enhance on
-            host numpy buffers: strided copy to pinned staging, H2D, graph,
-            D2H, copy out), called from E2E_THREADS host threads sharing one
-            enhancer (its worker pool), wall clock, max over ranks; plus the
-            single-thread milliseconds per image (the API's latency);
+  e2e       the same metric through the public API, config c3: C3_IMAGES
+            documents (each enqueued C3_PASSES times) drained from one shared
+            host queue (sdcb/gcdrnet_b200/dp.py) by every GPU process, each
+            with E2E_THREADS threads calling GcdrEnhancer.enhance on host
+            buffers (two shared, page-locked host pools: H2D, graph, D2H per
+            image), host monotonic clock from the common start to the last
+            rank's finish; plus the single-thread milliseconds per image (the
+            API's latency, pageable and page-locked buffers);
+  batched_launches  several images per CUDA-graph launch (batch plans);
   roofline  of the dominant kernel from a live per-op profile (CUDA events),
             against MEASURED_PEAKS.json;
   cpu_baseline  the CPU oracle (C restatement of the reference's CPU path) on
@@ -49,7 +53,7 @@ WORKLOAD = (f"enhance 1600x1152 Bgr24 synthetic documents (seeded paper/shading/
             "per step on concurrent worker streams")
 
 
-TRAFFIC_TABLE = os.path.join(ROOT, "profiles", "ncu_traffic_1600x1152.md")
+TRAFFIC_TABLE = os.path.join(ROOT, "profiles", "ncu_kernels_1600x1152.md")
 E2E_THREADS = 4   # concurrent GcdrEnhancer.enhance callers per GPU process in the end-to-end measurement
 C3_IMAGES = 512   # the end-to-end workload: documents drained from the shared host queue,
 C3_PASSES = 3     # every document enqueued this many times (the timed drain lasts long enough at 8 GPUs)
@@ -444,7 +448,8 @@ def main():
         return max_over_ranks(ms, dist)
 
     bw = workers[1]   # (workers[0] stays bound to the single-image plan the per-op profile below uses)
-    big_ms = timed_batch(bw, [t.data_ptr() for t in d_src], [t.data_ptr() for t in d_dst], W_IMG, H_IMG, STREAMS)
+    nb = min(len(d_src), len(d_dst))
+    big_ms = timed_batch(bw, [t.data_ptr() for t in d_src[:nb]], [t.data_ptr() for t in d_dst[:nb]], W_IMG, H_IMG, nb)
     sw, sh_ = 640, 480
     small = [torch.from_numpy(synth.document(sw, sh_, seed=900 + k).reshape(-1)).to(dev) for k in range(8)]
     small_out = [torch.empty_like(t) for t in small]
@@ -452,7 +457,7 @@ def main():
     small_one_ms = timed_batch(bw, sp, so, sw, sh_, 1)
     small_bat_ms = timed_batch(bw, sp, so, sw, sh_, 8)
     batching = {
-        "1600x1152_4_per_launch": whole_job_rate(world, args.steps * STREAMS, big_ms / 1000.0),
+        f"1600x1152_{nb}_per_launch": whole_job_rate(world, args.steps * nb, big_ms / 1000.0),
         "640x480_one_per_launch": whole_job_rate(world, args.steps * 8, small_one_ms / 1000.0),
         "640x480_8_per_launch": whole_job_rate(world, args.steps * 8, small_bat_ms / 1000.0),
         "unit": "images/s", "note": "inputs in HBM, one worker, CUDA events, L2 flushed between steps",
@@ -511,6 +516,13 @@ def main():
     ranks_seen = int(store.add("c3/ranks_seen", 0))
     ndone, requeued = queue.counts()
     e2e_value = jobs / e2e_s
+    # the API's single-image latency from one thread on the page-locked pools (no staging)
+    pinned_single_ms = None
+    if len(pinned_pools) == 2:
+        t0 = time.perf_counter()
+        for i in range(10):
+            work(i)
+        pinned_single_ms = (time.perf_counter() - t0) * 100.0
     for p in pinned_pools:
         unregister_host(p)
     # the same calls from one thread: the single-image latency of the API
@@ -588,7 +600,8 @@ def main():
                     "pools_page_locked": len(pinned_pools) == 2, "pool_dir": os.path.dirname(pool_in.path),
                     "page_lock_error": pin_error,
                     "images_done": ndone, "requeued": requeued, "check": c3_check,
-                    "host_threads": E2E_THREADS, "single_thread_ms_per_image": e2e_single_ms},
+                    "host_threads": E2E_THREADS, "single_thread_ms_per_image": e2e_single_ms,
+                    "single_thread_ms_per_image_page_locked": pinned_single_ms},
             "roofline": {"kernel": name, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak, "traffic": ncu_traffic(name),
                          "traffic_source": os.path.relpath(TRAFFIC_TABLE, ROOT), "peak_source": peak_src,
