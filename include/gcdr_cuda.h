@@ -12,9 +12,10 @@
  *                    GcdrEnhancer.cs:82-100, 181-271, 67-68, 325-331):
  *                    argument validation, top/left pad to /32, a pool of
  *                    workers rented per call, retry-once on device loss.
- *   gcdr_cuda_*      one worker: a CUDA stream, a device arena and one
- *                    CUDA graph per padded shape; NOT thread-safe
- *                    (the VkGcdrPipeline contract,
+ *   gcdr_cuda_*      one worker: a CUDA stream and a cache of shape plans
+ *                    (per image shape: a device arena, the op sequence and
+ *                    its CUDA graph; up to 8, least recently used evicted);
+ *                    NOT thread-safe (the VkGcdrPipeline contract,
  *                    Backends/Vulkan/VkPipeline2.cs:21-379).
  *
  * Plain pointers and sizes only.  Source and destination images are HOST
@@ -105,10 +106,11 @@ GCDR_API int gcdr_cuda_create(int device, const gcdr_model *m, int precision,
 GCDR_API int gcdr_cuda_create_from_onnx(int device, const void *gc_onnx, size_t gc_len,
                                         const void *dr_onnx, size_t dr_len,
                                         int precision, gcdr_cuda **out);
-/* Enhance one image (host buffers).  Binds the worker to the image's padded
- * shape first (arena replan + CUDA-graph capture on a new shape), then
- * copies the strided source to pinned staging, runs the graph, copies back
- * with the destination stride.  VkGcdrPipeline.Enhance (VkPipeline2.cs:296-327). */
+/* Enhance one image (host buffers).  Binds the worker to the image's shape
+ * plan first (a cached plan, or arena plan + CUDA-graph capture for a new
+ * shape), then copies the strided source in (through pinned staging, or by
+ * DMA when it is page-locked), runs the graph, copies back with the
+ * destination stride.  VkGcdrPipeline.Enhance (VkPipeline2.cs:296-327). */
 GCDR_API int gcdr_cuda_enhance(gcdr_cuda *w, const uint8_t *src, int width, int height,
                                int src_stride, uint8_t *dst, int dst_stride,
                                int pixel_format);
