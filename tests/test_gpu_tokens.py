@@ -147,6 +147,7 @@ def test_up_add_matches_oracle(nets, case):
 
 # (net, norm, H, W, ksplit, out layout, residual, with LN2 + shift)
 FIN_CASES = [("gc", "pe3", 6, 10, 3, 0, False, True), ("dr", "pe4", 3, 5, 9, 0, False, True),
+             ("gc", "pe4", 2, 3, 5, 0, False, True),          # H shift by +-2 on a 2-row grid: zero groups
              ("gc", "block1", 6, 10, 2, 2, True, False), ("dr", "block2", 4, 4, 4, 1, True, False),
              ("dr", "dblock2", 8, 6, 1, 1, True, False), ("gc", "dblock1", 5, 9, 5, 0, True, False)]
 
@@ -206,6 +207,27 @@ def test_ln_finalize_matches_oracle(nets, case):
         got2 = out2.float().cpu().numpy().reshape(H, W, N)
         assert not np.isnan(got2).any()
         _close(got2, want2, f"ln_finalize LN2 + H shift {case}")
+
+
+@pytest.mark.parametrize("off", [5, -7, 9])
+def test_shift_offset_beyond_width_zeros(off):
+    """A group shifted by |off| >= W is all zeros (EngineTests.cs:171-180 for the CPU
+    kernel): here through the depthwise kernel's W-shift scatter on a 5-wide grid."""
+    import torch
+    from sdcb.gcdrnet_b200 import lib
+    L = lib()
+    H, W, C = 4, 5, 16
+    x = torch.ones((H, W, C), dtype=torch.float16, device="cuda:0")
+    wt = torch.zeros((9, C), dtype=torch.float32, device="cuda:0")
+    wt[4] = 1.0                                       # centre tap: dw(x) = x
+    b = torch.zeros(C, dtype=torch.float32, device="cuda:0")
+    out = torch.full((H, W, C), -1.0, dtype=torch.float16, device="cuda:0")
+    sh = Shift.of([8, 16], [off, 0])                 # group 0 shifted, group 1 in place
+    assert L.gcdr_k_dw_gelu_shift(x.data_ptr(), H, W, C, wt.data_ptr(), b.data_ptr(), ctypes.byref(sh),
+                                  out.data_ptr(), None) == 0
+    got = out.float().cpu().numpy()
+    assert (got[:, :, :8] == 0).all(), "shifted-out group must be zeros"
+    assert np.allclose(got[:, :, 8:], 0.8413447, atol=2e-3), "unshifted group: gelu(1) = 0.8413"
 
 
 def test_token_entries_reject_bad_arguments():
