@@ -635,19 +635,38 @@ __global__ void nhwc2bgr_kernel(const float *y, int W, int ph, int pw, uint8_t *
     if (bpp == 4) d[3] = al;
 }
 
-__global__ void stem_in_kernel(const ImgSpec im, Act si, int *err) {
+// One block per (row, 256-pixel segment) of the padded image.  The segment's source bytes --
+// part of one row of the top/left replicate-padded image, a contiguous byte range of the
+// tight device copy -- are read with aligned 16-byte loads into shared memory (the device
+// copy carries 16 bytes of slack past its end, so the last word stays inside the
+// allocation), then each thread builds its pixel's 16-channel row [x, x, 0] and stores it as
+// two 16-byte stores (plus the reflect-border copies).
+constexpr int kStemInPx = 256;
+
+__global__ void __launch_bounds__(kStemInPx) stem_in_kernel(const ImgSpec im, Act si, int *err) {
+    __shared__ __align__(16) uint8_t seg[kStemInPx * 4 + 32];
     pdl_wait();
-    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx == 0 && err) *err = 0;   // the enhancement's first kernel clears the device error word
-    if (idx >= (long long)si.H * si.W) return;
-    const int y = (int)(idx / si.W), x = (int)(idx - (long long)y * si.W);
-    const int sy = max(y - im.ph, 0), sx = max(x - im.pw, 0);
-    const uint8_t *p = im.src + (size_t)sy * im.stride + (size_t)sx * im.bpp;
-    const int ob = im.swap ? 2 : 0;
-    const __half b = __ushort2half_rn(p[ob]), g = __ushort2half_rn(p[1]), r = __ushort2half_rn(p[2 - ob]);
-    const __half z = __ushort2half_rn(0);
-    __align__(16) __half v[16] = {b, g, r, b, g, r, z, z, z, z, z, z, z, z, z, z};
-    act_store(si, y, x, 0, v, 16);
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && err) *err = 0;   // the enhancement's first kernel
+    const int y = blockIdx.y, x0 = blockIdx.x * kStemInPx, x = x0 + (int)threadIdx.x;
+    const int sy = max(y - im.ph, 0);
+    const int sx_lo = max(x0 - im.pw, 0);
+    const int sx_hi = max(min(x0 + kStemInPx - 1 - im.pw, im.w - 1), sx_lo);
+    const uintptr_t rowp = reinterpret_cast<uintptr_t>(im.src) + (size_t)sy * im.stride;
+    const uintptr_t a_lo = (rowp + (size_t)sx_lo * im.bpp) & ~uintptr_t(15);
+    const uintptr_t a_hi = rowp + (size_t)(sx_hi + 1) * im.bpp;   // exclusive
+    const int nwords = (int)((a_hi - a_lo + 15) >> 4);           // <= 66
+    for (int i = threadIdx.x; i < nwords; i += kStemInPx)
+        reinterpret_cast<uint4 *>(seg)[i] = reinterpret_cast<const uint4 *>(a_lo)[i];
+    __syncthreads();
+    if (x < si.W) {
+        const int sx = max(x - im.pw, 0);
+        const uint8_t *p = seg + (rowp + (size_t)sx * im.bpp - a_lo);
+        const int ob = im.swap ? 2 : 0;
+        const __half b = __ushort2half_rn(p[ob]), g = __ushort2half_rn(p[1]), r = __ushort2half_rn(p[2 - ob]);
+        const __half z = __ushort2half_rn(0);
+        __align__(16) __half v[16] = {b, g, r, b, g, r, z, z, z, z, z, z, z, z, z, z};
+        act_store(si, y, x, 0, v, 16);
+    }
     pdl_trigger();
 }
 
@@ -673,9 +692,8 @@ bool pdl_enabled() {
 }
 
 int stem_in_launch(const ImgSpec &im, const Act &si, int *err, cudaStream_t st) {
-    if (si.C != 16 || si.kind != LAY_PADREFL) return -2;
-    if (launch_pdl(stem_in_kernel, dim3(grid_for((long long)si.H * si.W, 256)), dim3(256), 0, st, im, si, err) != cudaSuccess)
-        return launch_status();
+    if (si.C != 16 || si.kind != LAY_PADREFL || im.stride != im.w * im.bpp) return -2;
+    launch_pdl(stem_in_kernel, dim3(grid_for(si.W, kStemInPx), si.H), dim3(kStemInPx), 0, st, im, si, err);
     return launch_status();
 }
 

@@ -49,7 +49,9 @@ int head_launch(const HeadArgs &a, cudaStream_t st);
 // The GC stem input (the stem-input layout of epilogue.cuh, LAY_PADREFL
 // [H+2][W+2][16] fp16): [x, x, 0] with x the u8 pixel of the top/left
 // replicate-padded source in B,G,R order (GcdrEnhancer.cs:242-243 pads and reads it).
-// err (may be null): the device error word, cleared by the kernel (the enhancement's first)
+// err (may be null): the device error word, cleared by the kernel (the enhancement's first).
+// im.src: a tight device image (stride = w * bpp) with at least 16 bytes of slack past its
+// end (the kernel reads whole aligned 16-byte words).
 int stem_in_launch(const ImgSpec &im, const Act &si, int *err, cudaStream_t st);
 // CUDA error string of this thread's last failed launch of the kernels above.
 const char *last_launch_error();
