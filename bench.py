@@ -611,7 +611,8 @@ def main():
                             "share_of_step": tc_ms / total_prof_ms if total_prof_ms else None},
             "single_stream": {"value": single_value, "unit": "images/s", "ms_per_image": single_ms / args.steps},
             "batched_launches": batching,
-            "gpu_launches": launches * args.steps * STREAMS,
+            "gpu_launches": launches * args.steps * STREAMS * world,
+            "gpu_launches_per_gpu": launches * args.steps * STREAMS,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "parity": parity,
