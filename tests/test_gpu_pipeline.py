@@ -1,7 +1,7 @@
 """End-to-end GPU parity of the CUDA backend against the CPU oracle and the
 reference's onnxruntime goldens.
 
-Bars (BASELINE north star and the reference's own GPU ladder,
+Bars (the parity gate of this backend and the reference's own GPU ladder,
 tests/Sdcb.SimdGcdrNet.Tests/VulkanTests.cs:15-80):
   * u8 output within +-2 LSB of the oracle on >= 99.9% of the values, never
     more than 8 off;

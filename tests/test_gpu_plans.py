@@ -85,3 +85,36 @@ def test_enhancer_second_pass_runs_from_cached_plans():
     for a, b in zip(*outs):
         assert np.array_equal(a, b)
     assert times[1] < 0.8 * times[0], f"second pass {times[1]:.3f} s vs first {times[0]:.3f} s"
+
+
+def test_concurrent_callers_mixed_shapes_match_serial():
+    """Four threads (the pool's idle capacity) share one enhancer and draw among three
+    shapes: the pool rents workers holding the requested shape's plan or plans it, and every
+    result equals the serial one (the kernels are deterministic).  The reference's concurrency test is
+    EngineTests.cs:245-263 (one size)."""
+    import threading
+    from sdcb.gcdrnet_b200 import GcdrEnhancer
+    imgs = {s: _doc(s[0], s[1], s[2], seed=30 + i) for i, s in enumerate(SHAPES)}
+    with GcdrEnhancer.from_files(G.GC_PATH, G.DR_PATH) as enh:
+        want = {s: enh.enhance_image(imgs[s].ravel(), s[0], s[1], s[2]) for s in SHAPES}
+        rng = np.random.default_rng(5)
+        plan = [[SHAPES[j] for j in rng.integers(0, len(SHAPES), 12)] for _ in range(4)]
+        errors = []
+
+        def run(k):
+            try:
+                for s in plan[k]:
+                    got = enh.enhance_image(imgs[s].ravel(), s[0], s[1], s[2])
+                    if not np.array_equal(got, want[s]):
+                        errors.append(f"thread {k} shape {s} differs")
+            except Exception as ex:   # surfaced below
+                errors.append(repr(ex))
+
+        th = [threading.Thread(target=run, args=(k,)) for k in range(4)]
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        assert not errors, errors[:3]
+        pools, workers, evicted = enh.pool_stats
+        assert pools == 1 and evicted == 0 and 1 <= workers <= 4
