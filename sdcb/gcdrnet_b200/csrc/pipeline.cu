@@ -503,7 +503,8 @@ int Worker::plan_arena() {
     al.take(reinterpret_cast<void **>(&d_dst_), img + 16);
     al.take(reinterpret_cast<void **>(&d_err_), 256);
     const size_t wsf = std::max(partial_floats(w.gc, H_, W_, num_sms_), partial_floats(w.dr, H_, W_, num_sms_));
-    al.take(reinterpret_cast<void **>(&ws_), std::max(wsf, (size_t)64) * 4);
+    ws_floats_ = std::max(wsf, (size_t)64);
+    al.take(reinterpret_cast<void **>(&ws_), ws_floats_ * 4);
     // a batch plan holds nimg_ such image slices, one after another
     layout_ = al.items;
     slice_bytes_ = al.off;
@@ -597,6 +598,10 @@ int Worker::build_ops() {
                 a.ep.partial = ws_;
                 run_mode = EPI_PARTIAL;
             }
+        }
+        if (partial && (double)a.ksplit * a.tg.conv_h * a.tg.conv_w * a.N > (double)ws_floats_) {
+            bias_fail_ = true;   // the workspace must bound every split: a plan error, nothing launches
+            return;
         }
         OpInfo oi;
         oi.name = name;
@@ -813,7 +818,7 @@ int Worker::build_ops() {
             conv_op(a, EPI_HEAD, pre + "head", head_flops, head_bytes);
         }
     }
-    if (bias_fail_) return fail(GCDR_ERR_DEVICE, "conv bias copy failed");
+    if (bias_fail_) return fail(GCDR_ERR_DEVICE, "conv bias copy failed or split-K workspace too small");
     return info_.size() == ops_.size() ? GCDR_OK : fail(GCDR_ERR_DEVICE, "op metadata mismatch");
 }
 

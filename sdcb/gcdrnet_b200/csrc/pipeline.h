@@ -169,6 +169,7 @@ private:
     float *r_ = nullptr, *ism_ = nullptr, *ydbg_ = nullptr;
     Act si_gc_, si_dr_;     // stem inputs [H+2][W+2][16] fp16 (GC: from the image; DR: from the GC head)
     float *ws_ = nullptr;   // split-K partial sums (EPI_PARTIAL), shared by both nets
+    size_t ws_floats_ = 0;  // its capacity (planned with the arena)
     uint8_t *d_src_ = nullptr, *d_dst_ = nullptr;
     int *d_err_ = nullptr;
     // pinned staging, copied in kHostBands row bands by the caller and pool_'s helpers: each
