@@ -8,6 +8,9 @@
                                         pyramid at 1600x1152 through the layer entry gcdr_k_conv
   batch [--count N]                     64 (N) Bgra32 1600x1152 documents enhanced in place with
                                         row stride width*4+64 through GcdrEnhancer (host buffers)
+  corpus DIR [--mode smoke|bench] [--count N] [--synthetic]
+                                        corpus harness (manifest.json + NN_<kind> / NN_gt images):
+                                        PSNR against the ground truths, determinism, cold timing
   stress [--count N]                    odd-size Rgba32 documents (w 2000-4096, h 1500-3072,
                                         seed 7): first pass (plan + graph capture per shape) and
                                         a second pass (parity: tests/test_gpu_configs.py)
@@ -234,10 +237,31 @@ def cmd_stress(a):
                   f"{mp / total:.1f} MP/s, per image ms: " + " ".join(f"{1000 * t:.1f}" for t in lat))
 
 
+def cmd_corpus(a):
+    import json
+    from . import GcdrEnhancer, corpus
+    folder = a.folder
+    if a.synthetic:
+        sizes = [(640, 480), (1600, 1152), (1024, 768), (2000, 1500), (640, 480), (1280, 960)][: max(1, a.count)]
+        corpus.write_synthetic(folder, sizes)
+    with GcdrEnhancer.from_files(*_models(a), device=a.device) as enh:
+        doc = corpus.run(enh, folder, a.mode, a.count, a.max_mp)
+        doc["pool"] = dict(zip(("pools", "workers", "evicted"), enh.pool_stats))
+    s = doc["summary"]
+    print(f"corpus[{a.mode}] {s['timed']} timed, mean {s['meanMs']} ms, {s['mpPerSec']} MP/s"
+          + (f", psnr {s['psnr']} dB (input {s['psnrIn']} dB)" if s["psnr"] is not None else ""))
+    for e in doc["errors"]:
+        print("FAIL", e, file=sys.stderr)
+    if a.out:
+        with open(a.out, "w") as fh:
+            json.dump(doc, fh, indent=1)
+    return 0 if doc["ok"] else 3
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(prog="python -m sdcb.gcdrnet_b200")
     sub = ap.add_subparsers(dest="cmd", required=True)
-    for name in ("enhance", "run", "prof", "microbench", "batch", "stress"):
+    for name in ("enhance", "run", "prof", "microbench", "batch", "stress", "corpus"):
         p = sub.add_parser(name)
         p.add_argument("--gc")
         p.add_argument("--dr")
@@ -245,6 +269,13 @@ def main(argv=None):
         if name == "enhance":
             p.add_argument("input")
             p.add_argument("output")
+        elif name == "corpus":
+            p.add_argument("folder")
+            p.add_argument("--mode", choices=("smoke", "bench"), default="smoke")
+            p.add_argument("--count", type=int, default=5)
+            p.add_argument("--max-mp", type=float, default=1e9)
+            p.add_argument("--out")
+            p.add_argument("--synthetic", action="store_true", help="first write seeded synthetic pairs into folder")
         elif name == "microbench":
             p.add_argument("--iters", type=int, default=20)
         elif name in ("batch", "stress"):
@@ -259,9 +290,9 @@ def main(argv=None):
             p.add_argument("--format", type=int, default=0)
             p.add_argument("--iters", type=int, default=10)
     a = ap.parse_args(argv)
-    {"enhance": cmd_enhance, "run": cmd_run, "prof": cmd_prof, "microbench": cmd_microbench, "batch": cmd_batch,
-     "stress": cmd_stress}[a.cmd](a)
-    return 0
+    rc = {"enhance": cmd_enhance, "run": cmd_run, "prof": cmd_prof, "microbench": cmd_microbench, "batch": cmd_batch,
+          "stress": cmd_stress, "corpus": cmd_corpus}[a.cmd](a)
+    return rc or 0
 
 
 if __name__ == "__main__":

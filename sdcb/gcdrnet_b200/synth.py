@@ -36,6 +36,20 @@ def _bicubic_field(gains: np.ndarray, h: int, w: int) -> np.ndarray:
 
 
 def document(width: int = 1600, height: int = 1152, seed: int = 0, fmt: int = 0, strokes: int = 200) -> np.ndarray:
+    return _render(width, height, seed, fmt, strokes)[0]
+
+
+CLEAN_PAPER = 250.0   # the ground-truth page of document_pair: flat, no shading, no noise
+
+
+def document_pair(width: int, height: int, seed: int = 0, strokes: int = 200):
+    """(degraded, clean) Bgr24 pages of one seed: document(width, height, seed) and the same
+    strokes, unshaded, on a flat CLEAN_PAPER page without noise (a ground truth in the
+    corpus harness's layout)."""
+    return _render(width, height, seed, 0, strokes, clean=True)
+
+
+def _render(width, height, seed, fmt, strokes, clean=False):
     rng = np.random.default_rng(seed)
     paper = rng.uniform(200, 240, 3)
     gains = rng.uniform(0.35, 1.0, (4, 4))
@@ -62,9 +76,15 @@ def document(width: int = 1600, height: int = 1152, seed: int = 0, fmt: int = 0,
         ys_all.append(yy[keep])
         xs_all.append(xx[keep])
         vs_all.append(np.full(keep.sum(), val, np.float32))
+    gt = None
     if ys_all:
         ys, xs, vs = np.concatenate(ys_all), np.concatenate(xs_all), np.concatenate(vs_all)
         img[ys, xs, :] = vs[:, None] * shade[ys, xs][:, None]
+    if clean:
+        gt = np.full((height, width, 3), CLEAN_PAPER, np.float32)
+        if ys_all:
+            gt[ys, xs, :] = vs[:, None]
+        gt = np.ascontiguousarray(np.clip(np.rint(gt), 0, 255).astype(np.uint8))
     img += rng.standard_normal(img.shape, dtype=np.float32) * np.float32(3.0)
     bgr = np.clip(np.rint(img), 0, 255).astype(np.uint8)
     if fmt in (1, 3):
@@ -72,7 +92,7 @@ def document(width: int = 1600, height: int = 1152, seed: int = 0, fmt: int = 0,
     if fmt >= 2:
         a = rng.integers(0, 256, (height, width, 1), dtype=np.uint8)
         bgr = np.concatenate([bgr, a], axis=2)
-    return np.ascontiguousarray(bgr)
+    return np.ascontiguousarray(bgr), gt
 
 
 class DocumentMaker:
