@@ -173,3 +173,19 @@ def test_odd_shapes_match_oracle(enh, oracle, w, h, fmt, seed):
     ref = want.reshape(h, w, 4)
     assert np.array_equal(got[:, :, 3], src.reshape(h, w, 4)[:, :, 3]), "alpha must be copied bit-exact"
     u8_check(got[:, :, :3], ref[:, :, :3], f"{w}x{h} vs oracle")
+
+
+def test_from_bytes_and_streams_match_from_files():
+    """FromBytes / FromStreams give the bytes FromFiles gives (ModelsPackageTests.cs:24-35)."""
+    import io
+    from sdcb.gcdrnet_b200 import GcdrEnhancer
+    *_, oh, ow = G.dims("small")
+    src = G.bgr("small")
+    gc, dr = open(G.GC_PATH, "rb").read(), open(G.DR_PATH, "rb").read()
+    outs = []
+    for make in (lambda: GcdrEnhancer.from_files(G.GC_PATH, G.DR_PATH),
+                 lambda: GcdrEnhancer.from_bytes(gc, dr),
+                 lambda: GcdrEnhancer.from_streams(io.BytesIO(gc), io.BytesIO(dr))):
+        with make() as e:
+            outs.append(e.enhance_image(src, ow, oh))
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
