@@ -456,15 +456,15 @@ __device__ void epilogue_head_pair(const EpiParams &ep, const TileGeom &tg, int 
             uo = __hfma2(h1b[p], t_b, uo);
             uo = __hfma2(h2a[p], q_a, uo);
             uo = __hfma2(h2b[p], q_b, uo);
-            const float2 fe = __half22float2(ue), fo = __half22float2(uo);
+            // relu of the upsampled pair in fp16 (one max per pair; the widening is exact)
+            const __half2 zero2 = __float2half2_rn(0.0f);
+            const float2 fe = __half22float2(__hmax2(ue, zero2)), fo = __half22float2(__hmax2(uo, zero2));
             const int c = 8 * k + 2 * p, cl = c % 16;
             const float2 bias = make_float2(hp.b1[c], hp.b1[c + 1]);
             const float2 ta = __fadd2_rn(make_float2(__uint_as_float(ca[cl]), __uint_as_float(ca[cl + 1])), bias);
             const float2 tb = __fadd2_rn(make_float2(__uint_as_float(cb[cl]), __uint_as_float(cb[cl + 1])), bias);
-            const float2 sa = __fadd2_rn(make_float2(fmaxf(fe.x, 0.0f), fmaxf(fe.y, 0.0f)),
-                                         make_float2(fmaxf(ta.x, 0.0f), fmaxf(ta.y, 0.0f)));
-            const float2 sb = __fadd2_rn(make_float2(fmaxf(fo.x, 0.0f), fmaxf(fo.y, 0.0f)),
-                                         make_float2(fmaxf(tb.x, 0.0f), fmaxf(tb.y, 0.0f)));
+            const float2 sa = __fadd2_rn(fe, make_float2(fmaxf(ta.x, 0.0f), fmaxf(ta.y, 0.0f)));
+            const float2 sb = __fadd2_rn(fo, make_float2(fmaxf(tb.x, 0.0f), fmaxf(tb.y, 0.0f)));
 #pragma unroll
             for (int o = 0; o < 3; o++) {
                 const float2 w = make_float2(hp.fw[o * C1 + c], hp.fw[o * C1 + c + 1]);
