@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
 #include <utility>
 
 namespace gcdr {
@@ -91,6 +92,16 @@ struct Act {
     }
 };
 
+// Batched launches: the buffers of image k lie k * img_bytes past image 0's (a batch plan's
+// image slices, one after another in the shape's arena).  Callers test an optional pointer
+// for null before they offset it.  (Byte arithmetic on the pointer itself, not through an
+// integer: the compiler keeps knowing that a kernel parameter's pointer is global memory.)
+template <class T>
+__host__ __device__ inline T *img_at(T *p, size_t off) {
+    using B = typename std::conditional<std::is_const<T>::value, const char, char>::type;
+    return reinterpret_cast<T *>(reinterpret_cast<B *>(p) + off);
+}
+
 __host__ __device__ inline int refl_lo(int n) { return n > 1 ? 1 : 0; }      // source of padded index 0
 __host__ __device__ inline int refl_hi(int n) { return n > 1 ? n - 2 : 0; }  // source of padded index n+1
 
@@ -115,10 +126,12 @@ __device__ __forceinline__ void act_rows(const Act &a, int y, int x, F &&put) {
 }
 
 // Stores `n` halves (n multiple of 2, 4-byte aligned) at channel c0 of pixel
-// (y, x), plus the reflect-border copies for LAY_PADREFL.
-__device__ __forceinline__ void act_store(const Act &a, int y, int x, int c0, const __half *v, int n) {
+// (y, x), plus the reflect-border copies for LAY_PADREFL.  io: byte offset of the
+// image in a batched launch (the tensor of image k lies k * img_bytes past a.p).
+__device__ __forceinline__ void act_store(const Act &a, int y, int x, int c0, const __half *v, int n, size_t io = 0) {
+    __half *base = img_at(a.p, io);
     act_rows(a, y, x, [&](long long r) {
-        __half *d = a.p + r * a.C + c0;
+        __half *d = base + r * a.C + c0;
         if ((n & 7) == 0 && ((reinterpret_cast<uintptr_t>(d) & 15) == 0)) {
             for (int k = 0; k < n; k += 8) *reinterpret_cast<uint4 *>(d + k) = *reinterpret_cast<const uint4 *>(v + k);
         } else {
@@ -128,8 +141,9 @@ __device__ __forceinline__ void act_store(const Act &a, int y, int x, int c0, co
 }
 
 // Two channels (c even) by value.
-__device__ __forceinline__ void act_store2(const Act &a, int y, int x, int c, __half2 v) {
-    act_rows(a, y, x, [&](long long r) { *reinterpret_cast<__half2 *>(a.p + r * a.C + c) = v; });
+__device__ __forceinline__ void act_store2(const Act &a, int y, int x, int c, __half2 v, size_t io = 0) {
+    __half *base = img_at(a.p, io);
+    act_rows(a, y, x, [&](long long r) { *reinterpret_cast<__half2 *>(base + r * a.C + c) = v; });
 }
 
 __device__ inline const __half *act_ptr(const Act &a, int y, int x) { return a.p + a.row(y, x) * a.C; }
@@ -172,7 +186,8 @@ __device__ inline int shift_dest(int s, int off, int L, bool *zero) {
 // tensor with the group shift along `axis` (2 = H, 3 = W) applied as a scatter;
 // a pair in one group goes out as one 4-byte store.
 __device__ __forceinline__ void shift_store2(const Act &a, const ShiftSpec &s, int axis, int y, int x, int c, float v0,
-                                             float v1) {
+                                             float v1, size_t io = 0) {
+    __half *base = img_at(a.p, io);
     const int g0 = shift_group(s, c), g1 = shift_group(s, c + 1);
     int dy = y, dx = x;
     bool z = false;
@@ -180,7 +195,7 @@ __device__ __forceinline__ void shift_store2(const Act &a, const ShiftSpec &s, i
         if (axis == 2) dy = shift_dest(y, s.offs[g0], a.H, &z);
         else dx = shift_dest(x, s.offs[g0], a.W, &z);
     }
-    __half *d = a.p + ((size_t)dy * a.W + dx) * a.C + c;
+    __half *d = base + ((size_t)dy * a.W + dx) * a.C + c;
     if (g0 == g1) {
         *reinterpret_cast<__half2 *>(d) = z ? __float2half2_rn(0.0f) : __floats2half2_rn(v0, v1);
     } else {
@@ -191,15 +206,15 @@ __device__ __forceinline__ void shift_store2(const Act &a, const ShiftSpec &s, i
             if (axis == 2) ey = shift_dest(y, s.offs[g1], a.H, &z1);
             else ex = shift_dest(x, s.offs[g1], a.W, &z1);
         }
-        a.p[((size_t)ey * a.W + ex) * a.C + c + 1] = __float2half_rn(z1 ? 0.0f : v1);
+        base[((size_t)ey * a.W + ex) * a.C + c + 1] = __float2half_rn(z1 ? 0.0f : v1);
     }
 }
 
 // Stores the channels [c0, c0+n) (n even, c0 even) of token pixel (y, x) with
 // the group shift (shift_store2 per pair).
 __device__ inline void shift_store(const Act &a, const ShiftSpec &s, int axis, int y, int x, int c0,
-                                   const float *v, int n) {
-    for (int k = 0; k < n; k += 2) shift_store2(a, s, axis, y, x, c0 + k, v[k], v[k + 1]);
+                                   const float *v, int n, size_t io = 0) {
+    for (int k = 0; k < n; k += 2) shift_store2(a, s, axis, y, x, c0 + k, v[k], v[k + 1], io);
 }
 
 // Loads 8 consecutive halves (16-byte aligned) as floats.

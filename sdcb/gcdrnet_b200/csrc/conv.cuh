@@ -29,6 +29,8 @@ struct ConvArgs {
     TileGeom tg;
     EpiParams ep;
     int *err = nullptr;        // device error flag (GCDR_ERR_FLAG_*)
+    int nimg = 1;              // images per launch: work units run over every image's grid
+    long long img_bytes = 0;   // byte distance between consecutive images' buffers (nimg > 1)
     long long wait_cycles = 0; // bound of each mbarrier wait in SM cycles (0: the default, ~2 s)
     int timeout_probe = 0;     // test hook: issue no copies and no MMAs, so every wait runs out
 };
@@ -36,6 +38,12 @@ struct ConvArgs {
 // The wait bound a launch uses.
 __host__ __device__ inline long long wait_budget(const ConvArgs &a) {
     return a.wait_cycles > 0 ? a.wait_cycles : kWaitCycles;
+}
+
+// Byte stride of the image dimension of a tensor map over `bytes` per image: the images'
+// distance in a batched launch, else the (16-byte rounded) size of the one image.
+__host__ __device__ inline unsigned long long img_stride(const ConvArgs &a, unsigned long long bytes) {
+    return a.nimg > 1 ? (unsigned long long)a.img_bytes : (bytes + 15) & ~15ull;
 }
 
 // Work unit u -> (m unit, n slice, k split).

@@ -46,8 +46,15 @@ struct RwConfig {
 int fill_bias_consts(ConvArgs &a);
 
 int tc_pick_bk(int C);
-bool tma_encode_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1,
-                   uint32_t b2, std::string &err);
+// fp16 tensor map of `rank` dims (dims[0] contiguous, swizzled by its width in bytes:
+// 32/64/128), strides[i] = byte stride of dims[i + 1].
+bool tma_encode(CUtensorMap *m, const void *base, int rank, const uint64_t *dims, const uint64_t *strides,
+                const uint32_t *box, int swizzle_bytes, std::string &err);
+// The activation map of a conv (a.A): [nimg][a_rows][C] with the launch's image stride, a
+// box of box_inner channels x box_rows rows of one image.
+bool tma_encode_act(CUtensorMap *m, const ConvArgs &a, uint32_t box_inner, uint32_t box_rows, std::string &err);
+// Checks a launch's image count and stride (batched launches).
+bool batch_ok(const ConvArgs &a, std::string &err);
 bool tma_encode_2d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint32_t box_inner,
                    uint32_t box_outer, int bk, std::string &err);
 // 0 and a plan when the layer suits the row-window kernel, -1 otherwise.

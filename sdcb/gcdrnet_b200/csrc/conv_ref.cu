@@ -75,6 +75,7 @@ size_t ref_conv_scratch_floats(const ConvArgs &a) { return (size_t)ref_rows(a.tg
 
 int ref_conv_launch(const ConvArgs &a, int mode, float *scratch, cudaStream_t st, std::string &err) {
     if (a.N % 16 || a.tg.ntiles < 1 || a.nsplit != 1 || a.ksplit != 1) { err = "ref conv: bad shape"; return -1; }
+    if (a.nimg != 1) { err = "ref conv: one image per launch"; return -1; }
     if ((mode == EPI_POOL) != (a.tg.pool != 0)) { err = "ref conv: pool geometry / mode mismatch"; return -1; }
     if (a.tg.pool && (a.tg.conv_h % 2 || a.tg.conv_w % 2 || a.tg.pitch < a.tg.conv_w)) {
         err = "ref conv: bad pool geometry";

@@ -118,8 +118,13 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
     const bool b_loader = (warp == 0 && lane == 0);
     if (!b_loader) pdl_wait();              // activations of the previous kernels
 
-    // unit -> (first output row, first pixel); pool units cover R conv rows = R/2 pooled rows
-    auto unit_origin = [&](int u, int &y0, int &x0) {
+    // unit -> (image, first output row, first pixel); pool units cover R conv rows = R/2
+    // pooled rows; a batched launch runs the units of image 0, then image 1, ...
+    const int nunits = cfg.units * args.nimg;
+    const bool batched = args.nimg > 1;          // map ranks: activations 3 (else 2), dec5 4 (else 3)
+    auto unit_origin = [&](int u, int &img, int &y0, int &x0) {
+        img = u / cfg.units;
+        u -= img * cfg.units;
         const int yb = u / cfg.segs_x;
         y0 = yb * R;
         x0 = (u - yb * cfg.segs_x) * 128;
@@ -142,19 +147,22 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
             int g = 0, issued = 0;
             bool ok = true;
             // (the timeout probe issues nothing: every consumer's wait runs out)
-            for (int u = blockIdx.x; u < cfg.units && ok && !args.timeout_probe; u += gridDim.x) {
-                int y0, x0;
-                unit_origin(u, y0, x0);
+            for (int u = blockIdx.x; u < nunits && ok && !args.timeout_probe; u += gridDim.x) {
+                int img, y0, x0;
+                unit_origin(u, img, y0, x0);
                 for (int kb = 0; kb < kbs; kb++, g++) {
                     if (g % Roles::prod == p) {
                         if (!mbar_wait(&sh->empty[s], ph ^ 1u, abort_flag, args.err, budget)) { ok = false; break; }
                         uint8_t *stage = ring + (size_t)s * cfg.stage_bytes;
                         mbar_expect_tx(&sh->full[s], (uint32_t)((R + 2) * kSegRows * BK * 2 + cfg.win_tx));
                         for (int r = 0; r < R + 2; r++)
-                            tma_load_2d(stage + (size_t)r * cfg.seg_bytes, &tmA, kb * BK, (y0 + r) * pitch + x0, &sh->full[s]);
-                        if (MODE == EPI_HEAD)   // dec5 rows y0/2 - 1.., columns x0/2 - 1.. (edge: zero fill, never read)
-                            tma_load_3d(stage + (size_t)(R + 2) * cfg.seg_bytes, &tmC, 0, x0 / 2 - 1, y0 / 2 - 1,
-                                        &sh->full[s]);
+                            tma_load_act(stage + (size_t)r * cfg.seg_bytes, &tmA, kb * BK, (y0 + r) * pitch + x0, img,
+                                         batched, &sh->full[s]);
+                        if (MODE == EPI_HEAD) {   // dec5 rows y0/2 - 1.., columns x0/2 - 1.. (edge: zero fill, never read)
+                            uint8_t *win = stage + (size_t)(R + 2) * cfg.seg_bytes;
+                            if (batched) tma_load_4d(win, &tmC, 0, x0 / 2 - 1, y0 / 2 - 1, img, &sh->full[s]);
+                            else tma_load_3d(win, &tmC, 0, x0 / 2 - 1, y0 / 2 - 1, &sh->full[s]);
+                        }
                         issued++;
                     }
                     if (++s == cfg.stages) { s = 0; ph ^= 1u; }
@@ -174,7 +182,7 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
             uint32_t ph = 0;
             int t = 0, consumed = 0;
             bool ok = mbar_wait(&sh->bfull, 0, abort_flag, args.err, budget);
-            for (int u = blockIdx.x; u < cfg.units && ok; u += gridDim.x, t++) {
+            for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x, t++) {
                 const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
                 const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
                 if (!mbar_wait(&sh->tempty[ab], aph ^ 1u, abort_flag, args.err, budget)) break;
@@ -228,9 +236,10 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
         const int row = quad * 32 + lane;           // pixel within the unit's 128
         const uint32_t lane_base = tmem_base + ((uint32_t)(quad * 32) << 16);
         int t = 0;
-        for (int u = blockIdx.x; u < cfg.units; u += gridDim.x, t++) {
-            int y0, x0;
-            unit_origin(u, y0, x0);
+        for (int u = blockIdx.x; u < nunits; u += gridDim.x, t++) {
+            int img, y0, x0;
+            unit_origin(u, img, y0, x0);
+            const size_t io = (size_t)img * (size_t)args.img_bytes;
             const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
             const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
             bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err, budget);
@@ -255,7 +264,7 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
                     const int q = it / nch, ch = it - q * nch;
                     TmemLoader top{acc0 + (uint32_t)(2 * q * cfg.acc_cols)};
                     TmemLoader bot{acc0 + (uint32_t)((2 * q + 1) * cfg.acc_cols)};
-                    epilogue_pool(args.ep, tg, y0 / 2 + q, x, 0, N, top, bot, ch, nch);
+                    epilogue_pool(args.ep, tg, y0 / 2 + q, x, 0, N, top, bot, ch, nch, io);
                 }
             } else if (MODE == EPI_HEAD) {
                 // pixel pairs (rows 2q, 2q + 1: one shared dec5 row) taken in turn by the warps;
@@ -271,7 +280,7 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
                         const uint8_t *segs = ring + (size_t)hs * cfg.stage_bytes;
                         epilogue_head_pair<HC>(args.ep, tg, y0 + 2 * q, x, l0, l1, win, y0 / 2 - 1, x0 / 2 - 1,
                                                segs + (size_t)(2 * q + 1) * cfg.seg_bytes,
-                                               segs + (size_t)(2 * q + 2) * cfg.seg_bytes, row + 1);
+                                               segs + (size_t)(2 * q + 2) * cfg.seg_bytes, row + 1, io);
                     }
                 }
                 __syncwarp();
@@ -280,7 +289,7 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
                 for (int it = part; it < R * nch; it += Roles::parts) {
                     const int jj = it / nch, ch = it - jj * nch;
                     TmemLoader ld{acc0 + (uint32_t)(jj * cfg.acc_cols)};
-                    epilogue_plain_yx(args.ep, tg, y0 + jj, x, 0, N, ld, ch, nch, args.ep.bias_c);
+                    epilogue_plain_yx(args.ep, tg, y0 + jj, x, 0, N, ld, ch, nch, args.ep.bias_c, io);
                 }
             }
             tc_fence_before();
@@ -348,6 +357,17 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
         return -1;
     if (mode == EPI_HEAD && (a.C != kStemInC || (a.N != 16 && a.N != 32))) return -1;
     if (a.ntaps != 9 || a.N < 16 || a.N > 256 || a.N % 16) return -1;
+    // the k-block width orders the sums (taps within a k-block, k-blocks outermost): it is
+    // the one-image plan's in a batched launch too, so that each image gets the same bytes;
+    // the rows per unit change no sum and are sized for the whole launch
+    int bk_fixed = 0;
+    if (a.nimg > 1) {
+        ConvArgs one = a;
+        one.nimg = 1;
+        RwConfig c1;
+        if (rw_plan(one, mode, num_sms, c1)) return -1;
+        bk_fixed = c1.bk;
+    }
     const TileGeom &tg = a.tg;
     if (tg.pool && (tg.conv_h % 2 || tg.conv_w % 2)) return -1;
     int cols = 32;
@@ -367,7 +387,7 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
     // pass 1 (small layers): the fewest rows per unit that fit, for the most units
     for (int pass = 0; pass < 2 && !found; pass++) {
         for (int bk = tc_pick_bk(a.C); bk >= 16 && !found; bk >>= 1) {
-            if (a.C % bk) continue;
+            if (a.C % bk || (bk_fixed && bk != bk_fixed)) continue;
             if (mode == EPI_HEAD && bk != a.C) continue;   // one ring stage (and dec5 window) per head unit
             const int b_block = round1k(a.N * bk * 2);
             const int b_bytes = 9 * (a.C / bk) * b_block;
@@ -379,15 +399,16 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
                 const int R = mode == EPI_HEAD ? (pass == 0 ? 6 - 2 * i : 2 + 2 * i)
                               : pass == 0 ? (i == 0 ? (mode == EPI_POOL ? 8 : 4) : i == 1 ? 4 : 2) : (r_min << i);
                 if (R < r_min || R > (mode == EPI_HEAD ? 6 : mode == EPI_POOL ? 8 : 4)) continue;
-                const int units = ((tg.conv_h + R - 1) / R) * segs_x;
+                const int units = ((tg.conv_h + R - 1) / R) * segs_x;   // of one image
+                const long long all_units = (long long)units * a.nimg;
                 // head: the unit's dec5 window (R/2 + 2 rows of kHeadWinCols columns x N channels)
                 const int win_tx = mode == EPI_HEAD ? (R / 2 + 2) * kHeadWinCols * a.N * 2 : 0;
                 const int stage_bytes = (R + 2) * seg_bytes + round1k(win_tx);
                 const int stages = avail / stage_bytes;
                 if (2 * R * cols > 512 || stages < 3) continue;
-                if (pass == 0 && units < num_sms && !(tg.pool && R == 2)) continue;
+                if (pass == 0 && all_units < num_sms && !(tg.pool && R == 2)) continue;
                 // (8-row units: instantiated for 16-channel k-blocks, the stems)
-                if (R == 8 && (bk != 16 || (pass == 0 && units < 8 * num_sms))) continue;
+                if (R == 8 && (bk != 16 || (pass == 0 && all_units < 8 * num_sms))) continue;
                 cfg.bk = bk;
                 cfg.R = R;
                 cfg.b_block = b_block;
@@ -415,20 +436,25 @@ int rw_conv_launch(const ConvArgs &a, int mode, const RwConfig &cfg, int num_sms
         err = "operands must be 16-byte aligned";
         return -1;
     }
+    if (!batch_ok(a, err)) return -1;
     CUtensorMap ta, tb;
-    if (!tma_encode_2d(&ta, a.A, (uint64_t)a.C, (uint64_t)a.a_rows, (uint32_t)cfg.bk, (uint32_t)kSegRows, cfg.bk, err))
-        return -1;
+    if (!tma_encode_act(&ta, a, (uint32_t)cfg.bk, (uint32_t)kSegRows, err)) return -1;
     if (!tma_encode_2d(&tb, a.B, (uint64_t)a.C * 9, (uint64_t)a.N, (uint32_t)cfg.bk, (uint32_t)a.N, cfg.bk, err))
         return -1;
     CUtensorMap tc = tb;   // the head's dec5 window map (other modes: unused)
     if (mode == EPI_HEAD) {
         const __half *d5 = a.ep.head.dec5;
         if (!d5 || (reinterpret_cast<uintptr_t>(d5) & 15)) { err = "head: dec5 missing or misaligned"; return -1; }
-        if (!tma_encode_3d(&tc, d5, (uint64_t)a.N, (uint64_t)(a.tg.conv_w / 2), (uint64_t)(a.tg.conv_h / 2),
-                           (uint32_t)a.N, (uint32_t)kHeadWinCols, (uint32_t)(cfg.R / 2 + 2), err))
-            return -1;
+        // [nimg][H/2][W/2][N] fp16: a box of N channels x kHeadWinCols columns x (R/2 + 2) rows
+        const uint64_t w2 = (uint64_t)(a.tg.conv_w / 2), h2 = (uint64_t)(a.tg.conv_h / 2);
+        const uint64_t dims[4] = {(uint64_t)a.N, w2, h2, (uint64_t)a.nimg};
+        const uint64_t strides[3] = {(uint64_t)a.N * 2, (uint64_t)a.N * 2 * w2, img_stride(a, (unsigned long long)a.N * 2 * w2 * h2)};
+        const uint32_t box[4] = {(uint32_t)a.N, (uint32_t)kHeadWinCols, (uint32_t)(cfg.R / 2 + 2), 1};
+        if (!tma_encode(&tc, d5, a.nimg > 1 ? 4 : 3, dims, strides, box, a.N * 2, err)) return -1;
     }
-    const int grid = cfg.units < num_sms ? cfg.units : num_sms;
+    const long long all_units = (long long)cfg.units * a.nimg;
+    if (all_units > (1ll << 30)) { err = "too many work units"; return -1; }
+    const int grid = all_units < num_sms ? (int)all_units : num_sms;
     static const bool verbose = [] { const char *v = std::getenv("GCDR_CUDA_VERBOSE"); return v && v[0] == '1'; }();
     if (verbose)
         std::fprintf(stderr, "rw_conv mode %d C %d N %d H %d W %d | bk %d R %d units %d grid %d stages %d stage_bytes %d "

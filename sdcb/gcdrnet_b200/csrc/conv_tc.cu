@@ -69,7 +69,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     const int nst = MODE == EPI_POOL ? 2 * cfg.rt : cfg.rt;      // 128-row sub-tiles per unit
     const int munits = m_units(tg, cfg.rt);
     const int segs = MODE == EPI_POOL ? (tg.conv_w + 128 * cfg.rt - 1) / (128 * cfg.rt) : 1;
-    const int nunits = munits * args.nsplit * args.ksplit;
+    const int img_units = munits * args.nsplit * args.ksplit;   // units of one image
+    const int nunits = img_units * args.nimg;                    // image-major over a batch
+    const bool batched = args.nimg > 1;                          // the activation map's rank: 3, else 2
     const uint32_t a_bytes = 128u * nst * BK * 2u;
     const uint32_t b_bytes = (uint32_t)Ns * BK * 2u;
     const int nsub = (Ns + 255) / 256;
@@ -117,8 +119,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             bool ok = true;
             // (the timeout probe issues nothing: every consumer's wait runs out)
             for (int u = blockIdx.x; u < nunits && ok && !args.timeout_probe; u += gridDim.x) {
+                const int img = u / img_units;
                 int mu, ni, ki;
-                unit_coords(args, u, mu, ni, ki);
+                unit_coords(args, u - img * img_units, mu, ni, ki);
                 long long r0, r1;
                 if (MODE == EPI_POOL) {
                     const int y2 = mu / segs, x0 = (mu - y2 * segs) * 128 * cfg.rt;
@@ -139,8 +142,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                             uint8_t *sa = stage + (size_t)j * cfg.sub_bytes;
                             uint8_t *sb = sa + a_bytes;
                             const int off = args.tap_off[tap];
-                            tma_load_2d(sa, &tmA, cb * BK, (int)(r0 + off), &sh->full[s]);
-                            tma_load_2d(sa + a_bytes / 2, &tmA, cb * BK, (int)(r1 + off), &sh->full[s]);
+                            tma_load_act(sa, &tmA, cb * BK, (int)(r0 + off), img, batched, &sh->full[s]);
+                            tma_load_act(sa + a_bytes / 2, &tmA, cb * BK, (int)(r1 + off), img, batched, &sh->full[s]);
                             for (int h = 0; h < nsub; h++)
                                 tma_load_2d(sb + (size_t)h * 256 * BK * 2, &tmB, tap * args.C + cb * BK,
                                             ni * Ns + h * 256, &sh->full[s]);
@@ -212,8 +215,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             // LayerNorm modes: each set of four warps (one per lane quadrant) takes the units
             // of one accumulator buffer, one whole row per thread
             if (kLnUnits && (cfg.acc_bufs == 2 ? (t & 1) : 0) != part) continue;
+            const int img = u / img_units;
+            const size_t io = (size_t)img * (size_t)args.img_bytes;
             int mu, ni, ki;
-            unit_coords(args, u, mu, ni, ki);
+            unit_coords(args, u - img * img_units, mu, ni, ki);
             const int ab = cfg.acc_bufs == 2 ? (t & 1) : 0;
             const uint32_t aph = (uint32_t)((cfg.acc_bufs == 2 ? (t >> 1) : t) & 1);
             bool ok = mbar_wait(&sh->tfull[ab], aph, abort_flag, args.err, budget);
@@ -243,21 +248,21 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                 for (int i = 0; i < cfg.rt; i++) {
                     TmemLoader top{acc0 + (uint32_t)(i * cfg.acc_cols)};
                     TmemLoader bot{acc0 + (uint32_t)((cfg.rt + i) * cfg.acc_cols)};
-                    epilogue_pool(args.ep, tg, y2, x0 + 128 * i + row, ni * Ns, Ns, top, bot, part, 2);
+                    epilogue_pool(args.ep, tg, y2, x0 + 128 * i + row, ni * Ns, Ns, top, bot, part, 2, io);
                 }
             } else if (kLnUnits) {
                 for (int i = 0; i < cfg.rt; i++) {
                     const int tile = mu * cfg.rt + i;
                     if (tile >= tg.ntiles) break;
                     TmemLoader ld{acc0 + (uint32_t)(i * cfg.acc_cols)};
-                    epilogue_ln_row<MODE>(args.ep, tg, tile, row, N, ld);
+                    epilogue_ln_row<MODE>(args.ep, tg, tile, row, N, ld, io);
                 }
             } else {
                 for (int i = 0; i < cfg.rt; i++) {
                     const int tile = mu * cfg.rt + i;
                     if (tile >= tg.ntiles) break;
                     TmemLoader ld{acc0 + (uint32_t)(i * cfg.acc_cols)};
-                    epilogue_tile<MODE>(args.ep, tg, tile, row, ni * Ns, Ns, N, ki, ld, part, 2);
+                    epilogue_tile<MODE>(args.ep, tg, tile, row, ni * Ns, Ns, N, ki, ld, part, 2, io);
                 }
             }
             tc_fence_before();
@@ -367,22 +372,47 @@ int fill_bias_consts(ConvArgs &a) {
     return cudaMemcpy(a.ep.bias_c, a.ep.bias, (size_t)a.N * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
 }
 
-// [d2][d1][d0] fp16 (d0 contiguous, 32 or 64 bytes: the swizzle of that width), a box
-// of (b0, b1, b2); out-of-range elements of a box read as zero
-bool tma_encode_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1,
-                   uint32_t b2, std::string &err) {
+// fp16 tensor of `rank` dims (dims[0] contiguous, `swizzle_bytes` = its 32/64/128-byte
+// swizzle), strides[i] = byte stride of dims[i + 1]; a box of box[0..rank); out-of-range
+// elements of a box read as zero
+bool tma_encode(CUtensorMap *m, const void *base, int rank, const uint64_t *dims, const uint64_t *strides,
+                const uint32_t *box, int swizzle_bytes, std::string &err) {
     const auto encode = get_encoder(err);
     if (!encode) return false;
-    if (d0 * 2 != 32 && d0 * 2 != 64) { err = "tma 3d: inner extent must be 32 or 64 bytes"; return false; }
-    cuuint64_t dims[3] = {d0, d1, d2};
-    cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
-    cuuint32_t box[3] = {b0, b1, b2};
-    cuuint32_t es[3] = {1, 1, 1};
-    CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, d0 * 2 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (rank < 2 || rank > 5) { err = "tma: rank must be 2..5"; return false; }
+    cuuint64_t d[5], st[4];
+    cuuint32_t b[5], es[5];
+    for (int i = 0; i < rank; i++) {
+        d[i] = dims[i];
+        b[i] = box[i];
+        es[i] = 1;
+        if (i) st[i - 1] = strides[i - 1];
+    }
+    const CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swizzle_bytes == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                       : CU_TENSOR_MAP_SWIZZLE_32B;
+    CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank, const_cast<void *>(base), d, st, b, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
-        err = "cuTensorMapEncodeTiled (3d) failed (" + std::to_string((int)r) + ")";
+        err = "cuTensorMapEncodeTiled (" + std::to_string(rank) + "d) failed (" + std::to_string((int)r) + ")";
+        return false;
+    }
+    return true;
+}
+
+bool tma_encode_act(CUtensorMap *m, const ConvArgs &a, uint32_t box_inner, uint32_t box_rows, std::string &err) {
+    // one image: a 2-D map (the kernels issue 2-D loads then: a 3-D box costs more to issue)
+    const uint64_t dims[3] = {(uint64_t)a.C, (uint64_t)a.a_rows, (uint64_t)a.nimg};
+    const uint64_t strides[2] = {(uint64_t)a.C * 2, img_stride(a, (unsigned long long)a.a_rows * a.C * 2)};
+    const uint32_t box[3] = {box_inner, box_rows, 1};
+    return tma_encode(m, a.A, a.nimg > 1 ? 3 : 2, dims, strides, box, (int)box_inner * 2, err);
+}
+
+bool batch_ok(const ConvArgs &a, std::string &err) {
+    if (a.nimg < 1 || a.nimg > 65535) { err = "images per launch must be 1..65535"; return false; }
+    if (a.nimg > 1 && (a.img_bytes <= 0 || a.img_bytes % 16 || (unsigned long long)a.img_bytes < (unsigned long long)a.a_rows * a.C * 2)) {
+        err = "batched launch: the image stride must be a positive multiple of 16 bytes holding each image's input";
         return false;
     }
     return true;
@@ -417,7 +447,7 @@ int tc_plan(const ConvArgs &a, int mode, int num_sms, TcConfig &cfg, std::string
     for (int r = 4; r > 1; r >>= 1) {
         const int nst = a.tg.pool ? 2 * r : r;
         if (a.ksplit != 1 || nst > 4 || Ns > 256) continue;
-        if (2 * nst * cols <= 512 && m_units(a.tg, r) * a.nsplit >= num_sms) { cfg.rt = r; break; }
+        if (2 * nst * cols <= 512 && (long long)m_units(a.tg, r) * a.nsplit * a.nimg >= num_sms) { cfg.rt = r; break; }
     }
     if (mode == EPI_PLAIN && !a.tg.pool && a.ksplit == 1 && Ns <= 256) {
         // Plain layers: cost ~ waves x (rt A tiles + one B tile) per k-block.  Between one and
@@ -426,7 +456,7 @@ int tc_plan(const ConvArgs &a, int mode, int num_sms, TcConfig &cfg, std::string
         // only when each CTA has one unit.
         double best = 1e30;
         for (int r = 1; r <= 4; r <<= 1) {
-            const long long units = (long long)m_units(a.tg, r) * a.nsplit;
+            const long long units = (long long)m_units(a.tg, r) * a.nsplit * a.nimg;
             const int bufs = 2 * r * cols <= 512 ? 2 : 1;
             if (r * cols > 512 || (bufs == 1 && units > num_sms)) continue;
             const double cost = (double)((units + num_sms - 1) / num_sms) * (r * 128.0 + Ns);
@@ -469,26 +499,26 @@ int tc_conv_launch(const ConvArgs &a, int mode, int num_sms, cudaStream_t st, st
         return -1;
     }
     TcConfig cfg;
-    if (tc_plan(a, mode, num_sms, cfg, err)) return -1;
+    if (!batch_ok(a, err) || tc_plan(a, mode, num_sms, cfg, err)) return -1;
     if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) {
         err = "operands must be 16-byte aligned";
         return -1;
     }
     CUtensorMap ta, tb;
     const int box_rows = 64 * (a.tg.pool ? 2 * cfg.rt : cfg.rt);
-    if (!encode_2d(&ta, a.A, (uint64_t)a.C, (uint64_t)a.a_rows, (uint32_t)cfg.bk, (uint32_t)box_rows, cfg.bk, err))
-        return -1;
+    if (!tma_encode_act(&ta, a, (uint32_t)cfg.bk, (uint32_t)box_rows, err)) return -1;
     const int Ns = a.N / a.nsplit;
     if (!encode_2d(&tb, a.B, (uint64_t)a.C * a.ntaps, (uint64_t)a.N, (uint32_t)cfg.bk, (uint32_t)(Ns < 256 ? Ns : 256),
                    cfg.bk, err))
         return -1;
-    const int units = m_units(a.tg, cfg.rt) * a.nsplit * a.ksplit;
-    int grid = units < num_sms ? units : num_sms;
+    const long long units = (long long)m_units(a.tg, cfg.rt) * a.nsplit * a.ksplit * a.nimg;
+    if (units > (1ll << 30)) { err = "too many work units"; return -1; }
+    int grid = units < num_sms ? (int)units : num_sms;
     static const bool verbose = [] { const char *v = std::getenv("GCDR_CUDA_VERBOSE"); return v && v[0] == '1'; }();
     if (verbose)
         std::fprintf(stderr, "tc_conv mode %d C %d N %d taps %d tiles %d rt %d nsplit %d ksplit %d units %d grid %d | bk %d "
                              "kps %d stages %d stage_bytes %d tmem %d\n",
-                     mode, a.C, a.N, a.ntaps, a.tg.ntiles, cfg.rt, a.nsplit, a.ksplit, units, grid, cfg.bk, cfg.kps,
+                     mode, a.C, a.N, a.ntaps, a.tg.ntiles, cfg.rt, a.nsplit, a.ksplit, (int)units, grid, cfg.bk, cfg.kps,
                      cfg.stages, cfg.stage_bytes, cfg.tmem_cols);
     if (grid < 1) return 0;
     switch (cfg.bk) {

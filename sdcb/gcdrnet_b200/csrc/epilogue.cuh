@@ -97,15 +97,15 @@ __device__ __forceinline__ void load_cols(L &ld, int c0, int w, float *v) {
     else ld.load16(c0, v);
 }
 
-// t = acc + bias (+ residual) of columns [c0, c0+w) of the row.
+// t = acc + bias (+ residual `res`, this image's tokens) of columns [c0, c0+w) of the row.
 template <class L>
-__device__ __forceinline__ void row_vals(L &ld, const EpiParams &ep, int N, long long tok, bool use_res, int c0,
-                                         int w, float *v) {
+__device__ __forceinline__ void row_vals(L &ld, const EpiParams &ep, const __half *res, int N, long long tok,
+                                         bool use_res, int c0, int w, float *v) {
     load_cols(ld, c0, w, v);
     float r[32];
     if (use_res) {
-        load16h(ep.res + tok * N + c0, r);
-        if (w == 32) load16h(ep.res + tok * N + c0 + 16, r + 16);
+        load16h(res + tok * N + c0, r);
+        if (w == 32) load16h(res + tok * N + c0 + 16, r + 16);
     }
 #pragma unroll
     for (int k = 0; k < 32; k++)
@@ -114,9 +114,11 @@ __device__ __forceinline__ void row_vals(L &ld, const EpiParams &ep, int N, long
 
 // PLAIN epilogue of output pixel (y, x): bias [+ relu] -> fp16 store of the
 // column chunks c0 = part*cw, (part + nparts)*cw, ... (several warps may share a row).
+// io: byte offset of the unit's image (batched launches; 0 for image 0).
 template <class L>
 __device__ __forceinline__ void epilogue_plain_yx(const EpiParams &ep, const TileGeom &tg, int y, int x, int n0,
-                                                  int Nsub, L &ld, int part, int nparts, const float *bias) {
+                                                  int Nsub, L &ld, int part, int nparts, const float *bias,
+                                                  size_t io = 0) {
     float v[32];
     const int cw = (Nsub % 32 == 0) ? 32 : 16;
     const bool valid = y < tg.conv_h && x < tg.conv_w;
@@ -131,7 +133,7 @@ __device__ __forceinline__ void epilogue_plain_yx(const EpiParams &ep, const Til
                     h[k] = __float2half_rn(ep.relu ? fmaxf(t, 0.0f) : t);
                 }
             }
-            act_store(ep.out, y, x, n0 + c0, h, cw);
+            act_store(ep.out, y, x, n0 + c0, h, cw, io);
         }
     }
 }
@@ -140,7 +142,7 @@ __device__ __forceinline__ void epilogue_plain_yx(const EpiParams &ep, const Til
 // (several warps may share a row); the LayerNorm modes need the whole row (nparts = 1).
 template <int MODE, class L>
 __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile, int row, int n0, int Nsub, int N,
-                              int ksplit_idx, L &ld, int part = 0, int nparts = 1) {
+                              int ksplit_idx, L &ld, int part = 0, int nparts = 1, size_t io = 0) {
     float v[32];
     const int cw = (Nsub % 32 == 0) ? 32 : 16;
     const long long q = (long long)tile * 128 + row;
@@ -148,12 +150,12 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     const bool valid = y < tg.conv_h && x < tg.conv_w;
     const long long tok = valid ? (long long)y * tg.conv_w + x : 0;
     if (MODE == EPI_PLAIN) {
-        epilogue_plain_yx(ep, tg, y, x, n0, Nsub, ld, part, nparts, ep.bias_c);
+        epilogue_plain_yx(ep, tg, y, x, n0, Nsub, ld, part, nparts, ep.bias_c, io);
         return;
     }
     if (MODE == EPI_PARTIAL) {
         const long long T = (long long)tg.conv_h * tg.conv_w;
-        float *dst = ep.partial + ((long long)ksplit_idx * T + tok) * N + n0;
+        float *dst = img_at(ep.partial, io) + ((long long)ksplit_idx * T + tok) * N + n0;
         for (int c0 = part * cw; c0 < Nsub; c0 += nparts * cw) {
             load_cols(ld, c0, cw, v);
             if (valid) {
@@ -167,9 +169,10 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     // LayerNorm modes (the slice is the whole row: n0 = 0, Nsub = N): single-pass
     // statistics shifted by the row's first value.
     const bool use_res = MODE == EPI_RESLN;
+    const __half *res = use_res ? img_at(ep.res, io) : nullptr;
     float shift0 = 0.f, s1 = 0.f, s2 = 0.f;
     for (int c0 = 0; c0 < N; c0 += cw) {
-        row_vals(ld, ep, N, tok, use_res, c0, cw, v);
+        row_vals(ld, ep, res, N, tok, use_res, c0, cw, v);
         if (c0 == 0) shift0 = v[0];
 #pragma unroll
         for (int k = 0; k < 32; k++)
@@ -184,13 +187,13 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     const float rstd = rsqrtf(fmaxf(s2 / N - m1 * m1, 0.0f) + ep.eps1);
     if (MODE == EPI_RESLN) {
         for (int c0 = 0; c0 < N; c0 += cw) {
-            row_vals(ld, ep, N, tok, true, c0, cw, v);
+            row_vals(ld, ep, res, N, tok, true, c0, cw, v);
             if (valid) {
                 __align__(16) __half h[32];
 #pragma unroll
                 for (int k = 0; k < 32; k++)
                     if (k < cw) h[k] = __float2half_rn((v[k] - mean) * rstd * ep.g1[c0 + k] + ep.b1[c0 + k]);
-                act_store(ep.out, y, x, c0, h, cw);
+                act_store(ep.out, y, x, c0, h, cw, io);
             }
         }
         return;
@@ -198,7 +201,7 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
     // EPI_LN2: y0 = LN1(v) stored; LN2 statistics over the fp32 y0 (shifted by its first value).
     float t0 = 0.f, u1 = 0.f, u2 = 0.f;
     for (int c0 = 0; c0 < N; c0 += cw) {
-        row_vals(ld, ep, N, tok, false, c0, cw, v);
+        row_vals(ld, ep, res, N, tok, false, c0, cw, v);
         __align__(16) __half h[32];
 #pragma unroll
         for (int k = 0; k < 32; k++)
@@ -210,13 +213,13 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
                 u2 += d * d;
                 h[k] = __float2half_rn(t);
             }
-        if (valid) act_store(ep.out, y, x, c0, h, cw);
+        if (valid) act_store(ep.out, y, x, c0, h, cw, io);
     }
     const float mu = u1 / N;
     const float mean2 = t0 + mu;
     const float rstd2 = rsqrtf(fmaxf(u2 / N - mu * mu, 0.0f) + ep.eps2);
     for (int c0 = 0; c0 < N; c0 += cw) {
-        row_vals(ld, ep, N, tok, false, c0, cw, v);
+        row_vals(ld, ep, res, N, tok, false, c0, cw, v);
         if (valid) {
             float o[32];
 #pragma unroll
@@ -225,7 +228,7 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
                     const float t = (v[k] - mean) * rstd * ep.g1[c0 + k] + ep.b1[c0 + k];
                     o[k] = (t - mean2) * rstd2 * ep.g2[c0 + k] + ep.b2[c0 + k];
                 }
-            shift_store(ep.out2, ep.shift, 2, y, x, c0, o, cw);
+            shift_store(ep.out2, ep.shift, 2, y, x, c0, o, cw, io);
         }
     }
 }
@@ -236,7 +239,9 @@ __device__ void epilogue_tile(const EpiParams &ep, const TileGeom &tg, int tile,
 // the row's TMEM columns, and LN2 runs its two passes over the LN1 output, written back
 // the same way.  Warp-collective (TMEM); stores are masked.
 template <int MODE, class L>
-__device__ void epilogue_ln_row(const EpiParams &ep, const TileGeom &tg, int tile, int row, int N, L &ld) {
+__device__ void epilogue_ln_row(const EpiParams &ep, const TileGeom &tg, int tile, int row, int N, L &ld,
+                                size_t io = 0) {
+    const __half *res = MODE == EPI_RESLN ? img_at(ep.res, io) : nullptr;
     float v[32];
     const long long q = (long long)tile * 128 + row;
     const int y = (int)(q / tg.pitch), x = (int)(q - (long long)y * tg.pitch);
@@ -244,7 +249,7 @@ __device__ void epilogue_ln_row(const EpiParams &ep, const TileGeom &tg, int til
     const long long tok = valid ? (long long)y * tg.conv_w + x : 0;
     float s = 0.f;
     for (int c0 = 0; c0 < N; c0 += 32) {
-        row_vals(ld, ep, N, tok, MODE == EPI_RESLN, c0, 32, v);
+        row_vals(ld, ep, res, N, tok, MODE == EPI_RESLN, c0, 32, v);
 #pragma unroll
         for (int k = 0; k < 32; k++) s += v[k];
         ld.store32(c0, v);
@@ -272,7 +277,7 @@ __device__ void epilogue_ln_row(const EpiParams &ep, const TileGeom &tg, int til
             h[k] = __float2half_rn(t);
             v[k] = t;
         }
-        if (valid) act_store(ep.out, y, x, c0, h, 32);
+        if (valid) act_store(ep.out, y, x, c0, h, 32, io);
         if (MODE == EPI_LN2) ld.store32(c0, v);
     }
     if (MODE == EPI_RESLN) return;
@@ -295,7 +300,7 @@ __device__ void epilogue_ln_row(const EpiParams &ep, const TileGeom &tg, int til
 #pragma unroll
             for (int k = 0; k < 32; k += 2)
                 shift_store2(ep.out2, ep.shift, 2, y, x, c0 + k, (v[k] - mean2) * rstd2 * ep.g2[c0 + k] + ep.b2[c0 + k],
-                             (v[k + 1] - mean2) * rstd2 * ep.g2[c0 + k + 1] + ep.b2[c0 + k + 1]);
+                             (v[k + 1] - mean2) * rstd2 * ep.g2[c0 + k + 1] + ep.b2[c0 + k + 1], io);
         }
     }
 }
@@ -304,7 +309,7 @@ __device__ void epilogue_ln_row(const EpiParams &ep, const TileGeom &tg, int til
 // `bot` (same TMEM lane, two accumulators); lanes L and L^1 hold x and x^1.
 template <class L>
 __device__ void epilogue_pool(const EpiParams &ep, const TileGeom &tg, int y2, int x, int n0, int Nsub, L &top,
-                              L &bot, int part = 0, int nparts = 1) {
+                              L &bot, int part = 0, int nparts = 1, size_t io = 0) {
     float a[32], b[32];
     const int cw = (Nsub % 32 == 0) ? 32 : 16;
     const bool writer = (x & 1) == 0 && x < tg.conv_w;
@@ -320,7 +325,7 @@ __device__ void epilogue_pool(const EpiParams &ep, const TileGeom &tg, int y2, i
                 h[k] = __float2half_rn(fmaxf(v, 0.0f));
             }
         }
-        if (writer) act_store(ep.out, y2, x >> 1, n0 + c0, h, cw);
+        if (writer) act_store(ep.out, y2, x >> 1, n0 + c0, h, cw, io);
     }
 }
 
@@ -341,7 +346,8 @@ __device__ __forceinline__ float sigmoid_fast(float v) { return __fdividef(1.0f,
 
 // The per-pixel tail of the head: div6 into the DR stem input (GC) or the u8 output (DR).
 // xin: the pixel's first 8 stem-input channels (GC: the u8 image in channels 0-2).
-__device__ __forceinline__ void head_store(const HeadParams &hp, int W, int y, int x, const float *o, const uint4 xin) {
+__device__ __forceinline__ void head_store(const HeadParams &hp, int W, int y, int x, const float *o, const uint4 xin,
+                                           size_t io) {
     const size_t pix = (size_t)y * W + x;
     if (!hp.is_dr) {
         // div6: r = clamp(x / max(I_sm, 1e-6), 0, 1) with x = u8 / 255, written as the DR stem input
@@ -360,14 +366,14 @@ __device__ __forceinline__ void head_store(const HeadParams &hp, int W, int y, i
             v[6 + c] = rh;
             v[9 + c] = rl;
             v[12 + c] = rh;
-            if (hp.r_out) hp.r_out[pix * 3 + c] = r;
-            if (hp.ism_out) hp.ism_out[pix * 3 + c] = o[c];
+            if (hp.r_out) img_at(hp.r_out, io)[pix * 3 + c] = r;
+            if (hp.ism_out) img_at(hp.ism_out, io)[pix * 3 + c] = o[c];
         }
         v[15] = __float2half_rn(0.0f);
-        act_store(hp.si_out, y, x, 0, v, kStemInC);
+        act_store(hp.si_out, y, x, 0, v, kStemInC, io);
     } else {
         if (hp.y_out)
-            for (int c = 0; c < 3; c++) hp.y_out[pix * 3 + c] = o[c];
+            for (int c = 0; c < 3; c++) img_at(hp.y_out, io)[pix * 3 + c] = o[c];
         const ImgSpec &im = hp.img;
         const int oy = y - im.ph, ox = x - im.pw;
         if (oy < 0 || ox < 0) return;
@@ -379,13 +385,13 @@ __device__ __forceinline__ void head_store(const HeadParams &hp, int W, int y, i
             q[c] = (uint8_t)f;
         }
         const int ob = im.swap ? 2 : 0;
-        uint8_t *d = hp.dst + ((size_t)oy * im.w + ox) * im.bpp;
+        uint8_t *d = img_at(hp.dst, io) + ((size_t)oy * im.w + ox) * im.bpp;
         if (im.bpp == 4) {
             uchar4 v;
             v.x = ob ? q[2] : q[0];
             v.y = q[1];
             v.z = ob ? q[0] : q[2];
-            v.w = im.src[(size_t)oy * im.stride + (size_t)ox * 4 + 3];
+            v.w = img_at(im.src, io)[(size_t)oy * im.stride + (size_t)ox * 4 + 3];
             *reinterpret_cast<uchar4 *>(d) = v;
         } else {
             d[ob] = q[0];
@@ -406,7 +412,7 @@ __device__ __forceinline__ void head_store(const HeadParams &hp, int W, int y, i
 template <int C1, class L>
 __device__ void epilogue_head_pair(const EpiParams &ep, const TileGeom &tg, int y, int x, L &ld0, L &ld1,
                                    const uint8_t *win, int wy0, int wx0, const uint8_t *seg0, const uint8_t *seg1,
-                                   int slot) {
+                                   int slot, size_t io) {
     const HeadParams &hp = ep.head;
     // the TMEM loads below are warp-collective: a warp leaves only as a whole; lanes past
     // the image edge compute on in-window data and store nothing
@@ -484,8 +490,8 @@ __device__ void epilogue_head_pair(const EpiParams &ep, const TileGeom &tg, int 
             xa = *reinterpret_cast<const uint4 *>(seg0 + (off ^ sw));
             xb = *reinterpret_cast<const uint4 *>(seg1 + (off ^ sw));
         }
-        head_store(hp, tg.conv_w, y, x, ya, xa);
-        head_store(hp, tg.conv_w, y + 1, x, yb, xb);
+        head_store(hp, tg.conv_w, y, x, ya, xa, io);
+        head_store(hp, tg.conv_w, y + 1, x, yb, xb, io);
     }
 }
 

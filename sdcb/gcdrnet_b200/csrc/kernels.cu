@@ -225,7 +225,8 @@ constexpr int kDwMaxC = 512;
 
 template <int PX>
 __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *wt,
-                                                            const float *b, const ShiftSpec s, __half *out) {
+                                                            const float *b, const ShiftSpec s, __half *out,
+                                                            long long img_bytes) {
     extern __shared__ __align__(16) float ws[];   // [9][C]
     // the weights are constant: staged before the wait on the previous kernel
     for (int i = threadIdx.x * 4; i < 9 * C; i += blockDim.x * 4)
@@ -252,7 +253,8 @@ __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in,
                 acc[p][3] = make_float2(b1.z, b1.w);
             }
         }
-        const __half *col = in + c0;
+        const size_t io = (size_t)blockIdx.y * (size_t)img_bytes;   // this block's image
+        const __half *col = img_at(in, io) + c0;
 #pragma unroll
         for (int ky = 0; ky < 3; ky++) {
             const int yy = y + ky - 1;
@@ -289,7 +291,7 @@ __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in,
         const int ga = shift_group(s, c0), gb = shift_group(s, c0 + 7);
         const int offa = ga >= 0 ? s.offs[ga] : 0, offb = gb >= 0 ? s.offs[gb] : 0;
         const int split = ga == gb ? 8 : s.ends[ga] - c0;   // channels [0, split) shift by offa, the rest offb
-        __half *rowo = out + (size_t)y * W * C + c0;
+        __half *rowo = img_at(out, io) + (size_t)y * W * C + c0;
 #pragma unroll
         for (int p = 0; p < PX; p++) {
             if (x + p >= W) break;
@@ -331,6 +333,8 @@ __device__ __forceinline__ void bilin_coords(int Y, int n, int &a0, int &a1, flo
 template <int CH>
 __global__ void __launch_bounds__(256) up_add_pad_kernel(const UpAddArgs a) {
     pdl_wait();
+    const size_t io = (size_t)blockIdx.z * (size_t)a.img_bytes;   // this block's image
+    const __half *dd = img_at(a.d, io);
     const int C = CH ? CH * 8 : a.out.C, H = a.out.H, W = a.out.W, chunks = CH ? CH : C / 8;
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     const int Y = blockIdx.y;
@@ -341,11 +345,11 @@ __global__ void __launch_bounds__(256) up_add_pad_kernel(const UpAddArgs a) {
         float dy, dx;
         bilin_coords(Y, h, ya, yb, dy);
         bilin_coords(X, w, xa, xb, dx);
-        const uint4 r00 = *reinterpret_cast<const uint4 *>(a.d + ((size_t)ya * w + xa) * C + c0);
-        const uint4 r01 = *reinterpret_cast<const uint4 *>(a.d + ((size_t)ya * w + xb) * C + c0);
-        const uint4 r10 = *reinterpret_cast<const uint4 *>(a.d + ((size_t)yb * w + xa) * C + c0);
-        const uint4 r11 = *reinterpret_cast<const uint4 *>(a.d + ((size_t)yb * w + xb) * C + c0);
-        const uint4 rs = *reinterpret_cast<const uint4 *>(act_ptr(a.skip, Y, X) + c0);
+        const uint4 r00 = *reinterpret_cast<const uint4 *>(dd + ((size_t)ya * w + xa) * C + c0);
+        const uint4 r01 = *reinterpret_cast<const uint4 *>(dd + ((size_t)ya * w + xb) * C + c0);
+        const uint4 r10 = *reinterpret_cast<const uint4 *>(dd + ((size_t)yb * w + xa) * C + c0);
+        const uint4 r11 = *reinterpret_cast<const uint4 *>(dd + ((size_t)yb * w + xb) * C + c0);
+        const uint4 rs = *reinterpret_cast<const uint4 *>(img_at(act_ptr(a.skip, Y, X), io) + c0);
         const __half2 *h00 = reinterpret_cast<const __half2 *>(&r00), *h01 = reinterpret_cast<const __half2 *>(&r01);
         const __half2 *h10 = reinterpret_cast<const __half2 *>(&r10), *h11 = reinterpret_cast<const __half2 *>(&r11);
         const __half2 *hs = reinterpret_cast<const __half2 *>(&rs);
@@ -359,7 +363,7 @@ __global__ void __launch_bounds__(256) up_add_pad_kernel(const UpAddArgs a) {
             const float2 up = __ffma2_rn(bot, wy1, __fmul2_rn(top, wy0));
             o[k] = __float22half2_rn(__fadd2_rn(make_float2(fmaxf(up.x, 0.0f), fmaxf(up.y, 0.0f)), __half22float2(hs[k])));
         }
-        act_store(a.out, Y, X, c0, reinterpret_cast<const __half *>(o), 8);
+        act_store(a.out, Y, X, c0, reinterpret_cast<const __half *>(o), 8, io);
     }
     pdl_trigger();
 }
@@ -388,16 +392,17 @@ __device__ __forceinline__ uint4 pack8h(const float *v) {
 
 // H-shift scatter of channels [c0, c0+8) of token pixel (y, x) of a LAY_PLAIN
 // tensor: one 16-byte store when the chunk lies in one channel group.
-__device__ __forceinline__ void shift_store8(const Act &a, const ShiftSpec &s, int y, int x, int c0, const float *v) {
+__device__ __forceinline__ void shift_store8(const Act &a, const ShiftSpec &s, int y, int x, int c0, const float *v,
+                                             size_t io) {
     const int g0 = shift_group(s, c0), g7 = shift_group(s, c0 + 7);
     if (g0 == g7) {
         int dy = y;
         bool z = false;
         if (g0 >= 0) dy = shift_dest(y, s.offs[g0], a.H, &z);
-        *reinterpret_cast<uint4 *>(a.p + ((size_t)dy * a.W + x) * a.C + c0) = z ? make_uint4(0, 0, 0, 0) : pack8h(v);
+        *reinterpret_cast<uint4 *>(img_at(a.p, io) + ((size_t)dy * a.W + x) * a.C + c0) = z ? make_uint4(0, 0, 0, 0) : pack8h(v);
     } else {
 #pragma unroll
-        for (int k = 0; k < 4; k++) shift_store2(a, s, 2, y, x, c0 + 2 * k, v[2 * k], v[2 * k + 1]);
+        for (int k = 0; k < 4; k++) shift_store2(a, s, 2, y, x, c0 + 2 * k, v[2 * k], v[2 * k + 1], io);
     }
 }
 
@@ -406,6 +411,8 @@ __device__ __forceinline__ void shift_store8(const Act &a, const ShiftSpec &s, i
 template <int LP, int NCH>
 __global__ void __launch_bounds__(256) up_add_tok_kernel(const UpAddArgs a) {
     pdl_wait();
+    const size_t io = (size_t)blockIdx.z * (size_t)a.img_bytes;   // this block's image
+    const __half *dd = img_at(a.d, io);
     const int C = a.out.C, H = a.out.H, W = a.out.W, nchunk = C >> 3;
     const int gid = blockIdx.x * blockDim.x + threadIdx.x;
     const int p = gid / LP, l = gid - p * LP;
@@ -417,9 +424,10 @@ __global__ void __launch_bounds__(256) up_add_tok_kernel(const UpAddArgs a) {
     float dy, dx;
     bilin_coords(Y, h, ya, yb, dy);
     bilin_coords(X, w, xa, xb, dx);
-    const __half *d00 = a.d + ((size_t)ya * w + xa) * C, *d01 = a.d + ((size_t)ya * w + xb) * C;
-    const __half *d10 = a.d + ((size_t)yb * w + xa) * C, *d11 = a.d + ((size_t)yb * w + xb) * C;
-    const __half *sk = act_ptr(a.skip, Y, X);
+    const __half *d00 = dd + ((size_t)ya * w + xa) * C, *d01 = dd + ((size_t)ya * w + xb) * C;
+    const __half *d10 = dd + ((size_t)yb * w + xa) * C, *d11 = dd + ((size_t)yb * w + xb) * C;
+    const __half *sk = img_at(act_ptr(a.skip, Y, X), io);
+    __half *outp = img_at(a.out.p, io);
     const float2 wx0 = make_float2(1.0f - dx, 1.0f - dx), wx1 = make_float2(dx, dx);
     const float2 wy0 = make_float2(1.0f - dy, 1.0f - dy), wy1 = make_float2(dy, dy);
     float v[NCH][8];
@@ -449,7 +457,7 @@ __global__ void __launch_bounds__(256) up_add_tok_kernel(const UpAddArgs a) {
                 sum += r.x + r.y;
             }
             if (valid)
-                *reinterpret_cast<uint4 *>(a.out.p + a.out.row(Y, X) * C + c0) = pack8h(v[k]);
+                *reinterpret_cast<uint4 *>(outp + a.out.row(Y, X) * C + c0) = pack8h(v[k]);
         }
     }
     const float mean = group_sum<LP>(sum) / C;
@@ -473,7 +481,7 @@ __global__ void __launch_bounds__(256) up_add_tok_kernel(const UpAddArgs a) {
             load8f(a.b + c0, bb);
 #pragma unroll
             for (int e = 0; e < 8; e++) o[e] = (v[k][e] - mean) * rstd * g[e] + bb[e];
-            shift_store8(a.h, a.shift, Y, X, c0, o);
+            shift_store8(a.h, a.shift, Y, X, c0, o, io);
         }
     }
     pdl_trigger();
@@ -501,10 +509,11 @@ __global__ void __launch_bounds__(256) ln_finalize_kernel(const LnFinalizeArgs a
             for (int e = 0; e < 8; e++) v[k][e] = 0.f;
     }
     pdl_wait();   // (the bias is constant: read before the wait on the partials' producer)
+    const size_t io = (size_t)blockIdx.z * (size_t)a.img_bytes;   // this block's image
     // (unrolled: the loads of several partials in flight at once; the sum stays in k order)
 #pragma unroll 4
     for (int ks = 0; ks < a.ksplit; ks++) {
-        const float *pk = a.partial + ((size_t)ks * T + tt) * N;
+        const float *pk = img_at(a.partial, io) + ((size_t)ks * T + tt) * N;
 #pragma unroll
         for (int k = 0; k < NCH; k++) {
             const int ch = l + LP * k;
@@ -523,7 +532,7 @@ __global__ void __launch_bounds__(256) ln_finalize_kernel(const LnFinalizeArgs a
         if (ch < nchunk) {
             if (a.res) {
                 float r[8];
-                load16h8(a.res + (size_t)tt * N + ch * 8, r);
+                load16h8(img_at(a.res, io) + (size_t)tt * N + ch * 8, r);
 #pragma unroll
                 for (int e = 0; e < 8; e++) v[k][e] += r[e];
             }
@@ -558,7 +567,7 @@ __global__ void __launch_bounds__(256) ln_finalize_kernel(const LnFinalizeArgs a
             }
             if (valid) {
                 const uint4 u = pack8h(v[k]);
-                act_store(a.out, y, x, c0, reinterpret_cast<const __half *>(&u), 8);
+                act_store(a.out, y, x, c0, reinterpret_cast<const __half *>(&u), 8, io);
             }
         }
     }
@@ -584,7 +593,7 @@ __global__ void __launch_bounds__(256) ln_finalize_kernel(const LnFinalizeArgs a
                 load8f(a.b2 + c0, bb);
 #pragma unroll
                 for (int e = 0; e < 8; e++) o[e] = (v[k][e] - mean2) * rstd2 * g[e] + bb[e];
-                shift_store8(a.out2, a.shift, y, x, c0, o);
+                shift_store8(a.out2, a.shift, y, x, c0, o, io);
             }
         }
     }
@@ -643,15 +652,17 @@ __global__ void nhwc2bgr_kernel(const float *y, int W, int ph, int pw, uint8_t *
 // two 16-byte stores (plus the reflect-border copies).
 constexpr int kStemInPx = 256;
 
-__global__ void __launch_bounds__(kStemInPx) stem_in_kernel(const ImgSpec im, Act si, int *err) {
+__global__ void __launch_bounds__(kStemInPx) stem_in_kernel(const ImgSpec im, Act si, int *err, long long img_bytes) {
     __shared__ __align__(16) uint8_t seg[kStemInPx * 4 + 32];
     pdl_wait();
-    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && err) *err = 0;   // the enhancement's first kernel
+    const size_t io = (size_t)blockIdx.z * (size_t)img_bytes;   // this block's image
+    si.p = img_at(si.p, io);
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && err) *img_at(err, io) = 0;   // the enhancement's first kernel
     const int y = blockIdx.y, x0 = blockIdx.x * kStemInPx, x = x0 + (int)threadIdx.x;
     const int sy = max(y - im.ph, 0);
     const int sx_lo = max(x0 - im.pw, 0);
     const int sx_hi = max(min(x0 + kStemInPx - 1 - im.pw, im.w - 1), sx_lo);
-    const uintptr_t rowp = reinterpret_cast<uintptr_t>(im.src) + (size_t)sy * im.stride;
+    const uintptr_t rowp = reinterpret_cast<uintptr_t>(im.src) + io + (size_t)sy * im.stride;
     const uintptr_t a_lo = (rowp + (size_t)sx_lo * im.bpp) & ~uintptr_t(15);
     const uintptr_t a_hi = rowp + (size_t)(sx_hi + 1) * im.bpp;   // exclusive
     const int nwords = (int)((a_hi - a_lo + 15) >> 4);           // <= 66
@@ -691,9 +702,11 @@ bool pdl_enabled() {
     return on;
 }
 
-int stem_in_launch(const ImgSpec &im, const Act &si, int *err, cudaStream_t st) {
+int stem_in_launch(const ImgSpec &im, const Act &si, int *err, cudaStream_t st, int nimg, long long img_bytes) {
     if (si.C != 16 || si.kind != LAY_PADREFL || im.stride != im.w * im.bpp) return -2;
-    launch_pdl(stem_in_kernel, dim3(grid_for(si.W, kStemInPx), si.H), dim3(kStemInPx), 0, st, im, si, err);
+    if (nimg < 1 || nimg > 65535 || (nimg > 1 && (img_bytes <= 0 || img_bytes % 16))) return -2;
+    launch_pdl(stem_in_kernel, dim3(grid_for(si.W, kStemInPx), si.H, nimg), dim3(kStemInPx), 0, st, im, si, err,
+               img_bytes);
     return launch_status();
 }
 
@@ -745,8 +758,9 @@ int head_launch(const HeadArgs &a, cudaStream_t st) {
 }
 
 int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *wt, const float *b, const ShiftSpec &s,
-                         __half *out, cudaStream_t st) {
+                         __half *out, cudaStream_t st, int nimg, long long img_bytes) {
     if (C % 8 || C > kDwMaxC) return -2;
+    if (nimg < 1 || nimg > 65535 || (nimg > 1 && (img_bytes <= 0 || img_bytes % 16))) return -2;
     static const int nsm = [] {
         int d = 0, n = 148;
         if (cudaGetDevice(&d) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
@@ -754,19 +768,21 @@ int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *wt,
     }();
     const int blocks2 = grid_for((long long)((W + 1) / 2) * (C / 8) * H, 128);
     const size_t smem = (size_t)9 * C * sizeof(float);
-    if (blocks2 <= 7 * nsm)
-        launch_pdl(dw_gelu_shift_kernel<2>, dim3(blocks2), dim3(128), smem, st, in, H, W, C, wt, b, s, out);
+    if ((long long)blocks2 * nimg <= 7 * nsm)
+        launch_pdl(dw_gelu_shift_kernel<2>, dim3(blocks2, nimg), dim3(128), smem, st, in, H, W, C, wt, b, s, out,
+                   img_bytes);
     else
-        launch_pdl(dw_gelu_shift_kernel<4>, dim3(grid_for((long long)((W + 3) / 4) * (C / 8) * H, 128)), dim3(128), smem,
-                   st, in, H, W, C, wt, b, s, out);
+        launch_pdl(dw_gelu_shift_kernel<4>, dim3(grid_for((long long)((W + 3) / 4) * (C / 8) * H, 128), nimg), dim3(128),
+                   smem, st, in, H, W, C, wt, b, s, out, img_bytes);
     return launch_status();
 }
 
 int up_add_launch(const UpAddArgs &a, cudaStream_t st) {
     const int C = a.out.C;
+    if (a.nimg < 1 || a.nimg > 65535 || (a.nimg > 1 && (a.img_bytes <= 0 || a.img_bytes % 16))) return -2;
     if (!a.tokens) {
         if (C % 8) return -2;
-        const dim3 grid(grid_for((long long)a.out.W * (C / 8), 256), a.out.H);
+        const dim3 grid(grid_for((long long)a.out.W * (C / 8), 256), a.out.H, a.nimg);
         switch (C) {
             case 16: launch_pdl(up_add_pad_kernel<2>, grid, dim3(256), 0, st, a); break;
             case 32: launch_pdl(up_add_pad_kernel<4>, grid, dim3(256), 0, st, a); break;
@@ -778,21 +794,24 @@ int up_add_launch(const UpAddArgs &a, cudaStream_t st) {
         const int nchunk = C / 8;
         const int LP = nchunk <= 16 ? 16 : 32;
         const long long n = (long long)a.out.H * a.out.W * LP;
-        if (LP == 16) launch_pdl(up_add_tok_kernel<16, 1>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
-        else if (nchunk <= 32) launch_pdl(up_add_tok_kernel<32, 1>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
-        else launch_pdl(up_add_tok_kernel<32, 2>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
+        const dim3 grid(grid_for(n, 256), 1, a.nimg);
+        if (LP == 16) launch_pdl(up_add_tok_kernel<16, 1>, grid, dim3(256), 0, st, a);
+        else if (nchunk <= 32) launch_pdl(up_add_tok_kernel<32, 1>, grid, dim3(256), 0, st, a);
+        else launch_pdl(up_add_tok_kernel<32, 2>, grid, dim3(256), 0, st, a);
     }
     return launch_status();
 }
 
 int ln_finalize_launch(const LnFinalizeArgs &a, cudaStream_t st) {
     if (a.N % 8 || a.N > 512 || a.ksplit < 1) return -2;
+    if (a.nimg < 1 || a.nimg > 65535 || (a.nimg > 1 && (a.img_bytes <= 0 || a.img_bytes % 16))) return -2;
     const int nchunk = a.N / 8;
     const int LP = nchunk <= 16 ? 16 : 32;
     const long long n = (long long)a.H * a.W * LP;
-    if (LP == 16) launch_pdl(ln_finalize_kernel<16, 1>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
-    else if (nchunk <= 32) launch_pdl(ln_finalize_kernel<32, 1>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
-    else launch_pdl(ln_finalize_kernel<32, 2>, dim3(grid_for(n, 256)), dim3(256), 0, st, a);
+    const dim3 grid(grid_for(n, 256), 1, a.nimg);
+    if (LP == 16) launch_pdl(ln_finalize_kernel<16, 1>, grid, dim3(256), 0, st, a);
+    else if (nchunk <= 32) launch_pdl(ln_finalize_kernel<32, 1>, grid, dim3(256), 0, st, a);
+    else launch_pdl(ln_finalize_kernel<32, 2>, grid, dim3(256), 0, st, a);
     return launch_status();
 }
 

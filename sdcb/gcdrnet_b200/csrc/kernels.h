@@ -52,7 +52,9 @@ int head_launch(const HeadArgs &a, cudaStream_t st);
 // err (may be null): the device error word, cleared by the kernel (the enhancement's first).
 // im.src: a tight device image (stride = w * bpp) with at least 16 bytes of slack past its
 // end (the kernel reads whole aligned 16-byte words).
-int stem_in_launch(const ImgSpec &im, const Act &si, int *err, cudaStream_t st);
+// Batched launches (nimg > 1): image k's source, stem input and error word lie k * img_bytes
+// past image 0's (the same holds for every batched launch below).
+int stem_in_launch(const ImgSpec &im, const Act &si, int *err, cudaStream_t st, int nimg = 1, long long img_bytes = 0);
 // CUDA error string of this thread's last failed launch of the kernels above.
 const char *last_launch_error();
 // Stem conv weights for that layout: ONNX [C1][Cin][3][3] -> [C1][9 taps][16]
@@ -64,7 +66,7 @@ void pack_stem_conv(const float *w, int c1, int cin, __half *out);
 // (gc#85-95 with ChannelShift along W).  wt is tap-major [9][C] fp32 (ONNX
 // [C][1][3][3] transposed at upload), b [C]; both 16-byte aligned.
 int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *wt, const float *b, const ShiftSpec &s,
-                         __half *out, cudaStream_t st);
+                         __half *out, cudaStream_t st, int nimg = 1, long long img_bytes = 0);
 
 // Decoder join: out = relu(bilinear2x(d)) + skip  (gc#236-240, 444-446).
 //   tokens=false: out is an Act (LAY_PADREFL) for the next decoder conv.
@@ -79,6 +81,8 @@ struct UpAddArgs {
     float eps = 1e-5f;
     Act h;                          // tokens [H][W][C]
     ShiftSpec shift;
+    int nimg = 1;                   // images per launch (d, skip, out, h at image k's offset)
+    long long img_bytes = 0;
 };
 int up_add_launch(const UpAddArgs &a, cudaStream_t st);
 
@@ -100,6 +104,8 @@ struct LnFinalizeArgs {
     float eps2 = 1e-5f;
     ShiftSpec shift;
     Act out, out2;
+    int nimg = 1;                     // images per launch (partial, res, out, out2 at image k's offset)
+    long long img_bytes = 0;
 };
 int ln_finalize_launch(const LnFinalizeArgs &a, cudaStream_t st);
 

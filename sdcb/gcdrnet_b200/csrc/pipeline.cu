@@ -179,11 +179,6 @@ Worker::~Worker() {
     if (h_dst_) cudaFreeHost(h_dst_);
     if (h_err_) cudaFreeHost(h_err_);
     if (h_errs_) cudaFreeHost(h_errs_);
-    for (int k = 0; k < kMaxBatch; k++) {
-        if (fork_[k]) cudaStreamDestroy(fork_[k]);
-        if (join_ev_[k]) cudaEventDestroy(join_ev_[k]);
-    }
-    if (fork_ev_) cudaEventDestroy(fork_ev_);
     pool_.reset();
     if (flag_ev_) cudaEventDestroy(flag_ev_);
     for (auto &e : band_ev_)
@@ -207,7 +202,6 @@ int Worker::init(std::string &err) {
     if (cudaEventCreateWithFlags(&flag_ev_, cudaEventDisableTiming) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
     for (auto &e : band_ev_)
         if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
-    if (cudaEventCreateWithFlags(&fork_ev_, cudaEventDisableTiming) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
     if (cudaMallocHost(&h_errs_, sizeof(int) * kMaxBatch) != cudaSuccess) { err = "pinned alloc"; return GCDR_ERR_OOM; }
     pool_ = std::make_unique<HostPool>(kHostBands - 1, device_);
     const char *g = std::getenv("GCDR_CUDA_GRAPH");
@@ -240,7 +234,6 @@ void Worker::stash() {
     p.debug = plan_debug_;
     p.nimg = nimg_;
     p.slices = std::move(slices_);
-    p.slice_begin = std::move(slice_begin_);
     p.arena = arena_; p.arena_bytes = arena_bytes_;
     p.gcb = gcb_; p.drb = drb_;
     p.r = r_; p.ism = ism_; p.ydbg = ydbg_;
@@ -256,7 +249,7 @@ void Worker::stash() {
     arena_ = nullptr; arena_bytes_ = 0;
     graph_ = nullptr; exec_ = nullptr;
     ops_.clear(); info_.clear();
-    slices_.clear(); slice_begin_.clear();
+    slices_.clear();
     bound_ = false;
 }
 
@@ -265,7 +258,6 @@ void Worker::restore(ShapePlan &&p) {
     plan_debug_ = p.debug;
     nimg_ = p.nimg;
     slices_ = std::move(p.slices);
-    slice_begin_ = std::move(p.slice_begin);
     arena_ = p.arena; arena_bytes_ = p.arena_bytes;
     gcb_ = p.gcb; drb_ = p.drb;
     r_ = p.r; ism_ = p.ism; ydbg_ = p.ydbg;
@@ -285,7 +277,7 @@ void Worker::release_current() {
     if (arena_) cudaFree(arena_);
     exec_ = nullptr; graph_ = nullptr; arena_ = nullptr; arena_bytes_ = 0;
     ops_.clear(); info_.clear();
-    slices_.clear(); slice_begin_.clear();
+    slices_.clear();
     launches_ = 0;
     bound_ = false;
 }
@@ -418,7 +410,8 @@ struct Split {
 //   itself, on one tile per CTA, measured several times slower than any split.)
 Split split_policy(const ConvArgs &a, int mode, int nsm) {
     Split best;
-    if (a.tg.ntiles >= nsm) return best;
+    const long long tiles = (long long)a.tg.ntiles * a.nimg;   // of every image of the launch
+    if (tiles >= nsm) return best;
     auto valid_slice = [&](int ns) {
         if (a.N % ns) return false;
         const int Ns = a.N / ns;
@@ -426,20 +419,20 @@ Split split_policy(const ConvArgs &a, int mode, int nsm) {
     };
     if (mode == EPI_PLAIN) {
         for (int ns = 1; ns <= a.N / 32; ns++)
-            if (valid_slice(ns) && (long long)a.tg.ntiles * ns <= nsm) best.nsplit = ns;
+            if (valid_slice(ns) && tiles * ns <= nsm) best.nsplit = ns;
         return best;
     }
     const int bk = tc_pick_bk(a.C);
     if (!bk) return best;
     const int kblocks = a.ntaps * (a.C / bk);
-    const double T = (double)a.tg.conv_h * a.tg.conv_w;
+    const double T = (double)a.tg.conv_h * a.tg.conv_w * a.nimg;
     double best_us = 1e30;
     for (int ns = 1; ns <= a.N / 16; ns++) {
         if (!valid_slice(ns)) continue;
         const int Ns = a.N / ns;
         for (int ks = 1; ks <= kblocks; ks++) {
             if (kblocks % ks || (ns == 1 && ks == 1)) continue;
-            const long long units = (long long)a.tg.ntiles * ns * ks;
+            const long long units = tiles * ns * ks;
             const long long waves = (units + nsm - 1) / nsm;
             const double ksteps = (double)(kblocks / ks) * (bk / 16);
             const double conv = waves * (ksteps * 250.0 * (Ns > 256 ? 1.6 : 1.0) + 1000.0 + 128.0 * Ns * 4 / 8) / 1900.0;
@@ -460,12 +453,13 @@ bool uses_partial(const ConvArgs &a, int mode, int nsm) {
     if (no_split) return false;
     // small K with enough tiles: one kernel with the LayerNorm epilogue beats split-K + finalize
     // (measured: 1x1 fc2, K = 160, 57 tiles at 1600x1152)
-    if (a.ntaps * a.C <= 192 && a.tg.ntiles >= 32) return false;
+    if (a.ntaps * a.C <= 192 && (long long)a.tg.ntiles * a.nimg >= 32) return false;
     Split s = split_policy(a, mode, nsm);
     return s.nsplit > 1 || s.ksplit > 1;
 }
 
-// fp32 floats of the split-K workspace the LayerNorm layers of one net need.
+// fp32 floats of the split-K workspace the LayerNorm layers of one net need per image (the
+// split is decided for one image, batched or not).
 size_t partial_floats(const DevNet &n, int H, int W, int nsm) {
     const int H3 = H / 8, W3 = W / 8, H4 = H / 16, W4 = W / 16, H5 = H / 32, W5 = W / 32;
     Act t3, t4;
@@ -556,21 +550,40 @@ void Worker::use_slice(int k) {
 }
 
 int Worker::build_all_ops() {
+    // image slice 0's ops with every batched launch covering all nimg_ slices; an op that is
+    // not batched (the fp32 SIMT stem / head, the error-word reset of that path) runs once
+    // per slice, in slice order, where slice 0's would run
+    batch_ = nimg_;
+    use_slice(0);
+    int rc = build_ops();
+    batch_ = 1;
+    if (rc || nimg_ == 1) return rc;
+    bool all_batched = true;
+    for (const auto &oi : info_) all_batched = all_batched && oi.batched;
+    if (all_batched) return GCDR_OK;
+    std::vector<std::vector<std::function<int(cudaStream_t)>>> per(nimg_);
+    std::vector<std::vector<OpInfo>> per_info(nimg_);
+    per[0] = std::move(ops_);
+    per_info[0] = std::move(info_);
+    for (int k = 1; k < nimg_; k++) {
+        use_slice(k);
+        if ((rc = build_ops())) return rc;
+        if (ops_.size() != per[0].size()) return fail(GCDR_ERR_DEVICE, "batch plan: op lists differ between slices");
+        per[k] = std::move(ops_);
+        per_info[k] = std::move(info_);
+    }
+    use_slice(0);
     std::vector<std::function<int(cudaStream_t)>> all;
     std::vector<OpInfo> all_info;
-    slice_begin_.clear();
     int launches = 0;
-    for (int k = 0; k < nimg_; k++) {
-        use_slice(k);
-        const int rc = build_ops();
-        if (rc) return rc;
-        slice_begin_.push_back(all.size());
-        for (auto &op : ops_) all.push_back(std::move(op));
-        for (auto &oi : info_) all_info.push_back(oi);
-        launches += launches_;
+    for (size_t i = 0; i < per[0].size(); i++) {
+        const int copies = per_info[0][i].batched ? 1 : nimg_;
+        for (int k = 0; k < copies; k++) {
+            all.push_back(std::move(per[k][i]));
+            all_info.push_back(per_info[k][i]);
+            launches++;
+        }
     }
-    slice_begin_.push_back(all.size());
-    use_slice(0);
     ops_ = std::move(all);
     info_ = std::move(all_info);
     launches_ = launches;
@@ -584,13 +597,20 @@ int Worker::build_ops() {
     const DevWeights &wt = *weights_;
     const int nsm = num_sms_;
     int *errp = d_err_;
-    auto conv_op = [this, nsm, errp](ConvArgs a, int mode, const std::string &name, double flops_override = -1,
-                                      double bytes_override = -1) {
+    // batched launches cover batch_ images, image k's buffers slice_bytes_ * k past these
+    const int nb = batch_;
+    const long long ib = nb > 1 ? (long long)slice_bytes_ : 0;
+    auto conv_op = [this, nsm, errp, nb, ib](ConvArgs a, int mode, const std::string &name, double flops_override = -1,
+                                              double bytes_override = -1) {
         a.err = errp;
         if (fill_bias_consts(a)) bias_fail_ = true;
+        // split-K and the LayerNorm path fix the order of the sums: decided for one image
+        // (a.nimg is 1 here), so that a batch plan gives every image the bytes of a single-
+        // image plan; N slices change no sum and are sized for the whole launch
         const bool partial = uses_partial(a, mode, nsm);
         int run_mode = mode;
         if (mode == EPI_PLAIN || partial) {
+            if (!partial) a.nimg = nb;
             Split sp = split_policy(a, mode, nsm);
             a.nsplit = sp.nsplit;
             if (partial) {
@@ -599,6 +619,8 @@ int Worker::build_ops() {
                 run_mode = EPI_PARTIAL;
             }
         }
+        a.nimg = nb;
+        a.img_bytes = ib;
         if (partial && (double)a.ksplit * a.tg.conv_h * a.tg.conv_w * a.N > (double)ws_floats_) {
             bias_fail_ = true;   // the workspace must bound every split: a plan error, nothing launches
             return;
@@ -615,6 +637,9 @@ int Worker::build_ops() {
                             : out_px * a.N * 2 * (mode == EPI_LN2 ? 2 : 1) + (mode == EPI_RESLN ? px * a.N * 2 : 0));
         if (flops_override >= 0) oi.flops = flops_override;
         if (bytes_override >= 0) oi.bytes = bytes_override;
+        oi.flops *= nb;
+        oi.bytes *= nb;
+        oi.batched = 1;
         info_.push_back(oi);
         ops_.push_back([a, run_mode, nsm, this](cudaStream_t st) {
             std::string e;
@@ -637,22 +662,28 @@ int Worker::build_ops() {
             f.shift = a.ep.shift;
             f.out = a.ep.out;
             f.out2 = a.ep.out2;
+            f.nimg = nb;
+            f.img_bytes = ib;
             ops_.push_back([f, this](cudaStream_t st) {
                 return ln_finalize_launch(f, st) ? fail(GCDR_ERR_DEVICE, std::string("ln_finalize launch: ") + last_launch_error()) : 0;
             });
             launches_++;
             info_.push_back(OpInfo{name + ".ln", 0,
-                                   4.0 * px * a.N * a.ksplit + 2.0 * px * a.N * (f.ln2 ? 2 : 1) + (f.res ? 2.0 * px * a.N : 0),
-                                   0});
+                                   nb * (4.0 * px * a.N * a.ksplit + 2.0 * px * a.N * (f.ln2 ? 2 : 1) + (f.res ? 2.0 * px * a.N : 0)),
+                                   0, 1});
         }
     };
     info_.clear();
     if (simt_stem_) {
         // the first kernel of the tensor-core path (stem_in) clears the device error word itself
         ops_.push_back([errp](cudaStream_t st) { return cudaMemsetAsync(errp, 0, sizeof(int), st) == cudaSuccess ? 0 : GCDR_ERR_DEVICE; });
-        info_.push_back(OpInfo{"reset_error_flag", 0, 4, 0});
+        info_.push_back(OpInfo{"reset_error_flag", 0, 4, 0, 0});
     }
-    auto simt = [this](const std::string &name, double flops, double bytes) { info_.push_back(OpInfo{name, flops, bytes, 0}); };
+    // a SIMT op's metadata: batched ops cover nb images, the others (the fp32 stem / head) one
+    auto simt = [this, nb](const std::string &name, double flops, double bytes, bool batched = true) {
+        const int k = batched ? nb : 1;
+        info_.push_back(OpInfo{name, flops * k, bytes * k, 0, batched ? 1 : 0});
+    };
 
     ImgSpec img;
     img.src = d_src_;
@@ -682,14 +713,14 @@ int Worker::build_ops() {
             sa.w = n.enc1_w; sa.b = n.enc1_b; sa.out = b.t1;
             ops_.push_back([sa, this](cudaStream_t st) { return stem_launch(sa, st) ? fail(GCDR_ERR_DEVICE, std::string("stem launch: ") + last_launch_error()) : 0; });
             launches_++;
-            simt(pre + "stem", stem_flops, stem_bytes);
+            simt(pre + "stem", stem_flops, stem_bytes, false);
         } else {
             // the stem as a tensor-core conv over the stem input (GC: built from the image here;
             // DR: written by the GC head)
             if (!which) {
                 const Act si = si_gc_;
-                ops_.push_back([img, si, errp, this](cudaStream_t st) {
-                    return stem_in_launch(img, si, errp, st) ? fail(GCDR_ERR_DEVICE, std::string("stem input launch: ") + last_launch_error()) : 0;
+                ops_.push_back([img, si, errp, nb, ib, this](cudaStream_t st) {
+                    return stem_in_launch(img, si, errp, st, nb, ib) ? fail(GCDR_ERR_DEVICE, std::string("stem input launch: ") + last_launch_error()) : 0;
                 });
                 launches_++;
                 simt(pre + "stem_in", 0, (double)h_ * w_ * bpp_ + (double)(H_ + 2) * (W_ + 2) * kStemInC * 2);
@@ -710,7 +741,7 @@ int Worker::build_ops() {
             ShiftSpec sb = bk.sb;
             int C = bk.C;
             ops_.push_back([=](cudaStream_t st) {
-                return dw_gelu_shift_launch(f1, H, W, C, dw, db, sb, f2, st) ? fail(GCDR_ERR_DEVICE, std::string("dw launch: ") + last_launch_error()) : 0;
+                return dw_gelu_shift_launch(f1, H, W, C, dw, db, sb, f2, st, nb, ib) ? fail(GCDR_ERR_DEVICE, std::string("dw launch: ") + last_launch_error()) : 0;
             });
             launches_++;
             simt(bn + ".dw_gelu_shift", 2.0 * 9 * H * W * C, 4.0 * H * W * C);
@@ -752,6 +783,8 @@ int Worker::build_ops() {
             u.g = bk.n2_g; u.b = bk.n2_b; u.eps = bk.n2_eps;
             u.h = plain(b.hs, H, W, C);
             u.shift = bk.sa;
+            u.nimg = nb;
+            u.img_bytes = ib;
             ops_.push_back([u, this](cudaStream_t st) { return up_add_launch(u, st) ? fail(GCDR_ERR_DEVICE, std::string("up_add launch: ") + last_launch_error()) : 0; });
             launches_++;
             simt(pre + "join_ln" + std::to_string(H), 0, 2.0 * (H / 2) * (W / 2) * C + 6.0 * H * W * C);
@@ -761,6 +794,8 @@ int Worker::build_ops() {
             u.d = b.dconv;
             u.skip = skip;
             u.out = out;
+            u.nimg = nb;
+            u.img_bytes = ib;
             ops_.push_back([u, this](cudaStream_t st) { return up_add_launch(u, st) ? fail(GCDR_ERR_DEVICE, std::string("up_add launch: ") + last_launch_error()) : 0; });
             launches_++;
             simt(pre + "join" + std::to_string(out.H), 0, 2.0 * (out.H / 2) * (out.W / 2) * out.C + 4.0 * out.H * out.W * out.C);
@@ -796,7 +831,7 @@ int Worker::build_ops() {
             }
             ops_.push_back([ha, this](cudaStream_t st) { return head_launch(ha, st) ? fail(GCDR_ERR_DEVICE, std::string("head launch: ") + last_launch_error()) : 0; });
             launches_++;
-            simt(pre + "head", head_flops, head_bytes);
+            simt(pre + "head", head_flops, head_bytes, false);
         } else {
             ConvArgs a = conv_s1(which ? si_dr_ : si_gc_, n.stem_w16, n.enc1_b, n.c1, false);
             HeadParams &hp = a.ep.head;
@@ -858,32 +893,9 @@ int Worker::capture() {
     if (exec_) { cudaGraphExecDestroy(exec_); exec_ = nullptr; }
     if (graph_) { cudaGraphDestroy(graph_); graph_ = nullptr; }
     if (!use_graph_) return GCDR_OK;
-    for (int k = 1; k < nimg_; k++) {   // batch plans: one capture branch (stream) per image
-        if (!fork_[k] && cudaStreamCreateWithFlags(&fork_[k], cudaStreamNonBlocking) != cudaSuccess)
-            return fail(GCDR_ERR_DEVICE, "stream");
-        if (!join_ev_[k] && cudaEventCreateWithFlags(&join_ev_[k], cudaEventDisableTiming) != cudaSuccess)
-            return fail(GCDR_ERR_DEVICE, "event");
-    }
     if (cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
         return fail(GCDR_ERR_DEVICE, "graph capture begin failed");
-    int rc = GCDR_OK;
-    if (nimg_ == 1) {
-        rc = run_ops(stream_);
-    } else {
-        // image k's ops on branch k (image 0 on the capturing stream), forked from and joined
-        // back into it: one graph whose branches run concurrently
-        cudaError_t ce = cudaEventRecord(fork_ev_, stream_);
-        for (int k = 1; k < nimg_ && ce == cudaSuccess; k++) ce = cudaStreamWaitEvent(fork_[k], fork_ev_, 0);
-        for (int k = 0; k < nimg_ && !rc && ce == cudaSuccess; k++) {
-            cudaStream_t bs = k ? fork_[k] : stream_;
-            for (size_t i = slice_begin_[k]; i < slice_begin_[k + 1] && !rc; i++) rc = ops_[i](bs);
-        }
-        for (int k = 1; k < nimg_ && !rc && ce == cudaSuccess; k++) {
-            ce = cudaEventRecord(join_ev_[k], fork_[k]);
-            if (ce == cudaSuccess) ce = cudaStreamWaitEvent(stream_, join_ev_[k], 0);
-        }
-        if (!rc && ce != cudaSuccess) rc = fail(GCDR_ERR_DEVICE, std::string("batch capture: ") + cudaGetErrorString(ce));
-    }
+    const int rc = run_ops(stream_);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(stream_, &g);
     if (rc) { if (g) cudaGraphDestroy(g); return rc; }

@@ -67,6 +67,7 @@ struct OpInfo {
     double flops = 0;    // algorithmic FLOPs of one launch
     double bytes = 0;    // algorithmic HBM bytes of one launch (each tensor read/written once)
     int tensor = 0;      // 1: tcgen05 kernel
+    int batched = 0;     // 1: one launch covers every image of a batch plan (flops, bytes: all of them)
 };
 
 // Everything that depends on the bound shape (width, height, pixel format, debug mode): the
@@ -83,9 +84,8 @@ struct ImageSlice {
 struct ShapePlan {
     int w = 0, h = 0, fmt = -1, H = 0, W = 0, ph = 0, pw = 0, bpp = 3;
     bool debug = false;
-    int nimg = 1;                       // images per launch (a batch plan: one graph branch each)
+    int nimg = 1;                       // images per launch (a batch plan: each kernel covers them all)
     std::vector<ImageSlice> slices;
-    std::vector<size_t> slice_begin;    // first op of each image's branch
     uint8_t *arena = nullptr;
     size_t arena_bytes = 0;
     NetBufs gcb, drb;
@@ -110,9 +110,10 @@ public:
     int init(std::string &err);
     int enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8_t *dst, int dst_stride, int fmt);
     int enhance_device(const uint8_t *d_src, int w, int h, uint8_t *d_dst, int fmt, cudaStream_t st);
-    // n same-shape images in one CUDA-graph launch: a batch plan holds n image slices and its
-    // graph n concurrent branches (one per image).  Host buffers (staged, or by DMA when page-
-    // locked); dst[k] may alias src[k] at equal strides.
+    // n same-shape images in one CUDA-graph launch: a batch plan holds n image slices (each
+    // image's buffers at the same offset in its slice) and each of its kernels covers all n
+    // images, one launch per layer.  Host buffers (staged, or by DMA when page-locked); dst[k]
+    // may alias src[k] at equal strides.
     int enhance_host_batch(const uint8_t *const *src, int n, int w, int h, int src_stride, uint8_t *const *dst,
                            int dst_stride, int fmt);
     // The same with device-resident tight images, asynchronous on `st` (or the worker's stream).
@@ -144,7 +145,7 @@ public:
 private:
     int bind(int w, int h, int fmt, int nimg = 1);
     void use_slice(int k);          // points the buffer members at image slice k of the arena
-    int build_all_ops();            // build_ops for every image slice, concatenated
+    int build_all_ops();            // the plan's ops: batched launches, per-slice ops for the rest
     void stash();                   // current plan -> cache_
     void restore(ShapePlan &&p);    // cache entry -> current plan
     void release_current();
@@ -191,12 +192,10 @@ private:
     int launches_ = 0;
     bool plan_debug_ = false;       // debug mode the current plan was built in
     int nimg_ = 1;                  // images per launch of the current plan
+    int batch_ = 1;                 // images the batched ops of a build_ops call cover
     std::vector<ImageSlice> slices_;
-    std::vector<size_t> slice_begin_;
     std::vector<std::pair<void **, size_t>> layout_;   // buffer member -> offset in a slice
     size_t slice_bytes_ = 0;
-    cudaStream_t fork_[kMaxBatch] = {};                // capture branches of a batch plan
-    cudaEvent_t fork_ev_ = nullptr, join_ev_[kMaxBatch] = {};
     int *h_errs_ = nullptr;                            // pinned: one error word per image slice
     std::vector<ShapePlan> cache_;  // plans not bound right now
     uint64_t tick_ = 0;

@@ -72,6 +72,23 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, int c3,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// An activation box (channel x, row) of image `img`: a 3-D map in batched launches, 2-D
+// for one image (the rank the map was encoded with).
+__device__ __forceinline__ void tma_load_act(void *dst, const CUtensorMap *map, int x, int row, int img, bool batched,
+                                             uint64_t *bar) {
+    if (batched) tma_load_3d(dst, map, x, row, img, bar);
+    else tma_load_2d(dst, map, x, row, bar);
+}
+
 // UMMA shared-memory descriptor, K-major, swizzled (sm_100 format: start>>4 at
 // [0,14), LBO>>4 at [16,30) (unused for swizzled K-major: 1), SBO>>4 at
 // [32,46), version 1 at [46,48), layout at [61,64): 2 = 128B, 4 = 64B, 6 = 32B).

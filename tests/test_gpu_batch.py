@@ -1,8 +1,8 @@
 """Batched images per launch: n same-shape images in one CUDA-graph launch
-(gcdr_cuda_enhance_batch / _batch_device) give the same bytes as n single
-enhancements, in every pixel format, strided and in place.  The reference does
-not batch (README.md:182); the per-image results are the contract it defines
-(GcdrEnhancer.cs:181-271)."""
+(gcdr_cuda_enhance_batch / _batch_device), each kernel of the graph covering all
+n images, give the same bytes as n single enhancements, in every pixel format,
+strided and in place.  The reference does not batch (README.md:182); the
+per-image results are the contract it defines (GcdrEnhancer.cs:181-271)."""
 import numpy as np
 import pytest
 
@@ -23,7 +23,8 @@ def _docs(n, w, h, fmt, stride, seed0=40):
     return out
 
 
-@pytest.mark.parametrize("n,w,h,fmt,pad", [(3, 217, 150, 0, 0), (4, 160, 96, 2, 64), (2, 301, 203, 3, 5)])
+@pytest.mark.parametrize("n,w,h,fmt,pad", [(3, 217, 150, 0, 0), (4, 160, 96, 2, 64), (2, 301, 203, 3, 5),
+                                           (5, 45, 37, 1, 3), (16, 64, 64, 0, 0)])
 def test_batch_matches_single_images(n, w, h, fmt, pad):
     from sdcb.gcdrnet_b200 import CudaWorker
     bpp = 4 if fmt >= 2 else 3
@@ -40,6 +41,11 @@ def test_batch_matches_single_images(n, w, h, fmt, pad):
         for k in range(n):
             assert np.array_equal(dsts[k], want[k]), f"image {k} of the batch"
         caps = wk.plan_stats[0]
+        # one launch per layer for the whole batch: as many kernels as one image's graph
+        batch_launches = wk.launch_count
+        wk.enhance(srcs[0], w, h, stride, np.empty_like(srcs[0]), stride, fmt)
+        single_launches = wk.launch_count
+        assert batch_launches == single_launches, (batch_launches, single_launches)
         # in place, a second time: the batch plan is cached (no capture)
         io = [s.copy() for s in srcs]
         wk.enhance_batch(io, w, h, stride, io, stride, fmt)
@@ -66,6 +72,23 @@ def test_batch_device_matches_single():
         assert wk.plan_stats == (2, 2), "a single-image plan and a batch plan"
     for k in range(n):
         assert torch.equal(d_one[k], d_bat[k]), f"image {k}"
+
+
+def test_batch_full_size_matches_single():
+    """Two 1600x1152 documents in one batched graph (the shapes of the throughput workload)."""
+    from sdcb.gcdrnet_b200 import CudaWorker
+    n, w, h = 2, 1600, 1152
+    srcs = _docs(n, w, h, 0, w * 3, seed0=90)
+    with CudaWorker.from_files(G.GC_PATH, G.DR_PATH) as wk:
+        want = []
+        for s in srcs:
+            d = np.empty_like(s)
+            wk.enhance(s, w, h, w * 3, d, w * 3, 0)
+            want.append(d)
+        dsts = [np.empty_like(s) for s in srcs]
+        wk.enhance_batch(srcs, w, h, w * 3, dsts, w * 3, 0)
+    for k in range(n):
+        assert np.array_equal(dsts[k], want[k]), f"image {k}"
 
 
 def test_batch_rejects_bad_sizes():
