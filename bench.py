@@ -1,26 +1,30 @@
 #!/usr/bin/env python
 """Benchmark: 1600x1152 Bgr24 document enhancement (GC-Net -> div6 -> DR-Net).
 
-One step = STREAMS synthetic 1600x1152 documents (the seeded document
+One step = STREAMS x BATCH synthetic 1600x1152 documents (the seeded document
 generator: paper level, smooth shading, dark strokes, noise) enhanced by each
-GPU at once, one per worker and CUDA stream, as a server keeps several images
-in flight (per-image data parallelism, no
-inter-GPU traffic: scaling "weak").  Prints ONE JSON line on rank 0:
+GPU at once: STREAMS workers on concurrent CUDA streams, each running one
+batched launch of BATCH images (every kernel of a batch plan covers all of
+its images), as a server keeps several images in flight (per-image data
+parallelism, no inter-GPU traffic: scaling "weak").  Prints ONE JSON line on
+rank 0:
 
   value     images/s over all ranks, inputs resident in HBM, per-step CUDA
             events on the stream the workers' streams fork from and join
             back into, with an L2 flush (256 MB write) between steps, max over
-            ranks; the same loop with one image per step (one stream) is
-            reported beside it as single_stream;
+            ranks; the same loop with one image per step (one stream, one
+            single-image launch) is reported beside it as single_stream;
   e2e       the same metric through the public API, config c3: C3_IMAGES
             documents (each enqueued C3_PASSES times) drained from one shared
             host queue (sdcb/gcdrnet_b200/dp.py) by every GPU process, each
-            with E2E_THREADS threads calling GcdrEnhancer.enhance on host
-            buffers (two shared, page-locked host pools: H2D, graph, D2H per
-            image), host monotonic clock from the common start to the last
-            rank's finish; plus the single-thread milliseconds per image (the
-            API's latency, pageable and page-locked buffers);
-  batched_launches  several images per CUDA-graph launch (batch plans);
+            with E2E_THREADS threads calling GcdrEnhancer.enhance_batch with
+            up to E2E_BATCH documents on host buffers (two shared, page-locked
+            host pools: H2D, graph, D2H per image), host monotonic clock from
+            the common start to the last rank's finish; plus the single-thread
+            milliseconds per image of GcdrEnhancer.enhance (the API's latency,
+            pageable and page-locked buffers);
+  batched_launches  images per launch swept on one worker (1600x1152: 1, 4,
+            16; 640x480: 1 and 8);
   roofline  of the dominant kernel from a live per-op profile (CUDA events),
             against MEASURED_PEAKS.json;
   cpu_baseline  the CPU oracle (C restatement of the reference's CPU path) on
@@ -48,22 +52,40 @@ GC = os.path.join(MODELS, "gcdrnet_gcnet_sim.onnx")
 DR = os.path.join(MODELS, "gcdrnet_drnet_sim.onnx")
 METRIC = "1600x1152 images/sec"
 W_IMG, H_IMG = 1600, 1152
-STREAMS = 4       # images in flight per GPU and step: one worker (graph, arena) and stream each
-WORKLOAD = (f"enhance 1600x1152 Bgr24 synthetic documents (seeded paper/shading/strokes/noise generator), {STREAMS} images per GPU "
-            "per step on concurrent worker streams")
+STREAMS = 2       # workers (graph, arena, stream) per GPU, each with one batched launch per step
+BATCH = 8         # images per launch (a batch plan: every kernel covers all of them)
+WORKLOAD = (f"enhance 1600x1152 Bgr24 synthetic documents (seeded paper/shading/strokes/noise generator), "
+            f"{STREAMS * BATCH} images per GPU per step: {STREAMS} workers on concurrent streams, {BATCH} images "
+            "per launch")
 
 
 TRAFFIC_TABLE = os.path.join(ROOT, "profiles", "ncu_kernels_1600x1152.md")
-E2E_THREADS = 4   # concurrent GcdrEnhancer.enhance callers per GPU process in the end-to-end measurement
+# the batch plan's launches (BATCH images each), when captured
+TRAFFIC_TABLE_BATCH = os.path.join(ROOT, "profiles", f"ncu_top_kernels_1600x1152_batch{BATCH}.md")
+
+
+def launch_traffic(op: str):
+    """DRAM bytes of one batched launch of `op` and where they come from: the batch plan's
+    own ncu rows, else the one-image row times BATCH (each image's tensors are separate,
+    so the traffic grows with the images)."""
+    t = ncu_traffic(op, TRAFFIC_TABLE_BATCH)
+    if t is not None:
+        return t, os.path.relpath(TRAFFIC_TABLE_BATCH, ROOT)
+    t = ncu_traffic(op, TRAFFIC_TABLE)
+    if t is not None:
+        return t * BATCH, f"{os.path.relpath(TRAFFIC_TABLE, ROOT)} (one image) x {BATCH}"
+    return None, None
+E2E_THREADS = 4   # concurrent GcdrEnhancer.enhance_batch callers per GPU process in the end-to-end measurement
+E2E_BATCH = 4     # documents per call (fewer at the end of the queue)
 C3_IMAGES = 512   # the end-to-end workload: documents drained from the shared host queue,
 C3_PASSES = 3     # every document enqueued this many times (the timed drain lasts long enough at 8 GPUs)
 
 
-def ncu_traffic(op: str):
-    """DRAM bytes (read + write) of one launch of `op` from the committed ncu summary
+def ncu_traffic(op: str, table: str = None):
+    """DRAM bytes (read + write) of one launch of `op` from a committed ncu summary
     (a table row `| op | kernel | read MB | write MB | ... |`), or None."""
     try:
-        with open(TRAFFIC_TABLE) as fh:
+        with open(table or TRAFFIC_TABLE) as fh:
             for line in fh:
                 cells = [c.strip() for c in line.strip().strip("|").split("|")]
                 if len(cells) >= 4 and cells[0] == op:
@@ -376,7 +398,7 @@ def main():
     bpp = 3
     nbytes = W_IMG * H_IMG * bpp
     d_src = [torch.from_numpy(im.reshape(-1)).to(dev) for im in imgs]
-    d_dst = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(STREAMS)]
+    d_dst = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(STREAMS * BATCH)]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     main = torch.cuda.Stream(dev)   # a real stream handle (the legacy default stream is 0)
     torch.cuda.set_stream(main)
@@ -384,33 +406,39 @@ def main():
     workers = [CudaWorker.from_files(GC, DR, device=local) for _ in range(STREAMS)]
     worker = workers[0]
 
-    def step(i: int, nw: int):
-        # the step's nw images, one per worker stream, forked from and joined back into `main`
+    def step(i: int, nw: int, nb: int):
+        # the step's nw * nb images: one launch of nb images per worker stream (nb = 1: the
+        # single-image plan), forked from and joined back into `main`
         fork = torch.cuda.Event()
         fork.record(main)
         for k in range(nw):
             s = wstreams[k]
             s.wait_event(fork)
-            workers[k].enhance_device(d_src[(i * nw + k) % n_img].data_ptr(), W_IMG, H_IMG, d_dst[k].data_ptr(), 0,
-                                      s.cuda_stream)
+            first = (i * nw + k) * nb
+            srcs = [d_src[(first + j) % n_img].data_ptr() for j in range(nb)]
+            dsts = [d_dst[k * nb + j].data_ptr() for j in range(nb)]
+            if nb == 1:
+                workers[k].enhance_device(srcs[0], W_IMG, H_IMG, dsts[0], 0, s.cuda_stream)
+            else:
+                workers[k].enhance_batch_device(srcs, W_IMG, H_IMG, dsts, 0, s.cuda_stream)
             done = torch.cuda.Event()
             done.record(s)
             main.wait_event(done)
 
-    def timed(nw: int):
+    def timed(nw: int, nb: int):
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
         for i in range(args.steps):
             flush.zero_()
             ev[i][0].record(main)
-            step(i, nw)
+            step(i, nw, nb)
             ev[i][1].record(main)
         torch.cuda.synchronize(dev)
         return sum(a.elapsed_time(b) for a, b in ev)
 
-    for i in range(args.warmup):   # every worker's graph is captured here
-        step(i, STREAMS)
+    for i in range(args.warmup):   # every worker's batch plan is planned and captured here
+        step(i, STREAMS, BATCH)
     torch.cuda.synchronize(dev)
-    launches = worker.launch_count
+    launches = worker.launch_count   # kernels of one batched launch (the graph of BATCH images)
 
     barrier()
     torch.cuda.synchronize(dev)
@@ -419,17 +447,19 @@ def main():
     except Exception:
         uuid = None
     with ClockSampler(physical_index(local), uuid) as clk:
-        total_ms = timed(STREAMS)
+        total_ms = timed(STREAMS, BATCH)
     barrier()
     total_ms = max_over_ranks(total_ms, dist)
-    value = whole_job_rate(world, args.steps * STREAMS, total_ms / 1000.0)
+    value = whole_job_rate(world, args.steps * STREAMS * BATCH, total_ms / 1000.0)
     clocks = clk.summary()
     barrier()
-    single_ms = max_over_ranks(timed(1), dist)
+    for i in range(3):
+        step(i, 1, 1)               # the single-image plan (captured here)
+    single_ms = max_over_ranks(timed(1, 1), dist)
     single_value = whole_job_rate(world, args.steps, single_ms / 1000.0)
 
-    # batched launches (several images per CUDA-graph launch, one worker): the four 1600x1152
-    # documents, and eight 640x480 ones against one at a time (small images leave most SMs idle)
+    # images per launch on one worker: 1600x1152 one at a time, 4 and 16 per launch, and eight
+    # 640x480 documents one at a time against 8 per launch (small images leave most SMs idle)
     def timed_batch(wk, srcs, dsts, w, h, per_launch):
         for _ in range(2):
             for j in range(0, len(srcs), per_launch):
@@ -447,9 +477,10 @@ def main():
             ms += a.elapsed_time(b)
         return max_over_ranks(ms, dist)
 
-    bw = workers[1]   # (workers[0] stays bound to the single-image plan the per-op profile below uses)
-    nb = min(len(d_src), len(d_dst))
-    big_ms = timed_batch(bw, [t.data_ptr() for t in d_src[:nb]], [t.data_ptr() for t in d_dst[:nb]], W_IMG, H_IMG, nb)
+    bw = workers[1]
+    big_src = [d_src[k % n_img].data_ptr() for k in range(16)]
+    big_dst = [d_dst[k % len(d_dst)].data_ptr() for k in range(16)]
+    big_ms = {nb: timed_batch(bw, big_src[:nb], big_dst[:nb], W_IMG, H_IMG, nb) for nb in (1, 4, 16)}
     sw, sh_ = 640, 480
     small = [torch.from_numpy(synth.document(sw, sh_, seed=900 + k).reshape(-1)).to(dev) for k in range(8)]
     small_out = [torch.empty_like(t) for t in small]
@@ -457,7 +488,7 @@ def main():
     small_one_ms = timed_batch(bw, sp, so, sw, sh_, 1)
     small_bat_ms = timed_batch(bw, sp, so, sw, sh_, 8)
     batching = {
-        f"1600x1152_{nb}_per_launch": whole_job_rate(world, args.steps * nb, big_ms / 1000.0),
+        **{f"1600x1152_{nb}_per_launch": whole_job_rate(world, args.steps * nb, ms / 1000.0) for nb, ms in big_ms.items()},
         "640x480_one_per_launch": whole_job_rate(world, args.steps * 8, small_one_ms / 1000.0),
         "640x480_8_per_launch": whole_job_rate(world, args.steps * 8, small_bat_ms / 1000.0),
         "unit": "images/s", "note": "inputs in HBM, one worker, CUDA events, L2 flushed between steps",
@@ -465,16 +496,18 @@ def main():
 
     # end to end through the public API (host buffers), the c3 workload: C3_IMAGES documents
     # drained from one shared host queue by every rank (one process per GPU), each rank with
-    # E2E_THREADS host threads calling GcdrEnhancer.enhance on one shared enhancer (its worker
-    # pool rents each caller a worker: one image's host copies overlap another's kernels);
-    # results go back into a shared host pool.  Wall clock from the common start (a barrier)
-    # to the last rank's finish, on the host's monotonic clock (one clock for all ranks).
+    # E2E_THREADS host threads calling GcdrEnhancer.enhance_batch with up to E2E_BATCH documents
+    # on one shared enhancer (its worker pool rents each caller a worker: one batch's host
+    # copies overlap another's kernels); results go back into a shared host pool.  Wall clock
+    # from the common start (a barrier) to the last rank's finish, on the host's monotonic
+    # clock (one clock for all ranks).
     enh = GcdrEnhancer.from_files(GC, DR, device=local)
-    host_dst = [np.empty(nbytes, np.uint8) for _ in range(E2E_THREADS)]
+    host_dst = [[np.empty(nbytes, np.uint8) for _ in range(E2E_BATCH)] for _ in range(E2E_THREADS)]
 
     def warm(k: int):
-        for i in range(2):
-            enh.enhance(imgs[i % n_img], W_IMG, H_IMG, W_IMG * 3, host_dst[k], W_IMG * 3, 0)
+        # every caller's worker plans (and captures) the batch sizes the drain uses
+        for n in range(E2E_BATCH, 0, -1):
+            enh.enhance_batch(imgs[:1] * n, W_IMG, H_IMG, W_IMG * 3, host_dst[k][:n], W_IMG * 3, 0)
 
     th = [threading.Thread(target=warm, args=(k,)) for k in range(E2E_THREADS)]
     for t in th:
@@ -482,9 +515,14 @@ def main():
     for t in th:
         t.join()
 
-    def work(job: int):
+    def work_one(job: int):
         i = job % C3_IMAGES
         enh.enhance(pool_in.image(i), W_IMG, H_IMG, W_IMG * 3, pool_out.image(i), W_IMG * 3, 0)
+
+    def work(jobs: list):
+        ids = [j % C3_IMAGES for j in jobs]
+        enh.enhance_batch([pool_in.image(i) for i in ids], W_IMG, H_IMG, W_IMG * 3,
+                          [pool_out.image(i) for i in ids], W_IMG * 3, 0)
 
     # page-lock both pools (the enhancer then moves every image by DMA, with no staging copy);
     # left pageable when the host refuses
@@ -507,7 +545,7 @@ def main():
     barrier()
     torch.cuda.synchronize(dev)
     t0 = time.monotonic()
-    did = dp.drain(queue, work, E2E_THREADS)
+    did = dp.drain(queue, work, E2E_THREADS, batch=E2E_BATCH)
     t1 = time.monotonic()
     barrier()
     e2e_s = max_over_ranks(t1, dist) - min_over_ranks(t0, dist)
@@ -521,14 +559,14 @@ def main():
     if len(pinned_pools) == 2:
         t0 = time.perf_counter()
         for i in range(10):
-            work(i)
+            work_one(i)
         pinned_single_ms = (time.perf_counter() - t0) * 100.0
     for p in pinned_pools:
         unregister_host(p)
     # the same calls from one thread: the single-image latency of the API
     t0 = time.perf_counter()
     for i in range(min(args.steps, 10)):
-        enh.enhance(imgs[i % n_img], W_IMG, H_IMG, W_IMG * 3, host_dst[0], W_IMG * 3, 0)
+        enh.enhance(imgs[i % n_img], W_IMG, H_IMG, W_IMG * 3, host_dst[0][0], W_IMG * 3, 0)
     e2e_single_ms = (time.perf_counter() - t0) * 1000.0 / min(args.steps, 10)
 
     c3_check = None
@@ -542,7 +580,10 @@ def main():
             same += int(np.array_equal(ref, pool_out.image(i)))
         c3_check = {"images_checked": ids, "identical_to_a_direct_call": same == len(ids)}
 
-    # live per-op profile -> dominant kernel roofline
+    # live per-op profile of the timed region's launches (worker 0's batch plan: every op
+    # covers BATCH images) -> dominant kernel roofline
+    step(0, STREAMS, BATCH)
+    torch.cuda.synchronize(dev)
     prof = worker.profile(reps=3)
     if os.environ.get("GCDR_BENCH_PROFILE"):
         for p in prof:
@@ -563,6 +604,7 @@ def main():
     total_prof_ms = sum(p[1] for p in kern)
     tc_ms = sum(p[1] for p in kern if p[4])
     tc_flops = sum(p[2] for p in kern if p[4])
+    traffic, traffic_src = launch_traffic(name)
 
     cpu = None
     parity = None
@@ -581,17 +623,18 @@ def main():
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "images_per_step": STREAMS * world,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "images_per_step": STREAMS * BATCH * world,
             "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": WORKLOAD, "image_hw": [H_IMG, W_IMG],
                        "parallelism": f"dp{world} (independent images, no collective)",
-                       "streams_per_gpu": STREAMS,
+                       "streams_per_gpu": STREAMS, "images_per_launch": BATCH,
                        "l2": "256 MB flush between timed steps (outside the events)",
                        "precision": "fp16 tensor-core layers (fp32 accumulate), fp32 stem/head/div6"},
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": nbytes,
                     "d2h_bytes_per_step": nbytes, "step": "one image",
-                    "api": "GcdrEnhancer.enhance (host buffers: shared host pool in, shared host pool out)",
+                    "api": f"GcdrEnhancer.enhance_batch, up to {E2E_BATCH} documents per call (host buffers: "
+                           "shared host pool in, shared host pool out)",
                     "workload": f"{C3_IMAGES} 1600x1152 Bgr24 documents (seeds 0-{C3_IMAGES - 1}), each enqueued "
                                 f"{C3_PASSES} times, drained from one shared host queue by {world} GPU process(es), "
                                 f"{E2E_THREADS} calling threads each",
@@ -603,8 +646,8 @@ def main():
                     "host_threads": E2E_THREADS, "single_thread_ms_per_image": e2e_single_ms,
                     "single_thread_ms_per_image_page_locked": pinned_single_ms},
             "roofline": {"kernel": name, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                         "frac": achieved / peak, "traffic": ncu_traffic(name),
-                         "traffic_source": os.path.relpath(TRAFFIC_TABLE, ROOT), "peak_source": peak_src,
+                         "frac": achieved / peak, "images_per_launch": BATCH, "traffic": traffic,
+                         "traffic_source": traffic_src, "peak_source": peak_src,
                          "algorithmic_bytes": kbytes, "algorithmic_flops": kflops, "launch_ms": kms},
             "tensor_core": {"ms": tc_ms, "tflops": tc_flops / (tc_ms * 1e-3) / 1e12 if tc_ms else None,
                             "frac_of_peak": (tc_flops / (tc_ms * 1e-3) / 1e12) / tflops if tc_ms else None,

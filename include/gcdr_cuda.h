@@ -122,13 +122,15 @@ GCDR_API int gcdr_cuda_enhance_device(gcdr_cuda *w, const uint8_t *d_src, int wi
                                       uint8_t *d_dst, int pixel_format, void *stream);
 /* Batched images per launch: n (1..16) images of one shape and format in ONE
  * CUDA-graph launch.  The worker's batch plan for (width, height, format, n)
- * holds n image slices in its arena and its graph n concurrent branches, one
- * per image: the low-resolution layers of one image occupy only part of the
- * GPU, n branches fill it.  Host buffers as gcdr_cuda_enhance (dst[k] may
- * alias src[k] at equal strides; page-locked sources are copied by DMA
- * directly); the _device form takes tight device images and is asynchronous
- * on `stream`.  No counterpart in the reference: its README lists batching as
- * not covered (README.md:182). */
+ * holds n image slices in its arena (each image's buffers at the same offset
+ * of its slice) and every kernel of its graph covers all n images, one launch
+ * per layer: the low-resolution layers of one image occupy only part of the
+ * GPU, n images fill it.  Each image gets the bytes of a single-image enhance
+ * (the summation order of every layer is the one-image plan's).  Host buffers
+ * as gcdr_cuda_enhance (dst[k] may alias src[k] at equal strides; page-locked
+ * sources are copied by DMA directly); the _device form takes tight device
+ * images and is asynchronous on `stream`.  No counterpart in the reference:
+ * its README lists batching as not covered (README.md:182). */
 GCDR_API int gcdr_cuda_enhance_batch(gcdr_cuda *w, const uint8_t *const *src, int n, int width, int height,
                                      int src_stride, uint8_t *const *dst, int dst_stride, int pixel_format);
 GCDR_API int gcdr_cuda_enhance_batch_device(gcdr_cuda *w, const uint8_t *const *d_src, int n, int width,
@@ -184,6 +186,15 @@ GCDR_API int gcdr_enhancer_enhance(gcdr_enhancer *e, const uint8_t *src, size_t 
                                    int width, int height, int src_stride,
                                    uint8_t *dst, size_t dst_len, int dst_stride,
                                    int pixel_format, char *err, size_t err_cap);
+/* n (1..16) images of one shape and format through one pooled worker's batch
+ * plan (gcdr_cuda_enhance_batch): each image is validated as by
+ * gcdr_enhancer_enhance (src_len[k], dst_len[k] its buffer lengths) and gets the
+ * bytes a single enhance gives it.  Thread-safe; dst[k] may alias src[k] at
+ * equal strides.  No counterpart in the reference (README.md:182). */
+GCDR_API int gcdr_enhancer_enhance_batch(gcdr_enhancer *e, const uint8_t *const *src, const size_t *src_len, int n,
+                                         int width, int height, int src_stride, uint8_t *const *dst,
+                                         const size_t *dst_len, int dst_stride, int pixel_format, char *err,
+                                         size_t err_cap);
 /* GcdrEnhancer.PoolStats (GcdrEnhancer.cs:67-68): pools created, workers
  * created, pools evicted. */
 GCDR_API void gcdr_enhancer_pool_stats(const gcdr_enhancer *e, int64_t *pools,

@@ -143,6 +143,8 @@ def lib():
         L.gcdr_cuda_destroy.argtypes = [vp]
         L.gcdr_enhancer_create.argtypes = [i, vp, sz, vp, sz, i, ctypes.POINTER(vp), cp, sz]
         L.gcdr_enhancer_enhance.argtypes = [vp, vp, sz, i, i, i, vp, sz, i, i, cp, sz]
+        L.gcdr_enhancer_enhance_batch.argtypes = [vp, ctypes.POINTER(vp), ctypes.POINTER(sz), i, i, i, i,
+                                                  ctypes.POINTER(vp), ctypes.POINTER(sz), i, i, cp, sz]
         L.gcdr_enhancer_pool_stats.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(i64)]
         L.gcdr_enhancer_inject_device_loss.argtypes = [vp, i]
         L.gcdr_enhancer_destroy.argtypes = [vp]
@@ -273,6 +275,28 @@ class GcdrEnhancer:
         err = ctypes.create_string_buffer(512)
         rc = lib().gcdr_enhancer_enhance(self._h, s.ptr, s.len, int(width), int(height), int(src_stride),
                                          d.ptr, d.len, int(dst_stride), fmt, err, 512)
+        _raise(rc, err.value.decode(errors="replace"))
+
+    def enhance_batch(self, srcs, width: int, height: int, src_stride: int, dsts, dst_stride: int,
+                      format=GcdrPixelFormat.Bgr24) -> None:
+        """n (1..16) same-shape images through one pooled worker's batch plan (one launch per
+        layer for all of them, gcdr_enhancer_enhance_batch); each image gets the bytes that
+        enhance() gives it.  dsts[k] may be the same memory as srcs[k] at equal strides."""
+        if self._h is None:
+            raise GcdrError("enhancer disposed")
+        n = len(srcs)
+        if n != len(dsts):
+            raise ArgumentError("srcs and dsts differ in length")
+        if n == 0:
+            return
+        ss = [_Buf(s, False) for s in srcs]
+        ds = [_Buf(d, True) for d in dsts]
+        vp, sz = ctypes.c_void_p, ctypes.c_size_t
+        sp, sl = (vp * n)(*[b.ptr for b in ss]), (sz * n)(*[b.len for b in ss])
+        dp, dl = (vp * n)(*[b.ptr for b in ds]), (sz * n)(*[b.len for b in ds])
+        err = ctypes.create_string_buffer(512)
+        rc = lib().gcdr_enhancer_enhance_batch(self._h, sp, sl, n, int(width), int(height), int(src_stride),
+                                               dp, dl, int(dst_stride), int(format), err, 512)
         _raise(rc, err.value.decode(errors="replace"))
 
     def enhance_image(self, src, width: int, height: int, format=GcdrPixelFormat.Bgr24):

@@ -282,11 +282,10 @@ extern "C" int gcdr_enhancer_create(int device, const void *gc_onnx, size_t gc_l
     return GCDR_OK;
 }
 
-extern "C" int gcdr_enhancer_enhance(gcdr_enhancer *e, const uint8_t *src, size_t src_len, int width, int height,
-                                     int src_stride, uint8_t *dst, size_t dst_len, int dst_stride, int pixel_format,
-                                     char *err, size_t err_cap) {
-    if (!e) return GCDR_ERR_ARG;
-    // GcdrEnhancer.cs:184-192, in the same order
+// GcdrEnhancer.cs:184-192's argument checks, in the same order (one image's buffers).
+static int check_enhance_args(const uint8_t *src, size_t src_len, int width, int height, int src_stride,
+                              const uint8_t *dst, size_t dst_len, int dst_stride, int pixel_format, char *err,
+                              size_t err_cap) {
     if (pixel_format < 0 || pixel_format > 3) { put_err(err, err_cap, "unknown pixel format"); return GCDR_ERR_RANGE; }
     const int bpp = pixel_format >= 2 ? 4 : 3;
     if (width < 1) { put_err(err, err_cap, "width must be >= 1"); return GCDR_ERR_RANGE; }
@@ -303,6 +302,13 @@ extern "C" int gcdr_enhancer_enhance(gcdr_enhancer *e, const uint8_t *src, size_
                                   " rows of stride " + std::to_string(dst_stride) + " need more.");
         return GCDR_ERR_ARG;
     }
+    return GCDR_OK;
+}
+
+// Rents a worker for the shape, runs `run` on it, and on a device error drops the pool and
+// retries once on a fresh one (GcdrEnhancer's SizePool recovery).
+template <class F>
+static int with_worker(gcdr_enhancer *e, int width, int height, int pixel_format, char *err, size_t err_cap, F &&run) {
     for (int attempt = 0;; attempt++) {
         std::unique_ptr<Worker> w;
         uint64_t gen = 0;
@@ -310,7 +316,7 @@ extern "C" int gcdr_enhancer_enhance(gcdr_enhancer *e, const uint8_t *src, size_
         int rc = e->rent(w, gen, msg, width, height, pixel_format);
         if (rc) { put_err(err, err_cap, msg); return rc; }
         if (e->inject.load() > 0 && e->inject.fetch_sub(1) > 0) w->inject_device_loss = 1;
-        rc = w->enhance_host(src, width, height, src_stride, dst, dst_stride, pixel_format);
+        rc = run(*w);
         if (rc == GCDR_OK) {
             e->give_back(std::move(w), gen);
             return GCDR_OK;
@@ -326,6 +332,34 @@ extern "C" int gcdr_enhancer_enhance(gcdr_enhancer *e, const uint8_t *src, size_
         put_err(err, err_cap, msg);
         return rc;
     }
+}
+
+extern "C" int gcdr_enhancer_enhance(gcdr_enhancer *e, const uint8_t *src, size_t src_len, int width, int height,
+                                     int src_stride, uint8_t *dst, size_t dst_len, int dst_stride, int pixel_format,
+                                     char *err, size_t err_cap) {
+    if (!e) return GCDR_ERR_ARG;
+    int rc = check_enhance_args(src, src_len, width, height, src_stride, dst, dst_len, dst_stride, pixel_format, err,
+                                err_cap);
+    if (rc) return rc;
+    return with_worker(e, width, height, pixel_format, err, err_cap, [&](Worker &w) {
+        return w.enhance_host(src, width, height, src_stride, dst, dst_stride, pixel_format);
+    });
+}
+
+extern "C" int gcdr_enhancer_enhance_batch(gcdr_enhancer *e, const uint8_t *const *src, const size_t *src_len, int n,
+                                           int width, int height, int src_stride, uint8_t *const *dst,
+                                           const size_t *dst_len, int dst_stride, int pixel_format, char *err,
+                                           size_t err_cap) {
+    if (!e || !src || !dst || !src_len || !dst_len) return GCDR_ERR_ARG;
+    if (n < 1 || n > Worker::kMaxBatch) { put_err(err, err_cap, "batch size must be 1..16"); return GCDR_ERR_ARG; }
+    for (int k = 0; k < n; k++) {
+        int rc = check_enhance_args(src[k], src_len[k], width, height, src_stride, dst[k], dst_len[k], dst_stride,
+                                    pixel_format, err, err_cap);
+        if (rc) return rc;
+    }
+    return with_worker(e, width, height, pixel_format, err, err_cap, [&](Worker &w) {
+        return w.enhance_host_batch(src, n, width, height, src_stride, dst, dst_stride, pixel_format);
+    });
 }
 
 extern "C" void gcdr_enhancer_pool_stats(const gcdr_enhancer *e, int64_t *pools, int64_t *workers, int64_t *evicted) {

@@ -87,6 +87,13 @@ class SharedQueue:
             self.reap()
             time.sleep(poll_s)
 
+    def take_fresh(self):
+        """The next fresh index, or None once they are all handed out (never waits: a caller
+        that holds taken, unfinished indices may ask for more without waiting on itself)."""
+        self.heartbeat(force=False)
+        n = int(self.store.add(self._k("next"), 1)) - 1
+        return self._claim(n) if n < self.total else None
+
     def done(self, i: int):
         self.store.set(self._k("done", i), "1")
         self.store.add(self._k("ndone"), 1)
@@ -169,21 +176,40 @@ def fill_pool(pool: HostImagePool, indices, make, procs: int) -> None:
         p.map(_fill, [(pool.path, pool.count, pool.nbytes, c, make) for c in chunks if c])
 
 
-def drain(queue: SharedQueue, work, threads: int) -> int:
+def drain(queue: SharedQueue, work, threads: int, batch: int = 1) -> int:
     """Runs `threads` host threads that take indices from `queue` and call work(i)
-    (one image each) until every index is done; returns the indices this process did."""
+    (one image each) until every index is done; returns the indices this process did.
+    With batch > 1, work receives a list of up to `batch` fresh indices per call (one
+    batched enhancement); requeued indices (a dead worker's) come one at a time."""
     did = [0] * threads
     err = []
 
     def loop(k: int):
         try:
             while True:
-                i = queue.take()
-                if i is None:
-                    return
-                work(i)
-                queue.done(i)
-                did[k] += 1
+                if batch == 1:
+                    i = queue.take()
+                    if i is None:
+                        return
+                    work(i)
+                    queue.done(i)
+                    did[k] += 1
+                    continue
+                got = []
+                while len(got) < batch:
+                    i = queue.take_fresh()
+                    if i is None:
+                        break
+                    got.append(i)
+                if not got:
+                    i = queue.take()    # waits for requeued indices until every index is done
+                    if i is None:
+                        return
+                    got = [i]
+                work(got)
+                for i in got:
+                    queue.done(i)
+                did[k] += len(got)
         except BaseException as e:  # surfaced to the caller after the join
             err.append(e)
 

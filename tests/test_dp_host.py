@@ -39,6 +39,61 @@ def test_queue_hands_out_each_index_once_threads():
     assert q.take() is None
 
 
+def test_batched_drain_hands_out_each_index_once():
+    """drain(batch=k): every call gets 1..k fresh indices, every index is done once."""
+    from torch.distributed import HashStore
+    total = 203
+    q = dp.SharedQueue(HashStore(), total, rank=0, world=1)
+    seen, sizes = [], []
+    lock = threading.Lock()
+
+    def work(ids):
+        with lock:
+            seen.extend(ids)
+            sizes.append(len(ids))
+
+    assert dp.drain(q, work, threads=3, batch=4) == total
+    assert sorted(seen) == list(range(total))
+    assert max(sizes) == 4 and min(sizes) >= 1
+    assert q.counts() == (total, 0)
+    assert q.take_fresh() is None and q.take() is None
+
+
+def _batch_worker(port, rank, world, total, die_after, stale_s, threads):
+    st = _store(port)
+    q = dp.SharedQueue(st, total, rank=rank, world=world, stale_s=stale_s, beat_s=0.05)
+    calls = [0]
+
+    def work(ids):
+        if die_after is not None and calls[0] == die_after:
+            os._exit(17)                 # dies holding a whole batch (taken, never done)
+        for i in ids:
+            st.add(f"count/{i}", 1)      # the "enhancement" of image i
+        calls[0] += 1
+
+    n = dp.drain(q, work, threads=threads, batch=3)
+    st.set(f"did/{rank}", str(n))
+
+
+def test_batched_drain_requeues_a_dead_workers_batch():
+    st = _store()
+    total, stale = 60, 0.5
+    ctx = mp.get_context("spawn")
+    dying = ctx.Process(target=_batch_worker, args=(st.port, 0, 2, total, 2, stale, 1))
+    dying.start()
+    dying.join(60)
+    assert dying.exitcode == 17
+    # the survivor drains the fresh indices, then redoes the dead worker's held batch
+    alive = ctx.Process(target=_batch_worker, args=(st.port, 1, 2, total, None, stale, 2))
+    alive.start()
+    alive.join(60)
+    assert alive.exitcode == 0
+    counts = [int(st.add(f"count/{i}", 0)) for i in range(total)]
+    assert counts == [1] * total, "every index enhanced exactly once"
+    assert int(st.add("gcdrq/rq_len", 0)) == 3, "the held batch of three was requeued"
+    assert int(st.get("did/1")) == total - 6
+
+
 def _worker(port, rank, world, total, die_after, stale_s):
     st = _store(port)
     q = dp.SharedQueue(st, total, rank=rank, world=world, stale_s=stale_s, beat_s=0.05)

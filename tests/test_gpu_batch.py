@@ -97,3 +97,30 @@ def test_batch_rejects_bad_sizes():
         srcs = _docs(17, 32, 32, 0, 96)
         with pytest.raises(ArgumentError):
             wk.enhance_batch(srcs, 32, 32, 96, [s.copy() for s in srcs], 96, 0)
+
+
+def test_enhancer_batch_matches_enhance():
+    """The pooled enhancer's batch entry (gcdr_enhancer_enhance_batch): per image the bytes of
+    GcdrEnhancer.Enhance, strided and in place; argument errors as Enhance reports them."""
+    from sdcb.gcdrnet_b200 import ArgumentError, GcdrEnhancer
+    n, w, h, fmt = 3, 250, 170, 2
+    stride = w * 4 + 12
+    srcs = _docs(n, w, h, fmt, stride, seed0=120)
+    with GcdrEnhancer.from_files(G.GC_PATH, G.DR_PATH) as enh:
+        want = []
+        for s in srcs:
+            d = np.full_like(s, 0x5A)
+            enh.enhance(s, w, h, stride, d, stride, fmt)
+            want.append(d)
+        dsts = [np.full_like(s, 0x5A) for s in srcs]
+        enh.enhance_batch(srcs, w, h, stride, dsts, stride, fmt)
+        for k in range(n):
+            assert np.array_equal(dsts[k], want[k]), f"image {k}"
+        io = [s.copy() for s in srcs]
+        enh.enhance_batch(io, w, h, stride, io, stride, fmt)
+        for k in range(n):
+            assert np.array_equal(io[k], want[k]), f"in place, image {k}"
+        with pytest.raises(ArgumentError):
+            enh.enhance_batch(srcs, w, h, stride, [dsts[0], dsts[1][:stride * (h - 1)], dsts[2]], stride, fmt)
+        with pytest.raises(ArgumentError):
+            enh.enhance_batch(srcs * 6, w, h, stride, dsts * 6, stride, fmt)
