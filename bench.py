@@ -60,17 +60,18 @@ WORKLOAD = (f"enhance 1600x1152 Bgr24 synthetic documents (seeded paper/shading/
 
 
 TRAFFIC_TABLE = os.path.join(ROOT, "profiles", "ncu_kernels_1600x1152.md")
-# the batch plan's launches (BATCH images each), when captured
-TRAFFIC_TABLE_BATCH = os.path.join(ROOT, "profiles", f"ncu_top_kernels_1600x1152_batch{BATCH}.md")
+# a batch plan's launches captured at TRAFFIC_BATCH images (a smaller case of the BATCH-image
+# launches: each image's tensors are separate, so DRAM bytes grow in proportion to the images)
+TRAFFIC_BATCH = 2
+TRAFFIC_TABLE_BATCH = os.path.join(ROOT, "profiles", f"ncu_kernels_1600x1152_batch{TRAFFIC_BATCH}.md")
 
 
 def launch_traffic(op: str):
-    """DRAM bytes of one batched launch of `op` and where they come from: the batch plan's
-    own ncu rows, else the one-image row times BATCH (each image's tensors are separate,
-    so the traffic grows with the images)."""
+    """DRAM bytes of one BATCH-image launch of `op` and where they come from: the batch
+    plan's ncu row scaled by BATCH / TRAFFIC_BATCH, else the one-image row times BATCH."""
     t = ncu_traffic(op, TRAFFIC_TABLE_BATCH)
     if t is not None:
-        return t, os.path.relpath(TRAFFIC_TABLE_BATCH, ROOT)
+        return t * BATCH / TRAFFIC_BATCH, f"{os.path.relpath(TRAFFIC_TABLE_BATCH, ROOT)} x {BATCH}/{TRAFFIC_BATCH}"
     t = ncu_traffic(op, TRAFFIC_TABLE)
     if t is not None:
         return t * BATCH, f"{os.path.relpath(TRAFFIC_TABLE, ROOT)} (one image) x {BATCH}"

@@ -47,39 +47,49 @@ def cmd_enhance(a):
 
 
 def _worker_and_image(a):
+    """A worker and a.batch device-resident documents (seeds 0..) with their outputs."""
     import torch
     from . import CudaWorker, synth
     torch.cuda.set_device(a.device)
-    img = synth.document(a.width, a.height, seed=0, fmt=a.format)
-    src = torch.from_numpy(img.reshape(-1)).cuda()
-    dst = torch.empty_like(src)
+    srcs = [torch.from_numpy(synth.document(a.width, a.height, seed=k, fmt=a.format).reshape(-1)).cuda()
+            for k in range(a.batch)]
+    dsts = [torch.empty_like(s) for s in srcs]
     wk = CudaWorker.from_files(*_models(a), device=a.device)
-    return wk, src, dst
+    return wk, srcs, dsts
+
+
+def _launch(wk, a, srcs, dsts, stream):
+    """One enhancement of the documents: a single-image launch, or one batched launch."""
+    if a.batch == 1:
+        wk.enhance_device(srcs[0].data_ptr(), a.width, a.height, dsts[0].data_ptr(), a.format, stream)
+    else:
+        wk.enhance_batch_device([s.data_ptr() for s in srcs], a.width, a.height, [d.data_ptr() for d in dsts],
+                                a.format, stream)
 
 
 def cmd_run(a):
     import torch
-    wk, src, dst = _worker_and_image(a)
+    wk, srcs, dsts = _worker_and_image(a)
     s = torch.cuda.Stream()
     for _ in range(2):
-        wk.enhance_device(src.data_ptr(), a.width, a.height, dst.data_ptr(), a.format, s.cuda_stream)
+        _launch(wk, a, srcs, dsts, s.cuda_stream)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s)
     for _ in range(a.iters):
-        wk.enhance_device(src.data_ptr(), a.width, a.height, dst.data_ptr(), a.format, s.cuda_stream)
+        _launch(wk, a, srcs, dsts, s.cuda_stream)
     e1.record(s)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / a.iters
-    print(f"{a.width}x{a.height} fmt {a.format}: {ms:.3f} ms/image, {1000 / ms:.1f} images/s, "
-          f"{wk.launch_count} kernels/image")
+    ms = e0.elapsed_time(e1) / a.iters / a.batch
+    print(f"{a.width}x{a.height} fmt {a.format}, {a.batch} per launch: {ms:.3f} ms/image, {1000 / ms:.1f} images/s, "
+          f"{wk.launch_count} kernels/launch")
     wk.close()
 
 
 def cmd_prof(a):
     import torch
-    wk, src, dst = _worker_and_image(a)
-    wk.enhance_device(src.data_ptr(), a.width, a.height, dst.data_ptr(), a.format, 0)
+    wk, srcs, dsts = _worker_and_image(a)
+    _launch(wk, a, srcs, dsts, 0)
     torch.cuda.synchronize()
     prof = wk.profile(reps=a.iters)
     tot = sum(p[1] for p in prof)
@@ -289,6 +299,8 @@ def main(argv=None):
             p.add_argument("--height", type=int, default=1152)
             p.add_argument("--format", type=int, default=0)
             p.add_argument("--iters", type=int, default=10)
+            if name in ("run", "prof"):
+                p.add_argument("--batch", type=int, default=1, help="images per launch (a batch plan)")
     a = ap.parse_args(argv)
     rc = {"enhance": cmd_enhance, "run": cmd_run, "prof": cmd_prof, "microbench": cmd_microbench, "batch": cmd_batch,
           "stress": cmd_stress, "corpus": cmd_corpus}[a.cmd](a)
