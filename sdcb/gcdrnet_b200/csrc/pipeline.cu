@@ -581,7 +581,7 @@ int Worker::build_all_ops() {
         for (int k = 0; k < copies; k++) {
             all.push_back(std::move(per[k][i]));
             all_info.push_back(per_info[k][i]);
-            launches++;
+            launches += per_info[k][i].launch;
         }
     }
     ops_ = std::move(all);
@@ -677,7 +677,7 @@ int Worker::build_ops() {
     if (simt_stem_) {
         // the first kernel of the tensor-core path (stem_in) clears the device error word itself
         ops_.push_back([errp](cudaStream_t st) { return cudaMemsetAsync(errp, 0, sizeof(int), st) == cudaSuccess ? 0 : GCDR_ERR_DEVICE; });
-        info_.push_back(OpInfo{"reset_error_flag", 0, 4, 0, 0});
+        info_.push_back(OpInfo{"reset_error_flag", 0, 4, 0, 0, 0});
     }
     // a SIMT op's metadata: batched ops cover nb images, the others (the fp32 stem / head) one
     auto simt = [this, nb](const std::string &name, double flops, double bytes, bool batched = true) {

@@ -68,6 +68,7 @@ struct OpInfo {
     double bytes = 0;    // algorithmic HBM bytes of one launch (each tensor read/written once)
     int tensor = 0;      // 1: tcgen05 kernel
     int batched = 0;     // 1: one launch covers every image of a batch plan (flops, bytes: all of them)
+    int launch = 1;      // 1: a kernel launch (0: a memset node)
 };
 
 // Everything that depends on the bound shape (width, height, pixel format, debug mode): the

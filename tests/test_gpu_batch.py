@@ -124,3 +124,26 @@ def test_enhancer_batch_matches_enhance():
             enh.enhance_batch(srcs, w, h, stride, [dsts[0], dsts[1][:stride * (h - 1)], dsts[2]], stride, fmt)
         with pytest.raises(ArgumentError):
             enh.enhance_batch(srcs * 6, w, h, stride, dsts * 6, stride, fmt)
+
+
+def test_batch_with_per_image_ops_matches_single(monkeypatch):
+    """With the fp32 SIMT stem and head (GCDR_CUDA_STEM=simt), which run once per image, the
+    batch plan interleaves those per-image launches with the batched ones in plan order: each
+    image still gets the single-image bytes."""
+    from sdcb.gcdrnet_b200 import CudaWorker
+    monkeypatch.setenv("GCDR_CUDA_STEM", "simt")
+    n, w, h = 3, 200, 130
+    srcs = _docs(n, w, h, 0, w * 3, seed0=150)
+    with CudaWorker.from_files(G.GC_PATH, G.DR_PATH) as wk:
+        want = []
+        for s in srcs:
+            d = np.empty_like(s)
+            wk.enhance(s, w, h, w * 3, d, w * 3, 0)
+            want.append(d)
+        single_launches = wk.launch_count
+        dsts = [np.empty_like(s) for s in srcs]
+        wk.enhance_batch(srcs, w, h, w * 3, dsts, w * 3, 0)
+        # the per-image kernels (two stems, two heads) run n times, the rest once
+        assert wk.launch_count == single_launches + (n - 1) * 4, (wk.launch_count, single_launches)
+    for k in range(n):
+        assert np.array_equal(dsts[k], want[k]), f"image {k}"
