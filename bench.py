@@ -17,8 +17,9 @@ rank 0:
   e2e       the same metric through the public API, config c3: C3_IMAGES
             documents (each enqueued C3_PASSES times) drained from one shared
             host queue (sdcb/gcdrnet_b200/dp.py) by every GPU process, each
-            with E2E_THREADS threads calling GcdrEnhancer.enhance_batch with
-            up to E2E_BATCH documents on host buffers (two shared, page-locked
+            with E2E_THREADS threads calling GcdrEnhancer.enhance (one document a
+            call; the enhancer runs concurrent calls as batched launches) or, with
+            E2E_BATCH > 1, enhance_batch, on host buffers (two shared, page-locked
             host pools: H2D, graph, D2H per image), host monotonic clock from
             the common start to the last rank's finish; plus the single-thread
             milliseconds per image of GcdrEnhancer.enhance (the API's latency,
@@ -76,8 +77,9 @@ def launch_traffic(op: str):
     if t is not None:
         return t * BATCH, f"{os.path.relpath(TRAFFIC_TABLE, ROOT)} (one image) x {BATCH}"
     return None, None
-E2E_THREADS = 4   # concurrent GcdrEnhancer.enhance_batch callers per GPU process in the end-to-end measurement
-E2E_BATCH = 4     # documents per call (fewer at the end of the queue)
+E2E_THREADS = 24  # concurrent callers per GPU process in the end-to-end measurement (3 batches of 8 in flight)
+E2E_BATCH = 1     # documents per call: 1 = GcdrEnhancer.enhance (the reference's call; the enhancer
+                  # batches concurrent calls), > 1 = enhance_batch (fewer at the end of the queue)
 C3_IMAGES = 512   # the end-to-end workload: documents drained from the shared host queue,
 C3_PASSES = 3     # every document enqueued this many times (the timed drain lasts long enough at 8 GPUs)
 
@@ -497,20 +499,21 @@ def main():
 
     # end to end through the public API (host buffers), the c3 workload: C3_IMAGES documents
     # drained from one shared host queue by every rank (one process per GPU), each rank with
-    # E2E_THREADS host threads calling GcdrEnhancer.enhance_batch with up to E2E_BATCH documents
-    # on one shared enhancer (its worker pool rents each caller a worker: one batch's host
-    # copies overlap another's kernels); results go back into a shared host pool.  Wall clock
-    # from the common start (a barrier) to the last rank's finish, on the host's monotonic
-    # clock (one clock for all ranks).
+    # E2E_THREADS host threads calling GcdrEnhancer.enhance (or enhance_batch with up to
+    # E2E_BATCH documents) on one shared enhancer: concurrent calls run as batched launches on
+    # rented workers, one batch's host copies overlapping another's kernels; results go back
+    # into a shared host pool.  Wall clock from the common start (a barrier) to the last rank's
+    # finish, on the host's monotonic clock (one clock for all ranks).
     enh = GcdrEnhancer.from_files(GC, DR, device=local)
-    host_dst = [[np.empty(nbytes, np.uint8) for _ in range(E2E_BATCH)] for _ in range(E2E_THREADS)]
+    warm_sizes = [8, 4, 2, 1] if E2E_BATCH == 1 else list(range(E2E_BATCH, 0, -1))
+    host_dst = [[np.empty(nbytes, np.uint8) for _ in range(max(warm_sizes))] for _ in range(4)]
 
     def warm(k: int):
-        # every caller's worker plans (and captures) the batch sizes the drain uses
-        for n in range(E2E_BATCH, 0, -1):
+        # the pool's workers plan (and capture) the batch sizes the drain uses
+        for n in warm_sizes:
             enh.enhance_batch(imgs[:1] * n, W_IMG, H_IMG, W_IMG * 3, host_dst[k][:n], W_IMG * 3, 0)
 
-    th = [threading.Thread(target=warm, args=(k,)) for k in range(E2E_THREADS)]
+    th = [threading.Thread(target=warm, args=(k,)) for k in range(4)]
     for t in th:
         t.start()
     for t in th:
@@ -546,7 +549,11 @@ def main():
     barrier()
     torch.cuda.synchronize(dev)
     t0 = time.monotonic()
-    did = dp.drain(queue, work, E2E_THREADS, batch=E2E_BATCH)
+    if E2E_BATCH == 1:
+        did = dp.drain(queue, work_one, E2E_THREADS)
+    else:
+        did = dp.drain(queue, work, E2E_THREADS, batch=E2E_BATCH)
+    e2e_calls, e2e_launches = enh.batch_stats
     t1 = time.monotonic()
     barrier()
     e2e_s = max_over_ranks(t1, dist) - min_over_ranks(t0, dist)
@@ -634,8 +641,11 @@ def main():
                        "precision": "fp16 tensor-core layers (fp32 accumulate), fp32 stem/head/div6"},
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": nbytes,
                     "d2h_bytes_per_step": nbytes, "step": "one image",
-                    "api": f"GcdrEnhancer.enhance_batch, up to {E2E_BATCH} documents per call (host buffers: "
-                           "shared host pool in, shared host pool out)",
+                    "api": ("GcdrEnhancer.enhance, one document per call (concurrent calls batched by the "
+                            "enhancer" if E2E_BATCH == 1 else
+                            f"GcdrEnhancer.enhance_batch, up to {E2E_BATCH} documents per call") +
+                           "; host buffers: shared host pool in, shared host pool out)",
+                    "enhance_calls": e2e_calls, "worker_launches": e2e_launches,
                     "workload": f"{C3_IMAGES} 1600x1152 Bgr24 documents (seeds 0-{C3_IMAGES - 1}), each enqueued "
                                 f"{C3_PASSES} times, drained from one shared host queue by {world} GPU process(es), "
                                 f"{E2E_THREADS} calling threads each",

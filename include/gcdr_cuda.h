@@ -195,6 +195,18 @@ GCDR_API int gcdr_enhancer_enhance_batch(gcdr_enhancer *e, const uint8_t *const 
                                          int width, int height, int src_stride, uint8_t *const *dst,
                                          const size_t *dst_len, int dst_stride, int pixel_format, char *err,
                                          size_t err_cap);
+/* Concurrent gcdr_enhancer_enhance calls of one shape, format and stride pair are batched
+ * opportunistically: when no batch of that shape runs, or a full batch is queued and fewer than
+ * `max_running` run, a waiting caller takes the oldest queued calls (a power of two of them, at
+ * most `max_batch`) and runs them as one batch-plan launch for all; a lone call runs at once,
+ * alone.  Every call returns when its
+ * own image is written and gets the bytes a single-image plan gives it.  Defaults 8 and 3;
+ * max_batch = 1 turns the batching off.  No counterpart in the reference (every Enhance call
+ * runs alone there). */
+GCDR_API int gcdr_enhancer_set_batching(gcdr_enhancer *e, int max_batch, int max_running);
+/* Enhance calls so far, and the worker launches that ran them (launches < calls when calls
+ * were batched). */
+GCDR_API void gcdr_enhancer_batch_stats(const gcdr_enhancer *e, int64_t *calls, int64_t *launches);
 /* GcdrEnhancer.PoolStats (GcdrEnhancer.cs:67-68): pools created, workers
  * created, pools evicted. */
 GCDR_API void gcdr_enhancer_pool_stats(const gcdr_enhancer *e, int64_t *pools,

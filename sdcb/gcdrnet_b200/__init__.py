@@ -145,6 +145,9 @@ def lib():
         L.gcdr_enhancer_enhance.argtypes = [vp, vp, sz, i, i, i, vp, sz, i, i, cp, sz]
         L.gcdr_enhancer_enhance_batch.argtypes = [vp, ctypes.POINTER(vp), ctypes.POINTER(sz), i, i, i, i,
                                                   ctypes.POINTER(vp), ctypes.POINTER(sz), i, i, cp, sz]
+        L.gcdr_enhancer_set_batching.argtypes = [vp, i, i]
+        L.gcdr_enhancer_batch_stats.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64)]
+        L.gcdr_enhancer_batch_stats.restype = None
         L.gcdr_enhancer_pool_stats.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(i64)]
         L.gcdr_enhancer_inject_device_loss.argtypes = [vp, i]
         L.gcdr_enhancer_destroy.argtypes = [vp]
@@ -306,6 +309,21 @@ class GcdrEnhancer:
         dst = np.empty(stride * int(height), np.uint8)
         self.enhance(src, width, height, stride, dst, stride, format)
         return dst
+
+    def set_batching(self, max_batch: int = 8, max_running: int = 3) -> None:
+        """Concurrent enhance() calls of one shape run together: when no batch of that shape is
+        on the GPU, or a full batch is queued and fewer than max_running run, a waiting caller
+        runs the oldest queued calls (a power of two, at most max_batch) as one batched launch;
+        a lone call runs at once.  Results are the single-image bytes.  max_batch = 1 turns it
+        off."""
+        _raise(lib().gcdr_enhancer_set_batching(self._h, int(max_batch), int(max_running)), "bad batching limits")
+
+    @property
+    def batch_stats(self):
+        """(enhance calls, worker launches that ran them)."""
+        a, b = ctypes.c_int64(), ctypes.c_int64()
+        lib().gcdr_enhancer_batch_stats(self._h, ctypes.byref(a), ctypes.byref(b))
+        return a.value, b.value
 
     @property
     def pool_stats(self):

@@ -8,12 +8,17 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <condition_variable>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <deque>
+#include <map>
 #include <memory>
 #include <mutex>
 #include <string>
+#include <tuple>
+#include <vector>
 
 #include "../../../include/gcdr_cuda.h"
 #include "conv_launch.h"
@@ -204,6 +209,21 @@ extern "C" void gcdr_cuda_destroy(gcdr_cuda *w) { delete w; }
 
 // ---------------------------------------------------------------- enhancer
 
+// One Enhance call waiting to be run, possibly in another caller's batch.
+struct PendingEnhance {
+    const uint8_t *src = nullptr;
+    uint8_t *dst = nullptr;
+    bool done = false;
+    int rc = GCDR_OK;
+    std::string msg;
+};
+
+// Concurrent Enhance calls of one shape, format and stride pair.
+struct EnhanceLane {
+    std::deque<PendingEnhance *> queue;   // oldest first
+    int running = 0;                      // batches of this lane on the GPU now
+};
+
 struct gcdr_enhancer {
     int device = 0;
     Model model;
@@ -218,6 +238,19 @@ struct gcdr_enhancer {
     // device bytes of the idle workers beyond the first (VkPipeline2.cs:137-138 keeps 3 GB for
     // one arena; here a worker holds several shape plans, Worker::kPlanBudget each at most)
     static constexpr int64_t kIdleBudget = 32LL << 30;
+
+    // Opportunistic batching of concurrent Enhance calls: a call joins its lane's queue; when
+    // the lane has no batch on the GPU, or a full batch is queued and fewer than max_running
+    // run, a waiting caller takes the oldest queued calls -- a power of two of them, at most
+    // max_batch, so that a worker holds at most four batch plans per shape -- and runs them as
+    // one batch-plan launch on a rented worker for everyone; the other callers sleep until
+    // their call is done.  A lone call runs at once, alone.  Each image gets the bytes a
+    // single-image plan gives it.
+    std::mutex bmu;
+    std::condition_variable bcv;
+    std::map<std::tuple<int, int, int, int, int>, EnhanceLane> lanes;   // (w, h, fmt, src, dst stride)
+    int max_batch = 8, max_running = 3;
+    std::atomic<int64_t> calls{0}, launches{0};
 
     // An idle worker, preferring one that holds a plan (arena + graph) for this image shape,
     // else a new one.
@@ -306,15 +339,14 @@ static int check_enhance_args(const uint8_t *src, size_t src_len, int width, int
 }
 
 // Rents a worker for the shape, runs `run` on it, and on a device error drops the pool and
-// retries once on a fresh one (GcdrEnhancer's SizePool recovery).
+// retries once on a fresh one (GcdrEnhancer's SizePool recovery).  msg: the error text.
 template <class F>
-static int with_worker(gcdr_enhancer *e, int width, int height, int pixel_format, char *err, size_t err_cap, F &&run) {
+static int with_worker(gcdr_enhancer *e, int width, int height, int pixel_format, std::string &msg, F &&run) {
     for (int attempt = 0;; attempt++) {
         std::unique_ptr<Worker> w;
         uint64_t gen = 0;
-        std::string msg;
         int rc = e->rent(w, gen, msg, width, height, pixel_format);
-        if (rc) { put_err(err, err_cap, msg); return rc; }
+        if (rc) return rc;
         if (e->inject.load() > 0 && e->inject.fetch_sub(1) > 0) w->inject_device_loss = 1;
         rc = run(*w);
         if (rc == GCDR_OK) {
@@ -329,8 +361,63 @@ static int with_worker(gcdr_enhancer *e, int width, int height, int pixel_format
             continue;
         }
         e->give_back(std::move(w), gen);
-        put_err(err, err_cap, msg);
         return rc;
+    }
+}
+
+// Runs one Enhance call through its lane (see gcdr_enhancer::lanes).
+static int enhance_coalesced(gcdr_enhancer *e, const uint8_t *src, uint8_t *dst, int width, int height, int src_stride,
+                             int dst_stride, int fmt, std::string &msg) {
+    e->calls++;
+    PendingEnhance me;
+    me.src = src;
+    me.dst = dst;
+    std::unique_lock<std::mutex> lk(e->bmu);
+    const auto key = std::make_tuple(width, height, fmt, src_stride, dst_stride);
+    EnhanceLane &lane = e->lanes[key];
+    lane.queue.push_back(&me);
+    for (;;) {
+        if (me.done) {
+            msg = std::move(me.msg);
+            return me.rc;
+        }
+        // a batch starts when the lane has none on the GPU (a lone call waits for nobody), or
+        // when a full batch is queued and fewer than max_running run: under load the calls
+        // gather into full batches behind the running ones instead of trickling out in small ones
+        const bool start = !lane.queue.empty() && lane.running < e->max_running &&
+                           (lane.running == 0 || (int)lane.queue.size() >= e->max_batch);
+        if (start) {
+            size_t n = 1;
+            const size_t cap = std::min(lane.queue.size(), (size_t)std::max(e->max_batch, 1));
+            while (n * 2 <= cap) n *= 2;
+            std::vector<PendingEnhance *> batch(lane.queue.begin(), lane.queue.begin() + (long)n);
+            lane.queue.erase(lane.queue.begin(), lane.queue.begin() + (long)n);
+            lane.running++;
+            lk.unlock();
+            std::vector<const uint8_t *> srcs(n);
+            std::vector<uint8_t *> dsts(n);
+            for (size_t k = 0; k < n; k++) {
+                srcs[k] = batch[k]->src;
+                dsts[k] = batch[k]->dst;
+            }
+            std::string bmsg;
+            e->launches++;
+            const int rc = with_worker(e, width, height, fmt, bmsg, [&](Worker &w) {
+                return n == 1 ? w.enhance_host(srcs[0], width, height, src_stride, dsts[0], dst_stride, fmt)
+                              : w.enhance_host_batch(srcs.data(), (int)n, width, height, src_stride, dsts.data(),
+                                                     dst_stride, fmt);
+            });
+            lk.lock();
+            for (auto *r : batch) {
+                r->rc = rc;
+                r->msg = bmsg;
+                r->done = true;
+            }
+            lane.running--;
+            e->bcv.notify_all();
+            continue;
+        }
+        e->bcv.wait(lk);
     }
 }
 
@@ -341,9 +428,16 @@ extern "C" int gcdr_enhancer_enhance(gcdr_enhancer *e, const uint8_t *src, size_
     int rc = check_enhance_args(src, src_len, width, height, src_stride, dst, dst_len, dst_stride, pixel_format, err,
                                 err_cap);
     if (rc) return rc;
-    return with_worker(e, width, height, pixel_format, err, err_cap, [&](Worker &w) {
-        return w.enhance_host(src, width, height, src_stride, dst, dst_stride, pixel_format);
-    });
+    std::string msg;
+    rc = enhance_coalesced(e, src, dst, width, height, src_stride, dst_stride, pixel_format, msg);
+    if (rc) put_err(err, err_cap, msg);
+    {
+        // a lane nobody waits in any more goes away (shapes come and go)
+        std::lock_guard<std::mutex> g(e->bmu);
+        auto it = e->lanes.find(std::make_tuple(width, height, pixel_format, src_stride, dst_stride));
+        if (it != e->lanes.end() && it->second.queue.empty() && it->second.running == 0) e->lanes.erase(it);
+    }
+    return rc;
 }
 
 extern "C" int gcdr_enhancer_enhance_batch(gcdr_enhancer *e, const uint8_t *const *src, const size_t *src_len, int n,
@@ -357,9 +451,27 @@ extern "C" int gcdr_enhancer_enhance_batch(gcdr_enhancer *e, const uint8_t *cons
                                     pixel_format, err, err_cap);
         if (rc) return rc;
     }
-    return with_worker(e, width, height, pixel_format, err, err_cap, [&](Worker &w) {
+    std::string msg;
+    const int rc = with_worker(e, width, height, pixel_format, msg, [&](Worker &w) {
         return w.enhance_host_batch(src, n, width, height, src_stride, dst, dst_stride, pixel_format);
     });
+    if (rc) put_err(err, err_cap, msg);
+    return rc;
+}
+
+extern "C" int gcdr_enhancer_set_batching(gcdr_enhancer *e, int max_batch, int max_running) {
+    if (!e || max_batch < 1 || max_batch > Worker::kMaxBatch || max_running < 1 || max_running > 64)
+        return GCDR_ERR_ARG;
+    std::lock_guard<std::mutex> g(e->bmu);
+    e->max_batch = max_batch;
+    e->max_running = max_running;
+    return GCDR_OK;
+}
+
+extern "C" void gcdr_enhancer_batch_stats(const gcdr_enhancer *e, int64_t *calls, int64_t *launches) {
+    if (!e) return;
+    if (calls) *calls = e->calls.load();
+    if (launches) *launches = e->launches.load();
 }
 
 extern "C" void gcdr_enhancer_pool_stats(const gcdr_enhancer *e, int64_t *pools, int64_t *workers, int64_t *evicted) {

@@ -147,3 +147,49 @@ def test_batch_with_per_image_ops_matches_single(monkeypatch):
         assert wk.launch_count == single_launches + (n - 1) * 4, (wk.launch_count, single_launches)
     for k in range(n):
         assert np.array_equal(dsts[k], want[k]), f"image {k}"
+
+
+def test_concurrent_enhance_calls_are_batched():
+    """Concurrent GcdrEnhancer.enhance calls of one shape run as batched launches (fewer worker
+    launches than calls); every call gets the bytes of a single-image enhance.  With batching
+    off (max_batch 1) every call is its own launch."""
+    import threading
+    from sdcb.gcdrnet_b200 import CudaWorker, GcdrEnhancer
+    threads, per, w, h = 8, 4, 320, 224
+    docs = _docs(threads * per, w, h, 0, w * 3, seed0=200)
+    with CudaWorker.from_files(G.GC_PATH, G.DR_PATH) as wk:
+        want = []
+        for s in docs:
+            d = np.empty_like(s)
+            wk.enhance(s, w, h, w * 3, d, w * 3, 0)
+            want.append(d)
+    for max_batch in (8, 1):
+        got = [np.empty_like(s) for s in docs]
+        errors = []
+        with GcdrEnhancer.from_files(G.GC_PATH, G.DR_PATH) as enh:
+            enh.set_batching(max_batch, 1)   # one launch at a time: the other calls queue behind it
+            enh.enhance(docs[0], w, h, w * 3, got[0], w * 3, 0)   # plans the shape
+            go = threading.Barrier(threads)
+
+            def run(t):
+                try:
+                    go.wait()
+                    for i in range(t, len(docs), threads):
+                        enh.enhance(docs[i], w, h, w * 3, got[i], w * 3, 0)
+                except Exception as ex:   # surfaced below
+                    errors.append(repr(ex))
+
+            th = [threading.Thread(target=run, args=(t,)) for t in range(threads)]
+            for t in th:
+                t.start()
+            for t in th:
+                t.join()
+            calls, launches = enh.batch_stats
+        assert not errors, errors[:3]
+        for i in range(len(docs)):
+            assert np.array_equal(got[i], want[i]), f"max_batch {max_batch}: document {i}"
+        assert calls == len(docs) + 1
+        if max_batch == 1:
+            assert launches == calls
+        else:
+            assert launches < calls, (calls, launches)
