@@ -114,8 +114,12 @@ class SharedQueue:
         for r in range(self.world):
             if not self._is_dead(r, now):
                 continue
-            if self.store.compare_set(self._k("reaped", r), "", str(self.rank)) != str(self.rank).encode():
-                continue            # another survivor reaps it
+            # one reaper per dead rank: the first compare-and-set wins, with a token unique to
+            # this call (several threads of one survivor, and its later polls, must not
+            # requeue the same indices again)
+            token = f"{self.rank}:{threading.get_ident()}:{time.monotonic_ns()}"
+            if self.store.compare_set(self._k("reaped", r), "", token) != token.encode():
+                continue            # reaped already (by another survivor or an earlier call)
             for i in range(self.total):
                 if not self.store.check([self._k("claim", i)]) or self.store.check([self._k("done", i)]):
                     continue
