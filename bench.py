@@ -15,7 +15,7 @@ rank 0:
             ranks; the same loop with one image per step (one stream, one
             single-image launch) is reported beside it as single_stream;
   e2e       the same metric through the public API, config c3: C3_IMAGES
-            documents (each enqueued C3_PASSES times) drained from one shared
+            documents (each enqueued C3_PASSES times per GPU) drained from one shared
             host queue (sdcb/gcdrnet_b200/dp.py) by every GPU process, each
             with E2E_THREADS threads calling GcdrEnhancer.enhance (one document a
             call; the enhancer runs concurrent calls as batched launches) or, with
@@ -81,7 +81,8 @@ E2E_THREADS = 24  # concurrent callers per GPU process in the end-to-end measure
 E2E_BATCH = 1     # documents per call: 1 = GcdrEnhancer.enhance (the reference's call; the enhancer
                   # batches concurrent calls), > 1 = enhance_batch (fewer at the end of the queue)
 C3_IMAGES = 512   # the end-to-end workload: documents drained from the shared host queue,
-C3_PASSES = 3     # every document enqueued this many times (the timed drain lasts long enough at 8 GPUs)
+C3_PASSES = 3     # every document enqueued this many times per GPU: 1536 images per GPU process, so the
+                  # timed drain lasts about a second at every N (weak scaling, as `value`)
 
 
 def ncu_traffic(op: str, table: str = None):
@@ -543,7 +544,7 @@ def main():
     else:
         from torch.distributed import HashStore
         store = HashStore()
-    jobs = C3_IMAGES * C3_PASSES
+    jobs = C3_IMAGES * C3_PASSES * world
     queue = dp.SharedQueue(store, jobs, rank, world, prefix="c3")
     store.add("c3/ranks_seen", 1)
     barrier()
@@ -647,7 +648,7 @@ def main():
                            "; host buffers: shared host pool in, shared host pool out)",
                     "enhance_calls": e2e_calls, "worker_launches": e2e_launches,
                     "workload": f"{C3_IMAGES} 1600x1152 Bgr24 documents (seeds 0-{C3_IMAGES - 1}), each enqueued "
-                                f"{C3_PASSES} times, drained from one shared host queue by {world} GPU process(es), "
+                                f"{C3_PASSES * world} times, drained from one shared host queue by {world} GPU process(es), "
                                 f"{E2E_THREADS} calling threads each",
                     "seconds": e2e_s, "per_rank_images": per_rank, "per_rank_ms": per_rank_ms,
                     "ranks_seen": ranks_seen, "host_cpus": host_threads(),
