@@ -335,11 +335,22 @@ __device__ void epilogue_pool(const EpiParams &ep, const TileGeom &tg, int y2, i
 // address bits [8:7]), so that the two-column gathers of a warp hit distinct banks.
 constexpr int kHeadWinCols = 66;   // 128 pixels -> 64 dec5 columns + the clamp/interpolation halo
 
+// The swizzle of a window pixel's 16-byte chunk k depends on the pixel only: its row starts
+// on a multiple of C1 * 2 bytes, so chunk k's offset bits [5:4] (C1 = 32; bit 4 for 16) come
+// from k alone and address bits [8:7] from the pixel.  A HeadWinPix holds the pixel's byte
+// offset and its chunk XOR; chunk k then costs one XOR and one add.
+struct HeadWinPix {
+    uint32_t base, sw;
+};
+
 template <int C1>
-__device__ __forceinline__ uint4 head_win_ld(const uint8_t *win, int r, int c, int k) {
-    uint32_t off = (uint32_t)((r * kHeadWinCols + c) * (C1 * 2) + k * 16);
-    off ^= ((off >> 7) & (C1 == 32 ? 3u : 1u)) << 4;
-    return *reinterpret_cast<const uint4 *>(win + off);
+__device__ __forceinline__ HeadWinPix head_win_pix(int r, int c) {
+    const uint32_t b = (uint32_t)((r * kHeadWinCols + c) * (C1 * 2));
+    return HeadWinPix{b, (b >> 7) & (C1 == 32 ? 3u : 1u)};
+}
+
+__device__ __forceinline__ uint4 head_win_ld(const uint8_t *win, HeadWinPix px, int k) {
+    return *reinterpret_cast<const uint4 *>(win + px.base + ((((uint32_t)k) ^ px.sw) << 4));
 }
 
 __device__ __forceinline__ float sigmoid_fast(float v) { return __fdividef(1.0f, 1.0f + __expf(-v)); }
@@ -425,6 +436,9 @@ __device__ void epilogue_head_pair(const EpiParams &ep, const TileGeom &tg, int 
     const int r0 = max(M - 1, 0) - wy0, r1 = M - wy0, r2 = min(M + 1, Hh - 1) - wy0;
     // even x: columns n-1 (1/4), n (3/4); odd x: n (3/4), n+1 (1/4)
     const int cA = (xodd ? n : max(n - 1, 0)) - wx0, cB = (xodd ? min(n + 1, Wh - 1) : n) - wx0;
+    const HeadWinPix p0a = head_win_pix<C1>(r0, cA), p0b = head_win_pix<C1>(r0, cB);
+    const HeadWinPix p1a = head_win_pix<C1>(r1, cA), p1b = head_win_pix<C1>(r1, cB);
+    const HeadWinPix p2a = head_win_pix<C1>(r2, cA), p2b = head_win_pix<C1>(r2, cB);
     // the products of 1/4 and 3/4 are exact in fp16: the interpolation of the fp16 dec5
     // runs on channel pairs (HFMA2), the rest in fp32
     const float wa = xodd ? 0.75f : 0.25f, wb = 1.0f - wa;
@@ -446,9 +460,9 @@ __device__ void epilogue_head_pair(const EpiParams &ep, const TileGeom &tg, int 
             ld1.load16_nw(cb, 8 * k);
             L::wait_ld();
         }
-        const uint4 u0a = head_win_ld<C1>(win, r0, cA, k), u0b = head_win_ld<C1>(win, r0, cB, k);
-        const uint4 u1a = head_win_ld<C1>(win, r1, cA, k), u1b = head_win_ld<C1>(win, r1, cB, k);
-        const uint4 u2a = head_win_ld<C1>(win, r2, cA, k), u2b = head_win_ld<C1>(win, r2, cB, k);
+        const uint4 u0a = head_win_ld(win, p0a, k), u0b = head_win_ld(win, p0b, k);
+        const uint4 u1a = head_win_ld(win, p1a, k), u1b = head_win_ld(win, p1b, k);
+        const uint4 u2a = head_win_ld(win, p2a, k), u2b = head_win_ld(win, p2b, k);
         const __half2 *h0a = reinterpret_cast<const __half2 *>(&u0a), *h0b = reinterpret_cast<const __half2 *>(&u0b);
         const __half2 *h1a = reinterpret_cast<const __half2 *>(&u1a), *h1b = reinterpret_cast<const __half2 *>(&u1b);
         const __half2 *h2a = reinterpret_cast<const __half2 *>(&u2a), *h2b = reinterpret_cast<const __half2 *>(&u2b);
