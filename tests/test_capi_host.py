@@ -73,3 +73,26 @@ def test_enhancer_argument_validation_without_gpu():
     buf = (ctypes.c_uint8 * (32 * 32 * 4))()
     # a null enhancer handle is an argument error, never a crash
     assert L.gcdr_enhancer_enhance(None, buf, len(buf), 32, 32, 96, buf, len(buf), 128, 2, err, 256) == 1
+
+
+def test_enhancer_batching_controls_without_gpu():
+    """gcdr_enhancer_set_batching validates its limits and gcdr_enhancer_batch_stats counts
+    nothing before the first call; creating an enhancer only parses the models (no device
+    work), so this runs on CPU."""
+    from sdcb.gcdrnet_b200 import lib
+    L = lib()
+    gc, dr = open(G.GC_PATH, "rb").read(), open(G.DR_PATH, "rb").read()
+    h = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(256)
+    assert L.gcdr_enhancer_create(0, gc, len(gc), dr, len(dr), 0, ctypes.byref(h), err, 256) == 0, err.value
+    try:
+        for bad in ((0, 1), (17, 1), (8, 0), (8, 65)):
+            assert L.gcdr_enhancer_set_batching(h, *bad) == 1, bad
+        assert L.gcdr_enhancer_set_batching(h, 1, 1) == 0          # batching off
+        assert L.gcdr_enhancer_set_batching(h, 16, 64) == 0
+        calls, launches = ctypes.c_int64(-1), ctypes.c_int64(-1)
+        L.gcdr_enhancer_batch_stats(h, ctypes.byref(calls), ctypes.byref(launches))
+        assert (calls.value, launches.value) == (0, 0)
+        assert L.gcdr_enhancer_set_batching(None, 8, 3) == 1
+    finally:
+        L.gcdr_enhancer_destroy(h)

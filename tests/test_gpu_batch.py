@@ -193,3 +193,48 @@ def test_concurrent_enhance_calls_are_batched():
             assert launches == calls
         else:
             assert launches < calls, (calls, launches)
+
+
+def test_batched_calls_two_shapes_and_device_loss():
+    """Concurrent enhance calls of two shapes (two lanes) while the first worker run reports a
+    device loss (injected on the host): the batch that met it is retried on a fresh pool, and
+    every call returns its single-image bytes."""
+    import threading
+    from sdcb.gcdrnet_b200 import CudaWorker, GcdrEnhancer
+    shapes = [(256, 160), (192, 224)]
+    docs = {s: _docs(6, s[0], s[1], 0, s[0] * 3, seed0=300 + 10 * k) for k, s in enumerate(shapes)}
+    want = {}
+    with CudaWorker.from_files(G.GC_PATH, G.DR_PATH) as wk:
+        for s in shapes:
+            for i, d in enumerate(docs[s]):
+                out = np.empty_like(d)
+                wk.enhance(d, s[0], s[1], s[0] * 3, out, s[0] * 3, 0)
+                want[s, i] = out
+    got, errors = {}, []
+    with GcdrEnhancer.from_files(G.GC_PATH, G.DR_PATH) as enh:
+        enh.set_batching(4, 1)
+        evicted0 = enh.pool_stats[2]
+        enh.inject_device_loss(1)
+        go = threading.Barrier(6)
+
+        def run(t):
+            try:
+                go.wait()
+                s = shapes[t % 2]
+                for i in range(t // 2, 6, 3):
+                    out = np.empty_like(docs[s][i])
+                    enh.enhance(docs[s][i], s[0], s[1], s[0] * 3, out, s[0] * 3, 0)
+                    got[s, i] = out
+            except Exception as ex:   # surfaced below
+                errors.append(repr(ex))
+
+        th = [threading.Thread(target=run, args=(t,)) for t in range(6)]
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        assert enh.pool_stats[2] > evicted0, "the pool that met the device loss was dropped"
+    assert not errors, errors[:3]
+    assert set(got) == set(want)
+    for key in want:
+        assert np.array_equal(got[key], want[key]), f"{key}"
