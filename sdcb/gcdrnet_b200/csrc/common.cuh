@@ -107,9 +107,10 @@ __host__ __device__ inline int refl_hi(int n) { return n > 1 ? n - 2 : 0; }  // 
 
 // Calls put(r) for the row r of pixel (y, x) and, for LAY_PADREFL, for each
 // border copy that mirrors it (no arrays: interior pixels return after one put).
+// interior = false: the border copies only.
 template <class F>
-__device__ __forceinline__ void act_rows(const Act &a, int y, int x, F &&put) {
-    put(a.row(y, x));
+__device__ __forceinline__ void act_rows(const Act &a, int y, int x, F &&put, bool interior = true) {
+    if (interior) put(a.row(y, x));
     if (a.kind != LAY_PADREFL) return;
     const bool ylo = y == refl_lo(a.H), yhi = y == refl_hi(a.H);
     const bool xlo = x == refl_lo(a.W), xhi = x == refl_hi(a.W);
@@ -138,6 +139,54 @@ __device__ __forceinline__ void act_store(const Act &a, int y, int x, int c0, co
             for (int k = 0; k < n; k += 2) *reinterpret_cast<__half2 *>(d + k) = *reinterpret_cast<const __half2 *>(v + k);
         }
     });
+}
+
+// The reflect-border copies of act_store alone (LAY_PADREFL; nothing for other layouts).
+__device__ __forceinline__ void act_store_borders(const Act &a, int y, int x, int c0, const __half *v, int n,
+                                                  size_t io) {
+    if (a.kind != LAY_PADREFL) return;
+    __half *base = img_at(a.p, io);
+    act_rows(a, y, x, [&](long long r) {
+        __half *d = base + r * a.C + c0;
+        for (int k = 0; k < n; k += 8) *reinterpret_cast<uint4 *>(d + k) = *reinterpret_cast<const uint4 *>(v + k);
+    }, false);
+}
+
+// A warp's store of up to 32 consecutive pixels (y, x0 + p), p < npix, channels [c0, c0 + CW)
+// (CW = 16 or 32 halves; pixel p's values are in lane `src_lane(p)`'s h), staged through the
+// warp's shared-memory buffer `stg` (npix * CW * 2 bytes, 16-byte aligned) so that each store
+// instruction writes contiguous 16-byte chunks of consecutive pixels instead of one pixel's
+// chunk per lane: lanes write their pixel into the buffer (chunk j of pixel p at 16-byte slot
+// j ^ f(p), f spreading a quarter-warp over all banks), then each lane stores chunks
+// q = lane, lane + 32, ... (pixel q / (CW/8)) from it.  has_px: this lane holds pixel
+// `my_p`; valid(p): pixel p is inside the image.  Reflect-border copies (LAY_PADREFL) go out
+// per lane afterwards.  Warp-collective.
+template <int CW, class Valid>
+__device__ __forceinline__ void warp_store_staged(const Act &a, int y, int x0, int c0, const __half *h, bool has_px,
+                                                  int my_p, int npix, Valid &&valid, uint8_t *stg, size_t io) {
+    constexpr int CPP = CW / 8;                       // 16-byte chunks per pixel
+    constexpr int SPREAD = 8 / CPP;                   // pixels per 128 bytes
+    const int lane = threadIdx.x & 31;
+    if (has_px) {
+#pragma unroll
+        for (int j = 0; j < CPP; j++) {
+            const int slot = j ^ ((my_p / SPREAD) & (CPP - 1));
+            *reinterpret_cast<uint4 *>(stg + my_p * (CW * 2) + slot * 16) = *reinterpret_cast<const uint4 *>(h + 8 * j);
+        }
+    }
+    __syncwarp();
+    __half *base = img_at(a.p, io);
+#pragma unroll
+    for (int i = 0; i < CPP; i++) {
+        const int q = i * 32 + lane, p = q / CPP, j = q - p * CPP;
+        if (p < npix && valid(p)) {
+            const int slot = j ^ ((p / SPREAD) & (CPP - 1));
+            const uint4 d = *reinterpret_cast<const uint4 *>(stg + p * (CW * 2) + slot * 16);
+            *reinterpret_cast<uint4 *>(base + a.row(y, x0 + p) * a.C + c0 + 8 * j) = d;
+        }
+    }
+    __syncwarp();                                     // the buffer is free for the next store
+    if (has_px && valid(my_p)) act_store_borders(a, y, x0 + my_p, c0, h, CW, io);
 }
 
 // Two channels (c even) by value.

@@ -39,6 +39,7 @@ struct RwConfig {
     int b_bytes = 0;       // all weights: 9 * C/bk blocks
     int acc_cols = 32, acc_bufs = 1, tmem_cols = 32;
     int win_tx = 0;        // head: bytes of the dec5 window box per stage (0 otherwise)
+    int stg_bytes = 0;     // plain / pool: the epilogue warps' store staging buffers
 };
 
 // Copies the layer's bias (device, N floats) into a.ep.bias_c (synchronous; at op

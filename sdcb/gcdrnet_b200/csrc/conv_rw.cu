@@ -63,6 +63,11 @@ struct RwShared {
 
 __host__ __device__ inline int round1k(int b) { return (b + 1023) & ~1023; }
 
+// The epilogue warps' store staging buffers (plain and pool): one output row chunk of
+// 32 pixels x 32 halves per warp, after the shared block (128-byte aligned).
+constexpr int kStgWarpBytes = 32 * 32 * 2;
+constexpr int kRwSharedBytes = (int)((sizeof(RwShared) + 127) & ~size_t(127));
+
 // HC: the head's stem channels (16 or 32; a separate instantiation each: one register
 // allocation per width), 0 for the other modes.  ROWS: output rows per MMA warp (2 for the
 // head and the 8-row pool units; a compile-time bound keeps the issue loop unrolled)
@@ -231,6 +236,7 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
         }
     } else {
         const int e = warp - 1 - Roles::mma;        // epilogue warp 0..epi-1
+        uint8_t *stg = reinterpret_cast<uint8_t *>(sh) + kRwSharedBytes + (size_t)e * kStgWarpBytes;
         const int quad = warp & 3;                  // the TMEM lane quadrant this warp may read
         const int part = e >> 2;                    // 0..parts-1
         const int row = quad * 32 + lane;           // pixel within the unit's 128
@@ -264,7 +270,10 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
                     const int q = it / nch, ch = it - q * nch;
                     TmemLoader top{acc0 + (uint32_t)(2 * q * cfg.acc_cols)};
                     TmemLoader bot{acc0 + (uint32_t)((2 * q + 1) * cfg.acc_cols)};
-                    epilogue_pool(args.ep, tg, y0 / 2 + q, x, 0, N, top, bot, ch, nch, io);
+                    if (cw == 32)
+                        epilogue_pool_staged<32>(args.ep, tg, y0 / 2 + q, x - lane, ch * 32, top, bot, stg, io);
+                    else
+                        epilogue_pool_staged<16>(args.ep, tg, y0 / 2 + q, x - lane, ch * 16, top, bot, stg, io);
                 }
             } else if (MODE == EPI_HEAD) {
                 // pixel pairs (rows 2q, 2q + 1: one shared dec5 row) taken in turn by the warps;
@@ -289,7 +298,10 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
                 for (int it = part; it < R * nch; it += Roles::parts) {
                     const int jj = it / nch, ch = it - jj * nch;
                     TmemLoader ld{acc0 + (uint32_t)(jj * cfg.acc_cols)};
-                    epilogue_plain_yx(args.ep, tg, y0 + jj, x, 0, N, ld, ch, nch, args.ep.bias_c, io);
+                    if (cw == 32)
+                        epilogue_plain_staged<32>(args.ep, tg, y0 + jj, x - lane, ch * 32, ld, args.ep.bias_c, stg, io);
+                    else
+                        epilogue_plain_staged<16>(args.ep, tg, y0 + jj, x - lane, ch * 16, ld, args.ep.bias_c, stg, io);
                 }
             }
             tc_fence_before();
@@ -331,7 +343,7 @@ __global__ void __launch_bounds__(RwRoles<MODE>::threads, 1)
 }
 
 size_t rw_smem(const RwConfig &cfg) {
-    return 1024 + (size_t)cfg.b_bytes + (size_t)cfg.stages * cfg.stage_bytes + sizeof(RwShared);
+    return 1024 + (size_t)cfg.b_bytes + (size_t)cfg.stages * cfg.stage_bytes + kRwSharedBytes + cfg.stg_bytes;
 }
 
 template <int BK, int MODE, int HC = 0, int ROWS = 1>
@@ -393,7 +405,8 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
             const int b_bytes = 9 * (a.C / bk) * b_block;
             if (b_bytes > 96 * 1024) continue;
             const int seg_bytes = round1k(kSegRows * bk * 2);
-            const int avail = kRwSmemCap - 1024 - b_bytes - (int)sizeof(RwShared);
+            const int stg_bytes = mode == EPI_HEAD ? 0 : RwRoles<EPI_PLAIN>::epi * kStgWarpBytes;
+            const int avail = kRwSmemCap - 1024 - b_bytes - kRwSharedBytes - stg_bytes;
             for (int i = 0; i < 3 && !found; i++) {
                 // (head R <= 6: two rows per MMA warp at most)
                 const int R = mode == EPI_HEAD ? (pass == 0 ? 6 - 2 * i : 2 + 2 * i)
@@ -418,6 +431,7 @@ int rw_plan(const ConvArgs &a, int mode, int num_sms, RwConfig &cfg) {
                 cfg.units = units;
                 cfg.stage_bytes = stage_bytes;
                 cfg.win_tx = win_tx;
+                cfg.stg_bytes = stg_bytes;
                 cfg.stages = stages > kMaxStages ? kMaxStages : stages;
                 found = true;
             }

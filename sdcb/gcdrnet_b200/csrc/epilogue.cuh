@@ -138,6 +138,25 @@ __device__ __forceinline__ void epilogue_plain_yx(const EpiParams &ep, const Til
     }
 }
 
+// PLAIN epilogue of one warp's 32 consecutive pixels (y, x0w + lane), channels [c0, c0 + CW),
+// stored through the warp's staging buffer `stg` (32 * CW * 2 bytes): one store instruction
+// covers eight pixels' chunks instead of one chunk per lane.  Warp-collective (TMEM).
+template <int CW, class L>
+__device__ __forceinline__ void epilogue_plain_staged(const EpiParams &ep, const TileGeom &tg, int y, int x0w, int c0,
+                                                      L &ld, const float *bias, uint8_t *stg, size_t io) {
+    float v[32];
+    load_cols(ld, c0, CW, v);
+    if (y >= tg.conv_h) return;                       // (uniform over the warp: one output row)
+    __align__(16) __half h[CW];
+#pragma unroll
+    for (int k = 0; k < CW; k++) {
+        const float t = v[k] + bias[c0 + k];
+        h[k] = __float2half_rn(ep.relu ? fmaxf(t, 0.0f) : t);
+    }
+    const int lane = threadIdx.x & 31;
+    warp_store_staged<CW>(ep.out, y, x0w, c0, h, true, lane, 32, [&](int p) { return x0w + p < tg.conv_w; }, stg, io);
+}
+
 // PLAIN and PARTIAL finish the column chunks c0 = part*cw, (part + nparts)*cw, ...
 // (several warps may share a row); the LayerNorm modes need the whole row (nparts = 1).
 template <int MODE, class L>
@@ -327,6 +346,27 @@ __device__ void epilogue_pool(const EpiParams &ep, const TileGeom &tg, int y2, i
         }
         if (writer) act_store(ep.out, y2, x >> 1, n0 + c0, h, cw, io);
     }
+}
+
+// The pool epilogue of one warp's 32 conv pixels (2*y2 and 2*y2+1, x0w + lane; x0w even)
+// for channels [c0, c0 + CW): the 16 pooled pixels (y2, x0w/2 + p) are stored through the
+// warp's staging buffer.  Warp-collective (TMEM, shuffles).
+template <int CW, class L>
+__device__ __forceinline__ void epilogue_pool_staged(const EpiParams &ep, const TileGeom &tg, int y2, int x0w, int c0,
+                                                     L &top, L &bot, uint8_t *stg, size_t io) {
+    float a[32], b[32];
+    load_cols(top, c0, CW, a);
+    load_cols(bot, c0, CW, b);
+    __align__(16) __half h[CW];
+#pragma unroll
+    for (int k = 0; k < CW; k++) {
+        float v = fmaxf(a[k], b[k]);
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1)) + ep.bias_c[c0 + k];
+        h[k] = __float2half_rn(fmaxf(v, 0.0f));
+    }
+    const int lane = threadIdx.x & 31, xp0 = x0w >> 1, wp = tg.conv_w >> 1;
+    warp_store_staged<CW>(ep.out, y2, xp0, c0, h, (lane & 1) == 0, lane >> 1, 16,
+                          [&](int p) { return xp0 + p < wp; }, stg, io);
 }
 
 // dec5 window of one row-window unit in shared memory: a TMA box of C1 channels x
