@@ -152,18 +152,18 @@ __device__ __forceinline__ void act_store_borders(const Act &a, int y, int x, in
     }, false);
 }
 
-// A warp's store of up to 32 consecutive pixels (y, x0 + p), p < npix, channels [c0, c0 + CW)
-// (CW = 16 or 32 halves; pixel p's values are in lane `src_lane(p)`'s h), staged through the
-// warp's shared-memory buffer `stg` (npix * CW * 2 bytes, 16-byte aligned) so that each store
-// instruction writes contiguous 16-byte chunks of consecutive pixels instead of one pixel's
-// chunk per lane: lanes write their pixel into the buffer (chunk j of pixel p at 16-byte slot
-// j ^ f(p), f spreading a quarter-warp over all banks), then each lane stores chunks
-// q = lane, lane + 32, ... (pixel q / (CW/8)) from it.  has_px: this lane holds pixel
-// `my_p`; valid(p): pixel p is inside the image.  Reflect-border copies (LAY_PADREFL) go out
-// per lane afterwards.  Warp-collective.
-template <int CW, class Valid>
-__device__ __forceinline__ void warp_store_staged(const Act &a, int y, int x0, int c0, const __half *h, bool has_px,
-                                                  int my_p, int npix, Valid &&valid, uint8_t *stg, size_t io) {
+// A warp's store of up to 32 pixels p < npix (consecutive along a row, where the layout allows),
+// channels [c0, c0 + CW) (CW = 16 or 32 halves), staged through the warp's shared-memory buffer
+// `stg` (npix * CW * 2 bytes, 16-byte aligned) so that each store instruction writes contiguous
+// 16-byte chunks of consecutive pixels instead of one pixel's chunk per lane: lanes write their
+// pixel into the buffer (chunk j of pixel p at 16-byte slot j ^ f(p), f spreading a quarter-warp
+// over all banks), then each lane stores chunks q = lane, lane + 32, ... (pixel q / (CW/8)) from
+// it.  has_px: this lane holds pixel `my_p` in h; pix(p, y, x): pixel p's logical coordinates,
+// false when it is not stored.  Reflect-border copies (LAY_PADREFL) go out per lane afterwards.
+// Warp-collective.
+template <int CW, class Pix>
+__device__ __forceinline__ void warp_store_staged(const Act &a, int c0, const __half *h, bool has_px, int my_p,
+                                                  int npix, Pix &&pix, uint8_t *stg, size_t io) {
     constexpr int CPP = CW / 8;                       // 16-byte chunks per pixel
     constexpr int SPREAD = 8 / CPP;                   // pixels per 128 bytes
     const int lane = threadIdx.x & 31;
@@ -179,14 +179,16 @@ __device__ __forceinline__ void warp_store_staged(const Act &a, int y, int x0, i
 #pragma unroll
     for (int i = 0; i < CPP; i++) {
         const int q = i * 32 + lane, p = q / CPP, j = q - p * CPP;
-        if (p < npix && valid(p)) {
+        int y, x;
+        if (p < npix && pix(p, y, x)) {
             const int slot = j ^ ((p / SPREAD) & (CPP - 1));
             const uint4 d = *reinterpret_cast<const uint4 *>(stg + p * (CW * 2) + slot * 16);
-            *reinterpret_cast<uint4 *>(base + a.row(y, x0 + p) * a.C + c0 + 8 * j) = d;
+            *reinterpret_cast<uint4 *>(base + a.row(y, x) * a.C + c0 + 8 * j) = d;
         }
     }
     __syncwarp();                                     // the buffer is free for the next store
-    if (has_px && valid(my_p)) act_store_borders(a, y, x0 + my_p, c0, h, CW, io);
+    int y, x;
+    if (has_px && pix(my_p, y, x)) act_store_borders(a, y, x, c0, h, CW, io);
 }
 
 // Two channels (c even) by value.

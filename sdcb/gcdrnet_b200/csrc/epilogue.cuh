@@ -154,7 +154,11 @@ __device__ __forceinline__ void epilogue_plain_staged(const EpiParams &ep, const
         h[k] = __float2half_rn(ep.relu ? fmaxf(t, 0.0f) : t);
     }
     const int lane = threadIdx.x & 31;
-    warp_store_staged<CW>(ep.out, y, x0w, c0, h, true, lane, 32, [&](int p) { return x0w + p < tg.conv_w; }, stg, io);
+    warp_store_staged<CW>(ep.out, c0, h, true, lane, 32, [&](int p, int &yy, int &xx) {
+        yy = y;
+        xx = x0w + p;
+        return xx < tg.conv_w;
+    }, stg, io);
 }
 
 // PLAIN and PARTIAL finish the column chunks c0 = part*cw, (part + nparts)*cw, ...
@@ -365,8 +369,11 @@ __device__ __forceinline__ void epilogue_pool_staged(const EpiParams &ep, const 
         h[k] = __float2half_rn(fmaxf(v, 0.0f));
     }
     const int lane = threadIdx.x & 31, xp0 = x0w >> 1, wp = tg.conv_w >> 1;
-    warp_store_staged<CW>(ep.out, y2, xp0, c0, h, (lane & 1) == 0, lane >> 1, 16,
-                          [&](int p) { return xp0 + p < wp; }, stg, io);
+    warp_store_staged<CW>(ep.out, c0, h, (lane & 1) == 0, lane >> 1, 16, [&](int p, int &yy, int &xx) {
+        yy = y2;
+        xx = xp0 + p;
+        return xx < wp;
+    }, stg, io);
 }
 
 // dec5 window of one row-window unit in shared memory: a TMA box of C1 channels x
