@@ -6,6 +6,7 @@
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
+#include <thread>
 
 #include "../../../include/gcdr_cuda.h"
 #include "conv_launch.h"
@@ -181,9 +182,24 @@ Worker::~Worker() {
     if (h_errs_) cudaFreeHost(h_errs_);
     pool_.reset();
     if (flag_ev_) cudaEventDestroy(flag_ev_);
+    if (done_ev_) cudaEventDestroy(done_ev_);
     for (auto &e : band_ev_)
         if (e) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
+}
+
+cudaError_t Worker::wait_event(cudaEvent_t ev) {
+    for (;;) {
+        const cudaError_t e = cudaEventQuery(ev);
+        if (e != cudaErrorNotReady) return e;
+        std::this_thread::yield();
+    }
+}
+
+int Worker::wait_stream() {
+    cudaError_t e = cudaEventRecord(done_ev_, stream_);
+    if (e == cudaSuccess) e = wait_event(done_ev_);
+    return (int)e;
 }
 
 int Worker::fail(int code, const std::string &m) {
@@ -199,9 +215,11 @@ int Worker::init(std::string &err) {
     num_sms_ = prop.multiProcessorCount;
     if (cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking) != cudaSuccess) { err = "stream"; return GCDR_ERR_DEVICE; }
     if (cudaMallocHost(&h_err_, sizeof(int)) != cudaSuccess) { err = "pinned alloc"; return GCDR_ERR_OOM; }
-    if (cudaEventCreateWithFlags(&flag_ev_, cudaEventDisableTiming) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
+    const unsigned evf = cudaEventDisableTiming;
+    if (cudaEventCreateWithFlags(&flag_ev_, evf) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
     for (auto &e : band_ev_)
-        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
+        if (cudaEventCreateWithFlags(&e, evf) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
+    if (cudaEventCreateWithFlags(&done_ev_, evf) != cudaSuccess) { err = "event"; return GCDR_ERR_DEVICE; }
     if (cudaMallocHost(&h_errs_, sizeof(int) * kMaxBatch) != cudaSuccess) { err = "pinned alloc"; return GCDR_ERR_OOM; }
     pool_ = std::make_unique<HostPool>(kHostBands - 1, device_);
     const char *g = std::getenv("GCDR_CUDA_GRAPH");
@@ -909,7 +927,7 @@ int Worker::bind(int w, int h, int fmt, int nimg) {
     ++tick_;
     if (bound_ && w == w_ && h == h_ && fmt == fmt_ && plan_debug_ == debug_ && nimg_ == nimg) return GCDR_OK;
     if (cudaSetDevice(device_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "cudaSetDevice");
-    if (cudaStreamSynchronize(stream_) != cudaSuccess) return fail(GCDR_ERR_DEVICE, "stream sync");
+    if (wait_stream() != cudaSuccess) return fail(GCDR_ERR_DEVICE, "stream sync");
     // the shape's plan may be cached: swap it in, graph and all
     for (size_t i = 0; i < cache_.size(); i++) {
         ShapePlan &p = cache_[i];
@@ -1015,7 +1033,7 @@ int Worker::enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8
         // device error its contents are unspecified; the retry reads the untouched source)
         if (e == cudaSuccess)
             e = cudaMemcpy2DAsync(dst, dst_stride, d_dst_, row, row, h, cudaMemcpyDeviceToHost, stream_);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+        if (e == cudaSuccess) e = (cudaError_t)wait_stream();
         if (e != cudaSuccess) {
             cudaStreamSynchronize(stream_);
             return fail(GCDR_ERR_DEVICE, std::string("CUDA error: ") + cudaGetErrorString(e));
@@ -1031,7 +1049,7 @@ int Worker::enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8
             if (e == cudaSuccess) e = cudaEventRecord(band_ev_[b], stream_);
         }
     }
-    if (e == cudaSuccess) e = cudaEventSynchronize(flag_ev_);
+    if (e == cudaSuccess) e = wait_event(flag_ev_);
     if (e != cudaSuccess) {
         cudaStreamSynchronize(stream_);
         return fail(GCDR_ERR_DEVICE, std::string("CUDA error: ") + cudaGetErrorString(e));
@@ -1045,14 +1063,14 @@ int Worker::enhance_host(const uint8_t *src, int w, int h, int src_stride, uint8
     if (direct_out) {
         // page-locked destination overlapping the source (in place): DMA once the flag is clean
         e = cudaMemcpy2DAsync(dst, dst_stride, d_dst_, row, row, h, cudaMemcpyDeviceToHost, stream_);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+        if (e == cudaSuccess) e = (cudaError_t)wait_stream();
         return e == cudaSuccess ? GCDR_OK : fail(GCDR_ERR_DEVICE, "D2H copy failed");
     }
     std::atomic<int> down_fail{0};
     pool_->run(kHostBands, [&](int b) {
         int y0, y1;
         band(b, y0, y1);
-        if (cudaEventSynchronize(band_ev_[b]) != cudaSuccess) {
+        if (wait_event(band_ev_[b]) != cudaSuccess) {
             down_fail = 1;
             return;
         }
@@ -1120,7 +1138,7 @@ int Worker::enhance_host_batch(const uint8_t *const *src, int n, int w, int h, i
         e = cudaMemcpyAsync(h_errs_ + k, slices_[k].d_err, sizeof(int), cudaMemcpyDeviceToHost, stream_);
     for (int k = 0; k < n && e == cudaSuccess; k++)
         e = cudaMemcpyAsync(h_dst_ + (size_t)k * img, slices_[k].d_dst, img, cudaMemcpyDeviceToHost, stream_);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+    if (e == cudaSuccess) e = (cudaError_t)wait_stream();
     if (e != cudaSuccess) {
         cudaStreamSynchronize(stream_);
         return fail(GCDR_ERR_DEVICE, std::string("CUDA error: ") + cudaGetErrorString(e));

@@ -185,6 +185,12 @@ private:
     size_t pin_bytes_ = 0;
     std::unique_ptr<HostPool> pool_;
     cudaEvent_t flag_ev_ = nullptr, band_ev_[kHostBands] = {};
+    // the host-buffer calls wait by polling their events and yielding the core between polls:
+    // as quick as a spin when the host has cores to spare, and no core held when several
+    // workers per process and processes per host wait at once
+    cudaEvent_t done_ev_ = nullptr;
+    int wait_stream();                          // records done_ev_ on the worker's stream, waits
+    static cudaError_t wait_event(cudaEvent_t ev);
     // ops and graph
     std::vector<std::function<int(cudaStream_t)>> ops_;
     std::vector<OpInfo> info_;
