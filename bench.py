@@ -18,8 +18,10 @@ rank 0:
             documents (each enqueued C3_PASSES times per GPU) drained from one shared
             host queue (sdcb/gcdrnet_b200/dp.py) by every GPU process, each
             with E2E_THREADS threads calling GcdrEnhancer.enhance (one document a
-            call; the enhancer runs concurrent calls as batched launches) or, with
-            E2E_BATCH > 1, enhance_batch, on host buffers (two shared, page-locked
+            call; the enhancer runs concurrent calls as batched launches) when the
+            host has at least E2E_CPUS_PER_GPU cores per GPU process, else with
+            E2E_THREADS_LEAN threads calling enhance_batch with up to E2E_BATCH
+            documents (fewer caller threads where cores are few), on host buffers (two shared, page-locked
             host pools: H2D, graph, D2H per image), host monotonic clock from
             the common start to the last rank's finish; plus the single-thread
             milliseconds per image of GcdrEnhancer.enhance (the API's latency,
@@ -77,9 +79,12 @@ def launch_traffic(op: str):
     if t is not None:
         return t * BATCH, f"{os.path.relpath(TRAFFIC_TABLE, ROOT)} (one image) x {BATCH}"
     return None, None
-E2E_THREADS = 24  # concurrent callers per GPU process in the end-to-end measurement (3 batches of 8 in flight)
-E2E_BATCH = 1     # documents per call: 1 = GcdrEnhancer.enhance (the reference's call; the enhancer
-                  # batches concurrent calls), > 1 = enhance_batch (fewer at the end of the queue)
+E2E_THREADS = 24  # concurrent enhance() callers per GPU process in the end-to-end measurement (3 batches
+                  # of 8 in flight: the enhancer batches concurrent calls)
+E2E_CPUS_PER_GPU = 8   # below this many host cores per GPU process (8 GPUs on a 32-core share: 4),
+E2E_THREADS_LEAN = 4   # E2E_THREADS_LEAN threads call enhance_batch with
+E2E_BATCH = 4          # up to E2E_BATCH documents each instead (24 callers per process measured 6662
+                       # images/s on eight GPUs with 4 cores each, host-bound)
 C3_IMAGES = 512   # the end-to-end workload: documents drained from the shared host queue,
 C3_PASSES = 3     # every document enqueued this many times per GPU: 1536 images per GPU process, so the
                   # timed drain lasts about a second at every N (weak scaling, as `value`)
@@ -506,7 +511,9 @@ def main():
     # into a shared host pool.  Wall clock from the common start (a barrier) to the last rank's
     # finish, on the host's monotonic clock (one clock for all ranks).
     enh = GcdrEnhancer.from_files(GC, DR, device=local)
-    warm_sizes = [8, 4, 2, 1] if E2E_BATCH == 1 else list(range(E2E_BATCH, 0, -1))
+    per_call = 1 if host_threads() // world >= E2E_CPUS_PER_GPU else E2E_BATCH
+    callers = E2E_THREADS if per_call == 1 else E2E_THREADS_LEAN
+    warm_sizes = [8, 4, 2, 1] if per_call == 1 else list(range(per_call, 0, -1))
     host_dst = [[np.empty(nbytes, np.uint8) for _ in range(max(warm_sizes))] for _ in range(4)]
 
     def warm(k: int):
@@ -550,10 +557,10 @@ def main():
     barrier()
     torch.cuda.synchronize(dev)
     t0 = time.monotonic()
-    if E2E_BATCH == 1:
-        did = dp.drain(queue, work_one, E2E_THREADS)
+    if per_call == 1:
+        did = dp.drain(queue, work_one, callers)
     else:
-        did = dp.drain(queue, work, E2E_THREADS, batch=E2E_BATCH)
+        did = dp.drain(queue, work, callers, batch=per_call)
     e2e_calls, e2e_launches = enh.batch_stats
     t1 = time.monotonic()
     barrier()
@@ -643,19 +650,19 @@ def main():
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": nbytes,
                     "d2h_bytes_per_step": nbytes, "step": "one image",
                     "api": ("GcdrEnhancer.enhance, one document per call (concurrent calls batched by the "
-                            "enhancer" if E2E_BATCH == 1 else
-                            f"GcdrEnhancer.enhance_batch, up to {E2E_BATCH} documents per call") +
+                            "enhancer" if per_call == 1 else
+                            f"GcdrEnhancer.enhance_batch, up to {per_call} documents per call") +
                            "; host buffers: shared host pool in, shared host pool out)",
                     "enhance_calls": e2e_calls, "worker_launches": e2e_launches,
                     "workload": f"{C3_IMAGES} 1600x1152 Bgr24 documents (seeds 0-{C3_IMAGES - 1}), each enqueued "
                                 f"{C3_PASSES * world} times, drained from one shared host queue by {world} GPU process(es), "
-                                f"{E2E_THREADS} calling threads each",
+                                f"{callers} calling threads each",
                     "seconds": e2e_s, "per_rank_images": per_rank, "per_rank_ms": per_rank_ms,
                     "ranks_seen": ranks_seen, "host_cpus": host_threads(),
                     "pools_page_locked": len(pinned_pools) == 2, "pool_dir": os.path.dirname(pool_in.path),
                     "page_lock_error": pin_error,
                     "images_done": ndone, "requeued": requeued, "check": c3_check,
-                    "host_threads": E2E_THREADS, "single_thread_ms_per_image": e2e_single_ms,
+                    "host_threads": callers, "single_thread_ms_per_image": e2e_single_ms,
                     "single_thread_ms_per_image_page_locked": pinned_single_ms},
             "roofline": {"kernel": name, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak, "images_per_launch": BATCH, "traffic": traffic,
