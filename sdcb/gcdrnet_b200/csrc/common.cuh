@@ -211,6 +211,9 @@ struct ShiftSpec {
     // > 0 when group g covers [g*gs, min((g+1)*gs, C)) (ONNX Split into equal
     // ceil-sized chunks): the group of a channel is one division
     int gs = 0;
+    // 1 when a group is narrower than 8 channels (a chunk of 8 may then span three
+    // groups; the scatters fall back to channel pairs)
+    int narrow = 0;
 };
 
 // Group of channel c (-1 past the last group).

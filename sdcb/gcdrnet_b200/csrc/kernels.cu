@@ -210,23 +210,33 @@ __device__ __forceinline__ float2 gelu_exact2(float2 v) {
 }
 
 // out = shiftW(gelu(dw(in))): depthwise 3x3 (zero pad 1) + bias + exact GELU,
-// then the W shift that precedes fc2 (gc#95-126) as a scatter: channel group g
-// of pixel x goes to column x - off_g, and a source whose destination falls
-// outside the row writes the zero that its wrapped column must receive (each
-// output element is written exactly once).  A thread computes one 8-channel
-// chunk of PX consecutive pixels (x..x+PX-1) from a 3 x (PX+2) input window; each
-// tap's eight weights are read once from shared memory (tap-major [9][C] fp32)
-// and serve all PX pixels (PX = 2 for the small layers, where parallelism counts,
-// 4 for the large ones, where one wave of 128-thread blocks must hold the layer).  Only the stores of chunks that straddle a group
-// boundary split.  A flat grid of 128-thread blocks over (row, quad, chunk): no
-// partly empty block per row, and seven blocks per SM hold a /8 layer in one wave.
-// The tap sums and the GELU run on packed channel pairs (FFMA2), lane by lane as fmaf.
+// then the W shift that precedes fc2 (gc#95-126), applied as a gather: channel c
+// of output pixel x is the activation of source pixel x + off_g(c) (zero when
+// that column lies outside the row).  A thread computes one 8-channel chunk of
+// two consecutive output pixels (x, x+1): the chunk's channels [0, split) belong
+// to one shift group (offset offa), the rest, when the chunk straddles a group
+// boundary, to the next (offb).  Each row of the 3x3 window is read as four source
+// columns at offset offa and, for a straddling chunk, four more at offset offb;
+// one byte permutation per 32-bit word merges the two into the columns the chunk's
+// channels read, so every output chunk is one 16-byte store (a scatter splits the
+// straddling chunks into per-channel stores).  Each tap's eight weights are read
+// once from shared memory (tap-major [9][C] fp32) and serve both pixels.  (Four
+// pixels per thread measured no faster: the kernel is bound by the latency of its
+// loads, and the wider window spills registers.)  A flat grid of 128-thread blocks
+// over (row, pixel pair, chunk): no partly empty block per row.  The tap sums (in
+// the order ky, kx) and the GELU run on packed channel pairs (FFMA2), lane by lane
+// as fmaf.
 constexpr int kDwMaxC = 512;
+constexpr int kDwPx = 2;   // output pixels per thread
 
-template <int PX>
+__device__ __forceinline__ uint4 dw_col(const __half *rowp, int xx, int W, int C) {
+    return (xx >= 0 && xx < W) ? *reinterpret_cast<const uint4 *>(rowp + (size_t)xx * C) : make_uint4(0, 0, 0, 0);
+}
+
 __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in, int H, int W, int C, const float *wt,
                                                             const float *b, const ShiftSpec s, __half *out,
                                                             long long img_bytes) {
+    constexpr int PX = kDwPx;
     extern __shared__ __align__(16) float ws[];   // [9][C]
     // the weights are constant: staged before the wait on the previous kernel
     for (int i = threadIdx.x * 4; i < 9 * C; i += blockDim.x * 4)
@@ -234,13 +244,25 @@ __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in,
     __syncthreads();
     pdl_wait();
     const int chunks = C >> 3;
-    const int Wq = (W + PX - 1) / PX;                  // pixel groups per row
+    const int Wq = (W + PX - 1) / PX;                  // pixel pairs per row
     const int per_row = Wq * chunks;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int y = i / per_row, t = i - y * per_row;
     if (y < H) {
         const int xq = t / chunks, ch = t - xq * chunks;
         const int x = PX * xq, c0 = ch * 8;
+        // shift groups of the chunk: channels [0, split) offset offa, [split, 8) offb
+        // (the launcher checks that no chunk spans three groups)
+        const int ga = shift_group(s, c0), gb = shift_group(s, c0 + 7);
+        const int offa = ga >= 0 ? s.offs[ga] : 0, offb = gb >= 0 ? s.offs[gb] : 0;
+        const int split = ga == gb ? 8 : s.ends[ga] - c0;
+        const bool straddle = split < 8;
+        // per 32-bit word (a channel pair): its low and high halves from the offa
+        // column (bytes 0-3 of the permutation) or the offb column (bytes 4-7)
+        uint32_t sel[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            sel[k] = (2 * k < split ? 0x10u : 0x54u) | ((2 * k + 1 < split ? 0x32u : 0x76u) << 8);
         float2 acc[PX][4];   // channel pairs (c0 + 2i, c0 + 2i + 1): packed FFMA2, per lane as fmaf
         {
             const float4 b0 = __ldg(reinterpret_cast<const float4 *>(b + c0));
@@ -272,9 +294,15 @@ __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in,
             const __half *rowp = col + (size_t)yy * W * C;
 #pragma unroll
             for (int j = 0; j < PX + 2; j++) {
-                const int xx = x - 1 + j;             // pixel x + p uses columns x + p - 1 .. x + p + 1
-                if (xx < 0 || xx >= W) continue;
-                const uint4 raw = *reinterpret_cast<const uint4 *>(rowp + (size_t)xx * C);
+                // window column j: output pixel x + p reads it at tap kx = j - p, from source
+                // column x + j - 1 + off (zero outside the row: the conv's zero padding)
+                const uint4 ra = dw_col(rowp, x + j - 1 + offa, W, C);
+                const uint4 rb = straddle ? dw_col(rowp, x + j - 1 + offb, W, C) : ra;
+                uint4 raw;
+                raw.x = __byte_perm(ra.x, rb.x, sel[0]);
+                raw.y = __byte_perm(ra.y, rb.y, sel[1]);
+                raw.z = __byte_perm(ra.z, rb.z, sel[2]);
+                raw.w = __byte_perm(ra.w, rb.w, sel[3]);
                 const __half2 *hv = reinterpret_cast<const __half2 *>(&raw);
                 float2 f[4];
 #pragma unroll
@@ -288,13 +316,13 @@ __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in,
                 }
             }
         }
-        const int ga = shift_group(s, c0), gb = shift_group(s, c0 + 7);
-        const int offa = ga >= 0 ? s.offs[ga] : 0, offb = gb >= 0 ? s.offs[gb] : 0;
-        const int split = ga == gb ? 8 : s.ends[ga] - c0;   // channels [0, split) shift by offa, the rest offb
         __half *rowo = img_at(out, io) + (size_t)y * W * C + c0;
 #pragma unroll
         for (int p = 0; p < PX; p++) {
             if (x + p >= W) break;
+            // a channel whose source column lies outside the row receives zero
+            const bool va = x + p + offa >= 0 && x + p + offa < W;
+            const bool vb = x + p + offb >= 0 && x + p + offb < W;
             __align__(16) __half o[8];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
@@ -302,19 +330,13 @@ __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in,
                 o[2 * i] = __float2half_rn(g.x);
                 o[2 * i + 1] = __float2half_rn(g.y);
             }
-            bool za, zb;
-            const int da = shift_dest(x + p, offa, W, &za);
-            if (split == 8) {
-                if (za) *reinterpret_cast<uint4 *>(rowo + (size_t)da * C) = make_uint4(0, 0, 0, 0);
-                else *reinterpret_cast<uint4 *>(rowo + (size_t)da * C) = *reinterpret_cast<const uint4 *>(o);
-            } else {
-                const int db = shift_dest(x + p, offb, W, &zb);
+            if (!va || !vb) {
                 const __half zero = __float2half_rn(0.0f);
-                for (int k = 0; k < 8; k++) {
-                    if (k < split) rowo[(size_t)da * C + k] = za ? zero : o[k];
-                    else rowo[(size_t)db * C + k] = zb ? zero : o[k];
-                }
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if (k < split ? !va : !vb) o[k] = zero;
             }
+            *reinterpret_cast<uint4 *>(rowo + (size_t)(x + p) * C) = *reinterpret_cast<const uint4 *>(o);
         }
     }
     pdl_trigger();
@@ -390,16 +412,62 @@ __device__ __forceinline__ uint4 pack8h(const float *v) {
     return u;
 }
 
+__device__ __forceinline__ uint32_t word_of(const uint4 &u, int i) {
+    return i == 0 ? u.x : i == 1 ? u.y : i == 2 ? u.z : u.w;
+}
+
+// Halves [0, n) (0 < n < 8) of the packed chunk u to dst (16-byte aligned): one
+// naturally aligned store each of 4, 2 and 1 halves, as n's bits ask.
+__device__ __forceinline__ void store_prefix(__half *dst, const uint4 &u, int n) {
+    int k = 0;
+    if (n & 4) {
+        *reinterpret_cast<uint2 *>(dst) = make_uint2(u.x, u.y);
+        k = 4;
+    }
+    if (n & 2) {
+        *reinterpret_cast<uint32_t *>(dst + k) = word_of(u, k >> 1);
+        k += 2;
+    }
+    if (n & 1) *reinterpret_cast<unsigned short *>(dst + k) = (unsigned short)(word_of(u, k >> 1) & 0xFFFFu);
+}
+
+// Halves [n, 8) (0 < n < 8) of the packed chunk u to dst + n (dst 16-byte aligned).
+__device__ __forceinline__ void store_suffix(__half *dst, const uint4 &u, int n) {
+    int k = n;
+    if (k & 1) {
+        *reinterpret_cast<unsigned short *>(dst + k) = (unsigned short)(word_of(u, k >> 1) >> 16);
+        k++;
+    }
+    if (k & 2) {
+        *reinterpret_cast<uint32_t *>(dst + k) = word_of(u, k >> 1);
+        k += 2;
+    }
+    if (k & 4) *reinterpret_cast<uint2 *>(dst + k) = make_uint2(u.z, u.w);
+}
+
 // H-shift scatter of channels [c0, c0+8) of token pixel (y, x) of a LAY_PLAIN
-// tensor: one 16-byte store when the chunk lies in one channel group.
+// tensor: one 16-byte store when the chunk lies in one channel group; a chunk
+// across a group boundary goes out as its two parts, each in at most three
+// aligned stores (groups narrower than a chunk: per channel pair).
 __device__ __forceinline__ void shift_store8(const Act &a, const ShiftSpec &s, int y, int x, int c0, const float *v,
                                              size_t io) {
     const int g0 = shift_group(s, c0), g7 = shift_group(s, c0 + 7);
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    __half *base = img_at(a.p, io);
     if (g0 == g7) {
         int dy = y;
         bool z = false;
         if (g0 >= 0) dy = shift_dest(y, s.offs[g0], a.H, &z);
-        *reinterpret_cast<uint4 *>(img_at(a.p, io) + ((size_t)dy * a.W + x) * a.C + c0) = z ? make_uint4(0, 0, 0, 0) : pack8h(v);
+        *reinterpret_cast<uint4 *>(base + ((size_t)dy * a.W + x) * a.C + c0) = z ? zero : pack8h(v);
+    } else if (!s.narrow) {
+        // channels [c0, ends[g0]) in group g0 (g0 >= 0 here), the rest in g7 (-1: unshifted)
+        const uint4 u = pack8h(v);
+        const int split = s.ends[g0] - c0;
+        bool za, zb = false;
+        const int da = shift_dest(y, s.offs[g0], a.H, &za);
+        const int db = g7 >= 0 ? shift_dest(y, s.offs[g7], a.H, &zb) : y;
+        store_prefix(base + ((size_t)da * a.W + x) * a.C + c0, za ? zero : u, split);
+        store_suffix(base + ((size_t)db * a.W + x) * a.C + c0, zb ? zero : u, split);
     } else {
 #pragma unroll
         for (int k = 0; k < 4; k++) shift_store2(a, s, 2, y, x, c0 + 2 * k, v[2 * k], v[2 * k + 1], io);
@@ -761,19 +829,21 @@ int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *wt,
                          __half *out, cudaStream_t st, int nimg, long long img_bytes) {
     if (C % 8 || C > kDwMaxC) return -2;
     if (nimg < 1 || nimg > 65535 || (nimg > 1 && (img_bytes <= 0 || img_bytes % 16))) return -2;
-    static const int nsm = [] {
-        int d = 0, n = 148;
-        if (cudaGetDevice(&d) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
-        return n;
-    }();
-    const int blocks2 = grid_for((long long)((W + 1) / 2) * (C / 8) * H, 128);
-    const size_t smem = (size_t)9 * C * sizeof(float);
-    if ((long long)blocks2 * nimg <= 7 * nsm)
-        launch_pdl(dw_gelu_shift_kernel<2>, dim3(blocks2, nimg), dim3(128), smem, st, in, H, W, C, wt, b, s, out,
-                   img_bytes);
-    else
-        launch_pdl(dw_gelu_shift_kernel<4>, dim3(grid_for((long long)((W + 3) / 4) * (C / 8) * H, 128), nimg), dim3(128),
-                   smem, st, in, H, W, C, wt, b, s, out, img_bytes);
+    // the kernel gives a chunk of 8 channels at most two shift groups (a group boundary
+    // inside it): shift groups that put three into one chunk are rejected
+    for (int c0 = 0; c0 < C; c0 += 8) {
+        auto group = [&](int c) {
+            for (int g = 0; g < s.ngroups; g++)
+                if (c < s.ends[g]) return g;
+            return -1;
+        };
+        const int ga = group(c0), gb = group(c0 + 7);
+        for (int c = c0; c < c0 + 8; c++)
+            if (group(c) != ga && group(c) != gb) return -2;
+    }
+    const int blocks = grid_for((long long)((W + kDwPx - 1) / kDwPx) * (C / 8) * H, 128);
+    launch_pdl(dw_gelu_shift_kernel, dim3(blocks, nimg), dim3(128), (size_t)9 * C * sizeof(float), st, in, H, W, C,
+               wt, b, s, out, img_bytes);
     return launch_status();
 }
 

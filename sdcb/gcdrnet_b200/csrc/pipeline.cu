@@ -41,6 +41,8 @@ ShiftSpec make_shift(int ngroups, const int *ends, const int *offs) {
         for (int i = 0; i < o.ngroups - 1; i++) uniform = uniform && o.ends[i] == (i + 1) * gs;
         uniform = uniform && o.ends[o.ngroups - 1] > (o.ngroups - 1) * gs && o.ends[o.ngroups - 1] <= o.ngroups * gs;
         o.gs = uniform ? gs : 0;
+        for (int i = 0; i < o.ngroups; i++)
+            if (o.ends[i] - (i ? o.ends[i - 1] : 0) < 8) o.narrow = 1;
     }
     return o;
 }

@@ -87,6 +87,82 @@ def test_dw_gelu_shift_matches_oracle(nets, case):
     _close(got, want, f"dw_gelu_shift {case}")
 
 
+# (ends, offs): W-shift groups whose boundaries fall inside 8-channel chunks, with
+# offsets far apart (the gather reads each part of a chunk at its own offset)
+STRADDLE_SHIFTS = [([5, 19, 24], [3, -2, 1]), ([12, 20, 24], [-4, 0, 6]), ([8, 16, 24], [9, -9, 0])]
+
+
+@pytest.mark.parametrize("shift", STRADDLE_SHIFTS, ids=lambda s: "ends%s_offs%s" % tuple("_".join(map(str, v)) for v in s))
+def test_dw_shift_straddling_groups(shift):
+    import torch
+    from sdcb.gcdrnet_b200 import lib
+    L = lib()
+    ends, offs = shift
+    H, W, C = 5, 13, 24
+    rng = np.random.default_rng(sum(ends) + 7 * sum(offs))
+    x = _f16(rng.standard_normal((H, W, C)).astype(np.float32))
+    w = (rng.standard_normal((C, 1, 3, 3)) * 0.5).astype(np.float32)
+    b = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    want = O.shift(O.gelu(O.dwconv3x3(x, w, b)), 3, ends, offs)
+    wt = np.ascontiguousarray(w.reshape(C, 9).T)
+    out = torch.full((H, W, C), float("nan"), dtype=torch.float16, device="cuda:0")
+    dx, dwt, db = _dev(x, torch.float16), _dev(wt), _dev(b)
+    sh = Shift.of(ends, offs)
+    assert L.gcdr_k_dw_gelu_shift(dx.data_ptr(), H, W, C, dwt.data_ptr(), db.data_ptr(), ctypes.byref(sh),
+                                  out.data_ptr(), None) == 0
+    got = out.float().cpu().numpy()
+    assert not np.isnan(got).any(), "unwritten outputs"
+    _close(got, want, f"dw_gelu_shift {shift}")
+
+
+def test_dw_shift_rejects_three_groups_in_a_chunk():
+    """The depthwise gather gives a chunk of 8 channels two shift groups at most."""
+    import torch
+    from sdcb.gcdrnet_b200 import lib
+    L = lib()
+    H, W, C = 2, 4, 16
+    x = torch.zeros((H, W, C), dtype=torch.float16, device="cuda:0")
+    wt = torch.zeros((9, C), dtype=torch.float32, device="cuda:0")
+    b = torch.zeros(C, dtype=torch.float32, device="cuda:0")
+    sh = Shift.of([3, 6, 16], [1, 0, -1])
+    assert L.gcdr_k_dw_gelu_shift(x.data_ptr(), H, W, C, wt.data_ptr(), b.data_ptr(), ctypes.byref(sh),
+                                  x.data_ptr(), None) == 1
+
+
+# (ends, offs) of H-shift groups for the token join's LayerNorm scatter: boundaries
+# inside chunks (a chunk's two parts stored apart), and groups narrower than a chunk
+JOIN_SHIFTS = [([5, 19, 27, 40], [2, -1, 0, -2]), ([3, 6, 11, 30, 40], [2, 1, 0, -1, -2]),
+               ([13, 26, 40], [-3, 4, 1])]
+
+
+@pytest.mark.parametrize("shift", JOIN_SHIFTS, ids=lambda s: "ends%s" % "_".join(map(str, s[0])))
+def test_join_ln_shift_groups(shift):
+    import torch
+    from sdcb.gcdrnet_b200 import lib
+    L = lib()
+    ends, offs = shift
+    H, W, C = 8, 6, 40
+    rng = np.random.default_rng(sum(ends))
+    d = _f16(rng.standard_normal((H // 2, W // 2, C)).astype(np.float32))
+    skip = _f16(rng.standard_normal((H, W, C)).astype(np.float32))
+    g = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    bb = (0.1 * rng.standard_normal(C)).astype(np.float32)
+    want = O.add(O.relu(O.resize2x(d)), skip)
+    want_h = O.shift(O.layernorm(_f16(want), g, bb), 2, ends, offs)
+    dd, dskip = _dev(d, torch.float16), _dev(skip, torch.float16)
+    sk = Act(dskip.data_ptr(), H, W, C, 0)
+    out = torch.full((H * W * C,), float("nan"), dtype=torch.float16, device="cuda:0")
+    h = torch.full((H * W * C,), float("nan"), dtype=torch.float16, device="cuda:0")
+    oa = Act(out.data_ptr(), H, W, C, 0)
+    sh = Shift.of(ends, offs)
+    dg, db = _dev(g), _dev(bb)
+    assert L.gcdr_k_up_add(dd.data_ptr(), ctypes.byref(sk), ctypes.byref(oa), dg.data_ptr(), db.data_ptr(),
+                           ctypes.c_float(1e-5), ctypes.byref(sh), h.data_ptr(), None) == 0
+    got_h = h.float().cpu().numpy().reshape(H, W, C)
+    assert not np.isnan(got_h).any(), "unwritten outputs"
+    _close(got_h, want_h, f"join LN2 + H shift {shift}")
+
+
 # (net, block, H, W, skip layout, kind of join): the decoder joins at small grids
 JOIN_CASES = [("gc", "dblock1", 6, 10, 2, "tok"), ("dr", "dblock1", 4, 6, 2, "tok"),
               ("gc", "dblock2", 8, 14, 2, "tok"), ("dr", "dblock2", 10, 4, 2, "tok"),
