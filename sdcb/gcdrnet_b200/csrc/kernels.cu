@@ -342,6 +342,148 @@ __global__ void __launch_bounds__(128, 7) dw_gelu_shift_kernel(const __half *in,
     pdl_trigger();
 }
 
+// Tiled form of the same operator: a block computes R output rows x 2*TP pixels x CS
+// 8-channel chunks (TP * CS = 256 threads, two pixels of one chunk per thread and
+// row).  The block's input rows y0-1 .. y0+R, the columns its gather reads (its pixels
+// widened by the 3x3 halo and the layer's shift offsets) and its chunks are first
+// copied into shared memory with cp.async (16 bytes a copy, zero-filled outside the
+// image: the conv's zero padding), all of the block's copies in flight at once; the
+// taps then read shared memory.  The direct form above reads every input row once for
+// each output row that uses it, from L2, with the latency of its loads exposed.  The
+// arithmetic (tap order, GELU, zero fill) is the direct form's, so both give the same
+// bits.  Weights: [tap][half][chunk][4] fp32 in shared memory, so that the eight lanes
+// of a shared-memory phase read 128 consecutive bytes.
+struct DwTile {
+    int R = 4;              // output rows per block
+    int lcs = 4;            // log2 of the chunks per block (CS = 4, 8 or 16)
+    int span = 0;           // tile columns: 2 * TP + 2 + (hi - lo)
+    int lo = 0;             // lowest shift offset of the layer (<= 0)
+    int ntx = 0, nty = 0;   // column and row tiles of one image (the slabs multiply them)
+};
+
+__global__ void __launch_bounds__(256, 3) dw_tile_kernel(const __half *in, int H, int W, int C, const float *wt,
+                                                      const float *b, const ShiftSpec s, __half *out,
+                                                      long long img_bytes, const DwTile tl) {
+    constexpr int PX = kDwPx;
+    extern __shared__ __align__(16) uint8_t dsm[];
+    const int CS = 1 << tl.lcs, TW = PX * (256 >> tl.lcs);
+    const int tx = blockIdx.x % tl.ntx, rest = blockIdx.x / tl.ntx;
+    const int ty = rest % tl.nty, slab = rest / tl.nty;
+    const int y0 = ty * tl.R, x0 = tx * TW, cs0 = slab * CS * 8;      // first channel of the slab
+    float4 *ws = reinterpret_cast<float4 *>(dsm);                       // [9][2][CS] float4
+    uint4 *tile = reinterpret_cast<uint4 *>(dsm + (size_t)9 * 2 * CS * sizeof(float4));   // [R+2][span][CS]
+    // the weights are constant: staged before the wait on the previous kernel
+    for (int i = threadIdx.x; i < 9 * 2 * CS; i += blockDim.x) {
+        const int th = i >> tl.lcs, ch = i & (CS - 1);
+        ws[i] = __ldg(reinterpret_cast<const float4 *>(wt + (th >> 1) * C + cs0 + ch * 8 + (th & 1) * 4));
+    }
+    pdl_wait();
+    const size_t io = (size_t)blockIdx.y * (size_t)img_bytes;   // this block's image
+    const __half *src = img_at(in, io);
+    const int rowc = tl.span << tl.lcs;                          // copies per tile row
+    for (int r = 0; r < tl.R + 2; r++) {
+        const int gy = y0 - 1 + r;
+        for (int j = threadIdx.x; j < rowc; j += blockDim.x) {
+            const int gx = x0 + tl.lo - 1 + (j >> tl.lcs);
+            const bool ok = gy >= 0 && gy < H && gx >= 0 && gx < W;
+            const __half *g = ok ? src + ((size_t)gy * W + gx) * C + cs0 + (j & (CS - 1)) * 8 : src;
+            const uint32_t d = (uint32_t)__cvta_generic_to_shared(tile + (size_t)r * rowc + j);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(g), "r"(ok ? 16 : 0)
+                         : "memory");
+        }
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+
+    const int ch = threadIdx.x & (CS - 1), pr = threadIdx.x >> tl.lcs;
+    const int x = x0 + PX * pr, c0 = cs0 + ch * 8;
+    if (x < W) {
+        const int ga = shift_group(s, c0), gb = shift_group(s, c0 + 7);
+        const int offa = ga >= 0 ? s.offs[ga] : 0, offb = gb >= 0 ? s.offs[gb] : 0;
+        const int split = ga == gb ? 8 : s.ends[ga] - c0;
+        const bool straddle = split < 8;
+        uint32_t sel[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            sel[k] = (2 * k < split ? 0x10u : 0x54u) | ((2 * k + 1 < split ? 0x32u : 0x76u) << 8);
+        // tile column of window column 0 (source column x - 1 + off) for either offset
+        const int ca = PX * pr + offa - tl.lo, cb = PX * pr + offb - tl.lo;
+        const float4 b0 = __ldg(reinterpret_cast<const float4 *>(b + c0));
+        const float4 b1 = __ldg(reinterpret_cast<const float4 *>(b + c0 + 4));
+        for (int r = 0; r < tl.R; r++) {
+            const int y = y0 + r;
+            if (y >= H) break;
+            float2 acc[PX][4];
+#pragma unroll
+            for (int p = 0; p < PX; p++) {
+                acc[p][0] = make_float2(b0.x, b0.y);
+                acc[p][1] = make_float2(b0.z, b0.w);
+                acc[p][2] = make_float2(b1.x, b1.y);
+                acc[p][3] = make_float2(b1.z, b1.w);
+            }
+#pragma unroll
+            for (int ky = 0; ky < 3; ky++) {
+                const int yy = y + ky - 1;
+                if (yy < 0 || yy >= H) continue;
+                float2 w[3][4];
+#pragma unroll
+                for (int kx = 0; kx < 3; kx++) {
+                    const float4 w0 = ws[((ky * 3 + kx) * 2) * CS + ch];
+                    const float4 w1 = ws[((ky * 3 + kx) * 2 + 1) * CS + ch];
+                    w[kx][0] = make_float2(w0.x, w0.y);
+                    w[kx][1] = make_float2(w0.z, w0.w);
+                    w[kx][2] = make_float2(w1.x, w1.y);
+                    w[kx][3] = make_float2(w1.z, w1.w);
+                }
+                const uint4 *trow = tile + (size_t)(r + ky) * rowc + ch;   // column c at trow[c << lcs]
+#pragma unroll
+                for (int j = 0; j < PX + 2; j++) {
+                    const uint4 ra = trow[(ca + j) << tl.lcs];
+                    const uint4 rb = straddle ? trow[(cb + j) << tl.lcs] : ra;
+                    uint4 raw;
+                    raw.x = __byte_perm(ra.x, rb.x, sel[0]);
+                    raw.y = __byte_perm(ra.y, rb.y, sel[1]);
+                    raw.z = __byte_perm(ra.z, rb.z, sel[2]);
+                    raw.w = __byte_perm(ra.w, rb.w, sel[3]);
+                    const __half2 *hv = reinterpret_cast<const __half2 *>(&raw);
+                    float2 f[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) f[i] = __half22float2(hv[i]);
+#pragma unroll
+                    for (int p = 0; p < PX; p++) {
+                        const int kx = j - p;
+                        if (kx < 0 || kx > 2) continue;
+#pragma unroll
+                        for (int i = 0; i < 4; i++) acc[p][i] = __ffma2_rn(w[kx][i], f[i], acc[p][i]);
+                    }
+                }
+            }
+            __half *rowo = img_at(out, io) + (size_t)y * W * C + c0;
+#pragma unroll
+            for (int p = 0; p < PX; p++) {
+                if (x + p >= W) break;
+                const bool va = x + p + offa >= 0 && x + p + offa < W;
+                const bool vb = x + p + offb >= 0 && x + p + offb < W;
+                __align__(16) __half o[8];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float2 g = gelu_exact2(acc[p][i]);
+                    o[2 * i] = __float2half_rn(g.x);
+                    o[2 * i + 1] = __float2half_rn(g.y);
+                }
+                if (!va || !vb) {
+                    const __half zero = __float2half_rn(0.0f);
+#pragma unroll
+                    for (int k = 0; k < 8; k++)
+                        if (k < split ? !va : !vb) o[k] = zero;
+                }
+                *reinterpret_cast<uint4 *>(rowo + (size_t)(x + p) * C) = *reinterpret_cast<const uint4 *>(o);
+            }
+        }
+    }
+    pdl_trigger();
+}
+
 __device__ __forceinline__ void bilin_coords(int Y, int n, int &a0, int &a1, float &f) {
     const float fy = ((float)Y + 0.5f) / 2.0f - 0.5f;
     const int y0 = (int)floorf(fy);
@@ -840,6 +982,44 @@ int dw_gelu_shift_launch(const __half *in, int H, int W, int C, const float *wt,
         const int ga = group(c0), gb = group(c0 + 7);
         for (int c = c0; c < c0 + 8; c++)
             if (group(c) != ga && group(c) != gb) return -2;
+    }
+    // the tiled form when the chunks split into slabs of 4, 8 or 16 and the tile fits
+    const int nchunk = C / 8;
+    DwTile tl;
+    tl.lcs = nchunk % 16 == 0 ? 4 : nchunk % 8 == 0 ? 3 : nchunk % 4 == 0 ? 2 : -1;
+    if (tl.lcs > 0) {
+        int lo = 0, hi = 0;
+        for (int g = 0; g < s.ngroups; g++) {
+            lo = std::min(lo, s.offs[g]);
+            hi = std::max(hi, s.offs[g]);
+        }
+        static const int nsm = [] {
+            int d = 0, n = 148;
+            if (cudaGetDevice(&d) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+            return n;
+        }();
+        const int CS = 1 << tl.lcs, TW = kDwPx * (256 >> tl.lcs);
+        tl.lo = lo;
+        tl.span = TW + 2 + (hi - lo);
+        tl.ntx = (W + TW - 1) / TW;
+        // four output rows a block (the tile's two halo rows cost half its loads) while
+        // that still fills the GPU with three blocks per SM; fewer for small grids
+        long long blocks = 0;
+        for (tl.R = 4;; tl.R /= 2) {
+            tl.nty = (H + tl.R - 1) / tl.R;
+            blocks = (long long)tl.ntx * tl.nty * (nchunk / CS);
+            if (tl.R == 1 || blocks * nimg >= 3LL * nsm) break;
+        }
+        const size_t smem = (size_t)9 * 2 * CS * 16 + (size_t)(tl.R + 2) * tl.span * CS * 16;
+        if (hi - lo <= 64 && smem <= 96 * 1024 && blocks < (1ll << 31)) {
+            // one cap for every launch (the attribute is per kernel and device)
+            if (cudaFuncSetAttribute(dw_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) !=
+                cudaSuccess)
+                return -1;
+            launch_pdl(dw_tile_kernel, dim3((unsigned)blocks, nimg), dim3(256), smem, st, in, H, W, C, wt, b, s, out,
+                       img_bytes, tl);
+            return launch_status();
+        }
     }
     const int blocks = grid_for((long long)((W + kDwPx - 1) / kDwPx) * (C / 8) * H, 128);
     launch_pdl(dw_gelu_shift_kernel, dim3(blocks, nimg), dim3(128), (size_t)9 * C * sizeof(float), st, in, H, W, C,

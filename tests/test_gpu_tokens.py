@@ -87,18 +87,21 @@ def test_dw_gelu_shift_matches_oracle(nets, case):
     _close(got, want, f"dw_gelu_shift {case}")
 
 
-# (ends, offs): W-shift groups whose boundaries fall inside 8-channel chunks, with
-# offsets far apart (the gather reads each part of a chunk at its own offset)
-STRADDLE_SHIFTS = [([5, 19, 24], [3, -2, 1]), ([12, 20, 24], [-4, 0, 6]), ([8, 16, 24], [9, -9, 0])]
+# (C, H, W, ends, offs): W-shift groups whose boundaries fall inside 8-channel chunks,
+# with offsets far apart (the gather reads each part of a chunk at its own offset);
+# 24 channels take the direct kernel, 64 and 96 the tiled one (slabs of 8 and 4
+# chunks, several column and row tiles), offsets 80 apart the direct one again
+STRADDLE_SHIFTS = [(24, 5, 13, [5, 19, 24], [3, -2, 1]), (24, 5, 13, [12, 20, 24], [-4, 0, 6]),
+                   (24, 5, 13, [8, 16, 24], [9, -9, 0]), (64, 9, 70, [13, 26, 39, 52, 64], [2, 1, 0, -1, -2]),
+                   (96, 7, 300, [20, 45, 70, 96], [5, -3, 0, 1]), (64, 6, 100, [30, 64], [40, -40])]
 
 
-@pytest.mark.parametrize("shift", STRADDLE_SHIFTS, ids=lambda s: "ends%s_offs%s" % tuple("_".join(map(str, v)) for v in s))
+@pytest.mark.parametrize("shift", STRADDLE_SHIFTS, ids=lambda s: "C%d_%dx%d_ends%s" % (s[0], s[1], s[2], "_".join(map(str, s[3]))))
 def test_dw_shift_straddling_groups(shift):
     import torch
     from sdcb.gcdrnet_b200 import lib
     L = lib()
-    ends, offs = shift
-    H, W, C = 5, 13, 24
+    C, H, W, ends, offs = shift
     rng = np.random.default_rng(sum(ends) + 7 * sum(offs))
     x = _f16(rng.standard_normal((H, W, C)).astype(np.float32))
     w = (rng.standard_normal((C, 1, 3, 3)) * 0.5).astype(np.float32)
