@@ -66,6 +66,9 @@ struct EpiParams {
     Act out;                         // primary output (logical dims = conv or pooled output)
     // LN modes
     const float *g1 = nullptr, *b1 = nullptr, *g2 = nullptr, *b2 = nullptr;
+    // EPI_RESLN with 3 * N <= kMaxBiasConst: g1 and b1 by value in bias_c[N, 2N) and
+    // bias_c[2N, 3N) (constant-bank operands instead of two loads per element)
+    int ln_c = 0;
     float eps1 = 1e-5f, eps2 = 1e-5f;
     Act out2;                        // EPI_LN2: LN2 output, LAY_PLAIN tokens, H-shift scatter
     ShiftSpec shift;
@@ -289,6 +292,17 @@ __device__ void epilogue_ln_row(const EpiParams &ep, const TileGeom &tg, int til
         }
     }
     const float rstd = rsqrtf(sq / N + ep.eps1);
+    if (MODE == EPI_RESLN && ep.ln_c) {
+        for (int c0 = 0; c0 < N; c0 += 32) {
+            ld.load32(c0, v);
+            __align__(16) __half h[32];
+#pragma unroll
+            for (int k = 0; k < 32; k++)
+                h[k] = __float2half_rn((v[k] - mean) * rstd * ep.bias_c[N + c0 + k] + ep.bias_c[2 * N + c0 + k]);
+            if (valid) act_store(ep.out, y, x, c0, h, 32, io);
+        }
+        return;
+    }
     float s2 = 0.f;
     for (int c0 = 0; c0 < N; c0 += 32) {
         ld.load32(c0, v);

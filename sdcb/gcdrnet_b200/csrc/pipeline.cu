@@ -624,6 +624,16 @@ int Worker::build_ops() {
                                               double bytes_override = -1) {
         a.err = errp;
         if (fill_bias_consts(a)) bias_fail_ = true;
+        // the direct LayerNorm epilogue's g1 and b1 as kernel parameters, after the bias
+        if (mode == EPI_RESLN && a.ep.g1 && a.ep.b1 && 3 * a.N <= kMaxBiasConst) {
+            if (cudaMemcpy(a.ep.bias_c + a.N, a.ep.g1, (size_t)a.N * sizeof(float), cudaMemcpyDeviceToHost) !=
+                    cudaSuccess ||
+                cudaMemcpy(a.ep.bias_c + 2 * a.N, a.ep.b1, (size_t)a.N * sizeof(float), cudaMemcpyDeviceToHost) !=
+                    cudaSuccess)
+                bias_fail_ = true;
+            else
+                a.ep.ln_c = 1;
+        }
         // split-K and the LayerNorm path fix the order of the sums: decided for one image
         // (a.nimg is 1 here), so that a batch plan gives every image the bytes of a single-
         // image plan; N slices change no sum and are sized for the whole launch
